@@ -1,0 +1,114 @@
+// common.cuh -- shared device helpers for the B200 graft route/mount library.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <mutex>
+#include <string>
+
+#include "../../include/grm_b200.h"
+
+namespace grm_b200 {
+
+constexpr unsigned kFull = 0xFFFFFFFFu;
+constexpr uint32_t kNoRow = 0xFFFFFFFFu;
+
+// Status codes (include/grm_b200.h).
+inline int cuda_status(cudaError_t e) { return e == cudaSuccess ? 0 : GRM_B200_CUDA_BASE + (int)e; }
+
+// Handle-less error text, one per thread.
+void set_thread_error(const char* fmt, ...);
+
+// Per-handle error text.
+struct ErrorSlot {
+  std::string text;
+  int set(int rc, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    text = buf;
+    return rc;
+  }
+};
+
+// score_node_better (GraftRepository cpp/grm_runtime.cpp:75-82): score desc,
+// then row id asc.  Float comparison semantics, so -0 == +0.
+__device__ __forceinline__ bool better(float sa, uint32_t ia, float sb, uint32_t ib) {
+  return sa > sb || (sa == sb && ia < ib);
+}
+
+// Order-preserving float <-> int encoding for atomicMax on non-NaN floats.
+__device__ __forceinline__ int float_to_ordered(float f) {
+  int i = __float_as_int(f);
+  return i >= 0 ? i : i ^ 0x7FFFFFFF;
+}
+__device__ __forceinline__ float ordered_to_float(int i) {
+  return __int_as_float(i >= 0 ? i : i ^ 0x7FFFFFFF);
+}
+constexpr int kOrderedNegInf = (int)(0xFF800000u ^ 0x7FFFFFFFu);  // float_to_ordered(-inf)
+
+// A warp-wide sorted top-32 list: lane i holds entry i (best first).  Empty
+// entries are (-inf, kNoRow), which every finite candidate beats.
+struct WarpList {
+  float s;
+  uint32_t id;
+  __device__ __forceinline__ void init() { s = -INFINITY; id = kNoRow; }
+  // Insert a warp-uniform candidate.
+  __device__ __forceinline__ void insert(float cs, uint32_t cid, int lane) {
+    const unsigned ahead = __ballot_sync(kFull, better(s, id, cs, cid));
+    const int pos = __popc(ahead);
+    const float us = __shfl_up_sync(kFull, s, 1);
+    const uint32_t uid = __shfl_up_sync(kFull, id, 1);
+    if (lane == pos) {
+      s = cs;
+      id = cid;
+    } else if (lane > pos) {
+      s = us;
+      id = uid;
+    }
+  }
+  // Every lane offers its own (cs, cid); finite candidates that beat the
+  // current last entry are inserted one at a time.
+  __device__ __forceinline__ void offer(float cs, uint32_t cid, int lane) {
+    float ts = __shfl_sync(kFull, s, 31);
+    uint32_t tid = __shfl_sync(kFull, id, 31);
+    unsigned m = __ballot_sync(kFull, isfinite(cs) && better(cs, cid, ts, tid));
+    while (m) {
+      const int src = __ffs(m) - 1;
+      const float bs = __shfl_sync(kFull, cs, src);
+      const uint32_t bid = __shfl_sync(kFull, cid, src);
+      insert(bs, bid, lane);
+      m &= m - 1;
+      ts = __shfl_sync(kFull, s, 31);
+      tid = __shfl_sync(kFull, id, 31);
+      m &= __ballot_sync(kFull, better(cs, cid, ts, tid));
+    }
+  }
+};
+
+// 16-byte streaming load that bypasses L1 allocation (the bank is read once).
+__device__ __forceinline__ uint4 ld_stream(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+__host__ __device__ inline int64_t ceil_div64(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+// Device properties cached per device.
+struct DeviceInfo {
+  int sms = 0;
+  int cc_major = 0;
+};
+int device_info(int device, DeviceInfo* out);
+
+}  // namespace grm_b200

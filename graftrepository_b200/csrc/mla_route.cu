@@ -1,0 +1,966 @@
+// mla_route.cu -- MLA latent-centroid route on sm_100a.
+//
+// Law (GraftRepository cpp/grm_runtime.cpp): row norm = float(sqrt(sum_d
+// double(c_d)^2)) (:3240-3249); qnorm = sqrt(sum_d double(q_d)^2) (:4311-4315);
+// score = float(dot_fp64(q, c) / (qnorm * double(norm) + 1e-8)) with the dot
+// accumulated in fp64 in element order (:3518-3545); non-finite scores are
+// dropped and the rest ordered by score desc, node id asc (:75-82, :4352-4360).
+//
+// Design.  One streaming pass reads the bank once from HBM with coalesced
+// 16-byte loads: a warp takes 32 rows at a time, each lane dots its 16-byte
+// slice of every row with its slice of the unit-normalised query in fp32, and
+// a butterfly reduce-scatter leaves one row's approximate cosine per lane.
+// Each warp keeps a sorted top-32 of approximate scores in registers (one
+// entry per lane), blocks merge their warps, publish only entries within the
+// margin of the best block k-th score seen so far, and the last block to
+// finish merges those, picks every row whose approximate score is within
+// 2*kMargin of the approximate k-th best, and recomputes those rows with the
+// reference's exact fp64 arithmetic.  The fp32 approximation is within 21 ulp
+// of 1.0 of the reference score (|q'|=1, |s|<=1, <=13 rounding steps per dot);
+// kMargin = 2^-16 is >= 12x that bound, so every row that can be in the
+// exact top-k is recomputed.  If the approximate lists were saturated inside
+// the margin (near-ties, duplicate rows) or the query is outside the safe
+// range (zero, non-finite, |q| outside [1e-20, 1e20]), a second kernel
+// computes exact scores for every row above the threshold (or for all rows),
+// so the result is exact in every case.
+#include <algorithm>
+#include <cstring>
+#include <vector>
+
+#include "common.cuh"
+
+namespace grm_b200 {
+namespace mla {
+
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+constexpr float kMargin = 1.52587890625e-05f;  // 2^-16
+constexpr double kSafeLo = 1.0e-20, kSafeHi = 1.0e20;
+
+enum Status : int { kOk = 0, kOverflow = 1, kUnsafe = 2 };
+
+struct Result {
+  int status;
+  int count;
+  float thr;
+  int pad;
+  uint64_t ids[GRM_B200_MAX_TOPK];
+  float scores[GRM_B200_MAX_TOPK];
+};
+
+struct Header {
+  int lb;          // ordered float: best block k-th approximate score so far
+  unsigned done;   // blocks finished in this launch
+  int pad[14];
+};
+
+struct Entry {
+  float s;
+  uint32_t id;
+};
+
+struct Scratch {
+  unsigned char* base;
+  size_t stride;  // bytes per query
+  int blocks;
+  __device__ Header* hdr(int q) const { return reinterpret_cast<Header*>(base + stride * q); }
+  __device__ Entry* entries(int q) const {
+    return reinterpret_cast<Entry*>(base + stride * q + sizeof(Header));
+  }
+  __device__ int* counts(int q) const {
+    return reinterpret_cast<int*>(base + stride * q + sizeof(Header) + sizeof(Entry) * 32 * blocks);
+  }
+  __device__ float* floors(int q) const {
+    return reinterpret_cast<float*>(counts(q) + blocks);
+  }
+};
+
+inline size_t scratch_stride(int blocks) {
+  size_t b = sizeof(Header) + sizeof(Entry) * 32 * (size_t)blocks + 8 * (size_t)blocks;
+  return (b + 255) & ~(size_t)255;
+}
+
+template <typename T>
+struct Params {
+  const T* rows;
+  const float* norms;
+  int64_t nodes;
+  int dim;
+  const float* queries;  // [Q, dim]
+  int topk;
+  Scratch scratch;
+  Result* results;       // [Q]
+  uint64_t* out_ids;     // optional device outputs [Q, topk]
+  float* out_scores;
+  uint64_t id_offset;
+  int force_all;         // exact kernel: score every row (bank outside the fast path)
+};
+
+__device__ __forceinline__ float to_f(__half h) { return __half2float(h); }
+__device__ __forceinline__ float to_f(float f) { return f; }
+
+// The reference's exact score for one row (cpp/grm_runtime.cpp:3518-3545).
+// Products of two floats are exact in fp64, so fma(q, c, dot) == dot + q*c.
+template <typename T>
+__device__ float exact_score(const T* row, int dim, const float* q, double qnorm, float norm) {
+  double dot = 0.0;
+#pragma unroll 8
+  for (int d = 0; d < dim; ++d) dot = fma((double)__ldg(q + d), (double)to_f(row[d]), dot);
+  return (float)(dot / (qnorm * (double)norm + 1.0e-8));
+}
+
+// Reference query norm, element order (cpp/grm_runtime.cpp:4311-4315).
+__device__ double query_norm_seq(const float* q, int dim) {
+  double acc = 0.0;
+  for (int d = 0; d < dim; ++d) {
+    const double v = (double)__ldg(q + d);
+    acc = fma(v, v, acc);
+  }
+  return sqrt(acc);
+}
+
+// Butterfly reduce-scatter of N partial sums over N lanes: afterwards v[0]
+// holds the total of slot (lane & (N-1)) across the N lanes.
+template <int N>
+__device__ __forceinline__ float reduce_scatter(float (&v)[N], int lane) {
+#pragma unroll
+  for (int o = N / 2; o >= 1; o >>= 1) {
+    const bool upper = (lane & o) != 0;
+#pragma unroll
+    for (int i = 0; i < o; ++i) {
+      const float send = upper ? v[i] : v[i + o];
+      const float keep = upper ? v[i + o] : v[i];
+      v[i] = keep + __shfl_xor_sync(kFull, send, o);
+    }
+  }
+  return v[0];
+}
+
+template <typename T>
+__device__ __forceinline__ float dot16(const uint4& v, const float* qr, float acc) {
+  if constexpr (sizeof(T) == 2) {
+    const __half2* h = reinterpret_cast<const __half2*>(&v);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float2 f = __half22float2(h[k]);
+      acc = fmaf(f.x, qr[2 * k], acc);
+      acc = fmaf(f.y, qr[2 * k + 1], acc);
+    }
+  } else {
+    acc = fmaf(__uint_as_float(v.x), qr[0], acc);
+    acc = fmaf(__uint_as_float(v.y), qr[1], acc);
+    acc = fmaf(__uint_as_float(v.z), qr[2], acc);
+    acc = fmaf(__uint_as_float(v.w), qr[3], acc);
+  }
+  return acc;
+}
+
+// Merge the kWarps warp lists of this block into warp 0's list.
+__device__ __forceinline__ void block_merge(WarpList& list, int lane, int warp, float* sh_s,
+                                            uint32_t* sh_id) {
+  sh_s[warp * 32 + lane] = list.s;
+  sh_id[warp * 32 + lane] = list.id;
+  __syncthreads();
+  if (warp == 0) {
+    for (int w = 1; w < kWarps; ++w) list.offer(sh_s[w * 32 + lane], sh_id[w * 32 + lane], lane);
+  }
+}
+
+// Write the final top-k (warp 0 of the finishing block; `ex` sorted exact).
+template <typename T>
+__device__ void write_result(const Params<T>& p, int q, const WarpList& ex, int lane) {
+  Result* r = p.results + q;
+  const bool ok = lane < p.topk && isfinite(ex.s) && ex.id != kNoRow;
+  const unsigned m = __ballot_sync(kFull, ok);
+  if (lane < p.topk) {
+    const uint64_t id = ok ? (uint64_t)ex.id + p.id_offset : UINT64_MAX;
+    const float s = ok ? ex.s : __int_as_float(0x7FC00000);
+    r->ids[lane] = id;
+    r->scores[lane] = s;
+    if (p.out_ids) p.out_ids[(int64_t)q * p.topk + lane] = id;
+    if (p.out_scores) p.out_scores[(int64_t)q * p.topk + lane] = s;
+  }
+  if (lane == 0) {
+    r->count = __popc(m);
+    r->status = kOk;
+  }
+}
+
+// Approximate streaming pass (one launch per batch of queries: grid.y = query).
+template <int D, typename T>
+__global__ void __launch_bounds__(kThreads) mla_scan_kernel(Params<T> p) {
+  constexpr int E = 16 / (int)sizeof(T);
+  constexpr int CPR = D / E;
+  constexpr int L = CPR >= 32 ? 32 : CPR;
+  constexpr int R = 32 / L;
+  constexpr int CPL = CPR >= 32 ? CPR / 32 : 1;
+  constexpr int SLOTS = L;
+
+  __shared__ float sh_s[kWarps * 32];
+  __shared__ uint32_t sh_id[kWarps * 32];
+  __shared__ float sh_q[D];
+  __shared__ float sh_eq;
+  __shared__ int sh_safe;
+  __shared__ int sh_last;
+  __shared__ float sh_floor[kWarps];
+
+  const int q = blockIdx.y;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const float* query = p.queries + (int64_t)q * D;
+
+  // Prologue: unit-normalised query (any accurate norm will do for the
+  // approximate pass; the exact refine recomputes the reference norm).
+  if (warp == 0) {
+    double acc = 0.0;
+    for (int d = lane; d < D; d += 32) {
+      const double v = (double)query[d];
+      acc = fma(v, v, acc);
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) acc += __shfl_xor_sync(kFull, acc, o);
+    const double qn = sqrt(acc);
+    const bool safe = isfinite(qn) && qn > kSafeLo && qn < kSafeHi;
+    const float inv = safe ? (float)(1.0 / qn) : 0.0f;
+    for (int d = lane; d < D; d += 32) sh_q[d] = query[d] * inv;
+    if (lane == 0) {
+      sh_safe = safe;
+      sh_eq = safe ? (float)(1.0e-8 / qn) : 0.0f;
+    }
+  }
+  __syncthreads();
+  const bool safe = sh_safe != 0;
+  const float e_q = sh_eq;
+
+  float qr[CPL * E];
+#pragma unroll
+  for (int i = 0; i < CPL; ++i) {
+    const int c = (CPR >= 32) ? lane + 32 * i : lane % L;
+#pragma unroll
+    for (int e = 0; e < E; ++e) qr[i * E + e] = sh_q[c * E + e];
+  }
+
+  WarpList list;
+  list.init();
+  const int64_t groups = ceil_div64(p.nodes, 32);
+  if (safe) {
+    for (int64_t g = (int64_t)blockIdx.x * kWarps + warp; g < groups;
+         g += (int64_t)gridDim.x * kWarps) {
+      const int64_t row0 = g * 32;
+      float part[SLOTS];
+#pragma unroll
+      for (int j = 0; j < SLOTS; ++j) {
+        const int64_t row = row0 + j * R + lane / L;
+        float acc = 0.0f;
+        if (row < p.nodes) {
+          const T* rp = p.rows + row * D;
+#pragma unroll
+          for (int i = 0; i < CPL; ++i) {
+            const int c = (CPR >= 32) ? lane + 32 * i : lane % L;
+            acc = dot16<T>(ld_stream(rp + c * E), qr + i * E, acc);
+          }
+        }
+        part[j] = acc;
+      }
+      const float dot = reduce_scatter<SLOTS>(part, lane);
+      const int64_t row = row0 + (lane % L) * R + lane / L;
+      float s = -INFINITY;
+      if (row < p.nodes) {
+        const float nrm = __ldg(p.norms + row);
+        if (isfinite(nrm)) s = dot * __frcp_rn(nrm + e_q);
+      }
+      list.offer(s, (uint32_t)row, lane);
+    }
+  }
+
+  block_merge(list, lane, warp, sh_s, sh_id);
+  Header* hdr = p.scratch.hdr(q);
+  if (warp == 0) {
+    const float kth = __shfl_sync(kFull, list.s, p.topk - 1);
+    int lb_now = 0;
+    if (lane == 0) {
+      const int enc = isfinite(kth) ? float_to_ordered(kth) : kOrderedNegInf;
+      const int old = atomicMax(&hdr->lb, enc);
+      lb_now = old > enc ? old : enc;
+    }
+    lb_now = __shfl_sync(kFull, lb_now, 0);
+    const float wthr = ordered_to_float(lb_now) - 2.0f * kMargin;
+    const bool keep = isfinite(list.s) && list.s >= wthr;
+    const int cnt = __popc(__ballot_sync(kFull, keep));
+    Entry* ent = p.scratch.entries(q) + (int64_t)blockIdx.x * 32;
+    if (lane < cnt) ent[lane] = Entry{list.s, list.id};
+    const float last = __shfl_sync(kFull, list.s, 31);
+    if (lane == 0) {
+      p.scratch.counts(q)[blockIdx.x] = cnt;
+      p.scratch.floors(q)[blockIdx.x] = isfinite(last) ? last : -INFINITY;
+      __threadfence();
+      const unsigned ticket = atomicAdd(&hdr->done, 1u);
+      sh_last = (ticket == gridDim.x - 1);
+    }
+  }
+  __syncthreads();
+  if (!sh_last) return;
+  __threadfence();
+
+  // Last block: merge the published entries.
+  list.init();
+  float fmax = -INFINITY;
+  for (int b = warp; b < (int)gridDim.x; b += kWarps) {
+    const int cnt = __ldcg(p.scratch.counts(q) + b);
+    const Entry* ent = p.scratch.entries(q) + (int64_t)b * 32;
+    float s = -INFINITY;
+    uint32_t id = kNoRow;
+    if (lane < cnt) {
+      s = __ldcg(&ent[lane].s);
+      id = __ldcg(&ent[lane].id);
+    }
+    list.offer(s, id, lane);
+    fmax = fmaxf(fmax, __ldcg(p.scratch.floors(q) + b));
+  }
+  if (lane == 0) sh_floor[warp] = fmax;
+  __syncthreads();
+  block_merge(list, lane, warp, sh_s, sh_id);
+  if (warp != 0) return;
+  float floor_max = -INFINITY;
+  for (int w = 0; w < kWarps; ++w) floor_max = fmaxf(floor_max, sh_floor[w]);
+  const float T_k = __shfl_sync(kFull, list.s, p.topk - 1);
+  const float thr = isfinite(T_k) ? T_k - 2.0f * kMargin : -INFINITY;
+  const float last = __shfl_sync(kFull, list.s, 31);
+  const bool overflow = (isfinite(last) && last >= thr) || (isfinite(floor_max) && floor_max >= thr);
+  Result* r = p.results + q;
+  if (!safe || overflow) {
+    if (lane == 0) {
+      r->status = safe ? kOverflow : kUnsafe;
+      r->thr = thr;
+      r->count = 0;
+      hdr->lb = kOrderedNegInf;
+      hdr->done = 0;
+    }
+    return;
+  }
+  // Exact refine of the candidates (sorted approximate list, prefix >= thr).
+  const bool cand = isfinite(list.s) && list.s >= thr;
+  float es = -INFINITY;
+  if (cand) {
+    const double qnorm = query_norm_seq(query, D);
+    const int64_t row = list.id;
+    es = exact_score<T>(p.rows + row * D, D, query, qnorm, __ldg(p.norms + row));
+  }
+  WarpList ex;
+  ex.init();
+  ex.offer(es, list.id, lane);
+  write_result(p, q, ex, lane);
+  if (lane == 0) {
+    hdr->lb = kOrderedNegInf;
+    hdr->done = 0;
+  }
+}
+
+// Exact fallback: for each query whose approximate pass reported kOverflow,
+// compute exact scores for every row whose approximate score reaches the
+// threshold; for kUnsafe (or force_all) compute exact scores for all rows.
+// Queries whose status is kOk exit at once.  D == 0 means runtime dim
+// (force_all only).
+template <int D, typename T>
+__global__ void __launch_bounds__(kThreads) mla_exact_kernel(Params<T> p) {
+  __shared__ float sh_s[kWarps * 32];
+  __shared__ uint32_t sh_id[kWarps * 32];
+  __shared__ double sh_qnorm;
+  __shared__ float sh_eq;
+  __shared__ int sh_mode;
+  __shared__ int sh_last;
+  constexpr int DMAX = D > 0 ? D : 1;
+  __shared__ float sh_q[DMAX];
+
+  const int q = blockIdx.y;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int dim = D > 0 ? D : p.dim;
+  const float* query = p.queries + (int64_t)q * dim;
+  Result* r = p.results + q;
+
+  if (threadIdx.x == 0) {
+    const int st = p.force_all ? (int)kUnsafe : __ldcg(&r->status);
+    sh_mode = st;
+    if (st != kOk) {
+      const double qn = query_norm_seq(query, dim);
+      sh_qnorm = qn;
+      sh_eq = (float)(1.0e-8 / qn);
+    }
+  }
+  __syncthreads();
+  const int mode = sh_mode;
+  if (mode == kOk) return;
+  const double qnorm = sh_qnorm;
+
+  WarpList list;
+  list.init();
+  if (mode == kUnsafe || D == 0) {
+    // Every row, one row per lane, in reference arithmetic.
+    for (int64_t row0 = ((int64_t)blockIdx.x * kWarps + warp) * 32; row0 < p.nodes;
+         row0 += (int64_t)gridDim.x * kWarps * 32) {
+      const int64_t row = row0 + lane;
+      float es = -INFINITY;
+      if (row < p.nodes) {
+        const float nrm = __ldg(p.norms + row);
+        if (isfinite(nrm)) es = exact_score<T>(p.rows + row * dim, dim, query, qnorm, nrm);
+      }
+      list.offer(es, (uint32_t)row, lane);
+    }
+  } else if constexpr (D > 0) {
+    constexpr int E = 16 / (int)sizeof(T);
+    constexpr int CPR = D / E;
+    constexpr int L = CPR >= 32 ? 32 : CPR;
+    constexpr int R = 32 / L;
+    constexpr int CPL = CPR >= 32 ? CPR / 32 : 1;
+    constexpr int SLOTS = L;
+    const float thr = __ldcg(&r->thr);
+    const float e_q = sh_eq;
+    if (warp == 0) {
+      const float inv = (float)(1.0 / qnorm);
+      for (int d = lane; d < D; d += 32) sh_q[d] = query[d] * inv;
+    }
+    __syncthreads();
+    float qr[CPL * E];
+#pragma unroll
+    for (int i = 0; i < CPL; ++i) {
+      const int c = (CPR >= 32) ? lane + 32 * i : lane % L;
+#pragma unroll
+      for (int e = 0; e < E; ++e) qr[i * E + e] = sh_q[c * E + e];
+    }
+    const int64_t groups = ceil_div64(p.nodes, 32);
+    for (int64_t g = (int64_t)blockIdx.x * kWarps + warp; g < groups;
+         g += (int64_t)gridDim.x * kWarps) {
+      const int64_t row0 = g * 32;
+      float part[SLOTS];
+#pragma unroll
+      for (int j = 0; j < SLOTS; ++j) {
+        const int64_t row = row0 + j * R + lane / L;
+        float acc = 0.0f;
+        if (row < p.nodes) {
+          const T* rp = p.rows + row * D;
+#pragma unroll
+          for (int i = 0; i < CPL; ++i) {
+            const int c = (CPR >= 32) ? lane + 32 * i : lane % L;
+            acc = dot16<T>(*reinterpret_cast<const uint4*>(rp + c * E), qr + i * E, acc);
+          }
+        }
+        part[j] = acc;
+      }
+      const float dot = reduce_scatter<SLOTS>(part, lane);
+      const int64_t row = row0 + (lane % L) * R + lane / L;
+      float es = -INFINITY;
+      if (row < p.nodes) {
+        const float nrm = __ldg(p.norms + row);
+        if (isfinite(nrm)) {
+          const float s = dot * __frcp_rn(nrm + e_q);
+          if (s >= thr) es = exact_score<T>(p.rows + row * D, D, query, qnorm, nrm);
+        }
+      }
+      list.offer(es, (uint32_t)row, lane);
+    }
+  }
+
+  block_merge(list, lane, warp, sh_s, sh_id);
+  Header* hdr = p.scratch.hdr(q);
+  if (warp == 0) {
+    const bool keep = lane < p.topk && isfinite(list.s);
+    const int cnt = __popc(__ballot_sync(kFull, keep));
+    Entry* ent = p.scratch.entries(q) + (int64_t)blockIdx.x * 32;
+    if (lane < cnt) ent[lane] = Entry{list.s, list.id};
+    if (lane == 0) {
+      p.scratch.counts(q)[blockIdx.x] = cnt;
+      __threadfence();
+      const unsigned ticket = atomicAdd(&hdr->done, 1u);
+      sh_last = (ticket == gridDim.x - 1);
+    }
+  }
+  __syncthreads();
+  if (!sh_last) return;
+  __threadfence();
+  list.init();
+  for (int b = warp; b < (int)gridDim.x; b += kWarps) {
+    const int cnt = __ldcg(p.scratch.counts(q) + b);
+    const Entry* ent = p.scratch.entries(q) + (int64_t)b * 32;
+    float s = -INFINITY;
+    uint32_t id = kNoRow;
+    if (lane < cnt) {
+      s = __ldcg(&ent[lane].s);
+      id = __ldcg(&ent[lane].id);
+    }
+    list.offer(s, id, lane);
+  }
+  __syncthreads();
+  block_merge(list, lane, warp, sh_s, sh_id);
+  if (warp != 0) return;
+  write_result(p, q, list, lane);
+  if (lane == 0) {
+    hdr->lb = kOrderedNegInf;
+    hdr->done = 0;
+  }
+}
+
+template <typename T>
+__global__ void row_norms_kernel(const T* rows, int64_t n, int dim, float* norms,
+                                 unsigned* special) {
+  for (int64_t row = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; row < n;
+       row += (int64_t)gridDim.x * blockDim.x) {
+    const T* rp = rows + row * dim;
+    double acc = 0.0;
+    bool finite = true;
+    float maxabs = 0.0f;
+    for (int d = 0; d < dim; ++d) {
+      const float v = to_f(rp[d]);
+      finite = finite && isfinite(v);
+      maxabs = fmaxf(maxabs, fabsf(v));
+      acc = fma((double)v, (double)v, acc);
+    }
+    float nrm = (float)sqrt(acc);
+    if (!finite) {
+      nrm = __int_as_float(0x7FC00000);  // any non-finite value: the reference score is NaN
+    } else if (!isfinite(nrm) || maxabs > 1.0e30f) {
+      atomicAdd(special, 1u);            // outside the fast path's proven range
+    }
+    norms[row] = nrm;
+  }
+}
+
+__global__ void scratch_init_kernel(unsigned char* base, size_t stride, int queries) {
+  const int q = blockIdx.x * blockDim.x + threadIdx.x;
+  if (q < queries) {
+    Header* h = reinterpret_cast<Header*>(base + stride * q);
+    h->lb = kOrderedNegInf;
+    h->done = 0;
+  }
+}
+
+}  // namespace mla
+}  // namespace grm_b200
+
+using namespace grm_b200;
+using namespace grm_b200::mla;
+
+struct grm_b200_mla_bank {
+  int device = 0;
+  int dtype = GRM_B200_F16;
+  int64_t nodes = 0;
+  int dim = 0;
+  void* d_rows = nullptr;
+  float* d_norms = nullptr;
+  bool exact_only = false;
+  int grid_x = 1;
+  int scratch_queries = 0;
+  size_t stride = 0;
+  unsigned char* d_scratch = nullptr;
+  Result* d_results = nullptr;
+  Result* h_results = nullptr;
+  float* d_queries = nullptr;
+  size_t dq_cap = 0;
+  cudaStream_t stream = nullptr;
+  cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+  std::mutex mu;
+  ErrorSlot err;
+  uint64_t routes = 0, fallbacks = 0;
+};
+
+namespace {
+
+bool fast_dim(int dim) { return dim == 64 || dim == 128 || dim == 256 || dim == 512; }
+
+template <typename T>
+using ScanFn = void (*)(Params<T>);
+
+template <typename T>
+ScanFn<T> scan_fn(int dim) {
+  switch (dim) {
+    case 64: return mla_scan_kernel<64, T>;
+    case 128: return mla_scan_kernel<128, T>;
+    case 256: return mla_scan_kernel<256, T>;
+    case 512: return mla_scan_kernel<512, T>;
+  }
+  return nullptr;
+}
+
+template <typename T>
+ScanFn<T> exact_fn(int dim) {
+  switch (dim) {
+    case 64: return mla_exact_kernel<64, T>;
+    case 128: return mla_exact_kernel<128, T>;
+    case 256: return mla_exact_kernel<256, T>;
+    case 512: return mla_exact_kernel<512, T>;
+  }
+  return mla_exact_kernel<0, T>;
+}
+
+int pick_grid(grm_b200_mla_bank* b) {
+  DeviceInfo info;
+  int rc = device_info(b->device, &info);
+  if (rc) return rc;
+  int occ = 1;
+  cudaError_t e;
+  if (b->dtype == GRM_B200_F16) {
+    auto fn = fast_dim(b->dim) ? scan_fn<__half>(b->dim) : exact_fn<__half>(b->dim);
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, kThreads, 0);
+  } else {
+    auto fn = fast_dim(b->dim) ? scan_fn<float>(b->dim) : exact_fn<float>(b->dim);
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, kThreads, 0);
+  }
+  if (e != cudaSuccess) return cuda_status(e);
+  occ = std::max(1, occ);
+  const int64_t groups = ceil_div64(b->nodes, 32);
+  const int64_t want = ceil_div64(groups, kWarps);
+  b->grid_x = (int)std::max<int64_t>(1, std::min<int64_t>((int64_t)info.sms * occ, want));
+  return 0;
+}
+
+int reserve(grm_b200_mla_bank* b, int queries) {
+  if (queries <= b->scratch_queries) return 0;
+  const int n = std::max(queries, 8);
+  if (b->d_scratch) cudaFree(b->d_scratch);
+  if (b->d_results) cudaFree(b->d_results);
+  if (b->h_results) cudaFreeHost(b->h_results);
+  b->d_scratch = nullptr;
+  b->d_results = nullptr;
+  b->h_results = nullptr;
+  b->scratch_queries = 0;
+  b->stride = scratch_stride(b->grid_x);
+  cudaError_t e = cudaMalloc(&b->d_scratch, b->stride * n);
+  if (e == cudaSuccess) e = cudaMalloc(&b->d_results, sizeof(Result) * n);
+  if (e == cudaSuccess) e = cudaMallocHost(&b->h_results, sizeof(Result) * n);
+  if (e != cudaSuccess) return b->err.set(cuda_status(e), "scratch allocation failed: %s", cudaGetErrorString(e));
+  scratch_init_kernel<<<(n + 127) / 128, 128, 0, b->stream>>>(b->d_scratch, b->stride, n);
+  e = cudaGetLastError();
+  if (e == cudaSuccess) e = cudaStreamSynchronize(b->stream);
+  if (e != cudaSuccess) return b->err.set(cuda_status(e), "scratch init failed: %s", cudaGetErrorString(e));
+  b->scratch_queries = n;
+  return 0;
+}
+
+template <typename T>
+Params<T> make_params(grm_b200_mla_bank* b, const float* dq, int topk) {
+  Params<T> p;
+  p.rows = static_cast<const T*>(b->d_rows);
+  p.norms = b->d_norms;
+  p.nodes = b->nodes;
+  p.dim = b->dim;
+  p.queries = dq;
+  p.topk = topk;
+  p.scratch = Scratch{b->d_scratch, b->stride, b->grid_x};
+  p.results = b->d_results;
+  p.out_ids = nullptr;
+  p.out_scores = nullptr;
+  p.id_offset = 0;
+  p.force_all = b->exact_only ? 1 : 0;
+  return p;
+}
+
+template <typename T>
+int launch_scan(grm_b200_mla_bank* b, const Params<T>& p, int nq, cudaStream_t s) {
+  dim3 grid(b->grid_x, nq);
+  if (!b->exact_only) {
+    scan_fn<T>(b->dim)<<<grid, kThreads, 0, s>>>(p);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_status(e);
+  }
+  return 0;
+}
+
+template <typename T>
+int launch_exact(grm_b200_mla_bank* b, const Params<T>& p, int nq, cudaStream_t s) {
+  dim3 grid(b->grid_x, nq);
+  exact_fn<T>(b->exact_only ? 0 : b->dim)<<<grid, kThreads, 0, s>>>(p);
+  return cuda_status(cudaGetLastError());
+}
+
+// Route `nq` device queries synchronously into b->h_results[0..nq).
+template <typename T>
+int run_chunk(grm_b200_mla_bank* b, const float* dq, int nq, int topk) {
+  Params<T> p = make_params<T>(b, dq, topk);
+  int rc = launch_scan<T>(b, p, nq, b->stream);
+  if (rc) return b->err.set(rc, "MLA scan launch failed: %s", cudaGetErrorString(cudaGetLastError()));
+  bool need_exact = b->exact_only;
+  if (!b->exact_only) {
+    cudaError_t e = cudaMemcpyAsync(b->h_results, b->d_results, sizeof(Result) * nq,
+                                    cudaMemcpyDeviceToHost, b->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(b->stream);
+    if (e != cudaSuccess) return b->err.set(cuda_status(e), "MLA route failed: %s", cudaGetErrorString(e));
+    for (int i = 0; i < nq; ++i) need_exact = need_exact || b->h_results[i].status != kOk;
+  }
+  if (need_exact) {
+    b->fallbacks += 1;
+    rc = launch_exact<T>(b, p, nq, b->stream);
+    if (rc) return b->err.set(rc, "MLA exact pass launch failed");
+    cudaError_t e = cudaMemcpyAsync(b->h_results, b->d_results, sizeof(Result) * nq,
+                                    cudaMemcpyDeviceToHost, b->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(b->stream);
+    if (e != cudaSuccess) return b->err.set(cuda_status(e), "MLA exact pass failed: %s", cudaGetErrorString(e));
+  }
+  return 0;
+}
+
+int route_device_queries(grm_b200_mla_bank* b, const float* dq, int query_count, int warmup,
+                         int topk, uint64_t* out_ids, float* out_scores, float* elapsed) {
+  if (!dq || !out_ids || query_count <= 0 || warmup < 0 || warmup >= query_count || topk <= 0 ||
+      topk > GRM_B200_MAX_TOPK)
+    return b->err.set(GRM_B200_EINVAL, "invalid MLA route arguments (queries=%d warmup=%d topk=%d)",
+                      query_count, warmup, topk);
+  cudaError_t e = cudaSetDevice(b->device);
+  if (e != cudaSuccess) return b->err.set(cuda_status(e), "cudaSetDevice failed");
+  int rc = reserve(b, query_count);
+  if (rc) return rc;
+  auto chunk = [&](int q0, int nq) -> int {
+    rc = (b->dtype == GRM_B200_F16) ? run_chunk<__half>(b, dq + (int64_t)q0 * b->dim, nq, topk)
+                                    : run_chunk<float>(b, dq + (int64_t)q0 * b->dim, nq, topk);
+    if (rc) return rc;
+    for (int i = 0; i < nq; ++i) {
+      const Result& r = b->h_results[i];
+      for (int j = 0; j < topk; ++j) {
+        out_ids[(int64_t)(q0 + i) * topk + j] = r.ids[j];
+        if (out_scores) out_scores[(int64_t)(q0 + i) * topk + j] = r.scores[j];
+      }
+    }
+    return 0;
+  };
+  if (warmup > 0 && (rc = chunk(0, warmup))) return rc;
+  cudaEventRecord(b->ev0, b->stream);
+  if ((rc = chunk(warmup, query_count - warmup))) return rc;
+  cudaEventRecord(b->ev1, b->stream);
+  e = cudaEventSynchronize(b->ev1);
+  float ms = 0.0f;
+  if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, b->ev0, b->ev1);
+  if (e != cudaSuccess) return b->err.set(cuda_status(e), "MLA route timing failed");
+  if (elapsed) *elapsed = ms;
+  b->routes += (uint64_t)query_count;
+  return 0;
+}
+
+int bank_finish_create(grm_b200_mla_bank* b) {
+  cudaError_t e = cudaStreamCreateWithFlags(&b->stream, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaEventCreate(&b->ev0);
+  if (e == cudaSuccess) e = cudaEventCreate(&b->ev1);
+  if (e == cudaSuccess) e = cudaMalloc(&b->d_norms, sizeof(float) * (size_t)b->nodes);
+  if (e != cudaSuccess) return cuda_status(e);
+  unsigned* d_special = nullptr;
+  e = cudaMalloc(&d_special, sizeof(unsigned));
+  if (e == cudaSuccess) e = cudaMemsetAsync(d_special, 0, sizeof(unsigned), b->stream);
+  if (e != cudaSuccess) return cuda_status(e);
+  DeviceInfo info;
+  int rc = device_info(b->device, &info);
+  if (rc) return rc;
+  const int grid = (int)std::min<int64_t>(ceil_div64(b->nodes, 256), (int64_t)info.sms * 8);
+  if (b->dtype == GRM_B200_F16)
+    row_norms_kernel<__half><<<grid, 256, 0, b->stream>>>(static_cast<const __half*>(b->d_rows),
+                                                          b->nodes, b->dim, b->d_norms, d_special);
+  else
+    row_norms_kernel<float><<<grid, 256, 0, b->stream>>>(static_cast<const float*>(b->d_rows),
+                                                         b->nodes, b->dim, b->d_norms, d_special);
+  unsigned special = 0;
+  e = cudaGetLastError();
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(&special, d_special, sizeof(unsigned), cudaMemcpyDeviceToHost, b->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(b->stream);
+  cudaFree(d_special);
+  if (e != cudaSuccess) return cuda_status(e);
+  b->exact_only = !fast_dim(b->dim) || special > 0;
+  rc = pick_grid(b);
+  if (rc) return rc;
+  return reserve(b, 8);
+}
+
+void bank_free(grm_b200_mla_bank* b) {
+  if (!b) return;
+  cudaSetDevice(b->device);
+  if (b->stream) cudaStreamSynchronize(b->stream);
+  if (b->d_rows) cudaFree(b->d_rows);
+  if (b->d_norms) cudaFree(b->d_norms);
+  if (b->d_scratch) cudaFree(b->d_scratch);
+  if (b->d_results) cudaFree(b->d_results);
+  if (b->h_results) cudaFreeHost(b->h_results);
+  if (b->d_queries) cudaFree(b->d_queries);
+  if (b->ev0) cudaEventDestroy(b->ev0);
+  if (b->ev1) cudaEventDestroy(b->ev1);
+  if (b->stream) cudaStreamDestroy(b->stream);
+  delete b;
+}
+
+int create_common(const void* rows, bool host, int dtype, int64_t nodes, int dim, int device,
+                  grm_b200_mla_bank** out) {
+  if (!out) {
+    set_thread_error("out_bank is NULL");
+    return GRM_B200_EINVAL;
+  }
+  *out = nullptr;
+  if (!rows || nodes <= 0 || nodes >= (int64_t)0xFFFFFFFF || dim <= 0 || dim > 4096 ||
+      !(dtype == GRM_B200_F16 || dtype == GRM_B200_F32)) {
+    set_thread_error("invalid MLA bank arguments (nodes=%lld dim=%d dtype=%d)", (long long)nodes,
+                     dim, dtype);
+    return GRM_B200_EINVAL;
+  }
+  cudaError_t e = cudaSetDevice(device);
+  if (e != cudaSuccess) {
+    set_thread_error("cudaSetDevice(%d) failed: %s", device, cudaGetErrorString(e));
+    return cuda_status(e);
+  }
+  auto* b = new grm_b200_mla_bank();
+  b->device = device;
+  b->dtype = dtype;
+  b->nodes = nodes;
+  b->dim = dim;
+  const size_t bytes = (size_t)nodes * dim * (dtype == GRM_B200_F16 ? 2 : 4);
+  e = cudaMalloc(&b->d_rows, bytes);
+  if (e == cudaSuccess)
+    e = cudaMemcpy(b->d_rows, rows, bytes, host ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice);
+  int rc = cuda_status(e);
+  if (!rc) rc = bank_finish_create(b);
+  if (rc) {
+    set_thread_error("MLA bank create failed (%d): %s", rc, cudaGetErrorString(cudaGetLastError()));
+    bank_free(b);
+    return rc;
+  }
+  *out = b;
+  return 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+int grm_b200_mla_bank_create(const void* rows_host, int dtype, int64_t nodes, int dim, int device,
+                             grm_b200_mla_bank** out_bank) {
+  return create_common(rows_host, true, dtype, nodes, dim, device, out_bank);
+}
+
+int grm_b200_mla_bank_create_device(const void* rows_device, int dtype, int64_t nodes, int dim,
+                                    grm_b200_mla_bank** out_bank) {
+  int device = 0;
+  cudaGetDevice(&device);
+  return create_common(rows_device, false, dtype, nodes, dim, device, out_bank);
+}
+
+int grm_b200_mla_route(grm_b200_mla_bank* bank, const float* queries_host, int query_count, int dim,
+                       int warmup, int topk, uint64_t* out_ids_host, float* out_scores_host,
+                       float* elapsed_ms) {
+  if (!bank) return GRM_B200_EINVAL;
+  std::lock_guard<std::mutex> lock(bank->mu);
+  if (!queries_host || query_count <= 0 || dim != bank->dim)
+    return bank->err.set(GRM_B200_EINVAL, "invalid MLA route arguments (dim=%d, bank dim=%d)", dim,
+                         bank->dim);
+  cudaError_t e = cudaSetDevice(bank->device);
+  const size_t need = (size_t)query_count * dim;
+  if (e == cudaSuccess && need > bank->dq_cap) {
+    if (bank->d_queries) cudaFree(bank->d_queries);
+    bank->d_queries = nullptr;
+    bank->dq_cap = 0;
+    e = cudaMalloc(&bank->d_queries, need * sizeof(float));
+    if (e == cudaSuccess) bank->dq_cap = need;
+  }
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(bank->d_queries, queries_host, need * sizeof(float), cudaMemcpyHostToDevice,
+                        bank->stream);
+  if (e != cudaSuccess)
+    return bank->err.set(cuda_status(e), "MLA query upload failed: %s", cudaGetErrorString(e));
+  return route_device_queries(bank, bank->d_queries, query_count, warmup, topk, out_ids_host,
+                              out_scores_host, elapsed_ms);
+}
+
+int grm_b200_mla_route_device(grm_b200_mla_bank* bank, const float* queries_device, int query_count,
+                              int dim, int warmup, int topk, uint64_t* out_ids_host,
+                              float* out_scores_host, float* elapsed_ms) {
+  if (!bank) return GRM_B200_EINVAL;
+  std::lock_guard<std::mutex> lock(bank->mu);
+  if (dim != bank->dim)
+    return bank->err.set(GRM_B200_EINVAL, "query dim %d does not match bank dim %d", dim, bank->dim);
+  return route_device_queries(bank, queries_device, query_count, warmup, topk, out_ids_host,
+                              out_scores_host, elapsed_ms);
+}
+
+}  // extern "C"
+
+namespace {
+
+// phase: 1 = scan only, 2 = resolve only, 3 = both.
+int route_async_phases(grm_b200_mla_bank* bank, const float* queries_device, int query_count,
+                       int topk, uint64_t id_offset, uint64_t* out_ids_device,
+                       float* out_scores_device, void* stream, int phase) {
+  if (!bank) return GRM_B200_EINVAL;
+  std::lock_guard<std::mutex> lock(bank->mu);
+  if (!queries_device || query_count <= 0 || topk <= 0 || topk > GRM_B200_MAX_TOPK ||
+      (!out_ids_device && !out_scores_device))
+    return bank->err.set(GRM_B200_EINVAL, "invalid MLA async route arguments");
+  if (query_count > bank->scratch_queries)
+    return bank->err.set(GRM_B200_EINVAL,
+                         "query_count %d exceeds reserved scratch (%d): call grm_b200_mla_reserve",
+                         query_count, bank->scratch_queries);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int rc = 0;
+  if (bank->dtype == GRM_B200_F16) {
+    Params<__half> p = make_params<__half>(bank, queries_device, topk);
+    p.out_ids = out_ids_device;
+    p.out_scores = out_scores_device;
+    p.id_offset = id_offset;
+    if (phase & 1) rc = launch_scan<__half>(bank, p, query_count, s);
+    if (!rc && (phase & 2)) rc = launch_exact<__half>(bank, p, query_count, s);
+  } else {
+    Params<float> p = make_params<float>(bank, queries_device, topk);
+    p.out_ids = out_ids_device;
+    p.out_scores = out_scores_device;
+    p.id_offset = id_offset;
+    if (phase & 1) rc = launch_scan<float>(bank, p, query_count, s);
+    if (!rc && (phase & 2)) rc = launch_exact<float>(bank, p, query_count, s);
+  }
+  if (rc) return bank->err.set(rc, "MLA async route launch failed");
+  if (phase & 1) bank->routes += (uint64_t)query_count;
+  return 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+int grm_b200_mla_route_async(grm_b200_mla_bank* bank, const float* queries_device, int query_count,
+                             int topk, uint64_t id_offset, uint64_t* out_ids_device,
+                             float* out_scores_device, void* stream) {
+  return route_async_phases(bank, queries_device, query_count, topk, id_offset, out_ids_device,
+                            out_scores_device, stream, 3);
+}
+
+int grm_b200_mla_scan_async(grm_b200_mla_bank* bank, const float* queries_device, int query_count,
+                            int topk, uint64_t id_offset, uint64_t* out_ids_device,
+                            float* out_scores_device, void* stream) {
+  return route_async_phases(bank, queries_device, query_count, topk, id_offset, out_ids_device,
+                            out_scores_device, stream, 1);
+}
+
+int grm_b200_mla_resolve_async(grm_b200_mla_bank* bank, const float* queries_device,
+                               int query_count, int topk, uint64_t id_offset,
+                               uint64_t* out_ids_device, float* out_scores_device, void* stream) {
+  return route_async_phases(bank, queries_device, query_count, topk, id_offset, out_ids_device,
+                            out_scores_device, stream, 2);
+}
+
+int grm_b200_mla_reserve(grm_b200_mla_bank* bank, int max_queries) {
+  if (!bank || max_queries <= 0) return GRM_B200_EINVAL;
+  std::lock_guard<std::mutex> lock(bank->mu);
+  cudaSetDevice(bank->device);
+  return reserve(bank, max_queries);
+}
+
+int grm_b200_mla_bank_destroy(grm_b200_mla_bank* bank) {
+  bank_free(bank);
+  return 0;
+}
+
+const char* grm_b200_mla_last_error(grm_b200_mla_bank* bank) {
+  return bank ? bank->err.text.c_str() : grm_b200_last_error();
+}
+
+const float* grm_b200_mla_row_norms_device(grm_b200_mla_bank* bank) {
+  return bank ? bank->d_norms : nullptr;
+}
+
+int grm_b200_mla_stats(grm_b200_mla_bank* bank, uint64_t* routes, uint64_t* fallbacks) {
+  if (!bank) return GRM_B200_EINVAL;
+  if (routes) *routes = bank->routes;
+  if (fallbacks) *fallbacks = bank->fallbacks;
+  return 0;
+}
+
+}  // extern "C"

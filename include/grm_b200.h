@@ -1,0 +1,250 @@
+/*
+ * grm_b200.h -- C ABI of the B200 (sm_100a) graft route + mount library
+ * (graftrepository_b200/libgrm_b200.so).
+ *
+ * This is the drop-in replacement for the CUDA route sidecars of
+ * GraftRepository and for the device mount of routed grafts.  Each entry point
+ * names the reference interface it replaces (paths are relative to the
+ * GraftRepository checkout).  Conventions follow cpp/grm_runtime_c.h and the
+ * sidecar ABI in scripts/grm_mla_cuda_probe.py:60-66:
+ *
+ *   - every function returns an int status: 0 ok, -1 invalid argument,
+ *     1000 + cudaError_t for a CUDA runtime failure, 3000 + n for an error
+ *     detected inside a kernel (3001 = a bounded device wait gave up);
+ *   - a human-readable message is kept per handle (grm_b200_*_last_error) and
+ *     per thread for handle-less calls (grm_b200_last_error);
+ *   - a handle owns all the device memory it allocates (bank copy, row norms,
+ *     route scratch); the caller owns every host buffer it passes;
+ *   - route outputs are host arrays ids[query_count * topk] (uint64) and,
+ *     optionally, scores[query_count * topk] (float); slots past the number of
+ *     finite scores hold UINT64_MAX / NaN (the UINT64_MAX sentinel law of
+ *     core/grm_cuda_router.py:465-475);
+ *   - ids are bank row indices 0..nodes-1; callers map them to node ids;
+ *   - calls on one handle are serialised by a mutex inside the handle; use one
+ *     handle per stream for concurrency.
+ *
+ * Results are bit-exact against the reference's CPU route laws: the MLA
+ * cosine of cpp/grm_runtime.cpp:3518-3545 (fp64 dot, fp64 query norm, fp32 row
+ * norm) and the GQA raw |q.k| law of cpp/grm_runtime.cpp:3588-3671 (sequential
+ * fp32), ordered by score desc then row asc (score_node_better, :75-82), with
+ * non-finite scores dropped.
+ */
+#ifndef GRM_B200_H
+#define GRM_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+/* Element types of a bank or a query buffer. */
+#define GRM_B200_F32 0
+#define GRM_B200_F16 1
+#define GRM_B200_BF16 2
+
+#define GRM_B200_OK 0
+#define GRM_B200_EINVAL (-1)
+#define GRM_B200_CUDA_BASE 1000
+#define GRM_B200_KERNEL_BASE 3000
+/* Largest top-k a route call accepts (the reference caps at 16:
+ * scripts/grm_mla_cuda_probe.py:357). */
+#define GRM_B200_MAX_TOPK 32
+
+typedef struct grm_b200_mla_bank grm_b200_mla_bank;
+typedef struct grm_b200_gqa_bank grm_b200_gqa_bank;
+
+/* ---------------------------------------------------------------- MLA route */
+
+/* Upload a dense MLA centroid bank rows[nodes, dim] (row-major, element type
+ * GRM_B200_F32 or GRM_B200_F16) to `device` and compute the fp32 row norms
+ * (fp64 accumulate, cpp/grm_runtime.cpp:3240-3249).
+ * Replaces grm_mla_cuda_arena_create (scripts/grm_mla_cuda_probe.py:286-336). */
+int grm_b200_mla_bank_create(const void* rows_host, int dtype, int64_t nodes, int dim,
+                             int device, grm_b200_mla_bank** out_bank);
+
+/* Same, from rows already resident on the current device; the bank copies
+ * them (the caller may free its buffer afterwards). */
+int grm_b200_mla_bank_create_device(const void* rows_device, int dtype, int64_t nodes,
+                                    int dim, grm_b200_mla_bank** out_bank);
+
+/* Route host queries[query_count, dim] (fp32).  Queries [0, warmup) are routed
+ * but not timed; *elapsed_ms (may be NULL) is the device time of the rest.
+ * out_scores may be NULL.
+ * Replaces grm_mla_cuda_arena_route (scripts/grm_mla_cuda_probe.py:437-467). */
+int grm_b200_mla_route(grm_b200_mla_bank* bank, const float* queries_host, int query_count,
+                       int dim, int warmup, int topk, uint64_t* out_ids_host,
+                       float* out_scores_host, float* elapsed_ms);
+
+/* Route device-resident queries (no H2D copy).
+ * Replaces grm_mla_cuda_arena_route_device (scripts/grm_mla_cuda_probe.py:473-488). */
+int grm_b200_mla_route_device(grm_b200_mla_bank* bank, const float* queries_device,
+                              int query_count, int dim, int warmup, int topk,
+                              uint64_t* out_ids_host, float* out_scores_host,
+                              float* elapsed_ms);
+
+/* Stream-ordered route with device outputs and no host synchronisation (for
+ * CUDA-graph capture and the node-sharded multi-GPU route): writes
+ * out_ids_device[query_count * topk] and out_scores_device[...] on `stream`
+ * (a cudaStream_t, NULL = legacy default stream).  `id_offset` is added to
+ * every returned row id (the first global row of this shard).  query_count
+ * must not exceed the capacity reserved by an earlier synchronous call or by
+ * grm_b200_mla_reserve.  No reference counterpart (the reference is
+ * single-GPU and always synchronises). */
+int grm_b200_mla_route_async(grm_b200_mla_bank* bank, const float* queries_device,
+                             int query_count, int topk, uint64_t id_offset,
+                             uint64_t* out_ids_device, float* out_scores_device,
+                             void* stream);
+
+/* The two phases of grm_b200_mla_route_async, for callers that overlap or
+ * time them separately (same arguments; call scan then resolve on one
+ * stream).  Scan streams the bank once and resolves every query whose
+ * candidates it can prove; resolve runs the exact fallback for the rest and
+ * exits at once when there is none. */
+int grm_b200_mla_scan_async(grm_b200_mla_bank* bank, const float* queries_device,
+                            int query_count, int topk, uint64_t id_offset,
+                            uint64_t* out_ids_device, float* out_scores_device, void* stream);
+int grm_b200_mla_resolve_async(grm_b200_mla_bank* bank, const float* queries_device,
+                               int query_count, int topk, uint64_t id_offset,
+                               uint64_t* out_ids_device, float* out_scores_device,
+                               void* stream);
+
+/* Pre-size the per-query route scratch for up to `max_queries` queries per call. */
+int grm_b200_mla_reserve(grm_b200_mla_bank* bank, int max_queries);
+
+/* Replaces grm_mla_cuda_arena_destroy (scripts/grm_mla_cuda_probe.py:522-525). */
+int grm_b200_mla_bank_destroy(grm_b200_mla_bank* bank);
+const char* grm_b200_mla_last_error(grm_b200_mla_bank* bank);
+
+/* Device pointer to the bank's fp32 row norms (nodes floats), for callers
+ * that keep their own bank copy. */
+const float* grm_b200_mla_row_norms_device(grm_b200_mla_bank* bank);
+
+/* Counters of the exactness machinery since bank creation: routes that needed
+ * the exact fallback pass (margin saturated by near-ties, or a query outside
+ * the fast path's safe range). */
+int grm_b200_mla_stats(grm_b200_mla_bank* bank, uint64_t* routes, uint64_t* fallbacks);
+
+/* ---------------------------------------------------------------- GQA route */
+
+/* Ragged (CSR) GQA key bank.  Node i owns tokens [token_offsets[i],
+ * token_offsets[i+1]); its keys are the contiguous block
+ * keys + token_offsets[i] * kv_heads * head_dim laid out [kv_heads, T_i,
+ * head_dim] (layers concatenated on the head axis).  dtype GRM_B200_BF16,
+ * GRM_B200_F16 or GRM_B200_F32; token_offsets has nodes + 1 entries starting
+ * at 0.  Replaces grm_gqa_cuda_arena_create (scripts/grm_gqa_cuda_probe.py:
+ * 297-365), whose dense zero-padded bank is dropped for CSR. */
+int grm_b200_gqa_bank_create(const void* keys_host, int dtype, const uint64_t* token_offsets,
+                             int64_t nodes, int kv_heads, int head_dim, int device,
+                             grm_b200_gqa_bank** out_bank);
+
+/* Same over keys already resident on the current device.  The bank BORROWS
+ * keys_device (no copy: a 100k-node bank is ~216 GB); the caller keeps it
+ * alive until grm_b200_gqa_bank_destroy. */
+int grm_b200_gqa_bank_create_device(const void* keys_device, int dtype,
+                                    const uint64_t* token_offsets, int64_t nodes,
+                                    int kv_heads, int head_dim,
+                                    grm_b200_gqa_bank** out_bank);
+
+/* Route host queries[query_count, query_heads, query_tokens, head_dim] (fp32).
+ * query_heads must be a multiple of kv_heads (GQA group = query_heads /
+ * kv_heads).  Replaces grm_gqa_cuda_arena_route
+ * (scripts/grm_gqa_cuda_probe.py:484-516). */
+int grm_b200_gqa_route(grm_b200_gqa_bank* bank, const float* queries_host, int query_count,
+                       int query_heads, int query_tokens, int warmup, int topk,
+                       uint64_t* out_ids_host, float* out_scores_host, float* elapsed_ms);
+
+/* Replaces grm_gqa_cuda_arena_route_device (scripts/grm_gqa_cuda_probe.py:524-537). */
+int grm_b200_gqa_route_device(grm_b200_gqa_bank* bank, const float* queries_device,
+                              int query_count, int query_heads, int query_tokens,
+                              int warmup, int topk, uint64_t* out_ids_host,
+                              float* out_scores_host, float* elapsed_ms);
+
+/* Replaces grm_gqa_cuda_arena_destroy (scripts/grm_gqa_cuda_probe.py:584-587). */
+int grm_b200_gqa_bank_destroy(grm_b200_gqa_bank* bank);
+const char* grm_b200_gqa_last_error(grm_b200_gqa_bank* bank);
+int grm_b200_gqa_stats(grm_b200_gqa_bank* bank, uint64_t* routes, uint64_t* refined_nodes);
+
+/* ------------------------------------------------------------------- mount */
+
+/* Fused dequantise + scatter of routed grafts into a preallocated bf16 arena
+ * arena[layers, arena_seats, width] (device).  Graft g's layer l block of
+ * `tokens` rows lands at arena[l, seats[g] .. seats[g] + tokens).  seats is a
+ * host array of n_grafts (<= 64) non-negative offsets with
+ * seats[g] + tokens <= arena_seats.  Runs on `stream` without synchronising.
+ *
+ * grm_b200_mount_ref: the reference storage format of core/graft_quant.py
+ * (:93-144, pack_kv_arrays :177-217): int8 codes (one byte per code at every
+ * bit depth) in groups of 32 along the value stream, fp32 scales; output
+ * bf16(fp16(fp32(code) * scale)) -- the fp16 dequant of
+ * dequantize_symmetric_group32 followed by the bf16 upload cast of
+ * core/graft_arena.py:3490.  codes[n_grafts, layers, tokens * width],
+ * scales[n_grafts, layers, tokens * width / 32].
+ * Replaces unpack_node's host dequant + upload (core/graft_arena.py:3479-3492)
+ * and the splice of core/graft_arena.py:1933-1995. */
+int grm_b200_mount_ref(const int8_t* codes_device, const float* scales_device,
+                       int64_t n_grafts, int64_t layers, int64_t tokens, int64_t width,
+                       const int64_t* seats_host, uint16_t* arena_device,
+                       int64_t arena_seats, void* stream);
+
+/* grm_b200_mount_packed: the packed format -- codes bit-packed little-endian at
+ * `bits` in {8, 6, 4} in groups of `group` (64) values along the flattened
+ * (token, value) stream of each (graft, layer), one fp16 scale per group;
+ * output bf16(fp32(code) * fp32(scale)).  codes[n_grafts, layers,
+ * tokens * width * bits / 8], scales[n_grafts, layers, tokens * width / group].
+ * No reference counterpart (graft_quant keeps one byte per code and fp32
+ * scales); same quantisation law with the scale rounded to fp16. */
+int grm_b200_mount_packed(const uint8_t* codes_device, const uint16_t* scales_device,
+                          int bits, int group, int64_t n_grafts, int64_t layers,
+                          int64_t tokens, int64_t width, const int64_t* seats_host,
+                          uint16_t* arena_device, int64_t arena_seats, void* stream);
+
+/* Device byte splice out = old[:sink] | mount | old[tail_start:] per outer row,
+ * tail_start = min(sink + old_mount_tokens, input_tokens).  old[outer,
+ * input_tokens, row_bytes], mount[outer, mount_tokens, row_bytes], out[outer,
+ * sink + mount_tokens + (input_tokens - tail_start), row_bytes]; row_bytes a
+ * multiple of 16.  *out_tokens receives the output sequence length.  Replaces
+ * the host byte splice DeviceArena::apply_swap_tensor
+ * (cpp/grm_runtime.cpp:4941-5064) / tc.arena_row_pair_transaction. */
+int grm_b200_arena_splice(const void* old_device, int64_t outer, int64_t input_tokens,
+                          const void* mount_device, int64_t mount_tokens, int64_t row_bytes,
+                          int64_t sink_tokens, int64_t old_mount_tokens, void* out_device,
+                          int64_t* out_tokens, void* stream);
+
+/* ----------------------------------------------------- multi-GPU top-k merge */
+
+/* Merge `lists` candidate lists of `per_list` (score, id) entries each (device
+ * arrays scores[lists * per_list], ids[...], UINT64_MAX = empty) into the best
+ * `topk` by score desc then id asc, dropping non-finite scores.  Used after an
+ * NCCL all-gather of per-shard route results.  No reference counterpart (the
+ * reference is single-GPU). */
+int grm_b200_merge_topk(const float* scores_device, const uint64_t* ids_device, int queries,
+                        int lists, int per_list, int topk, float* out_scores_device,
+                        uint64_t* out_ids_device, void* stream);
+
+/* ----------------------------------------------------------------- helpers */
+
+/* Upload a host buffer to a fresh device allocation on the current device.
+ * Replaces grm_{mla,gqa}_cuda_upload_queries (scripts/grm_mla_cuda_probe.py:493-513). */
+int grm_b200_upload(const void* host, size_t bytes, void** out_device);
+/* Replaces grm_{mla,gqa}_cuda_free_device_ptr (scripts/grm_mla_cuda_probe.py:515-520). */
+int grm_b200_free_device_ptr(void* device);
+/* Message of the last failed handle-less call on this thread. */
+const char* grm_b200_last_error(void);
+/* Library version string. */
+const char* grm_b200_version(void);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GRM_B200_H */

@@ -1,0 +1,118 @@
+"""Fused dequant + scatter mount and the arena splice on the GPU, against the
+reference goldens (core/graft_quant.py, DeviceArena::apply_swap_tensor) and the
+CPU oracle.  Bytes must be bit-exact; seats outside the mount keep the fill."""
+
+import numpy as np
+import pytest
+
+import oracle as O
+from graftrepository_b200 import GrmB200Error, graft_mount, synth
+
+pytestmark = pytest.mark.gpu
+SENTINEL = 0x7F81  # a NaN bf16 pattern no dequant produces
+
+
+def _u16(t):
+    import torch
+    return t.view(torch.int16).cpu().numpy().view(np.uint16)
+
+
+@pytest.mark.parametrize("bits", [8, 6, 4, 3, 2])
+def test_ref_format_golden(golden, bits):
+    import torch
+
+    g = golden("quant_g32.npz")
+    x = g["x_f16"].view(np.float16)                      # [2, 3, 8, 96]
+    # treat axis 0 as grafts, axis 1 as layers, (8 tokens x 96 values) per slice
+    codes = torch.from_numpy(g[f"codes{bits}"].reshape(2, 3, -1)).cuda()
+    scales = torch.from_numpy(g[f"scales{bits}"].reshape(2, 3, -1)).cuda()
+    seats = np.array([5, 20], dtype=np.int64)
+    m = graft_mount.ArenaMount(3, 40, 96, fill=SENTINEL)
+    m.mount_ref(codes, scales, seats, tokens=8)
+    got = _u16(m.arena)
+    want = np.full((3, 40, 96), SENTINEL, np.uint16)
+    deq = g[f"dequant_bf16_{bits}"].reshape(2, 3, 8, 96)
+    want = O.mount_scatter(deq, seats, want)
+    assert np.array_equal(got, want)
+    assert x.shape == (2, 3, 8, 96)
+
+
+@pytest.mark.parametrize("bits", [8, 6, 4])
+def test_packed_format_matches_oracle(bits):
+    import torch
+
+    vals = synth.grafts(40 + bits, 3, 5, 128, 288)
+    codes, scales = graft_mount.quantize_packed(vals.reshape(3, 5, -1), bits)
+    seats = synth.seat_offsets(bits, 3, 128, 1000)
+    m = graft_mount.ArenaMount(5, 1000, 288, fill=SENTINEL)
+    m.mount_packed(torch.from_numpy(codes).cuda(),
+                   torch.from_numpy(scales.view(np.uint16)).cuda(), seats, 128, bits)
+    deq = O.dequant_packed(codes.reshape(-1), scales.view(np.uint16).reshape(-1), bits)
+    want = O.mount_scatter(deq.reshape(3, 5, 128, 288), seats,
+                           np.full((5, 1000, 288), SENTINEL, np.uint16))
+    assert np.array_equal(_u16(m.arena), want)
+
+
+def test_full_size_config5_int4_and_ref():
+    """3 grafts x 62 layers x 2048 tokens x 288 values into arena [62, 8192, 288]."""
+    import torch
+
+    vals = synth.grafts(4)
+    seats = synth.seat_offsets(4, 3, 2048, 8192)
+    for bits in (4, 6, 8):
+        codes, scales = graft_mount.quantize_packed(vals.reshape(3, 62, -1), bits)
+        m = graft_mount.ArenaMount(62, 8192, 288, fill=SENTINEL)
+        m.mount_packed(torch.from_numpy(codes).cuda(),
+                       torch.from_numpy(scales.view(np.uint16)).cuda(), seats, 2048, bits)
+        got = _u16(m.arena)
+        deq = O.dequant_packed(codes.reshape(-1), scales.view(np.uint16).reshape(-1), bits)
+        want = O.mount_scatter(deq.reshape(3, 62, 2048, 288), seats,
+                               np.full((62, 8192, 288), SENTINEL, np.uint16))
+        assert np.array_equal(got, want), bits
+        del m
+    # reference format (graft_quant group 32, fp32 scales) at full size
+    c32, s32 = O.quant_ref(vals, 8)
+    m = graft_mount.ArenaMount(62, 8192, 288, fill=SENTINEL)
+    m.mount_ref(torch.from_numpy(c32.reshape(3, 62, -1)).cuda(),
+                torch.from_numpy(s32.reshape(3, 62, -1)).cuda(), seats, tokens=2048)
+    _, bf = O.dequant_ref(c32, s32)
+    want = O.mount_scatter(bf.reshape(3, 62, 2048, 288), seats,
+                           np.full((62, 8192, 288), SENTINEL, np.uint16))
+    assert np.array_equal(_u16(m.arena), want)
+
+
+def test_seat_overflow_is_rejected():
+    import torch
+
+    codes = torch.zeros(1024, dtype=torch.uint8, device="cuda")
+    scales = torch.zeros(32, dtype=torch.int16, device="cuda")
+    arena = torch.zeros((1, 10, 64), dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(GrmB200Error):
+        graft_mount.mount_packed(codes, scales, [5], arena, bits=8, layers=1, tokens=8, width=64)
+
+
+def test_splice_golden(golden):
+    import torch
+
+    g = golden("splice.npz")
+    i = 0
+    while f"c{i}_params" in g:
+        sink, width, old_mount = (int(v) for v in g[f"c{i}_params"])
+        old = g[f"c{i}_old"]
+        mnt = g[f"c{i}_mount"]
+        outer, tin, inner = old.shape
+        # pad rows to a 16-byte multiple: 10 uint16 -> 16 uint16
+        pad = 16 - inner
+        oldp = np.concatenate([old, np.zeros((outer, tin, pad), np.uint16)], axis=2)
+        mntp = np.concatenate([mnt, np.zeros((outer, mnt.shape[1], pad), np.uint16)], axis=2)
+        exp = g[f"c{i}_out"]
+        out = torch.zeros((outer, exp.shape[1], 16), dtype=torch.int16, device="cuda")
+        t_old = torch.from_numpy(oldp.view(np.int16)).cuda()
+        t_m = torch.from_numpy(mntp.view(np.int16)).cuda() if mnt.shape[1] else None
+        got_t = graft_mount.arena_splice(t_old, t_m, out, outer=outer, input_tokens=tin,
+                                         mount_tokens=mnt.shape[1], row_bytes=32,
+                                         sink_tokens=sink, old_mount_tokens=old_mount)
+        assert got_t == exp.shape[1]
+        got = out.cpu().numpy().view(np.uint16)[:, :, :inner]
+        assert np.array_equal(got, exp), i
+        i += 1
