@@ -109,6 +109,42 @@ __device__ float exact_score(const T* row, int dim, const float* q, double qnorm
   return (float)(dot / (qnorm * (double)norm + 1.0e-8));
 }
 
+// Same score with the row norm computed from the row itself in the same pass
+// (rebuild_mla_arena's norm, cpp/grm_runtime.cpp:3240-3249: fp64 sum of squares
+// in element order, cast to float).  Used where no precomputed norms exist.
+template <typename T>
+__device__ float exact_score_inline_norm(const T* row, int dim, const float* q, double qnorm) {
+  double dot = 0.0, n2 = 0.0;
+#pragma unroll 8
+  for (int d = 0; d < dim; ++d) {
+    const double c = (double)to_f(row[d]);
+    dot = fma((double)__ldg(q + d), c, dot);
+    n2 = fma(c, c, n2);
+  }
+  const float norm = (float)sqrt(n2);
+  return (float)(dot / (qnorm * (double)norm + 1.0e-8));
+}
+
+// Sum of squares of one 16-byte slice (approximate row norm, fp32).
+template <typename T>
+__device__ __forceinline__ float sq16(const uint4& v, float acc) {
+  if constexpr (sizeof(T) == 2) {
+    const __half2* h = reinterpret_cast<const __half2*>(&v);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float2 f = __half22float2(h[k]);
+      acc = fmaf(f.x, f.x, acc);
+      acc = fmaf(f.y, f.y, acc);
+    }
+  } else {
+    acc = fmaf(__uint_as_float(v.x), __uint_as_float(v.x), acc);
+    acc = fmaf(__uint_as_float(v.y), __uint_as_float(v.y), acc);
+    acc = fmaf(__uint_as_float(v.z), __uint_as_float(v.z), acc);
+    acc = fmaf(__uint_as_float(v.w), __uint_as_float(v.w), acc);
+  }
+  return acc;
+}
+
 // Reference query norm, element order (cpp/grm_runtime.cpp:4311-4315).
 __device__ double query_norm_seq(const float* q, int dim) {
   double acc = 0.0;
@@ -187,7 +223,10 @@ __device__ void write_result(const Params<T>& p, int q, const WarpList& ex, int 
 }
 
 // Approximate streaming pass (one launch per batch of queries: grid.y = query).
-template <int D, typename T>
+// INL: no precomputed norms -- the approximate row norm is accumulated from
+// the same loads (fp32, <= 8 ulp relative, inside the margin) and the exact
+// refine recomputes the reference norm.
+template <int D, typename T, bool INL = false>
 __global__ void __launch_bounds__(kThreads) mla_scan_kernel(Params<T> p) {
   constexpr int E = 16 / (int)sizeof(T);
   constexpr int CPR = D / E;
@@ -247,25 +286,31 @@ __global__ void __launch_bounds__(kThreads) mla_scan_kernel(Params<T> p) {
          g += (int64_t)gridDim.x * kWarps) {
       const int64_t row0 = g * 32;
       float part[SLOTS];
+      float sq[INL ? SLOTS : 1];
 #pragma unroll
       for (int j = 0; j < SLOTS; ++j) {
         const int64_t row = row0 + j * R + lane / L;
-        float acc = 0.0f;
+        float acc = 0.0f, sacc = 0.0f;
         if (row < p.nodes) {
           const T* rp = p.rows + row * D;
 #pragma unroll
           for (int i = 0; i < CPL; ++i) {
             const int c = (CPR >= 32) ? lane + 32 * i : lane % L;
-            acc = dot16<T>(ld_stream(rp + c * E), qr + i * E, acc);
+            const uint4 v = ld_stream(rp + c * E);
+            acc = dot16<T>(v, qr + i * E, acc);
+            if constexpr (INL) sacc = sq16<T>(v, sacc);
           }
         }
         part[j] = acc;
+        if constexpr (INL) sq[j] = sacc;
       }
       const float dot = reduce_scatter<SLOTS>(part, lane);
+      float n2 = 0.0f;
+      if constexpr (INL) n2 = reduce_scatter<SLOTS>(sq, lane);
       const int64_t row = row0 + (lane % L) * R + lane / L;
       float s = -INFINITY;
       if (row < p.nodes) {
-        const float nrm = __ldg(p.norms + row);
+        const float nrm = INL ? sqrtf(n2) : __ldg(p.norms + row);
         if (isfinite(nrm)) s = dot * __frcp_rn(nrm + e_q);
       }
       list.offer(s, (uint32_t)row, lane);
@@ -343,7 +388,10 @@ __global__ void __launch_bounds__(kThreads) mla_scan_kernel(Params<T> p) {
   if (cand) {
     const double qnorm = query_norm_seq(query, D);
     const int64_t row = list.id;
-    es = exact_score<T>(p.rows + row * D, D, query, qnorm, __ldg(p.norms + row));
+    if constexpr (INL)
+      es = exact_score_inline_norm<T>(p.rows + row * D, D, query, qnorm);
+    else
+      es = exact_score<T>(p.rows + row * D, D, query, qnorm, __ldg(p.norms + row));
   }
   WarpList ex;
   ex.init();
@@ -359,8 +407,8 @@ __global__ void __launch_bounds__(kThreads) mla_scan_kernel(Params<T> p) {
 // compute exact scores for every row whose approximate score reaches the
 // threshold; for kUnsafe (or force_all) compute exact scores for all rows.
 // Queries whose status is kOk exit at once.  D == 0 means runtime dim
-// (force_all only).
-template <int D, typename T>
+// (force_all only).  INL: row norms computed inline (see mla_scan_kernel).
+template <int D, typename T, bool INL = false>
 __global__ void __launch_bounds__(kThreads) mla_exact_kernel(Params<T> p) {
   __shared__ float sh_s[kWarps * 32];
   __shared__ uint32_t sh_id[kWarps * 32];
@@ -400,8 +448,12 @@ __global__ void __launch_bounds__(kThreads) mla_exact_kernel(Params<T> p) {
       const int64_t row = row0 + lane;
       float es = -INFINITY;
       if (row < p.nodes) {
-        const float nrm = __ldg(p.norms + row);
-        if (isfinite(nrm)) es = exact_score<T>(p.rows + row * dim, dim, query, qnorm, nrm);
+        if constexpr (INL) {
+          es = exact_score_inline_norm<T>(p.rows + row * dim, dim, query, qnorm);
+        } else {
+          const float nrm = __ldg(p.norms + row);
+          if (isfinite(nrm)) es = exact_score<T>(p.rows + row * dim, dim, query, qnorm, nrm);
+        }
       }
       list.offer(es, (uint32_t)row, lane);
     }
@@ -431,28 +483,39 @@ __global__ void __launch_bounds__(kThreads) mla_exact_kernel(Params<T> p) {
          g += (int64_t)gridDim.x * kWarps) {
       const int64_t row0 = g * 32;
       float part[SLOTS];
+      float sq[INL ? SLOTS : 1];
 #pragma unroll
       for (int j = 0; j < SLOTS; ++j) {
         const int64_t row = row0 + j * R + lane / L;
-        float acc = 0.0f;
+        float acc = 0.0f, sacc = 0.0f;
         if (row < p.nodes) {
           const T* rp = p.rows + row * D;
 #pragma unroll
           for (int i = 0; i < CPL; ++i) {
             const int c = (CPR >= 32) ? lane + 32 * i : lane % L;
-            acc = dot16<T>(*reinterpret_cast<const uint4*>(rp + c * E), qr + i * E, acc);
+            const uint4 v = *reinterpret_cast<const uint4*>(rp + c * E);
+            acc = dot16<T>(v, qr + i * E, acc);
+            if constexpr (INL) sacc = sq16<T>(v, sacc);
           }
         }
         part[j] = acc;
+        if constexpr (INL) sq[j] = sacc;
       }
       const float dot = reduce_scatter<SLOTS>(part, lane);
+      float n2 = 0.0f;
+      if constexpr (INL) n2 = reduce_scatter<SLOTS>(sq, lane);
       const int64_t row = row0 + (lane % L) * R + lane / L;
       float es = -INFINITY;
       if (row < p.nodes) {
-        const float nrm = __ldg(p.norms + row);
+        const float nrm = INL ? sqrtf(n2) : __ldg(p.norms + row);
         if (isfinite(nrm)) {
           const float s = dot * __frcp_rn(nrm + e_q);
-          if (s >= thr) es = exact_score<T>(p.rows + row * D, D, query, qnorm, nrm);
+          if (s >= thr) {
+            if constexpr (INL)
+              es = exact_score_inline_norm<T>(p.rows + row * D, D, query, qnorm);
+            else
+              es = exact_score<T>(p.rows + row * D, D, query, qnorm, nrm);
+          }
         }
       }
       list.offer(es, (uint32_t)row, lane);
@@ -964,3 +1027,171 @@ int grm_b200_mla_stats(grm_b200_mla_bank* bank, uint64_t* routes, uint64_t* fall
 }
 
 }  // extern "C"
+
+// ----------------------------------------------------------------------------
+// Allocation-free route.
+//
+// Some callers cannot call cudaMalloc on the route path: a serving engine that
+// reserves all of HBM for its KV cache and hands out memory only through its
+// own pool, code that routes while a CUDA graph is being captured (cudaMalloc
+// is not a capturable operation), or a latency-critical decode loop that must
+// never hit the implicit device synchronisation of an allocation.  Such
+// callers own their centroid rows and output buffers already; this entry point
+// routes over them using only a fixed scratch array compiled into the library.
+//
+// The scratch is a file-scope __device__ array of kNoAllocScratchBytes (2 MiB).
+// Every GPU that loads this library holds it until the process exits.  All
+// calls on a device share it and it keeps the last call's contents, so each
+// call first clears the per-query counters it relies on; calls whose kernels
+// overlap on the GPU (different streams, or concurrent host threads) race on
+// it and must be serialised by the caller.  Host code only ever passes the
+// address returned by cudaGetSymbolAddress, fetched once per device on the
+// first call made with that device current; that first call should therefore
+// come before any stream capture.
+
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t(2) << 20;
+constexpr int kNoAllocMaxQueries = 16;
+
+__device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+std::mutex g_noalloc_mu;
+unsigned char* g_noalloc_ptr[64] = {};
+int g_noalloc_occ[64][4] = {};
+
+int dim_slot(int dim) {
+  switch (dim) {
+    case 64: return 0;
+    case 128: return 1;
+    case 256: return 2;
+    case 512: return 3;
+  }
+  return -1;
+}
+
+ScanFn<__half> scan_fn_inline(int dim) {
+  switch (dim) {
+    case 64: return mla_scan_kernel<64, __half, true>;
+    case 128: return mla_scan_kernel<128, __half, true>;
+    case 256: return mla_scan_kernel<256, __half, true>;
+    case 512: return mla_scan_kernel<512, __half, true>;
+  }
+  return nullptr;
+}
+
+ScanFn<__half> exact_fn_inline(int dim) {
+  switch (dim) {
+    case 64: return mla_exact_kernel<64, __half, true>;
+    case 128: return mla_exact_kernel<128, __half, true>;
+    case 256: return mla_exact_kernel<256, __half, true>;
+    case 512: return mla_exact_kernel<512, __half, true>;
+  }
+  return nullptr;
+}
+
+// Per-device set-up: the device address of the scratch array and the
+// occupancy of the inline scan kernels.  Runs under g_noalloc_mu.
+int noalloc_setup(int dev, int slot, unsigned char** base, int* occ) {
+  if (dev < 0 || dev >= 64) return GRM_B200_EINVAL;
+  if (!g_noalloc_ptr[dev]) {
+    void* ptr = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (e != cudaSuccess) {
+      set_thread_error("cudaGetSymbolAddress(scratch) failed on device %d: %s", dev,
+                       cudaGetErrorString(e));
+      return cuda_status(e);
+    }
+    g_noalloc_ptr[dev] = static_cast<unsigned char*>(ptr);
+  }
+  if (!g_noalloc_occ[dev][slot]) {
+    int o = 0;
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+        &o, scan_fn_inline(64 << slot), kThreads, 0);
+    if (e != cudaSuccess) {
+      set_thread_error("occupancy query failed: %s", cudaGetErrorString(e));
+      return cuda_status(e);
+    }
+    g_noalloc_occ[dev][slot] = std::max(1, o);
+  }
+  *base = g_noalloc_ptr[dev];
+  *occ = g_noalloc_occ[dev][slot];
+  return 0;
+}
+
+}  // namespace
+
+extern "C" int grm_b200_mla_route_noalloc(const void* rows_device, int64_t nodes, int dim,
+                                          const float* queries_device, int query_count, int topk,
+                                          uint64_t* out_ids_device, float* out_scores_device,
+                                          void* stream) {
+  const int slot = dim_slot(dim);
+  if (!rows_device || !queries_device || !out_ids_device || !out_scores_device || nodes <= 0 ||
+      nodes >= (int64_t)0xFFFFFFFF || slot < 0 || topk <= 0 || topk > GRM_B200_MAX_TOPK ||
+      query_count <= 0) {
+    set_thread_error("invalid allocation-free MLA route arguments (nodes=%lld dim=%d topk=%d "
+                     "queries=%d; dim must be 64, 128, 256 or 512)",
+                     (long long)nodes, dim, topk, query_count);
+    return GRM_B200_EINVAL;
+  }
+  if (query_count > kNoAllocMaxQueries) {
+    set_thread_error("allocation-free MLA route takes at most %d queries per call (got %d)",
+                     kNoAllocMaxQueries, query_count);
+    return GRM_B200_EINVAL;
+  }
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    set_thread_error("cudaGetDevice failed: %s", cudaGetErrorString(e));
+    return cuda_status(e);
+  }
+  DeviceInfo info;
+  int rc = device_info(dev, &info);
+  if (rc) {
+    set_thread_error("device query failed");
+    return rc;
+  }
+  unsigned char* base = nullptr;
+  int occ = 1;
+  {
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    rc = noalloc_setup(dev, slot, &base, &occ);
+  }
+  if (rc) return rc;
+  const int64_t groups = ceil_div64(nodes, 32);
+  const int grid_x = (int)std::max<int64_t>(
+      1, std::min<int64_t>((int64_t)info.sms * occ, ceil_div64(groups, kWarps)));
+  const size_t results_bytes = (sizeof(Result) * (size_t)query_count + 255) & ~(size_t)255;
+  const size_t stride = scratch_stride(grid_x);
+  const size_t need = results_bytes + stride * (size_t)query_count;
+  if (need > kNoAllocScratchBytes) {
+    set_thread_error("allocation-free MLA route needs %zu scratch bytes, the fixed array holds %zu",
+                     need, kNoAllocScratchBytes);
+    return GRM_B200_EINVAL;
+  }
+  Params<__half> p;
+  p.rows = static_cast<const __half*>(rows_device);
+  p.norms = nullptr;
+  p.nodes = nodes;
+  p.dim = dim;
+  p.queries = queries_device;
+  p.topk = topk;
+  p.scratch = Scratch{base + results_bytes, stride, grid_x};
+  p.results = reinterpret_cast<Result*>(base);
+  p.out_ids = out_ids_device;
+  p.out_scores = out_scores_device;
+  p.id_offset = 0;
+  p.force_all = 0;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  scratch_init_kernel<<<(query_count + 127) / 128, 128, 0, s>>>(base + results_bytes, stride,
+                                                                 query_count);
+  dim3 grid(grid_x, query_count);
+  scan_fn_inline(dim)<<<grid, kThreads, 0, s>>>(p);
+  exact_fn_inline(dim)<<<grid, kThreads, 0, s>>>(p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_thread_error("allocation-free MLA route launch failed: %s", cudaGetErrorString(e));
+    return cuda_status(e);
+  }
+  return 0;
+}

@@ -130,6 +130,25 @@ const float* grm_b200_mla_row_norms_device(grm_b200_mla_bank* bank);
  * the fast path's safe range). */
 int grm_b200_mla_stats(grm_b200_mla_bank* bank, uint64_t* routes, uint64_t* fallbacks);
 
+/* Allocation-free MLA route.  No counterpart in the reference.  For callers
+ * that must not allocate device memory on the route path -- an engine that owns
+ * all of HBM through its own pool, a route issued during CUDA-graph capture, a
+ * decode loop that cannot afford an allocation's implicit synchronisation.
+ * The caller passes fp16 rows[nodes, dim] (dim 64, 128, 256 or 512) and fp32
+ * queries[query_count, dim] (query_count <= 16) in device memory and receives
+ * ids/scores[query_count, topk] in its own device buffers on `stream`; row
+ * norms are computed inline, results are bit-exact with the bank entry
+ * points.  Scratch is a fixed 2 MiB __device__ array inside the library (held
+ * by every GPU that loads it until exit), shared by all calls: calls that
+ * overlap on the GPU race and must be serialised by the caller.  The first
+ * call on each device looks up the array's device address; make it before any
+ * stream capture.  Oversized requests return -1 with a message in
+ * grm_b200_last_error(). */
+int grm_b200_mla_route_noalloc(const void* rows_device, int64_t nodes, int dim,
+                               const float* queries_device, int query_count, int topk,
+                               uint64_t* out_ids_device, float* out_scores_device,
+                               void* stream);
+
 /* ---------------------------------------------------------------- GQA route */
 
 /* Ragged (CSR) GQA key bank.  Node i owns tokens [token_offsets[i],
