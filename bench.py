@@ -54,6 +54,11 @@ def parse():
     p.add_argument("--warmup", type=int, default=20)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--workload", default="mla_1m_b1",
+                   choices=["mla_1m_b1", "gqa_512", "gqa_100k", "mount_int4", "mount_int6",
+                            "mount_int8", "mount_ref8"],
+                   help="mla_1m_b1 is the headline (BASELINE config 2); the others measure "
+                        "the GQA route (configs 3/4) and the quantised mount (config 5)")
     return p.parse_args()
 
 
@@ -269,31 +274,42 @@ def run_ours(args):
     ms_i = torch.empty((1, TOPK), dtype=torch.int64, device="cuda")
 
     def step(i, ev):
+        """One route: scan + resolve (programmatic dependent launch) [+ gather + merge]."""
         q = qs_dev[i:i + 1]
         if ev:
             ev[0].record(stream)
-        rc = lib.grm_b200_mla_scan_async(bank._h, q.data_ptr(), 1, TOPK, a, out_i.data_ptr(),
-                                         out_s.data_ptr(), sptr)
-        if ev:
-            ev[1].record(stream)
-        rc |= lib.grm_b200_mla_resolve_async(bank._h, q.data_ptr(), 1, TOPK, a, out_i.data_ptr(),
-                                             out_s.data_ptr(), sptr)
+        rc = lib.grm_b200_mla_route_async(bank._h, q.data_ptr(), 1, TOPK, a, out_i.data_ptr(),
+                                          out_s.data_ptr(), sptr)
         if world > 1:
             dist.all_gather_into_tensor(gs, out_s.view(-1))
             dist.all_gather_into_tensor(gi, out_i.view(-1))
             rc |= lib.grm_b200_merge_topk(gs.data_ptr(), gi.data_ptr(), 1, world, TOPK, TOPK,
                                           ms_s.data_ptr(), ms_i.data_ptr(), sptr)
         if ev:
-            ev[2].record(stream)
+            ev[1].record(stream)
         if rc:
             raise RuntimeError("route launch failed")
+
+    def scan_only(i, ev):
+        """The dominant kernel alone, event-timed on its stream (roofline)."""
+        q = qs_dev[i:i + 1]
+        ev[0].record(stream)
+        rc = lib.grm_b200_mla_scan_async(bank._h, q.data_ptr(), 1, TOPK, a, out_i.data_ptr(),
+                                         out_s.data_ptr(), sptr)
+        ev[1].record(stream)
+        rc |= lib.grm_b200_mla_resolve_async(bank._h, q.data_ptr(), 1, TOPK, a,
+                                             out_i.data_ptr(), out_s.data_ptr(), sptr)
+        if rc:
+            raise RuntimeError("scan launch failed")
 
     for i in range(args.warmup):
         if flush is not None:
             flush.zero_()
         step(i, None)
     torch.cuda.synchronize()
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(args.steps)]
+    n_scan = min(args.steps, 1000)
+    sevs = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(n_scan)]
     with ClockSampler(local) as clk:
         if world > 1:
             dist.barrier()
@@ -307,8 +323,13 @@ def run_ours(args):
         wall = time.perf_counter() - wall0
         if world > 1:
             dist.barrier()
-    step_ms = [e[0].elapsed_time(e[2]) for e in evs]
-    scan_ms = [e[0].elapsed_time(e[1]) for e in evs]
+        for i in range(n_scan):
+            if flush is not None:
+                flush.zero_()
+            scan_only(args.warmup + i, sevs[i])
+        torch.cuda.synchronize()
+    step_ms = [e[0].elapsed_time(e[1]) for e in evs]
+    scan_ms = [e[0].elapsed_time(e[1]) for e in sevs]
     tot = torch.tensor([sum(step_ms)], dtype=torch.float64, device="cuda")
     if world > 1:
         dist.all_reduce(tot, op=dist.ReduceOp.MAX)
@@ -382,6 +403,7 @@ def run_ours(args):
                 "d2h_bytes_per_step": d2h, "steps": e2e_steps,
                 "api": "CudaMLARouteBank.route_topk" if world == 1 else "ShardedMLARoute.route"},
         "gpu_launches": args.steps * (2 if world == 1 else 3),
+        "roofline_launches": n_scan,
         "clocks": clocks,
         "wall_s_timed_region": wall,
     }
@@ -390,10 +412,311 @@ def run_ours(args):
         bank.close()
 
 
+# ------------------------------------------------------------ secondary workloads
+
+def _dist_setup():
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def run_gqa(args):
+    """Ragged GQA route: config 3 (512 nodes, T ~ U{16..1024}) or config 4
+    (100k nodes, lognormal T).  A step routes one probe over the whole bank
+    (1 GPU: the largest node prefix that fits, for config 4); at N GPUs the
+    bank is node-range sharded balanced by tokens, candidates all-gathered."""
+    import torch
+    import torch.distributed as dist
+
+    from graftrepository_b200 import _lib, synth
+    from graftrepository_b200.cuda_router import CudaGQARouteSidecar
+    from graftrepository_b200.sharded import gqa_shard_range
+
+    world, rank, local = _dist_setup()
+    lib = _lib.load()
+    KH, D, H = 32, 128, 128
+    if args.workload == "gqa_512":
+        lengths = synth.gqa_lengths(2, 512, "uniform")
+        seed = 2
+    else:
+        lengths = synth.gqa_lengths(3, 100_000, "lognormal")
+        seed = 3
+    off_all = synth.offsets(lengths)
+    a, b = gqa_shard_range(off_all, world, rank)
+    prefix_note = None
+    if world == 1 and args.workload == "gqa_100k":
+        cap_tokens = int(150e9 // (KH * D * 2))           # largest resident prefix: 150 GB
+        b = int(np.searchsorted(off_all, cap_tokens, side="right")) - 1
+        prefix_note = f"resident prefix of {b} of 100000 nodes ({int(off_all[b])} tokens)"
+    sub_len = lengths[a:b]
+    # draw this shard's keys directly (the seed is offset by the shard's first node)
+    keys, off = synth.gqa_bank_device(seed * 1000 + a, sub_len)
+    bank = CudaGQARouteSidecar(device=local).create_bank_device(
+        keys.data_ptr(), 2, off, KH, D, keepalive=keys)
+    tokens = int(off[-1])
+    bytes_per_probe = tokens * KH * D * 2
+    n_q = args.warmup + args.steps
+    qs_host = torch.from_numpy(synth.gqa_query(seed, count=n_q)).pin_memory()
+    qs_dev = qs_host.cuda()
+    k = TOPK
+    out_s = torch.empty((1, k), dtype=torch.float32, device="cuda")
+    out_i = torch.empty((1, k), dtype=torch.int64, device="cuda")
+    gs = torch.empty((world, k), dtype=torch.float32, device="cuda")
+    gi = torch.empty((world, k), dtype=torch.int64, device="cuda")
+    ms_s = torch.empty((1, k), dtype=torch.float32, device="cuda")
+    ms_i = torch.empty((1, k), dtype=torch.int64, device="cuda")
+    stream = torch.cuda.current_stream()
+    qsz = H * D
+
+    def step(i):
+        rc = lib.grm_b200_gqa_route_async(bank._h, qs_dev[i].data_ptr(), 1, H, 1, k, a,
+                                          out_i.data_ptr(), out_s.data_ptr(), stream.cuda_stream)
+        if world > 1:
+            dist.all_gather_into_tensor(gs, out_s.view(-1))
+            dist.all_gather_into_tensor(gi, out_i.view(-1))
+            rc |= lib.grm_b200_merge_topk(gs.data_ptr(), gi.data_ptr(), 1, world, k, k,
+                                          ms_s.data_ptr(), ms_i.data_ptr(), stream.cuda_stream)
+        if rc:
+            raise RuntimeError(bank._err())
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(args.steps)]
+    with ClockSampler(local) as clk:
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        for i in range(args.steps):
+            evs[i][0].record(stream)
+            step(args.warmup + i)
+            evs[i][1].record(stream)
+        torch.cuda.synchronize()
+    step_ms = [e[0].elapsed_time(e[1]) for e in evs]
+    tot = torch.tensor([sum(step_ms)], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(tot, op=dist.ReduceOp.MAX)
+    total_ms = float(tot.item())
+    value = args.steps / (total_ms / 1e3)
+    # e2e: public API, host query in, host ids out
+    e2e_steps = min(args.steps, 50)
+    qn = qs_host.numpy()
+    if world == 1:
+        for i in range(2):
+            bank.route_topk(qn[i], topk=k)
+        t0 = time.perf_counter()
+        for i in range(e2e_steps):
+            bank.route_topk(qn[(args.warmup + i) % n_q], topk=k)
+        e2e_s = time.perf_counter() - t0
+    else:
+        qbuf = torch.empty((H, 1, D), dtype=torch.float32, device="cuda")
+        dist.barrier()
+        t0 = time.perf_counter()
+        for i in range(e2e_steps):
+            qbuf.copy_(qs_host[(args.warmup + i) % n_q], non_blocking=True)
+            lib.grm_b200_gqa_route_async(bank._h, qbuf.data_ptr(), 1, H, 1, k, a,
+                                         out_i.data_ptr(), out_s.data_ptr(), stream.cuda_stream)
+            dist.all_gather_into_tensor(gs, out_s.view(-1))
+            dist.all_gather_into_tensor(gi, out_i.view(-1))
+            lib.grm_b200_merge_topk(gs.data_ptr(), gi.data_ptr(), 1, world, k, k,
+                                    ms_s.data_ptr(), ms_i.data_ptr(), stream.cuda_stream)
+            ms_i.cpu(), ms_s.cpu()
+        e2e_s = time.perf_counter() - t0
+        t = torch.tensor([e2e_s], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    routes, refined = bank.stats()
+    peak, peak_kind = peaks()
+    step_mean = statistics.mean(step_ms)
+    achieved = bytes_per_probe / (step_mean / 1e3) / 1e9
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_gqa_baseline(keys, off, qn[0], KH, D)
+    if world > 1:
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    total_tokens = int(off_all[-1]) if prefix_note is None else tokens
+    print(json.dumps({
+        "metric": f"ragged GQA route throughput ({args.workload})", "value": value,
+        "unit": "probes/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": total_ms / args.steps, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16 keys, bf16x2 tensor-core q.k, f32 exact refine",
+        "data": "synthetic",
+        "config": {"workload": args.workload, "nodes": int(len(lengths)) if prefix_note is None
+                   else b, "tokens_total": total_tokens, "kv_heads": KH, "q_heads": H,
+                   "head_dim": D, "topk": k, "prefix": prefix_note,
+                   "shard_tokens_rank0": tokens,
+                   "l2": "bank larger than L2" if bytes_per_probe > 4 * L2_BYTES else "small bank"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "peak_kind": peak_kind,
+                     "kernel": "whole route step (gqa_scan_kernel dominant)",
+                     "algorithmic_bytes_per_launch": bytes_per_probe, "traffic": None,
+                     "step_us_mean": step_mean * 1e3},
+        "refined_nodes_per_route": refined / max(routes, 1),
+        "cpu_baseline": cpu,
+        "e2e": {"value": e2e_steps / e2e_s, "unit": "probes/s", "h2d_bytes_per_step": qsz * 4,
+                "d2h_bytes_per_step": 400 if world == 1 else k * 12, "steps": e2e_steps},
+        "gpu_launches": args.steps * (6 + (1 if world > 1 else 0)),
+        "clocks": clk.summary(),
+    }), flush=True)
+
+
+def cpu_gqa_baseline(keys_dev, off, q, KH, D, max_tokens=40_000, budget_s=8.0):
+    """Reference GQA route (oracle/_ref OpenMP build) on a node prefix of the
+    bank with <= max_tokens tokens (its store keeps ~5 fp32 copies per key),
+    reported per token scaled to the measured bank's token count."""
+    import oracle as O
+
+    n = int(np.searchsorted(off, max_tokens, side="right")) - 1
+    n = max(1, n)
+    t = int(off[n])
+    keys = keys_dev[: t * KH * D].view(__import__("torch").int16).cpu().numpy().view(np.uint16)
+    cores = len(os.sched_getaffinity(0))
+    if O.ref_available(omp=True):
+        st = O.RefStore(omp=True).load_gqa(keys, off[: n + 1], KH, D)
+        st.route(q, TOPK)
+        route = lambda: st.route(q, TOPK)  # noqa: E731
+        kind = "reference"
+    else:
+        route = lambda: O.gqa_route(keys, off[: n + 1], KH, D, q, TOPK)  # noqa: E731
+        kind = "port"
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while (time.perf_counter() < t_end or len(times) < 3) and len(times) < 50:
+        t0 = time.perf_counter()
+        route()
+        times.append(time.perf_counter() - t0)
+    per_token = statistics.median(times) / t
+    return {"value": 1.0 / (per_token * int(off[-1])), "unit": "probes/s", "cores": cores,
+            "kind": kind,
+            "sample": f"{n}-node prefix ({t} tokens), median {statistics.median(times)*1e3:.1f} ms,"
+                      f" scaled per token to {int(off[-1])} tokens"}
+
+
+def run_mount(args):
+    """Config 5: 3 grafts x 62 layers x 2048 tokens x 288 values, quantised,
+    dequantised + scattered into a bf16 arena [62, 8192, 288].  A step is one
+    mount of all three grafts.  Replicas only at N > 1 (no collective)."""
+    import torch
+    import torch.distributed as dist
+
+    import oracle as O
+    from graftrepository_b200 import graft_mount, synth
+
+    world, rank, local = _dist_setup()
+    G, L, T, W, S = 3, 62, 2048, 288, 8192
+    vals = synth.grafts(4, G, L, T, W)
+    seats = synth.seat_offsets(4, G, T, S)
+    arena = graft_mount.ArenaMount(L, S, W, device=f"cuda:{local}", fill=0x7F81)
+    stream = torch.cuda.current_stream()
+    V = G * L * T * W
+    if args.workload == "mount_ref8":
+        c, sc = O.quant_ref(vals, 8)              # graft_quant format (group 32, fp32 scales)
+        codes = torch.from_numpy(c.reshape(G, L, -1)).cuda()
+        scales = torch.from_numpy(sc.reshape(G, L, -1)).cuda()
+        bytes_per = V + V // 32 * 4 + 2 * V
+        fn = lambda: arena.mount_ref(codes, scales, seats, T, stream=stream)  # noqa: E731
+        bits = 8
+    else:
+        bits = int(args.workload[-1])
+        c, sc = graft_mount.quantize_packed(vals.reshape(G, L, -1), bits)
+        codes = torch.from_numpy(c).cuda()
+        scales = torch.from_numpy(sc.view(np.uint16)).cuda()
+        bytes_per = V * bits // 8 + V // 64 * 2 + 2 * V
+        fn = lambda: arena.mount_packed(codes, scales, seats, T, bits, stream=stream)  # noqa: E731
+    flush = torch.empty(2 * L2_BYTES, dtype=torch.uint8, device="cuda")
+    for _ in range(args.warmup):
+        fn()
+    torch.cuda.synchronize()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(args.steps)]
+    with ClockSampler(local) as clk:
+        for i in range(args.steps):
+            flush.zero_()
+            evs[i][0].record(stream)
+            fn()
+            evs[i][1].record(stream)
+        torch.cuda.synchronize()
+    ms = [e[0].elapsed_time(e[1]) for e in evs]
+    total_ms = sum(ms)
+    # e2e: host codes/scales -> device, mount, arena checksum back to host
+    ch, sh = torch.from_numpy(c).pin_memory(), torch.from_numpy(np.ascontiguousarray(sc)).pin_memory()
+    e2e_steps = min(args.steps, 20)
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        codes.view(-1).copy_(ch.view(-1).view(codes.dtype), non_blocking=True)
+        scales.view(-1).copy_(sh.view(-1).view(scales.dtype), non_blocking=True)
+        fn()
+        arena.arena[0, 0, :8].cpu()
+    torch.cuda.synchronize()
+    e2e_s = time.perf_counter() - t0
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline:
+        cpu = cpu_mount_baseline(vals, bits, args.workload)
+    peak, peak_kind = peaks()
+    achieved = bytes_per / (statistics.mean(ms) / 1e3) / 1e9
+    if world > 1:
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    print(json.dumps({
+        "metric": f"quantised graft mount ({args.workload})", "value": args.steps / (total_ms / 1e3),
+        "unit": "mounts/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": total_ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": f"int{bits} codes -> bf16", "data": "synthetic",
+        "config": {"workload": args.workload, "grafts": G, "layers": L, "tokens": T, "width": W,
+                   "arena_seats": S, "l2": "256 MB L2 flush before every step, outside events"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "peak_kind": peak_kind,
+                     "algorithmic_bytes_per_launch": bytes_per, "traffic": None,
+                     "kernel": "mount_ref_kernel" if bits == 8 and args.workload == "mount_ref8"
+                     else f"mount_packed_kernel<{bits}>"},
+        "cpu_baseline": cpu,
+        "e2e": {"value": e2e_steps / e2e_s, "unit": "mounts/s",
+                "h2d_bytes_per_step": int(c.nbytes + sc.nbytes), "d2h_bytes_per_step": 16,
+                "steps": e2e_steps},
+        "gpu_launches": args.steps, "clocks": clk.summary(),
+    }), flush=True)
+
+
+def cpu_mount_baseline(vals, bits, workload):
+    """The reference's CPU dequant (core/graft_quant.dequantize_symmetric_group32
+    restated by the oracle, group 32, fp32 scales) + the bf16 cast, per mount,
+    on one graft layer scaled to the 3 x 62 layers (the reference does it per
+    layer on the host, core/graft_arena.py:3485-3492)."""
+    import oracle as O
+
+    one = vals[0, 0]
+    c, s = O.quant_ref(one, 8 if bits == 8 else bits)
+    times = []
+    for _ in range(5):
+        t0 = time.perf_counter()
+        O.dequant_ref(c, s)
+        times.append(time.perf_counter() - t0)
+    per_layer = statistics.median(times)
+    layers = vals.shape[0] * vals.shape[1]
+    return {"value": 1.0 / (per_layer * layers), "unit": "mounts/s", "cores":
+            len(os.sched_getaffinity(0)), "kind": "port",
+            "sample": f"dequant of one [2048, 288] layer x {layers} layers "
+                      f"(median {per_layer*1e3:.2f} ms/layer, OpenMP C restatement)"}
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload.startswith("gqa"):
+        run_gqa(args)
+    elif args.workload.startswith("mount"):
+        run_mount(args)
     else:
         run_ours(args)
 

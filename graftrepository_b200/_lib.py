@@ -60,6 +60,7 @@ _SIGS = {
     "grm_b200_gqa_bank_create_device": (_I, [_P, _I, _P, _I64, _I, _I, _P]),
     "grm_b200_gqa_route": (_I, [_P, _P, _I, _I, _I, _I, _I, _P, _P, _P]),
     "grm_b200_gqa_route_device": (_I, [_P, _P, _I, _I, _I, _I, _I, _P, _P, _P]),
+    "grm_b200_gqa_route_async": (_I, [_P, _P, _I, _I, _I, _I, _U64, _P, _P, _P]),
     "grm_b200_gqa_bank_destroy": (_I, [_P]),
     "grm_b200_gqa_last_error": (ctypes.c_char_p, [_P]),
     "grm_b200_gqa_stats": (_I, [_P, _P, _P]),

@@ -14,7 +14,7 @@
 // node asc; the first topk are returned (:4800-4838).
 //
 // Design.  The bank is CSR: node i owns the contiguous block
-// [KH, T_i, D] at token offset off[i].  Work items are (node, kv head, 64-token
+// [KH, T_i, D] at token offset off[i].  Work items are (node, kv head, 128-token
 // chunk); a warp computes q.k for 16 key tokens x up to 16 query vectors per
 // mma.sync.m16n8k16 (bf16 or f16 operands, fp32 accumulate), with the fp32
 // query split into hi + lo halves of the key type so the products carry ~16
@@ -40,7 +40,7 @@ namespace gqa {
 
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
-constexpr int kChunk = 64;       // key tokens per work item
+constexpr int kChunk = 128;      // key tokens per work item
 constexpr float kEps = 2.44140625e-4f;  // 2^-12 relative to |q||k|: >= 5x the proven bound
 constexpr float kHuge = 1.0e30f;
 constexpr int kRefineY = 32;     // candidates refined concurrently
@@ -51,6 +51,16 @@ struct Result {
   uint64_t ids[GRM_B200_MAX_TOPK];
   float scores[GRM_B200_MAX_TOPK];
 };
+
+// One scan work item: up to kChunk key tokens of one (node, kv head).
+// base: element offset of the item's first key row; ntok: rows in the item.
+struct Item {
+  uint64_t base;
+  uint32_t node;
+  uint16_t kh;
+  uint16_t ntok;
+};
+static_assert(sizeof(Item) == 16, "one 16-byte load per item");
 
 struct QueryInfo {
   int finite;      // every query value finite
@@ -163,7 +173,7 @@ struct RouteParams {
   int nv;          // query vectors per kv head = group * qt
   float inv_denom;
   const float* query;          // [H, qt, D] of this query
-  const uint64_t* items;       // work items
+  const Item* items;           // work items
   int64_t n_items;
   const float* kmax;           // [N, KH]
   const unsigned char* key_bad;
@@ -175,53 +185,63 @@ struct RouteParams {
   uint32_t* frag;              // query fragments [KH][NT][32][16]
   float* qnorm_h;              // [H] max_qi |q_{h,qi}|
   QueryInfo* qinfo;
+  int* qparts;                 // [KH] per-kv-head query flags (bit 0 non-finite, bit 1 too large)
+  unsigned* qcount;            // query_prep blocks finished (re-armed by the last one)
   int topk;
   int fast;                    // 1 = approximate pass available for this bank
   Result* result;
   int qt4;                     // reference query_tokens == 4 path
+  uint64_t* out_ids;           // optional device outputs (topk entries of this query)
+  float* out_scores;
+  uint64_t id_offset;          // added to returned node rows (first row of this shard)
 };
 
-// Query preparation: hi/lo fragments in mma B layout, per-head norms, finite flag.
-// One block; K permutation: k-step s, slot (c, j) <-> dim 32*c + 4*s + j for
-// D == 128 (16*c + 4*s + j for D == 64).
+// Query preparation, one block per kv head: hi/lo fragments in mma B layout,
+// the norms of that kv head's query heads, and the finite / range flags of
+// its query values.  The last block to finish combines the flags into
+// p.qinfo (and re-arms the counter).  K permutation: k-step s, slot (c, j)
+// <-> dim (D/4)*c + 4*s + j.
 template <typename KT, int D, int NT>
-__global__ void query_prep_kernel(RouteParams p) {
+__global__ void __launch_bounds__(128) query_prep_kernel(RouteParams p) {
   constexpr int KSTEPS = D / 16;
   constexpr int NVP = NT * 4;  // padded vector count: hi cols [0, NVP), lo cols [NVP, 2 NVP)
-  __shared__ int s_bad, s_big;
-  if (threadIdx.x == 0) {
-    s_bad = 0;
-    s_big = 0;
-  }
-  __syncthreads();
-  const int nq = p.heads * p.qt * D;
+  const int kh = blockIdx.x;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const float limit =
+      (sizeof(KT) == 2 && !std::is_same<KT, __nv_bfloat16>::value) ? 6.0e4f : kHuge;
+  // this kv head's query values: heads [kh*group, (kh+1)*group) x qt tokens
+  const float* qkh = p.query + (int64_t)kh * p.group * p.qt * D;
+  const int nq = p.group * p.qt * D;
+  int bad = 0, big = 0;
   for (int i = threadIdx.x; i < nq; i += blockDim.x) {
-    const float v = p.query[i];
-    if (!isfinite(v)) s_bad = 1;
-    if (fabsf(v) > (sizeof(KT) == 2 && !std::is_same<KT, __nv_bfloat16>::value ? 6.0e4f : kHuge))
-      s_big = 1;
+    const float v = qkh[i];
+    bad |= !isfinite(v);
+    big |= fabsf(v) > limit;
   }
-  // per-head norm (max over query tokens)
-  for (int h = threadIdx.x; h < p.heads; h += blockDim.x) {
+  bad = __syncthreads_or(bad);
+  big = __syncthreads_or(big);
+  // head norms (max over query tokens), one warp per head
+  for (int lh = warp; lh < p.group; lh += blockDim.x / 32) {
+    const int h = kh * p.group + lh;
     float mx = 0.0f;
     for (int qi = 0; qi < p.qt; ++qi) {
       const float* q = p.query + ((int64_t)h * p.qt + qi) * D;
       float ss = 0.0f;
-      for (int d = 0; d < D; ++d) ss = fmaf(q[d], q[d], ss);
+      for (int d = lane; d < D; d += 32) ss = fmaf(q[d], q[d], ss);
+#pragma unroll
+      for (int o = 16; o >= 1; o >>= 1) ss += __shfl_xor_sync(kFull, ss, o);
       mx = fmaxf(mx, sqrtf(ss));
     }
-    p.qnorm_h[h] = mx * (1.0f + 9.765625e-4f);
+    if (lane == 0) p.qnorm_h[h] = mx * (1.0f + 9.765625e-4f);
   }
-  __syncthreads();
   if constexpr (D == 128 || D == 64) {
-    // fragments: [kh][t][lane][2*s + r]
-    const int total = p.kh_n * NT * 32 * KSTEPS;
+    // fragments of this kv head: [t][lane][2*s + r]
+    const int total = NT * 32 * KSTEPS;
     for (int i = threadIdx.x; i < total; i += blockDim.x) {
       const int s = i % KSTEPS;
-      const int lane = (i / KSTEPS) % 32;
-      const int t = (i / (KSTEPS * 32)) % NT;
-      const int kh = i / (KSTEPS * 32 * NT);
-      const int g = lane >> 2, c = lane & 3;
+      const int ln = (i / KSTEPS) % 32;
+      const int t = i / (KSTEPS * 32);
+      const int g = ln >> 2, c = ln & 3;
       const int col = t * 8 + g;
       const bool is_lo = col >= NVP;
       const int vi = is_lo ? col - NVP : col;
@@ -238,18 +258,27 @@ __global__ void query_prep_kernel(RouteParams p) {
           v[j] = is_lo ? (x - xh) : xh;
         }
       }
-      uint32_t* dst = p.frag + ((((int64_t)kh * NT + t) * 32 + lane) * (2 * KSTEPS));
+      uint32_t* dst = p.frag + ((((int64_t)kh * NT + t) * 32 + ln) * (2 * KSTEPS));
       dst[2 * s] = pack2<KT>(v[0], v[1]);
       dst[2 * s + 1] = pack2<KT>(v[2], v[3]);
     }
   }
   if (threadIdx.x == 0) {
-    p.qinfo->finite = !s_bad;
-    p.qinfo->fast_ok = !s_bad && !s_big;
+    p.qparts[kh] = (bad ? 1 : 0) | (big ? 2 : 0);
+    __threadfence();
+    const unsigned ticket = atomicAdd(p.qcount, 1u);
+    if (ticket == gridDim.x - 1) {
+      __threadfence();
+      int flags = 0;
+      for (int k = 0; k < (int)gridDim.x; ++k) flags |= __ldcg(p.qparts + k);
+      p.qinfo->finite = !(flags & 1);
+      p.qinfo->fast_ok = !flags;
+      *p.qcount = 0u;
+    }
   }
 }
 
-// Approximate pass: one warp per work item (node, kv head, 64-token chunk).
+// Approximate pass: one warp per work item (node, kv head, 128-token chunk).
 template <typename KT, int D, int NT>
 __global__ void __launch_bounds__(kThreads) gqa_scan_kernel(RouteParams p) {
   constexpr int KSTEPS = D / 16;
@@ -261,15 +290,20 @@ __global__ void __launch_bounds__(kThreads) gqa_scan_kernel(RouteParams p) {
   const int64_t wid = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
   const KT* keys = static_cast<const KT*>(p.keys);
+  // items are read 16 bytes at a time, the next one prefetched during this one
+  uint4 cur = wid < p.n_items ? __ldg(reinterpret_cast<const uint4*>(p.items + wid))
+                              : make_uint4(0, 0, 0, 0);
   for (int64_t it = wid; it < p.n_items; it += nw) {
-    const uint64_t item = p.items[it];
-    const int64_t node = (int64_t)(item >> 32);
-    const int kh = (int)((item >> 24) & 0xFF);
-    const int chunk = (int)(item & 0xFFFFFF);
-    const int64_t T = (int64_t)(p.off[node + 1] - p.off[node]);
-    const int64_t t0 = (int64_t)chunk * kChunk;
-    const int64_t tend = min(T, t0 + kChunk);
-    const KT* base = keys + ((int64_t)p.off[node] * p.kh_n + (int64_t)kh * T) * D;
+    const uint4 nxt_raw = (it + nw < p.n_items)
+                              ? __ldg(reinterpret_cast<const uint4*>(p.items + it + nw))
+                              : make_uint4(0, 0, 0, 0);
+    const uint64_t base_off = (uint64_t)cur.x | ((uint64_t)cur.y << 32);
+    const int64_t node = (int64_t)cur.z;
+    const int kh = (int)(cur.w & 0xFFFF);
+    const int64_t t0 = 0;
+    const int64_t tend = (int64_t)(cur.w >> 16);
+    cur = nxt_raw;
+    const KT* base = keys + base_off;
     // query fragments for this kv head
     uint32_t bq[NT][2 * KSTEPS];
     const uint32_t* fsrc = p.frag + ((int64_t)kh * NT * 32 + lane) * (2 * KSTEPS);
@@ -280,18 +314,9 @@ __global__ void __launch_bounds__(kThreads) gqa_scan_kernel(RouteParams p) {
     float mx[NT][2];
 #pragma unroll
     for (int t = 0; t < NT; ++t) mx[t][0] = mx[t][1] = 0.0f;
-    for (int64_t tt = t0; tt < tend; tt += 16) {
-      // this thread's 2 rows x (D/4) contiguous dims
-      uint32_t ra[2 * KSTEPS], rb[2 * KSTEPS];
-      const int64_t r0 = tt + g, r1 = tt + g + 8;
-#pragma unroll
-      for (int w = 0; w < W; ++w) {
-        uint4 va = make_uint4(0, 0, 0, 0), vb = make_uint4(0, 0, 0, 0);
-        if (r0 < tend) va = ld_stream(base + r0 * D + (D / 4) * c + 8 * w);
-        if (r1 < tend) vb = ld_stream(base + r1 * D + (D / 4) * c + 8 * w);
-        ra[4 * w + 0] = va.x; ra[4 * w + 1] = va.y; ra[4 * w + 2] = va.z; ra[4 * w + 3] = va.w;
-        rb[4 * w + 0] = vb.x; rb[4 * w + 1] = vb.y; rb[4 * w + 2] = vb.z; rb[4 * w + 3] = vb.w;
-      }
+    // 16 key tokens x this thread's (D/4) contiguous dims of rows g and g+8:
+    // 8 MMAs per n-tile, then hi + lo and |.| max over the two rows.
+    auto tile = [&](const uint32_t (&ra)[2 * KSTEPS], const uint32_t (&rb)[2 * KSTEPS]) {
       float acc[NT][4];
 #pragma unroll
       for (int t = 0; t < NT; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.0f;
@@ -301,7 +326,6 @@ __global__ void __launch_bounds__(kThreads) gqa_scan_kernel(RouteParams p) {
 #pragma unroll
         for (int t = 0; t < NT; ++t) mma16816<KT>(acc[t], a, bq[t][2 * s], bq[t][2 * s + 1]);
       }
-      // combine hi + lo and take |.| max over the two rows
       if constexpr (NT == 1) {
         float o[4];
 #pragma unroll
@@ -319,6 +343,37 @@ __global__ void __launch_bounds__(kThreads) gqa_scan_kernel(RouteParams p) {
           mx[t][1] = fmaxf(mx[t][1], fmaxf(fabsf(o1), fabsf(o3)));
         }
       }
+    };
+    auto put = [](uint32_t* r, const uint4& v) {
+      r[0] = v.x; r[1] = v.y; r[2] = v.z; r[3] = v.w;
+    };
+    int64_t tt = t0;
+    // full pairs of tiles: 4 rows x W unchecked 16-byte loads in flight per thread
+    for (; tt + 32 <= tend; tt += 32) {
+      uint32_t ra0[2 * KSTEPS], rb0[2 * KSTEPS], ra1[2 * KSTEPS], rb1[2 * KSTEPS];
+      const KT* p0 = base + (tt + g) * D + (D / 4) * c;
+#pragma unroll
+      for (int w = 0; w < W; ++w) {
+        put(ra0 + 4 * w, ld_nc16(p0 + 8 * w));
+        put(rb0 + 4 * w, ld_nc16(p0 + 8 * D + 8 * w));
+        put(ra1 + 4 * w, ld_nc16(p0 + 16 * D + 8 * w));
+        put(rb1 + 4 * w, ld_nc16(p0 + 24 * D + 8 * w));
+      }
+      tile(ra0, rb0);
+      tile(ra1, rb1);
+    }
+    for (; tt < tend; tt += 16) {
+      uint32_t ra[2 * KSTEPS], rb[2 * KSTEPS];
+      const int64_t r0 = tt + g, r1 = tt + g + 8;
+#pragma unroll
+      for (int w = 0; w < W; ++w) {
+        uint4 va = make_uint4(0, 0, 0, 0), vb = make_uint4(0, 0, 0, 0);
+        if (r0 < tend) va = ld_nc16(base + r0 * D + (D / 4) * c + 8 * w);
+        if (r1 < tend) vb = ld_nc16(base + r1 * D + (D / 4) * c + 8 * w);
+        put(ra + 4 * w, va);
+        put(rb + 4 * w, vb);
+      }
+      tile(ra, rb);
     }
     // max across the 8 row groups (lanes with equal c)
 #pragma unroll
@@ -440,53 +495,89 @@ __global__ void __launch_bounds__(1024) select_kernel(RouteParams p) {
   }
 }
 
-// Exact refine: grid.y strides candidates, grid.x x threads stride the
-// (head, key token) units of one candidate.  Per unit the reference's
-// sequential fp32 dot; the per-head max goes through atomicMax on the bits of
-// a non-negative float (NaN candidates skipped, exactly as std::max does).
-template <typename KT>
-__global__ void refine_kernel(RouteParams p) {
+// Exact refine: grid.y strides candidates; grid.x x threads stride warp-aligned
+// units (kv head, key token): a warp always works on 32 tokens of one kv head
+// (tokens padded to a multiple of 32 per head).  Each thread reads its key row
+// once with 16-byte loads and computes the dots of every query vector of that
+// kv head (the reference's sequential fp32 arithmetic, products and sums
+// rounded separately), four vectors at a time; the query sits in shared memory
+// when it fits (SMEM).  The per-head maximum is reduced across the warp first
+// (fmaxf never returns a NaN over a number, matching std::max(best, v) keeping
+// best), then one atomicMax on the bits of the non-negative float per warp
+// and head.
+template <typename KT, bool SMEM>
+__global__ void __launch_bounds__(256) refine_kernel(RouteParams p) {
+  extern __shared__ float sh_query[];
   const int count = *p.cand_count;
+  if ((int)blockIdx.y >= count) return;
+  const int qvals = p.heads * p.qt * p.dim;
+  if constexpr (SMEM) {
+    for (int i = threadIdx.x; i < qvals; i += blockDim.x) sh_query[i] = p.query[i];
+    __syncthreads();
+  }
+  const float* qbase = SMEM ? sh_query : p.query;
+  constexpr int E = 16 / (int)sizeof(KT);       // keys per 16-byte load
   const KT* keys = static_cast<const KT*>(p.keys);
+  const int lane = threadIdx.x & 31;
+  const int nvec = p.group * p.qt;               // query vectors per kv head
+  const int dim = p.dim;
   for (int ci = blockIdx.y; ci < count; ci += gridDim.y) {
     const int64_t node = p.cand[ci];
     const int64_t T = (int64_t)(p.off[node + 1] - p.off[node]);
     if (T == 0 || p.key_bad[node] || !p.qinfo->finite) continue;
-    const KT* base = keys + (int64_t)p.off[node] * p.kh_n * p.dim;
+    const int64_t Tp = (T + 31) & ~(int64_t)31;
+    const KT* base = keys + (int64_t)p.off[node] * p.kh_n * dim;
     unsigned* best_out = p.headmax + (int64_t)ci * p.heads;
-    const int64_t units = (int64_t)p.heads * T * (p.qt4 ? 1 : p.qt);
-    for (int64_t u = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; u < units;
-         u += (int64_t)gridDim.x * blockDim.x) {
-      const int64_t t = u % T;
-      const int64_t hq = u / T;
-      float v;
-      int h;
-      if (p.qt4) {
-        h = (int)hq;
-        const int kh = h / p.group;
-        const KT* k = base + ((int64_t)kh * T + t) * p.dim;
-        const float* q0 = p.query + (int64_t)h * 4 * p.dim;
-        float d0 = 0.0f, d1 = 0.0f, d2 = 0.0f, d3 = 0.0f;
-        for (int d = 0; d < p.dim; ++d) {
-          const float kv = key_to_f(k[d]);
-          d0 = __fadd_rn(d0, __fmul_rn(q0[d], kv));
-          d1 = __fadd_rn(d1, __fmul_rn(q0[p.dim + d], kv));
-          d2 = __fadd_rn(d2, __fmul_rn(q0[2 * p.dim + d], kv));
-          d3 = __fadd_rn(d3, __fmul_rn(q0[3 * p.dim + d], kv));
+    const int64_t units = (int64_t)p.kh_n * Tp;
+    for (int64_t u0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) & ~(int64_t)31; u0 < units;
+         u0 += (int64_t)gridDim.x * blockDim.x) {
+      const int kh = (int)(u0 / Tp);
+      const int64_t t = u0 - (int64_t)kh * Tp + lane;
+      const bool live = t < T;
+      const KT* k = base + ((int64_t)kh * T + (live ? t : 0)) * dim;
+      for (int v0 = 0; v0 < nvec; v0 += 4) {
+        float dot[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        const float* qv[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int vi = min(v0 + j, nvec - 1);
+          const int h = kh * p.group + vi / p.qt, qi = vi % p.qt;
+          qv[j] = qbase + ((int64_t)h * p.qt + qi) * dim;
         }
-        const float rb = std_max(std_max(fabsf(d0), fabsf(d1)), std_max(fabsf(d2), fabsf(d3)));
-        v = __fmul_rn(rb, p.inv_denom);
-      } else {
-        h = (int)(hq / p.qt);
-        const int qi = (int)(hq % p.qt);
-        const int kh = h / p.group;
-        const KT* k = base + ((int64_t)kh * T + t) * p.dim;
-        const float* q = p.query + ((int64_t)h * p.qt + qi) * p.dim;
-        float dot = 0.0f;
-        for (int d = 0; d < p.dim; ++d) dot = __fadd_rn(dot, __fmul_rn(q[d], key_to_f(k[d])));
-        v = __fmul_rn(fabsf(dot), p.inv_denom);
+        for (int d0 = 0; d0 < dim; d0 += E) {
+          const uint4 raw = *reinterpret_cast<const uint4*>(k + d0);
+          const KT* kk = reinterpret_cast<const KT*>(&raw);
+#pragma unroll
+          for (int e = 0; e < E; ++e) {
+            const float kvf = key_to_f(kk[e]);
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              dot[j] = __fadd_rn(dot[j], __fmul_rn(qv[j][d0 + e], kvf));
+          }
+        }
+        if (p.qt4) {
+          // vectors v0..v0+3 are the four query tokens of one head
+          const float rb = std_max(std_max(fabsf(dot[0]), fabsf(dot[1])),
+                                   std_max(fabsf(dot[2]), fabsf(dot[3])));
+          float v = live ? __fmul_rn(rb, p.inv_denom) : 0.0f;
+          if (!(v == v)) v = 0.0f;   // a NaN row never raises best
+#pragma unroll
+          for (int o = 16; o >= 1; o >>= 1) v = fmaxf(v, __shfl_xor_sync(kFull, v, o));
+          if (lane == 0 && v > 0.0f)
+            atomicMax(best_out + kh * p.group + v0 / 4, __float_as_uint(v));
+        } else {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            if (v0 + j >= nvec) break;
+            float v = live ? __fmul_rn(fabsf(dot[j]), p.inv_denom) : 0.0f;
+            if (!(v == v)) v = 0.0f;
+#pragma unroll
+            for (int o = 16; o >= 1; o >>= 1) v = fmaxf(v, __shfl_xor_sync(kFull, v, o));
+            if (lane == 0 && v > 0.0f)
+              atomicMax(best_out + kh * p.group + (v0 + j) / p.qt, __float_as_uint(v));
+          }
+        }
       }
-      if (v > 0.0f) atomicMax(best_out + h, __float_as_uint(v));  // NaN and 0 never raise best
     }
   }
 }
@@ -522,8 +613,12 @@ __global__ void finalize_kernel(RouteParams p) {
   const bool ok = lane < p.topk && isfinite(list.s) && list.id != kNoRow;
   const unsigned m = __ballot_sync(kFull, ok);
   if (lane < p.topk) {
-    p.result->ids[lane] = ok ? (uint64_t)list.id : UINT64_MAX;
-    p.result->scores[lane] = ok ? list.s : __int_as_float(0x7FC00000);
+    const uint64_t id = ok ? (uint64_t)list.id + p.id_offset : UINT64_MAX;
+    const float sc = ok ? list.s : __int_as_float(0x7FC00000);
+    p.result->ids[lane] = id;
+    p.result->scores[lane] = sc;
+    if (p.out_ids) p.out_ids[lane] = id;
+    if (p.out_scores) p.out_scores[lane] = sc;
   }
   if (lane == 0) {
     p.result->count = __popc(m);
@@ -548,7 +643,7 @@ struct grm_b200_gqa_bank {
   void* d_keys = nullptr;
   uint64_t* d_off = nullptr;
   std::vector<uint64_t> h_off;
-  uint64_t* d_items = nullptr;
+  Item* d_items = nullptr;
   int64_t n_items = 0;
   float* d_kmax = nullptr;
   unsigned char* d_key_bad = nullptr;
@@ -563,6 +658,8 @@ struct grm_b200_gqa_bank {
   float* d_qnorm = nullptr;
   int qnorm_cap = 0;
   QueryInfo* d_qinfo = nullptr;
+  int* d_qparts = nullptr;
+  unsigned* d_qcount = nullptr;
   Result* d_result = nullptr;
   Result* h_result = nullptr;
   float* d_queries = nullptr;
@@ -586,7 +683,7 @@ int nt_for(int nv) { return nv <= 4 ? 1 : (nv <= 8 ? 2 : (nv <= 16 ? 4 : 0)); }
 
 template <typename KT, int D, int NT>
 void launch_fast(grm_b200_gqa_bank* b, const RouteParams& p) {
-  query_prep_kernel<KT, D, NT><<<1, 256, 0, b->stream>>>(p);
+  query_prep_kernel<KT, D, NT><<<b->kh_n, 128, 0, b->stream>>>(p);
   if (b->n_items > 0)
     gqa_scan_kernel<KT, D, NT><<<b->grid_scan, kThreads, 0, b->stream>>>(p);
 }
@@ -621,10 +718,23 @@ __global__ void query_info_kernel(RouteParams p) {
   }
 }
 
+constexpr int kRefineSmemMax = 96 * 1024;
+
 template <typename KT>
 void launch_refine(grm_b200_gqa_bank* b, const RouteParams& p) {
-  dim3 grid(std::max(1, b->sms / 4), kRefineY);
-  refine_kernel<KT><<<grid, 256, 0, b->stream>>>(p);
+  dim3 grid(std::max(1, b->sms), kRefineY);
+  const size_t qbytes = sizeof(float) * (size_t)p.heads * p.qt * p.dim;
+  if (qbytes <= (size_t)kRefineSmemMax) {
+    static bool attr_set[64] = {};
+    if (!attr_set[b->device]) {
+      cudaFuncSetAttribute(refine_kernel<KT, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           kRefineSmemMax);
+      attr_set[b->device] = true;
+    }
+    refine_kernel<KT, true><<<grid, 256, qbytes, b->stream>>>(p);
+  } else {
+    refine_kernel<KT, false><<<grid, 256, 0, b->stream>>>(p);
+  }
 }
 
 int ensure_heads(grm_b200_gqa_bank* b, int heads, int nt) {
@@ -635,6 +745,8 @@ int ensure_heads(grm_b200_gqa_bank* b, int heads, int nt) {
     const size_t n = (size_t)b->nodes * heads;
     cudaError_t e = cudaMalloc(&b->d_headmax, n * sizeof(unsigned));
     if (e == cudaSuccess) e = cudaMemsetAsync(b->d_headmax, 0, n * sizeof(unsigned), b->stream);
+    // later launches may use another stream: finish the zero fill now (first use only)
+    if (e == cudaSuccess) e = cudaStreamSynchronize(b->stream);
     if (e != cudaSuccess) return b->err.set(cuda_status(e), "GQA scratch allocation failed");
     b->headmax_heads = heads;
   }
@@ -658,7 +770,13 @@ int ensure_heads(grm_b200_gqa_bank* b, int heads, int nt) {
   return 0;
 }
 
-int route_one(grm_b200_gqa_bank* b, const float* dq, int heads, int qt, int topk) {
+// `use_bank_stream`: launch on the bank's private stream (synchronous entry
+// points); otherwise on `stream`, where 0 is the legacy default stream.
+int route_one(grm_b200_gqa_bank* b, const float* dq, int heads, int qt, int topk,
+              bool use_bank_stream = true, cudaStream_t stream = nullptr,
+              uint64_t* out_ids = nullptr, float* out_scores = nullptr,
+              uint64_t id_offset = 0) {
+  if (use_bank_stream) stream = b->stream;
   const int group = heads / b->kh_n;
   const int nv = group * qt;
   const int nt = nt_for(nv);
@@ -689,10 +807,22 @@ int route_one(grm_b200_gqa_bank* b, const float* dq, int heads, int qt, int topk
   p.frag = b->d_frag;
   p.qnorm_h = b->d_qnorm;
   p.qinfo = b->d_qinfo;
+  p.qparts = b->d_qparts;
+  p.qcount = b->d_qcount;
   p.topk = topk;
   p.fast = fast ? 1 : 0;
   p.result = b->d_result;
   p.qt4 = (qt == 4) ? 1 : 0;
+  p.out_ids = out_ids;
+  p.out_scores = out_scores;
+  p.id_offset = id_offset;
+  cudaStream_t saved = b->stream;
+  b->stream = stream;  // every launch below goes to the caller's stream
+  struct Restore {
+    grm_b200_gqa_bank* b;
+    cudaStream_t s;
+    ~Restore() { b->stream = s; }
+  } restore{b, saved};
   if (fast) {
     rc = (b->dtype == GRM_B200_BF16) ? launch_fast_dims<__nv_bfloat16>(b, p, nt)
                                      : launch_fast_dims<__half>(b, p, nt);
@@ -758,7 +888,7 @@ void bank_free(grm_b200_gqa_bank* b) {
   if (b->owns_keys && b->d_keys) cudaFree(b->d_keys);
   void* ptrs[] = {b->d_off, b->d_items, b->d_kmax, b->d_key_bad, b->d_headmax, b->d_lo, b->d_hi,
                   b->d_cand, b->d_cand_count, b->d_frag, b->d_qnorm, b->d_qinfo, b->d_result,
-                  b->d_queries};
+                  b->d_queries, b->d_qparts, b->d_qcount};
   for (void* q : ptrs)
     if (q) cudaFree(q);
   if (b->h_result) cudaFreeHost(b->h_result);
@@ -786,6 +916,9 @@ int finish_create(grm_b200_gqa_bank* b) {
   if (e == cudaSuccess) e = cudaMalloc(&b->d_cand_count, sizeof(int));
   if (e == cudaSuccess) e = cudaMemsetAsync(b->d_cand_count, 0, sizeof(int), b->stream);
   if (e == cudaSuccess) e = cudaMalloc(&b->d_qinfo, sizeof(QueryInfo));
+  if (e == cudaSuccess) e = cudaMalloc(&b->d_qparts, sizeof(int) * b->kh_n);
+  if (e == cudaSuccess) e = cudaMalloc(&b->d_qcount, sizeof(unsigned));
+  if (e == cudaSuccess) e = cudaMemsetAsync(b->d_qcount, 0, sizeof(unsigned), b->stream);
   if (e == cudaSuccess) e = cudaMalloc(&b->d_result, sizeof(Result));
   if (e == cudaSuccess) e = cudaMallocHost(&b->h_result, sizeof(Result));
   if (e != cudaSuccess) return cuda_status(e);
@@ -793,20 +926,26 @@ int finish_create(grm_b200_gqa_bank* b) {
   int rc = device_info(b->device, &info);
   if (rc) return rc;
   b->sms = info.sms;
-  // work items (node, kv head, chunk) for nodes with key tokens
-  std::vector<uint64_t> items;
+  // work items (node, kv head, chunk of up to kChunk tokens) for nodes with key tokens
+  std::vector<Item> items;
   for (int64_t n = 0; n < b->nodes; ++n) {
     const uint64_t T = b->h_off[n + 1] - b->h_off[n];
     const uint64_t chunks = (T + kChunk - 1) / kChunk;
     for (int kh = 0; kh < b->kh_n; ++kh)
-      for (uint64_t c = 0; c < chunks; ++c)
-        items.push_back(((uint64_t)n << 32) | ((uint64_t)kh << 24) | c);
+      for (uint64_t c = 0; c < chunks; ++c) {
+        Item it;
+        it.base = (b->h_off[n] * (uint64_t)b->kh_n + (uint64_t)kh * T + c * kChunk) * (uint64_t)b->dim;
+        it.node = (uint32_t)n;
+        it.kh = (uint16_t)kh;
+        it.ntok = (uint16_t)std::min<uint64_t>(kChunk, T - c * kChunk);
+        items.push_back(it);
+      }
   }
   b->n_items = (int64_t)items.size();
   if (!items.empty()) {
-    e = cudaMalloc(&b->d_items, sizeof(uint64_t) * items.size());
+    e = cudaMalloc(&b->d_items, sizeof(Item) * items.size());
     if (e == cudaSuccess)
-      e = cudaMemcpyAsync(b->d_items, items.data(), sizeof(uint64_t) * items.size(),
+      e = cudaMemcpyAsync(b->d_items, items.data(), sizeof(Item) * items.size(),
                           cudaMemcpyHostToDevice, b->stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(b->stream);
     if (e != cudaSuccess) return cuda_status(e);
@@ -864,6 +1003,11 @@ int create_common(const void* keys, bool host, int dtype, const uint64_t* off, i
   }
   if (off[0] != 0) {
     set_thread_error("token_offsets must start at 0");
+    return GRM_B200_EINVAL;
+  }
+  if ((dim * (dtype == GRM_B200_F32 ? 4 : 2)) % 16 != 0) {
+    // key rows are read with 16-byte loads
+    set_thread_error("head_dim * element size must be a multiple of 16 bytes (head_dim=%d)", dim);
     return GRM_B200_EINVAL;
   }
   for (int64_t i = 0; i < nodes; ++i) {
@@ -959,6 +1103,30 @@ int grm_b200_gqa_route_device(grm_b200_gqa_bank* bank, const float* queries_devi
   std::lock_guard<std::mutex> lock(bank->mu);
   return route_device_queries(bank, queries_device, query_count, query_heads, query_tokens, warmup,
                               topk, out_ids_host, out_scores_host, elapsed_ms);
+}
+
+int grm_b200_gqa_route_async(grm_b200_gqa_bank* bank, const float* queries_device,
+                             int query_count, int query_heads, int query_tokens, int topk,
+                             uint64_t id_offset, uint64_t* out_ids_device,
+                             float* out_scores_device, void* stream) {
+  if (!bank) return GRM_B200_EINVAL;
+  std::lock_guard<std::mutex> lock(bank->mu);
+  if (!queries_device || query_count <= 0 || query_heads <= 0 || query_tokens <= 0 ||
+      query_heads % bank->kh_n != 0 || topk <= 0 || topk > GRM_B200_MAX_TOPK ||
+      !out_ids_device || !out_scores_device)
+    return bank->err.set(GRM_B200_EINVAL, "invalid GQA async route arguments");
+  cudaError_t e = cudaSetDevice(bank->device);
+  if (e != cudaSuccess) return bank->err.set(cuda_status(e), "cudaSetDevice failed");
+  const int64_t qsize = (int64_t)query_heads * query_tokens * bank->dim;
+  for (int i = 0; i < query_count; ++i) {
+    const int rc = route_one(bank, queries_device + i * qsize, query_heads, query_tokens, topk,
+                             false, static_cast<cudaStream_t>(stream),
+                             out_ids_device + (int64_t)i * topk,
+                             out_scores_device + (int64_t)i * topk, id_offset);
+    if (rc) return rc;
+  }
+  bank->routes += (uint64_t)query_count;
+  return 0;
 }
 
 int grm_b200_gqa_bank_destroy(grm_b200_gqa_bank* bank) {

@@ -36,8 +36,9 @@ constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
 constexpr float kMargin = 1.52587890625e-05f;  // 2^-16
 constexpr double kSafeLo = 1.0e-20, kSafeHi = 1.0e20;
+constexpr int kInlineMax = 512;  // largest dim a query can travel inline
 
-enum Status : int { kOk = 0, kOverflow = 1, kUnsafe = 2 };
+enum Status : int { kOk = 0, kOverflow = 1, kUnsafe = 2, kError = 3 };
 
 struct Result {
   int status;
@@ -51,7 +52,9 @@ struct Result {
 struct Header {
   int lb;          // ordered float: best block k-th approximate score so far
   unsigned done;   // blocks finished in this launch
-  int pad[14];
+  int err;         // a bounded device wait gave up in this launch
+  unsigned next;   // next 32-row group to hand out (bulk scan work queue)
+  int pad[12];
 };
 
 struct Entry {
@@ -94,7 +97,15 @@ struct Params {
   float* out_scores;
   uint64_t id_offset;
   int force_all;         // exact kernel: score every row (bank outside the fast path)
+  // A single query may travel inside the launch parameters (queries == nullptr):
+  // the synchronous host entry then needs no host-to-device copy.
+  float qinline[kInlineMax];
 };
+
+template <typename T>
+__device__ __forceinline__ const float* query_ptr(const Params<T>& p, int q, int dim) {
+  return p.queries ? p.queries + (int64_t)q * dim : p.qinline;
+}
 
 __device__ __forceinline__ float to_f(__half h) { return __half2float(h); }
 __device__ __forceinline__ float to_f(float f) { return f; }
@@ -105,7 +116,7 @@ template <typename T>
 __device__ float exact_score(const T* row, int dim, const float* q, double qnorm, float norm) {
   double dot = 0.0;
 #pragma unroll 8
-  for (int d = 0; d < dim; ++d) dot = fma((double)__ldg(q + d), (double)to_f(row[d]), dot);
+  for (int d = 0; d < dim; ++d) dot = fma((double)q[d], (double)to_f(row[d]), dot);
   return (float)(dot / (qnorm * (double)norm + 1.0e-8));
 }
 
@@ -118,7 +129,7 @@ __device__ float exact_score_inline_norm(const T* row, int dim, const float* q, 
 #pragma unroll 8
   for (int d = 0; d < dim; ++d) {
     const double c = (double)to_f(row[d]);
-    dot = fma((double)__ldg(q + d), c, dot);
+    dot = fma((double)q[d], c, dot);
     n2 = fma(c, c, n2);
   }
   const float norm = (float)sqrt(n2);
@@ -149,7 +160,7 @@ __device__ __forceinline__ float sq16(const uint4& v, float acc) {
 __device__ double query_norm_seq(const float* q, int dim) {
   double acc = 0.0;
   for (int d = 0; d < dim; ++d) {
-    const double v = (double)__ldg(q + d);
+    const double v = (double)q[d];
     acc = fma(v, v, acc);
   }
   return sqrt(acc);
@@ -191,14 +202,15 @@ __device__ __forceinline__ float dot16(const uint4& v, const float* qr, float ac
   return acc;
 }
 
-// Merge the kWarps warp lists of this block into warp 0's list.
+// Merge the NW warp lists of this block into warp 0's list.
+template <int NW = kWarps>
 __device__ __forceinline__ void block_merge(WarpList& list, int lane, int warp, float* sh_s,
                                             uint32_t* sh_id) {
   sh_s[warp * 32 + lane] = list.s;
   sh_id[warp * 32 + lane] = list.id;
   __syncthreads();
   if (warp == 0) {
-    for (int w = 1; w < kWarps; ++w) list.offer(sh_s[w * 32 + lane], sh_id[w * 32 + lane], lane);
+    for (int w = 1; w < NW; ++w) list.offer(sh_s[w * 32 + lane], sh_id[w * 32 + lane], lane);
   }
 }
 
@@ -222,12 +234,121 @@ __device__ void write_result(const Params<T>& p, int q, const WarpList& ex, int 
   }
 }
 
+// Everything after the streaming loop: merge the warps' lists, publish the
+// entries within the margin of the best block k-th score so far, and in the
+// last block to finish merge all blocks, select the candidates and recompute
+// them with the reference arithmetic (or flag the exact fallback).
+template <int D, typename T, bool INL, int NW>
+__device__ __forceinline__ void scan_finish(const Params<T>& p, WarpList& list, bool safe,
+                                            const float* query, int q, int lane, int warp,
+                                            float* sh_s, uint32_t* sh_id, float* sh_floor,
+                                            int* sh_last) {
+  block_merge<NW>(list, lane, warp, sh_s, sh_id);
+  Header* hdr = p.scratch.hdr(q);
+  if (warp == 0) {
+    const float kth = __shfl_sync(kFull, list.s, p.topk - 1);
+    int lb_now = 0;
+    if (lane == 0) {
+      const int enc = isfinite(kth) ? float_to_ordered(kth) : kOrderedNegInf;
+      const int old = atomicMax(&hdr->lb, enc);
+      lb_now = old > enc ? old : enc;
+    }
+    lb_now = __shfl_sync(kFull, lb_now, 0);
+    const float wthr = ordered_to_float(lb_now) - 2.0f * kMargin;
+    const bool keep = isfinite(list.s) && list.s >= wthr;
+    const int cnt = __popc(__ballot_sync(kFull, keep));
+    Entry* ent = p.scratch.entries(q) + (int64_t)blockIdx.x * 32;
+    if (lane < cnt) ent[lane] = Entry{list.s, list.id};
+    const float last = __shfl_sync(kFull, list.s, 31);
+    if (lane == 0) {
+      p.scratch.counts(q)[blockIdx.x] = cnt;
+      p.scratch.floors(q)[blockIdx.x] = isfinite(last) ? last : -INFINITY;
+      __threadfence();
+      const unsigned ticket = atomicAdd(&hdr->done, 1u);
+      *sh_last = (ticket == gridDim.x - 1);
+    }
+  }
+  __syncthreads();
+  if (!*sh_last) return;
+  __threadfence();
+
+  // Last block: merge the published entries.
+  list.init();
+  float fmax = -INFINITY;
+  for (int b = warp; b < (int)gridDim.x; b += NW) {
+    const int cnt = __ldcg(p.scratch.counts(q) + b);
+    const Entry* ent = p.scratch.entries(q) + (int64_t)b * 32;
+    float s = -INFINITY;
+    uint32_t id = kNoRow;
+    if (lane < cnt) {
+      s = __ldcg(&ent[lane].s);
+      id = __ldcg(&ent[lane].id);
+    }
+    list.offer(s, id, lane);
+    fmax = fmaxf(fmax, __ldcg(p.scratch.floors(q) + b));
+  }
+  if (lane == 0) sh_floor[warp] = fmax;
+  __syncthreads();
+  block_merge<NW>(list, lane, warp, sh_s, sh_id);
+  if (warp != 0) return;
+  float floor_max = -INFINITY;
+  for (int w = 0; w < NW; ++w) floor_max = fmaxf(floor_max, sh_floor[w]);
+  const float T_k = __shfl_sync(kFull, list.s, p.topk - 1);
+  const float thr = isfinite(T_k) ? T_k - 2.0f * kMargin : -INFINITY;
+  const float last = __shfl_sync(kFull, list.s, 31);
+  const bool overflow = (isfinite(last) && last >= thr) || (isfinite(floor_max) && floor_max >= thr);
+  Result* r = p.results + q;
+  const bool failed = __ldcg(&hdr->err) != 0;
+  if (failed) {
+    if (lane == 0) {
+      r->status = kError;
+      r->count = 0;
+      hdr->lb = kOrderedNegInf;
+      hdr->done = 0;
+      hdr->err = 0;
+      hdr->next = 0;
+    }
+    return;
+  }
+  if (!safe || overflow) {
+    if (lane == 0) {
+      r->status = safe ? kOverflow : kUnsafe;
+      r->thr = thr;
+      r->count = 0;
+      hdr->lb = kOrderedNegInf;
+      hdr->done = 0;
+      hdr->next = 0;
+    }
+    return;
+  }
+  // Exact refine of the candidates (sorted approximate list, prefix >= thr).
+  const bool cand = isfinite(list.s) && list.s >= thr;
+  float es = -INFINITY;
+  if (cand) {
+    const double qnorm = query_norm_seq(query, D);
+    const int64_t row = list.id;
+    if constexpr (INL)
+      es = exact_score_inline_norm<T>(p.rows + row * D, D, query, qnorm);
+    else
+      es = exact_score<T>(p.rows + row * D, D, query, qnorm, __ldg(p.norms + row));
+  }
+  WarpList ex;
+  ex.init();
+  ex.offer(es, list.id, lane);
+  write_result(p, q, ex, lane);
+  if (lane == 0) {
+    hdr->lb = kOrderedNegInf;
+    hdr->done = 0;
+    hdr->next = 0;
+  }
+}
+
 // Approximate streaming pass (one launch per batch of queries: grid.y = query).
 // INL: no precomputed norms -- the approximate row norm is accumulated from
 // the same loads (fp32, <= 8 ulp relative, inside the margin) and the exact
 // refine recomputes the reference norm.
 template <int D, typename T, bool INL = false>
-__global__ void __launch_bounds__(kThreads) mla_scan_kernel(Params<T> p) {
+__global__ void __launch_bounds__(kThreads) mla_scan_kernel(const __grid_constant__ Params<T> p) {
   constexpr int E = 16 / (int)sizeof(T);
   constexpr int CPR = D / E;
   constexpr int L = CPR >= 32 ? 32 : CPR;
@@ -241,11 +362,12 @@ __global__ void __launch_bounds__(kThreads) mla_scan_kernel(Params<T> p) {
   __shared__ float sh_eq;
   __shared__ int sh_safe;
   __shared__ int sh_last;
+  __shared__ int sh_next;
   __shared__ float sh_floor[kWarps];
 
   const int q = blockIdx.y;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const float* query = p.queries + (int64_t)q * D;
+  const float* query = query_ptr(p, q, D);
 
   // Prologue: unit-normalised query (any accurate norm will do for the
   // approximate pass; the exact refine recomputes the reference norm).
@@ -281,126 +403,282 @@ __global__ void __launch_bounds__(kThreads) mla_scan_kernel(Params<T> p) {
   WarpList list;
   list.init();
   const int64_t groups = ceil_div64(p.nodes, 32);
+  // Each block streams one contiguous range of 32-row groups (equal to +-1
+  // group per block, so every SM moves the same bytes); its warps take groups
+  // from that range through a shared-memory counter.
+  const int64_t g_begin = groups * blockIdx.x / gridDim.x;
+  const int64_t g_end = groups * (blockIdx.x + 1) / gridDim.x;
+  if (threadIdx.x == 0) sh_next = kWarps;
+  __syncthreads();
   if (safe) {
-    for (int64_t g = (int64_t)blockIdx.x * kWarps + warp; g < groups;
-         g += (int64_t)gridDim.x * kWarps) {
+    constexpr int B = 8;  // 16-byte loads in flight per lane per batch
+    for (int64_t g = g_begin + warp; g < g_end;) {
       const int64_t row0 = g * 32;
+      const int64_t my_row = row0 + (lane % L) * R + lane / L;
+      const float nrm_pre = (!INL && my_row < p.nodes) ? __ldg(p.norms + my_row) : 0.0f;
       float part[SLOTS];
       float sq[INL ? SLOTS : 1];
+      if (row0 + 32 <= p.nodes) {
+        // full group: unchecked, batched loads
+        const T* base = p.rows + (row0 + lane / L) * D;
 #pragma unroll
-      for (int j = 0; j < SLOTS; ++j) {
-        const int64_t row = row0 + j * R + lane / L;
-        float acc = 0.0f, sacc = 0.0f;
-        if (row < p.nodes) {
-          const T* rp = p.rows + row * D;
+        for (int jb = 0; jb < SLOTS; jb += B) {
+          uint4 v[B][CPL];
 #pragma unroll
-          for (int i = 0; i < CPL; ++i) {
-            const int c = (CPR >= 32) ? lane + 32 * i : lane % L;
-            const uint4 v = ld_stream(rp + c * E);
-            acc = dot16<T>(v, qr + i * E, acc);
-            if constexpr (INL) sacc = sq16<T>(v, sacc);
+          for (int b = 0; b < B; ++b)
+#pragma unroll
+            for (int i = 0; i < CPL; ++i) {
+              const int c = (CPR >= 32) ? lane + 32 * i : lane % L;
+              v[b][i] = ld_nc16(base + (int64_t)(jb + b) * R * D + c * E);
+            }
+#pragma unroll
+          for (int b = 0; b < B; ++b) {
+            float acc = 0.0f, sacc = 0.0f;
+#pragma unroll
+            for (int i = 0; i < CPL; ++i) {
+              acc = dot16<T>(v[b][i], qr + i * E, acc);
+              if constexpr (INL) sacc = sq16<T>(v[b][i], sacc);
+            }
+            part[jb + b] = acc;
+            if constexpr (INL) sq[jb + b] = sacc;
           }
         }
-        part[j] = acc;
-        if constexpr (INL) sq[j] = sacc;
+      } else {
+#pragma unroll
+        for (int j = 0; j < SLOTS; ++j) {
+          const int64_t row = row0 + j * R + lane / L;
+          float acc = 0.0f, sacc = 0.0f;
+          if (row < p.nodes) {
+            const T* rp = p.rows + row * D;
+#pragma unroll
+            for (int i = 0; i < CPL; ++i) {
+              const int c = (CPR >= 32) ? lane + 32 * i : lane % L;
+              const uint4 v = ld_nc16(rp + c * E);
+              acc = dot16<T>(v, qr + i * E, acc);
+              if constexpr (INL) sacc = sq16<T>(v, sacc);
+            }
+          }
+          part[j] = acc;
+          if constexpr (INL) sq[j] = sacc;
+        }
       }
       const float dot = reduce_scatter<SLOTS>(part, lane);
       float n2 = 0.0f;
       if constexpr (INL) n2 = reduce_scatter<SLOTS>(sq, lane);
-      const int64_t row = row0 + (lane % L) * R + lane / L;
       float s = -INFINITY;
-      if (row < p.nodes) {
-        const float nrm = INL ? sqrtf(n2) : __ldg(p.norms + row);
+      if (my_row < p.nodes) {
+        const float nrm = INL ? sqrtf(n2) : nrm_pre;
         if (isfinite(nrm)) s = dot * __frcp_rn(nrm + e_q);
       }
-      list.offer(s, (uint32_t)row, lane);
+      list.offer(s, (uint32_t)my_row, lane);
+      int nxt = 0;
+      if (lane == 0) nxt = atomicAdd(&sh_next, 1);
+      g = g_begin + __shfl_sync(kFull, nxt, 0);
     }
   }
+  // The resolve kernel may be scheduled as blocks leave the streaming loop;
+  // it waits for this whole grid before reading anything (griddepcontrol.wait).
+  asm volatile("griddepcontrol.launch_dependents;");
+  scan_finish<D, T, INL, kWarps>(p, list, safe, query, q, lane, warp, sh_s, sh_id, sh_floor,
+                                 &sh_last);
+}
 
-  block_merge(list, lane, warp, sh_s, sh_id);
-  Header* hdr = p.scratch.hdr(q);
+// Packed fp32x2 FMA (sm_100 FFMA2): d = a * b + c on both lanes of a float2.
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
+
+// One 16-byte slice dotted with its 16/sizeof(T) query values, two partial
+// sums (even / odd elements) in a float2.
+template <typename T>
+__device__ __forceinline__ float2 dot16x2(const uint4& v, const float2* q2, float2 acc) {
+  if constexpr (sizeof(T) == 2) {
+    const __half2* h = reinterpret_cast<const __half2*>(&v);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) acc = ffma2(__half22float2(h[k]), q2[k], acc);
+  } else {
+    acc = ffma2(make_float2(__uint_as_float(v.x), __uint_as_float(v.y)), q2[0], acc);
+    acc = ffma2(make_float2(__uint_as_float(v.z), __uint_as_float(v.w)), q2[1], acc);
+  }
+  return acc;
+}
+
+// Bulk-copy streaming pass: the same law and epilogue as mla_scan_kernel.
+// Each of the kBulkWarps warps streams its 32-row groups as two 16-row halves
+// through two shared-memory buffers filled by cp.async.bulk (the next group's
+// half is in flight while the current one is consumed), so the bytes in
+// flight per SM no longer depend on registers, and 12 warps hide the
+// arithmetic latency.  Used when a 16-row half is at most 8 KB (fp16
+// D <= 256, fp32 D <= 128).  The dot products use packed f32x2 FMAs (two
+// partial sums per slot): the approximation bound gains one rounding step.
+constexpr int kBulkWarps = 12;
+constexpr int kHalfBytes = 8192;
+constexpr int kBulkSmem = kBulkWarps * 2 * kHalfBytes;
+
+template <int D, typename T>
+__global__ void __launch_bounds__(kBulkWarps * 32, 1)
+    mla_scan_bulk_kernel(const __grid_constant__ Params<T> p) {
+  constexpr int NW = kBulkWarps;
+  constexpr int E = 16 / (int)sizeof(T);
+  constexpr int CPR = D / E;
+  constexpr int L = CPR >= 32 ? 32 : CPR;
+  constexpr int R = 32 / L;
+  constexpr int SLOTS = L;
+  constexpr int HS = SLOTS / 2;  // slots per 16-row half
+  static_assert(CPR <= 32 && 16 * D * (int)sizeof(T) <= kHalfBytes, "half group must fit");
+
+  extern __shared__ __align__(128) unsigned char dsmem[];
+  __shared__ __align__(8) uint64_t sh_bar[NW][2];
+  __shared__ float sh_s[NW * 32];
+  __shared__ uint32_t sh_id[NW * 32];
+  __shared__ float sh_q[D];
+  __shared__ float sh_eq;
+  __shared__ int sh_safe;
+  __shared__ int sh_last;
+  __shared__ int sh_next;
+  __shared__ float sh_floor[NW];
+
+  const int q = blockIdx.y;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const float* query = query_ptr(p, q, D);
+
   if (warp == 0) {
-    const float kth = __shfl_sync(kFull, list.s, p.topk - 1);
-    int lb_now = 0;
+    double acc = 0.0;
+    for (int d = lane; d < D; d += 32) {
+      const double v = (double)query[d];
+      acc = fma(v, v, acc);
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) acc += __shfl_xor_sync(kFull, acc, o);
+    const double qn = sqrt(acc);
+    const bool safe = isfinite(qn) && qn > kSafeLo && qn < kSafeHi;
+    const float inv = safe ? (float)(1.0 / qn) : 0.0f;
+    for (int d = lane; d < D; d += 32) sh_q[d] = query[d] * inv;
     if (lane == 0) {
-      const int enc = isfinite(kth) ? float_to_ordered(kth) : kOrderedNegInf;
-      const int old = atomicMax(&hdr->lb, enc);
-      lb_now = old > enc ? old : enc;
-    }
-    lb_now = __shfl_sync(kFull, lb_now, 0);
-    const float wthr = ordered_to_float(lb_now) - 2.0f * kMargin;
-    const bool keep = isfinite(list.s) && list.s >= wthr;
-    const int cnt = __popc(__ballot_sync(kFull, keep));
-    Entry* ent = p.scratch.entries(q) + (int64_t)blockIdx.x * 32;
-    if (lane < cnt) ent[lane] = Entry{list.s, list.id};
-    const float last = __shfl_sync(kFull, list.s, 31);
-    if (lane == 0) {
-      p.scratch.counts(q)[blockIdx.x] = cnt;
-      p.scratch.floors(q)[blockIdx.x] = isfinite(last) ? last : -INFINITY;
-      __threadfence();
-      const unsigned ticket = atomicAdd(&hdr->done, 1u);
-      sh_last = (ticket == gridDim.x - 1);
+      sh_safe = safe;
+      sh_eq = safe ? (float)(1.0e-8 / qn) : 0.0f;
+      sh_next = NW;
     }
   }
-  __syncthreads();
-  if (!sh_last) return;
-  __threadfence();
-
-  // Last block: merge the published entries.
-  list.init();
-  float fmax = -INFINITY;
-  for (int b = warp; b < (int)gridDim.x; b += kWarps) {
-    const int cnt = __ldcg(p.scratch.counts(q) + b);
-    const Entry* ent = p.scratch.entries(q) + (int64_t)b * 32;
-    float s = -INFINITY;
-    uint32_t id = kNoRow;
-    if (lane < cnt) {
-      s = __ldcg(&ent[lane].s);
-      id = __ldcg(&ent[lane].id);
-    }
-    list.offer(s, id, lane);
-    fmax = fmaxf(fmax, __ldcg(p.scratch.floors(q) + b));
-  }
-  if (lane == 0) sh_floor[warp] = fmax;
-  __syncthreads();
-  block_merge(list, lane, warp, sh_s, sh_id);
-  if (warp != 0) return;
-  float floor_max = -INFINITY;
-  for (int w = 0; w < kWarps; ++w) floor_max = fmaxf(floor_max, sh_floor[w]);
-  const float T_k = __shfl_sync(kFull, list.s, p.topk - 1);
-  const float thr = isfinite(T_k) ? T_k - 2.0f * kMargin : -INFINITY;
-  const float last = __shfl_sync(kFull, list.s, 31);
-  const bool overflow = (isfinite(last) && last >= thr) || (isfinite(floor_max) && floor_max >= thr);
-  Result* r = p.results + q;
-  if (!safe || overflow) {
-    if (lane == 0) {
-      r->status = safe ? kOverflow : kUnsafe;
-      r->thr = thr;
-      r->count = 0;
-      hdr->lb = kOrderedNegInf;
-      hdr->done = 0;
-    }
-    return;
-  }
-  // Exact refine of the candidates (sorted approximate list, prefix >= thr).
-  const bool cand = isfinite(list.s) && list.s >= thr;
-  float es = -INFINITY;
-  if (cand) {
-    const double qnorm = query_norm_seq(query, D);
-    const int64_t row = list.id;
-    if constexpr (INL)
-      es = exact_score_inline_norm<T>(p.rows + row * D, D, query, qnorm);
-    else
-      es = exact_score<T>(p.rows + row * D, D, query, qnorm, __ldg(p.norms + row));
-  }
-  WarpList ex;
-  ex.init();
-  ex.offer(es, list.id, lane);
-  write_result(p, q, ex, lane);
   if (lane == 0) {
-    hdr->lb = kOrderedNegInf;
-    hdr->done = 0;
+    mbar_init(&sh_bar[warp][0], 1);
+    mbar_init(&sh_bar[warp][1], 1);
+    mbar_fence_init();
   }
+  __syncthreads();
+  const bool safe = sh_safe != 0;
+  const float e_q = sh_eq;
+  const int c = lane % L;
+  float2 q2[E / 2];
+#pragma unroll
+  for (int e = 0; e < E / 2; ++e) q2[e] = make_float2(sh_q[c * E + 2 * e], sh_q[c * E + 2 * e + 1]);
+
+  unsigned char* const buf0 = dsmem + (warp * 2) * kHalfBytes;
+  const int64_t groups = ceil_div64(p.nodes, 32);
+  // Groups come from one work queue per query (hdr->next), so every SM keeps
+  // streaming until the bank is exhausted; each warp asks one group ahead so
+  // the atomic's latency hides behind a group's arithmetic.
+  unsigned* const queue = &p.scratch.hdr(q)->next;
+  // Lane 0 holds the ticket of the group after next in a register; it is
+  // broadcast one iteration later, so the atomic's round trip overlaps a
+  // group's arithmetic instead of stalling the warp.
+  unsigned ticket = 0u;
+  auto request = [&]() {
+    if (lane == 0) ticket = atomicAdd(queue, 1u);
+  };
+  auto take = [&]() -> int64_t { return (int64_t)__shfl_sync(kFull, ticket, 0); };
+  // half h of group g -> buffer h (lane 0 only)
+  auto issue = [&](int64_t g, int h) {
+    const int64_t r0 = g * 32 + 16 * h;
+    const int64_t rows = max((int64_t)0, min((int64_t)16, p.nodes - r0));
+    const unsigned bytes = (unsigned)(rows * D * (int64_t)sizeof(T));
+    if (bytes == 0) {
+      mbar_arrive_expect_tx(&sh_bar[warp][h], 0);  // completes the phase at once
+      return;
+    }
+    mbar_arrive_expect_tx(&sh_bar[warp][h], bytes);
+    bulk_g2s(buf0 + h * kHalfBytes, p.rows + r0 * D, bytes, &sh_bar[warp][h]);
+  };
+
+  WarpList list;
+  list.init();
+  bool failed = false;
+  unsigned phase_bits = 0u;    // bit h: parity of the next phase to wait for on buffer h
+  unsigned pending_bits = 0u;  // bit h: a copy into buffer h is in flight
+  if (safe) {
+    request();
+    int64_t g = take();
+    request();
+    int64_t gn = take();
+    request();                                   // the group after gn, taken next iteration
+    if (g < groups) {
+      if (lane == 0) {
+        issue(g, 0);
+        issue(g, 1);
+      }
+      pending_bits = 3u;
+    }
+    while (g < groups) {
+      const int64_t gnn = take();                // requested one iteration ago
+      request();
+      const int64_t row0 = g * 32;
+      const int64_t my_row = row0 + (lane % L) * R + lane / L;
+      const float nrm_pre = my_row < p.nodes ? __ldg(p.norms + my_row) : 0.0f;
+      const int valid = (int)min((int64_t)32, p.nodes - row0);
+      float part[SLOTS];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        if (!mbar_wait(&sh_bar[warp][h], (phase_bits >> h) & 1u, kWaitLimit)) {
+          failed = true;
+          break;
+        }
+        phase_bits ^= 1u << h;
+        pending_bits &= ~(1u << h);
+        const T* sb = reinterpret_cast<const T*>(buf0 + h * kHalfBytes);
+        if (valid == 32) {  // every group but possibly the bank's last one
+#pragma unroll
+          for (int jj = 0; jj < HS; ++jj) {
+            const int r = jj * R + lane / L;  // row within the half
+            const uint4 v = *reinterpret_cast<const uint4*>(sb + r * D + c * E);
+            const float2 a2 = dot16x2<T>(v, q2, make_float2(0.0f, 0.0f));
+            part[h * HS + jj] = a2.x + a2.y;
+          }
+        } else {
+#pragma unroll
+          for (int jj = 0; jj < HS; ++jj) {
+            const int r = jj * R + lane / L;
+            const uint4 v = (16 * h + r) < valid
+                                ? *reinterpret_cast<const uint4*>(sb + r * D + c * E)
+                                : make_uint4(0, 0, 0, 0);
+            const float2 a2 = dot16x2<T>(v, q2, make_float2(0.0f, 0.0f));
+            part[h * HS + jj] = a2.x + a2.y;
+          }
+        }
+        // this half's buffer is free again: start the next group's half
+        __syncwarp();
+        fence_proxy_async_smem();
+        if (gn < groups) {
+          if (lane == 0) issue(gn, h);
+          pending_bits |= 1u << h;
+        }
+      }
+      if (failed) break;
+      const float dot = reduce_scatter<SLOTS>(part, lane);
+      float s = -INFINITY;
+      if (my_row < p.nodes && isfinite(nrm_pre)) s = dot * __frcp_rn(nrm_pre + e_q);
+      list.offer(s, (uint32_t)my_row, lane);
+      g = gn;
+      gn = gnn;
+    }
+    if (failed) {
+      // drain this warp's copies still in flight before the block can exit
+      for (int k = 0; k < 2; ++k)
+        if ((pending_bits >> k) & 1u)
+          mbar_wait(&sh_bar[warp][k], (phase_bits >> k) & 1u, kWaitLimit);
+      if (lane == 0) atomicOr(&p.scratch.hdr(q)->err, 1);
+    }
+  }
+  asm volatile("griddepcontrol.launch_dependents;");
+  scan_finish<D, T, false, NW>(p, list, safe, query, q, lane, warp, sh_s, sh_id, sh_floor,
+                               &sh_last);
 }
 
 // Exact fallback: for each query whose approximate pass reported kOverflow,
@@ -409,7 +687,7 @@ __global__ void __launch_bounds__(kThreads) mla_scan_kernel(Params<T> p) {
 // Queries whose status is kOk exit at once.  D == 0 means runtime dim
 // (force_all only).  INL: row norms computed inline (see mla_scan_kernel).
 template <int D, typename T, bool INL = false>
-__global__ void __launch_bounds__(kThreads) mla_exact_kernel(Params<T> p) {
+__global__ void __launch_bounds__(kThreads) mla_exact_kernel(const __grid_constant__ Params<T> p) {
   __shared__ float sh_s[kWarps * 32];
   __shared__ uint32_t sh_id[kWarps * 32];
   __shared__ double sh_qnorm;
@@ -419,10 +697,13 @@ __global__ void __launch_bounds__(kThreads) mla_exact_kernel(Params<T> p) {
   constexpr int DMAX = D > 0 ? D : 1;
   __shared__ float sh_q[DMAX];
 
+  // Launched with programmatic dependent launch after the scan: wait until the
+  // scan grid has completed and its writes are visible (no-op otherwise).
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int q = blockIdx.y;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int dim = D > 0 ? D : p.dim;
-  const float* query = p.queries + (int64_t)q * dim;
+  const float* query = query_ptr(p, q, dim);
   Result* r = p.results + q;
 
   if (threadIdx.x == 0) {
@@ -436,7 +717,7 @@ __global__ void __launch_bounds__(kThreads) mla_exact_kernel(Params<T> p) {
   }
   __syncthreads();
   const int mode = sh_mode;
-  if (mode == kOk) return;
+  if (mode == kOk || mode == kError) return;
   const double qnorm = sh_qnorm;
 
   WarpList list;
@@ -558,6 +839,7 @@ __global__ void __launch_bounds__(kThreads) mla_exact_kernel(Params<T> p) {
   if (lane == 0) {
     hdr->lb = kOrderedNegInf;
     hdr->done = 0;
+    hdr->next = 0;
   }
 }
 
@@ -592,6 +874,8 @@ __global__ void scratch_init_kernel(unsigned char* base, size_t stride, int quer
     Header* h = reinterpret_cast<Header*>(base + stride * q);
     h->lb = kOrderedNegInf;
     h->done = 0;
+    h->err = 0;
+    h->next = 0;
   }
 }
 
@@ -609,12 +893,14 @@ struct grm_b200_mla_bank {
   void* d_rows = nullptr;
   float* d_norms = nullptr;
   bool exact_only = false;
+  bool bulk = false;         // scan with the bulk-copy kernel
   int grid_x = 1;
   int scratch_queries = 0;
   size_t stride = 0;
   unsigned char* d_scratch = nullptr;
-  Result* d_results = nullptr;
-  Result* h_results = nullptr;
+  Result* d_results = nullptr;         // async entries
+  Result* h_results = nullptr;         // mapped pinned host memory (synchronous entries)
+  Result* d_results_mapped = nullptr;  // its device alias
   float* d_queries = nullptr;
   size_t dq_cap = 0;
   cudaStream_t stream = nullptr;
@@ -629,7 +915,29 @@ namespace {
 bool fast_dim(int dim) { return dim == 64 || dim == 128 || dim == 256 || dim == 512; }
 
 template <typename T>
-using ScanFn = void (*)(Params<T>);
+using ScanFn = void (*)(const Params<T>);
+
+bool bulk_ok(int dtype, int dim) {
+  return (dtype == GRM_B200_F16 && (dim == 64 || dim == 128 || dim == 256)) ||
+         (dtype == GRM_B200_F32 && (dim == 64 || dim == 128));
+}
+
+template <typename T>
+ScanFn<T> scan_bulk_fn(int dim) {
+  if constexpr (sizeof(T) == 2) {
+    switch (dim) {
+      case 64: return mla_scan_bulk_kernel<64, T>;
+      case 128: return mla_scan_bulk_kernel<128, T>;
+      case 256: return mla_scan_bulk_kernel<256, T>;
+    }
+  } else {
+    switch (dim) {
+      case 64: return mla_scan_bulk_kernel<64, T>;
+      case 128: return mla_scan_bulk_kernel<128, T>;
+    }
+  }
+  return nullptr;
+}
 
 template <typename T>
 ScanFn<T> scan_fn(int dim) {
@@ -659,7 +967,14 @@ int pick_grid(grm_b200_mla_bank* b) {
   if (rc) return rc;
   int occ = 1;
   cudaError_t e;
-  if (b->dtype == GRM_B200_F16) {
+  b->bulk = !b->exact_only && bulk_ok(b->dtype, b->dim);
+  if (b->bulk) {
+    const void* fn = b->dtype == GRM_B200_F16 ? (const void*)scan_bulk_fn<__half>(b->dim)
+                                              : (const void*)scan_bulk_fn<float>(b->dim);
+    e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kBulkSmem);
+    if (e == cudaSuccess)
+      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, kBulkWarps * 32, kBulkSmem);
+  } else if (b->dtype == GRM_B200_F16) {
     auto fn = fast_dim(b->dim) ? scan_fn<__half>(b->dim) : exact_fn<__half>(b->dim);
     e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, kThreads, 0);
   } else {
@@ -669,7 +984,7 @@ int pick_grid(grm_b200_mla_bank* b) {
   if (e != cudaSuccess) return cuda_status(e);
   occ = std::max(1, occ);
   const int64_t groups = ceil_div64(b->nodes, 32);
-  const int64_t want = ceil_div64(groups, kWarps);
+  const int64_t want = ceil_div64(groups, b->bulk ? kBulkWarps : kWarps);
   b->grid_x = (int)std::max<int64_t>(1, std::min<int64_t>((int64_t)info.sms * occ, want));
   return 0;
 }
@@ -683,11 +998,16 @@ int reserve(grm_b200_mla_bank* b, int queries) {
   b->d_scratch = nullptr;
   b->d_results = nullptr;
   b->h_results = nullptr;
+  b->d_results_mapped = nullptr;
   b->scratch_queries = 0;
   b->stride = scratch_stride(b->grid_x);
   cudaError_t e = cudaMalloc(&b->d_scratch, b->stride * n);
   if (e == cudaSuccess) e = cudaMalloc(&b->d_results, sizeof(Result) * n);
-  if (e == cudaSuccess) e = cudaMallocHost(&b->h_results, sizeof(Result) * n);
+  if (e == cudaSuccess)
+    e = cudaHostAlloc(reinterpret_cast<void**>(&b->h_results), sizeof(Result) * n,
+                      cudaHostAllocMapped);
+  if (e == cudaSuccess)
+    e = cudaHostGetDevicePointer(reinterpret_cast<void**>(&b->d_results_mapped), b->h_results, 0);
   if (e != cudaSuccess) return b->err.set(cuda_status(e), "scratch allocation failed: %s", cudaGetErrorString(e));
   scratch_init_kernel<<<(n + 127) / 128, 128, 0, b->stream>>>(b->d_scratch, b->stride, n);
   e = cudaGetLastError();
@@ -718,6 +1038,10 @@ Params<T> make_params(grm_b200_mla_bank* b, const float* dq, int topk) {
 template <typename T>
 int launch_scan(grm_b200_mla_bank* b, const Params<T>& p, int nq, cudaStream_t s) {
   dim3 grid(b->grid_x, nq);
+  if (b->bulk) {
+    scan_bulk_fn<T>(b->dim)<<<grid, kBulkWarps * 32, kBulkSmem, s>>>(p);
+    return cuda_status(cudaGetLastError());
+  }
   if (!b->exact_only) {
     scan_fn<T>(b->dim)<<<grid, kThreads, 0, s>>>(p);
     cudaError_t e = cudaGetLastError();
@@ -726,42 +1050,67 @@ int launch_scan(grm_b200_mla_bank* b, const Params<T>& p, int nq, cudaStream_t s
   return 0;
 }
 
+// pdl: launch as a programmatic dependent of the preceding scan on `s`, so the
+// launch overlaps the scan's tail instead of following it.
 template <typename T>
-int launch_exact(grm_b200_mla_bank* b, const Params<T>& p, int nq, cudaStream_t s) {
+int launch_exact(grm_b200_mla_bank* b, const Params<T>& p, int nq, cudaStream_t s,
+                 bool pdl = false) {
   dim3 grid(b->grid_x, nq);
-  exact_fn<T>(b->exact_only ? 0 : b->dim)<<<grid, kThreads, 0, s>>>(p);
-  return cuda_status(cudaGetLastError());
+  auto fn = exact_fn<T>(b->exact_only ? 0 : b->dim);
+  if (!pdl || b->exact_only) {
+    fn<<<grid, kThreads, 0, s>>>(p);
+    return cuda_status(cudaGetLastError());
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cuda_status(cudaLaunchKernelEx(&cfg, fn, p));
 }
 
-// Route `nq` device queries synchronously into b->h_results[0..nq).
+// Route `nq` queries synchronously into b->h_results[0..nq).  The queries are
+// device memory (dq), or one host query carried inline in the launch
+// parameters (dq == nullptr, q_host != nullptr).  Results are written by the
+// kernels straight into mapped pinned host memory (no copy-back call).
 template <typename T>
-int run_chunk(grm_b200_mla_bank* b, const float* dq, int nq, int topk) {
+int run_chunk(grm_b200_mla_bank* b, const float* dq, const float* q_host, int nq, int topk) {
   Params<T> p = make_params<T>(b, dq, topk);
+  p.results = b->d_results_mapped;
+  if (!dq) std::memcpy(p.qinline, q_host, sizeof(float) * (size_t)b->dim);
   int rc = launch_scan<T>(b, p, nq, b->stream);
   if (rc) return b->err.set(rc, "MLA scan launch failed: %s", cudaGetErrorString(cudaGetLastError()));
   bool need_exact = b->exact_only;
   if (!b->exact_only) {
-    cudaError_t e = cudaMemcpyAsync(b->h_results, b->d_results, sizeof(Result) * nq,
-                                    cudaMemcpyDeviceToHost, b->stream);
-    if (e == cudaSuccess) e = cudaStreamSynchronize(b->stream);
+    cudaError_t e = cudaStreamSynchronize(b->stream);
     if (e != cudaSuccess) return b->err.set(cuda_status(e), "MLA route failed: %s", cudaGetErrorString(e));
-    for (int i = 0; i < nq; ++i) need_exact = need_exact || b->h_results[i].status != kOk;
+    for (int i = 0; i < nq; ++i) {
+      const int st = ((volatile Result*)b->h_results)[i].status;
+      if (st == kError)
+        return b->err.set(GRM_B200_KERNEL_BASE + 1,
+                          "MLA scan: a bounded device wait gave up (query %d)", i);
+      need_exact = need_exact || st != kOk;
+    }
   }
   if (need_exact) {
     b->fallbacks += 1;
     rc = launch_exact<T>(b, p, nq, b->stream);
     if (rc) return b->err.set(rc, "MLA exact pass launch failed");
-    cudaError_t e = cudaMemcpyAsync(b->h_results, b->d_results, sizeof(Result) * nq,
-                                    cudaMemcpyDeviceToHost, b->stream);
-    if (e == cudaSuccess) e = cudaStreamSynchronize(b->stream);
+    cudaError_t e = cudaStreamSynchronize(b->stream);
     if (e != cudaSuccess) return b->err.set(cuda_status(e), "MLA exact pass failed: %s", cudaGetErrorString(e));
   }
   return 0;
 }
 
 int route_device_queries(grm_b200_mla_bank* b, const float* dq, int query_count, int warmup,
-                         int topk, uint64_t* out_ids, float* out_scores, float* elapsed) {
-  if (!dq || !out_ids || query_count <= 0 || warmup < 0 || warmup >= query_count || topk <= 0 ||
+                         int topk, uint64_t* out_ids, float* out_scores, float* elapsed,
+                         const float* q_host = nullptr) {
+  if ((!dq && !q_host) || !out_ids || query_count <= 0 || warmup < 0 || warmup >= query_count || topk <= 0 ||
       topk > GRM_B200_MAX_TOPK)
     return b->err.set(GRM_B200_EINVAL, "invalid MLA route arguments (queries=%d warmup=%d topk=%d)",
                       query_count, warmup, topk);
@@ -770,8 +1119,9 @@ int route_device_queries(grm_b200_mla_bank* b, const float* dq, int query_count,
   int rc = reserve(b, query_count);
   if (rc) return rc;
   auto chunk = [&](int q0, int nq) -> int {
-    rc = (b->dtype == GRM_B200_F16) ? run_chunk<__half>(b, dq + (int64_t)q0 * b->dim, nq, topk)
-                                    : run_chunk<float>(b, dq + (int64_t)q0 * b->dim, nq, topk);
+    const float* qd = dq ? dq + (int64_t)q0 * b->dim : nullptr;
+    rc = (b->dtype == GRM_B200_F16) ? run_chunk<__half>(b, qd, q_host, nq, topk)
+                                    : run_chunk<float>(b, qd, q_host, nq, topk);
     if (rc) return rc;
     for (int i = 0; i < nq; ++i) {
       const Result& r = b->h_results[i];
@@ -907,6 +1257,9 @@ int grm_b200_mla_route(grm_b200_mla_bank* bank, const float* queries_host, int q
     return bank->err.set(GRM_B200_EINVAL, "invalid MLA route arguments (dim=%d, bank dim=%d)", dim,
                          bank->dim);
   cudaError_t e = cudaSetDevice(bank->device);
+  if (e == cudaSuccess && query_count == 1 && dim <= kInlineMax)
+    return route_device_queries(bank, nullptr, 1, warmup, topk, out_ids_host, out_scores_host,
+                                elapsed_ms, queries_host);
   const size_t need = (size_t)query_count * dim;
   if (e == cudaSuccess && need > bank->dq_cap) {
     if (bank->d_queries) cudaFree(bank->d_queries);
@@ -960,14 +1313,14 @@ int route_async_phases(grm_b200_mla_bank* bank, const float* queries_device, int
     p.out_scores = out_scores_device;
     p.id_offset = id_offset;
     if (phase & 1) rc = launch_scan<__half>(bank, p, query_count, s);
-    if (!rc && (phase & 2)) rc = launch_exact<__half>(bank, p, query_count, s);
+    if (!rc && (phase & 2)) rc = launch_exact<__half>(bank, p, query_count, s, true);
   } else {
     Params<float> p = make_params<float>(bank, queries_device, topk);
     p.out_ids = out_ids_device;
     p.out_scores = out_scores_device;
     p.id_offset = id_offset;
     if (phase & 1) rc = launch_scan<float>(bank, p, query_count, s);
-    if (!rc && (phase & 2)) rc = launch_exact<float>(bank, p, query_count, s);
+    if (!rc && (phase & 2)) rc = launch_exact<float>(bank, p, query_count, s, true);
   }
   if (rc) return bank->err.set(rc, "MLA async route launch failed");
   if (phase & 1) bank->routes += (uint64_t)query_count;

@@ -32,94 +32,119 @@ __device__ __forceinline__ uint32_t bf16x2_bits(float a, float b) {
 }
 
 // Reference format: int8 codes, groups of 32, fp32 scales; output
-// bf16(fp16(code * scale)).  One thread per 16 values.
+// bf16(fp16(code * scale)).  Grid: x strides 16-value chunks of one
+// (graft, layer) slice, y = slice.  Each thread handles kU consecutive chunks
+// with all loads issued before any store; consecutive threads write
+// consecutive 32-byte pieces, so a warp stores 1 KB contiguously.
+constexpr int kU = 2;
+
+__device__ __forceinline__ void store_bf16x16(uint16_t* dst, const float (&f)[16]) {
+  uint32_t o[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) o[j] = bf16x2_bits(f[2 * j], f[2 * j + 1]);
+  reinterpret_cast<uint4*>(dst)[0] = make_uint4(o[0], o[1], o[2], o[3]);
+  reinterpret_cast<uint4*>(dst)[1] = make_uint4(o[4], o[5], o[6], o[7]);
+}
+
 __global__ void __launch_bounds__(256) mount_ref_kernel(const int8_t* __restrict__ codes,
                                                         const float* __restrict__ scales,
-                                                        int64_t grafts, int64_t layers,
-                                                        int64_t vals, int64_t width, Seats seats,
-                                                        uint16_t* __restrict__ arena,
+                                                        int64_t layers, int64_t vals, int64_t width,
+                                                        Seats seats, uint16_t* __restrict__ arena,
                                                         int64_t arena_seats) {
-  const int64_t per_slice = vals / 16;
-  const int64_t total = grafts * layers * per_slice;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t slice = i / per_slice;
-    const int64_t v0 = (i - slice * per_slice) * 16;
-    const int64_t g = slice / layers, l = slice - g * layers;
-    const uint4 c = ld_stream(codes + slice * vals + v0);
-    const float s = __ldg(scales + (slice * vals + v0) / 32);
-    const int8_t* cb = reinterpret_cast<const int8_t*>(&c);
-    uint32_t o[8];
+  const int64_t slice = blockIdx.y;
+  const int64_t g = slice / layers, l = slice - g * layers;
+  const int64_t chunks = vals / 16;
+  const int8_t* src = codes + slice * vals;
+  const float* sc = scales + slice * (vals / 32);
+  uint16_t* dst = arena + (l * arena_seats + seats.seat[g]) * width;
+  for (int64_t c0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * kU; c0 < chunks;
+       c0 += (int64_t)gridDim.x * blockDim.x * kU) {
+    uint4 v[kU];
+    float s[kU];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      // fp16 first (dequantize_symmetric_group32), then the bf16 upload cast
-      const float a = __half2float(__float2half_rn((float)cb[2 * j] * s));
-      const float b = __half2float(__float2half_rn((float)cb[2 * j + 1] * s));
-      o[j] = bf16x2_bits(a, b);
+    for (int u = 0; u < kU; ++u) {
+      if (c0 + u < chunks) {
+        v[u] = ld_stream(src + (c0 + u) * 16);
+        s[u] = __ldg(sc + ((c0 + u) * 16) / 32);
+      }
     }
-    uint16_t* dst = arena + (l * arena_seats + seats.seat[g]) * width + v0;
-    reinterpret_cast<uint4*>(dst)[0] = make_uint4(o[0], o[1], o[2], o[3]);
-    reinterpret_cast<uint4*>(dst)[1] = make_uint4(o[4], o[5], o[6], o[7]);
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      if (c0 + u >= chunks) break;
+      const int8_t* cb = reinterpret_cast<const int8_t*>(&v[u]);
+      float f[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j)  // fp16 first (dequantize_symmetric_group32), then bf16
+        f[j] = __half2float(__float2half_rn((float)cb[j] * s[u]));
+      store_bf16x16(dst + (c0 + u) * 16, f);
+    }
   }
 }
 
+// 16 codes of one chunk from the chunk's little-endian bit stream.
 template <int BITS>
-__device__ __forceinline__ int code_at(const uint32_t* w, int j) {
-  if constexpr (BITS == 8) {
-    return (int)(int8_t)((w[j >> 2] >> (8 * (j & 3))) & 0xFF);
-  } else if constexpr (BITS == 4) {
-    const uint32_t n = (w[j >> 3] >> (4 * (j & 7))) & 0xF;
-    return (int)(n << 28) >> 28;
-  } else {  // 6 bits: 4 codes per little-endian 24-bit triple
-    const int bit = 6 * j;
-    const int word = bit >> 5, sh = bit & 31;
-    uint32_t v = w[word] >> sh;
-    if (sh > 26) v |= w[word + 1] << (32 - sh);
-    return (int)((v & 0x3F) << 26) >> 26;
+struct Chunk {
+  static constexpr int kWords = 16 * BITS / 32;  // 4 / 3 / 2 words
+  uint32_t w[kWords];
+  __device__ __forceinline__ void load(const uint8_t* p) {
+    if constexpr (BITS == 8) {
+      const uint4 v = ld_stream(p);
+      w[0] = v.x; w[1] = v.y; w[2] = v.z; w[3] = v.w;
+    } else if constexpr (BITS == 4) {
+      const uint2 v = __ldg(reinterpret_cast<const uint2*>(p));
+      w[0] = v.x; w[1] = v.y;
+    } else {
+      const uint32_t* q = reinterpret_cast<const uint32_t*>(p);
+      w[0] = __ldg(q); w[1] = __ldg(q + 1); w[2] = __ldg(q + 2);
+    }
   }
-}
+  __device__ __forceinline__ int code(int j) const {
+    if constexpr (BITS == 8) {
+      return (int)(int8_t)((w[j >> 2] >> (8 * (j & 3))) & 0xFF);
+    } else if constexpr (BITS == 4) {
+      return (int)(((w[j >> 3] >> (4 * (j & 7))) & 0xF) << 28) >> 28;
+    } else {
+      const int bit = 6 * j, word = bit >> 5, sh = bit & 31;
+      uint32_t v = w[word] >> sh;
+      if (sh > 26) v |= w[word + 1] << (32 - sh);
+      return (int)((v & 0x3F) << 26) >> 26;
+    }
+  }
+};
 
 // Packed format: `BITS`-bit codes, groups of 64 values, fp16 scales; output
-// bf16(code * scale).  One thread per group (64 values, 128 output bytes).
+// bf16(code * scale).  Same grid shape as mount_ref_kernel.
 template <int BITS>
 __global__ void __launch_bounds__(256) mount_packed_kernel(const uint8_t* __restrict__ codes,
                                                            const __half* __restrict__ scales,
-                                                           int64_t grafts, int64_t layers,
-                                                           int64_t vals, int64_t width, Seats seats,
+                                                           int64_t layers, int64_t vals,
+                                                           int64_t width, Seats seats,
                                                            uint16_t* __restrict__ arena,
                                                            int64_t arena_seats) {
-  constexpr int G = 64;
-  constexpr int GB = G * BITS / 8;  // bytes per group: 64 / 48 / 32
-  const int64_t per_slice = vals / G;
-  const int64_t total = grafts * layers * per_slice;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t slice = i / per_slice;
-    const int64_t gi = i - slice * per_slice;
-    const int64_t g = slice / layers, l = slice - g * layers;
-    uint32_t w[GB / 4 + 1];
-    const uint8_t* src = codes + i * GB;
+  const int64_t slice = blockIdx.y;
+  const int64_t g = slice / layers, l = slice - g * layers;
+  const int64_t chunks = vals / 16;
+  const uint8_t* src = codes + slice * (vals * BITS / 8);
+  const __half* sc = scales + slice * (vals / 64);
+  uint16_t* dst = arena + (l * arena_seats + seats.seat[g]) * width;
+  for (int64_t c0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * kU; c0 < chunks;
+       c0 += (int64_t)gridDim.x * blockDim.x * kU) {
+    Chunk<BITS> ch[kU];
+    float s[kU];
 #pragma unroll
-    for (int k = 0; k < GB / 16; ++k) {
-      const uint4 v = ld_stream(src + 16 * k);
-      w[4 * k] = v.x;
-      w[4 * k + 1] = v.y;
-      w[4 * k + 2] = v.z;
-      w[4 * k + 3] = v.w;
-    }
-    w[GB / 4] = 0;
-    const float s = __half2float(scales[i]);
-    uint16_t* dst = arena + (l * arena_seats + seats.seat[g]) * width + gi * G;
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      uint32_t o[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int c0 = code_at<BITS>(w, 8 * k + 2 * j);
-        const int c1 = code_at<BITS>(w, 8 * k + 2 * j + 1);
-        o[j] = bf16x2_bits((float)c0 * s, (float)c1 * s);
+    for (int u = 0; u < kU; ++u) {
+      if (c0 + u < chunks) {
+        ch[u].load(src + (c0 + u) * (2 * BITS));  // 16 codes = 2*BITS bytes
+        s[u] = __half2float(sc[(c0 + u) >> 2]);
       }
-      reinterpret_cast<uint4*>(dst)[k] = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      if (c0 + u >= chunks) break;
+      float f[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) f[j] = (float)ch[u].code(j) * s[u];
+      store_bf16x16(dst + (c0 + u) * 16, f);
     }
   }
 }
@@ -155,6 +180,13 @@ int grid_for(int64_t work) {
   return (int)std::max<int64_t>(1, std::min<int64_t>(ceil_div64(work, 256), (int64_t)info.sms * 8));
 }
 
+// x: enough 256-thread blocks for kU chunks per thread of one slice (capped,
+// then grid-strided); y: one row of blocks per (graft, layer) slice.
+dim3 slice_grid(int64_t slices, int64_t chunks) {
+  const int64_t per = ceil_div64(chunks, 256 * kU);
+  return dim3((unsigned)std::max<int64_t>(1, std::min<int64_t>(per, 1024)), (unsigned)slices);
+}
+
 bool seats_ok(const int64_t* seats, int64_t n, int64_t tokens, int64_t arena_seats, Seats* out) {
   if (!seats || n <= 0 || n > kMaxGrafts) return false;
   for (int64_t g = 0; g < n; ++g) {
@@ -183,9 +215,9 @@ int grm_b200_mount_ref(const int8_t* codes_device, const float* scales_device, i
     return GRM_B200_EINVAL;
   }
   const int64_t vals = tokens * width;
-  const int64_t work = n_grafts * layers * (vals / 16);
-  mount_ref_kernel<<<grid_for(work), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      codes_device, scales_device, n_grafts, layers, vals, width, seats, arena_device, arena_seats);
+  const dim3 grid = slice_grid(n_grafts * layers, vals / 16);
+  mount_ref_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      codes_device, scales_device, layers, vals, width, seats, arena_device, arena_seats);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     set_thread_error("mount_ref launch failed: %s", cudaGetErrorString(e));
@@ -208,19 +240,18 @@ int grm_b200_mount_packed(const uint8_t* codes_device, const uint16_t* scales_de
                      (long long)width);
     return GRM_B200_EINVAL;
   }
-  const int64_t work = n_grafts * layers * (vals / 64);
-  const int grid = grid_for(work);
+  const dim3 grid = slice_grid(n_grafts * layers, vals / 16);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const __half* sc = reinterpret_cast<const __half*>(scales_device);
   if (bits == 8)
-    mount_packed_kernel<8><<<grid, 256, 0, s>>>(codes_device, sc, n_grafts, layers, vals, width,
-                                                seats, arena_device, arena_seats);
+    mount_packed_kernel<8><<<grid, 256, 0, s>>>(codes_device, sc, layers, vals, width, seats,
+                                                arena_device, arena_seats);
   else if (bits == 6)
-    mount_packed_kernel<6><<<grid, 256, 0, s>>>(codes_device, sc, n_grafts, layers, vals, width,
-                                                seats, arena_device, arena_seats);
+    mount_packed_kernel<6><<<grid, 256, 0, s>>>(codes_device, sc, layers, vals, width, seats,
+                                                arena_device, arena_seats);
   else
-    mount_packed_kernel<4><<<grid, 256, 0, s>>>(codes_device, sc, n_grafts, layers, vals, width,
-                                                seats, arena_device, arena_seats);
+    mount_packed_kernel<4><<<grid, 256, 0, s>>>(codes_device, sc, layers, vals, width, seats,
+                                                arena_device, arena_seats);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     set_thread_error("mount_packed launch failed: %s", cudaGetErrorString(e));

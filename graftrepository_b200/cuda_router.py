@@ -179,6 +179,7 @@ class CudaMLARouteBank:
         self.signature = signature
         self.dtype = dtype
         self.last_scores: np.ndarray | None = None
+        self._fn_route = _lib.load().grm_b200_mla_route
 
     @property
     def handle(self) -> ctypes.c_void_p:
@@ -239,7 +240,7 @@ class CudaMLARouteBank:
         rows = scores = None
         for _ in range(repeats):
             rows, scores, dev, wall = self._route_raw(
-                _lib.load().grm_b200_mla_route, q.ctypes.data, q.shape[0], int(topk), int(warmup))
+                self._fn_route, q.ctypes.data, q.shape[0], int(topk), int(warmup))
             walls.append(wall)
             devs.append(dev)
         return self._finish(rows, scores, walls, devs, q.shape[0], warmup, repeats)

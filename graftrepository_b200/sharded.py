@@ -27,7 +27,7 @@ import numpy as np
 U64MAX = np.iinfo(np.uint64).max
 
 __all__ = ["mla_shard_range", "gqa_shard_range", "merge_topk_host", "ShardedRoute",
-           "ShardedMLARoute"]
+           "ShardedMLARoute", "ShardedGQARoute"]
 
 
 def mla_shard_range(nodes: int, world: int, rank: int) -> tuple[int, int]:
@@ -145,6 +145,49 @@ class ShardedMLARoute(ShardedRoute):
         if rc != 0:
             raise RuntimeError("merge_topk failed")
         return out_i, out_s
+
+    def close(self) -> None:
+        self.bank.close()
+
+
+class ShardedGQARoute(ShardedRoute):
+    """The ragged GQA route over this rank's token-balanced node range."""
+
+    def __init__(self, group, keys_shard_device, token_offsets_shard, first_row: int,
+                 kv_heads: int, head_dim: int, dtype_code: int = 2, device: int = 0,
+                 stream=None):
+        import torch
+
+        from . import _lib
+        from .cuda_router import CudaGQARouteSidecar
+
+        self.torch = torch
+        self.first_row = int(first_row)
+        self.bank = CudaGQARouteSidecar(device=device).create_bank_device(
+            keys_shard_device.data_ptr(), dtype_code, token_offsets_shard, kv_heads, head_dim,
+            keepalive=keys_shard_device)
+        self._lib = _lib.load()
+        self.stream = stream
+        super().__init__(group, self._local, self._merge)
+
+    def _stream(self) -> int:
+        s = self.stream or self.torch.cuda.current_stream()
+        return int(s.cuda_stream)
+
+    def _local(self, queries, k: int):
+        """queries: device fp32 [Q, H, qt, D]."""
+        torch = self.torch
+        Q, H, qt, _ = queries.shape
+        s = torch.empty((Q, k), dtype=torch.float32, device=queries.device)
+        i = torch.empty((Q, k), dtype=torch.int64, device=queries.device)
+        rc = self._lib.grm_b200_gqa_route_async(self.bank._h, queries.data_ptr(), Q, H, qt, k,
+                                                self.first_row, i.data_ptr(), s.data_ptr(),
+                                                self._stream())
+        if rc != 0:
+            raise RuntimeError(self.bank._err())
+        return s, i
+
+    _merge = ShardedMLARoute._merge
 
     def close(self) -> None:
         self.bank.close()

@@ -184,6 +184,16 @@ int grm_b200_gqa_route_device(grm_b200_gqa_bank* bank, const float* queries_devi
                               int warmup, int topk, uint64_t* out_ids_host,
                               float* out_scores_host, float* elapsed_ms);
 
+/* Stream-ordered GQA route with device outputs (no host synchronisation):
+ * out_ids_device / out_scores_device [query_count * topk] on `stream`;
+ * `id_offset` is added to every returned node row (the first row of this
+ * shard).  Calls on one bank must not overlap on the GPU (shared scratch).
+ * No reference counterpart (the reference GQA route always synchronises). */
+int grm_b200_gqa_route_async(grm_b200_gqa_bank* bank, const float* queries_device,
+                             int query_count, int query_heads, int query_tokens, int topk,
+                             uint64_t id_offset, uint64_t* out_ids_device,
+                             float* out_scores_device, void* stream);
+
 /* Replaces grm_gqa_cuda_arena_destroy (scripts/grm_gqa_cuda_probe.py:584-587). */
 int grm_b200_gqa_bank_destroy(grm_b200_gqa_bank* bank);
 const char* grm_b200_gqa_last_error(grm_b200_gqa_bank* bank);

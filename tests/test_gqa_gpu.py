@@ -181,3 +181,24 @@ def test_full_size_config3(sidecar):
     routes, refined = bank.stats()
     assert routes == 2 and refined >= 6
     bank.close()
+
+
+def test_async_route_device_outputs_and_offset(sidecar):
+    import torch
+
+    keys, off = _ragged(12, 50, 8, 128, 200, zero_nodes=(7,), dup=(10, 11))
+    bank = sidecar.create_bank_csr(keys, off, 8, 128, dtype="bf16")
+    qs = np.random.default_rng(12).standard_normal((3, 32, 1, 128), dtype=np.float32)
+    want_ids, want_s = raw_route(bank, qs, 4)
+    dq = torch.from_numpy(qs).cuda()
+    ids = torch.empty((3, 4), dtype=torch.int64, device="cuda")
+    sc = torch.empty((3, 4), dtype=torch.float32, device="cuda")
+    rc = _lib.load().grm_b200_gqa_route_async(bank._h, dq.data_ptr(), 3, 32, 1, 4, 1000,
+                                              ids.data_ptr(), sc.data_ptr(),
+                                              torch.cuda.current_stream().cuda_stream)
+    assert rc == 0
+    torch.cuda.synchronize()
+    got = ids.cpu().numpy().view(np.uint64)
+    assert np.array_equal(got, want_ids + 1000)
+    assert np.array_equal(sc.cpu().numpy(), want_s)
+    bank.close()

@@ -191,3 +191,27 @@ def test_full_size_config2(sidecar):
     assert np.all(ids < n)
     bank.close()
     torch.cuda.synchronize()
+
+
+def test_async_route_resolves_ties_after_scan(sidecar):
+    """The programmatic-dependent resolve kernel handles a saturated margin."""
+    import torch
+
+    rng = np.random.default_rng(44)
+    base = rng.standard_normal((2, 256)).astype(np.float16)
+    rows = np.repeat(base, 5000, axis=0)
+    bank = sidecar.create_bank_raw(rows, 1)
+    bank.reserve(2)
+    qs = base.astype(np.float32)
+    dq = torch.from_numpy(qs).cuda()
+    ids = torch.empty((2, 6), dtype=torch.int64, device="cuda")
+    sc = torch.empty((2, 6), dtype=torch.float32, device="cuda")
+    bank.route_async(dq.data_ptr(), 2, 6, ids.data_ptr(), sc.data_ptr(),
+                     torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    rows32 = rows.astype(np.float32)
+    for i in range(2):
+        want, want_s = O.mla_route(rows32, qs[i], 6)
+        assert ids[i].cpu().numpy().view(np.uint64).tolist() == want.tolist()
+        assert np.array_equal(sc[i].cpu().numpy(), want_s)
+    bank.close()
