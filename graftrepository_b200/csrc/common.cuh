@@ -91,6 +91,29 @@ struct WarpList {
       m &= __ballot_sync(kFull, better(cs, cid, ts, tid));
     }
   }
+  // offer() that also skips candidates below the list's k-th score minus
+  // `margin2`.  Used where only rows within margin2 of the final k-th best
+  // matter: the list's k-th score only grows, so a skipped row can never get
+  // within margin2 of the final k-th best.  The list's last entry still
+  // bounds the rows dropped for lack of room.
+  __device__ __forceinline__ void offer_margin(float cs, uint32_t cid, int lane, int k,
+                                               float margin2) {
+    float ts = __shfl_sync(kFull, s, 31);
+    uint32_t tid = __shfl_sync(kFull, id, 31);
+    float tk = __shfl_sync(kFull, s, k - 1) - margin2;
+    unsigned m = __ballot_sync(kFull, isfinite(cs) && cs >= tk && better(cs, cid, ts, tid));
+    while (m) {
+      const int src = __ffs(m) - 1;
+      const float bs = __shfl_sync(kFull, cs, src);
+      const uint32_t bid = __shfl_sync(kFull, cid, src);
+      insert(bs, bid, lane);
+      m &= m - 1;
+      ts = __shfl_sync(kFull, s, 31);
+      tid = __shfl_sync(kFull, id, 31);
+      tk = __shfl_sync(kFull, s, k - 1) - margin2;
+      m &= __ballot_sync(kFull, cs >= tk && better(cs, cid, ts, tid));
+    }
+  }
 };
 
 // 16-byte streaming load that bypasses L1 allocation (the bank is read once).
@@ -161,6 +184,24 @@ __device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gmem_src, u
   asm volatile(
       "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
       ::"r"(smem_u32(smem_dst)), "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// An L2 policy that marks lines evict-first: a stream read once (the bank)
+// then leaves the rest of L2 -- code, scratch, results -- in place.
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
+// bulk_g2s with an L2 cache policy (l2_evict_first_policy for streamed data).
+__device__ __forceinline__ void bulk_g2s_hint(void* smem_dst, const void* gmem_src, unsigned bytes,
+                                              uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1], %2, [%3], %4;"
+      ::"r"(smem_u32(smem_dst)), "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
       : "memory");
 }
 

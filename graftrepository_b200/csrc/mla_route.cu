@@ -53,8 +53,7 @@ struct Header {
   int lb;          // ordered float: best block k-th approximate score so far
   unsigned done;   // blocks finished in this launch
   int err;         // a bounded device wait gave up in this launch
-  unsigned next;   // next 32-row group to hand out (bulk scan work queue)
-  int pad[12];
+  int pad[13];
 };
 
 struct Entry {
@@ -97,6 +96,7 @@ struct Params {
   float* out_scores;
   uint64_t id_offset;
   int force_all;         // exact kernel: score every row (bank outside the fast path)
+  unsigned long long* fallback_count;  // queries that took the exact pass (optional)
   // A single query may travel inside the launch parameters (queries == nullptr):
   // the synchronous host entry then needs no host-to-device copy.
   float qinline[kInlineMax];
@@ -234,69 +234,135 @@ __device__ void write_result(const Params<T>& p, int q, const WarpList& ex, int 
   }
 }
 
-// Everything after the streaming loop: merge the warps' lists, publish the
-// entries within the margin of the best block k-th score so far, and in the
-// last block to finish merge all blocks, select the candidates and recompute
-// them with the reference arithmetic (or flag the exact fallback).
-template <int D, typename T, bool INL, int NW>
-__device__ __forceinline__ void scan_finish(const Params<T>& p, WarpList& list, bool safe,
-                                            const float* query, int q, int lane, int warp,
-                                            float* sh_s, uint32_t* sh_id, float* sh_floor,
-                                            int* sh_last) {
-  block_merge<NW>(list, lane, warp, sh_s, sh_id);
-  Header* hdr = p.scratch.hdr(q);
-  if (warp == 0) {
-    const float kth = __shfl_sync(kFull, list.s, p.topk - 1);
-    int lb_now = 0;
-    if (lane == 0) {
-      const int enc = isfinite(kth) ? float_to_ordered(kth) : kOrderedNegInf;
-      const int old = atomicMax(&hdr->lb, enc);
-      lb_now = old > enc ? old : enc;
-    }
-    lb_now = __shfl_sync(kFull, lb_now, 0);
-    const float wthr = ordered_to_float(lb_now) - 2.0f * kMargin;
-    const bool keep = isfinite(list.s) && list.s >= wthr;
-    const int cnt = __popc(__ballot_sync(kFull, keep));
-    Entry* ent = p.scratch.entries(q) + (int64_t)blockIdx.x * 32;
-    if (lane < cnt) ent[lane] = Entry{list.s, list.id};
-    const float last = __shfl_sync(kFull, list.s, 31);
-    if (lane == 0) {
-      p.scratch.counts(q)[blockIdx.x] = cnt;
-      p.scratch.floors(q)[blockIdx.x] = isfinite(last) ? last : -INFINITY;
-      __threadfence();
-      const unsigned ticket = atomicAdd(&hdr->done, 1u);
-      *sh_last = (ticket == gridDim.x - 1);
-    }
-  }
-  __syncthreads();
-  if (!*sh_last) return;
-  __threadfence();
+// Shared memory of the merge/refine epilogue.  qraw holds the query as given
+// (the exact refine reads it many times); s/id double as the candidate list
+// of the final merge.
+template <int NW, int D>
+struct FinishSmem {
+  float s[NW * 32];
+  uint32_t id[NW * 32];
+  float kth[NW];
+  float floor[NW];
+  float qraw[D];
+  double qn;
+  int last;
+  int ncand;
+};
 
-  // Last block: merge the published entries.
-  list.init();
-  float fmax = -INFINITY;
-  for (int b = warp; b < (int)gridDim.x; b += NW) {
-    const int cnt = __ldcg(p.scratch.counts(q) + b);
-    const Entry* ent = p.scratch.entries(q) + (int64_t)b * 32;
-    float s = -INFINITY;
-    uint32_t id = kNoRow;
-    if (lane < cnt) {
-      s = __ldcg(&ent[lane].s);
-      id = __ldcg(&ent[lane].id);
-    }
-    list.offer(s, id, lane);
-    fmax = fmaxf(fmax, __ldcg(p.scratch.floors(q) + b));
+// The reference query norm (query_norm_seq's order) for a compile-time dim.
+template <int D>
+__device__ __forceinline__ double query_norm_seq_t(const float* q) {
+  double acc = 0.0;
+#pragma unroll 8
+  for (int d = 0; d < D; ++d) {
+    const double v = (double)q[d];
+    acc = fma(v, v, acc);
   }
-  if (lane == 0) sh_floor[warp] = fmax;
+  return sqrt(acc);
+}
+
+// exact_score / exact_score_inline_norm for the final refine: the row's
+// cache lines are prefetched first, then read 64 bytes per step in a short
+// loop.  The final merge runs in a single block right after the bank stream
+// has flushed L2, so its code is fetched cold: it is kept small on purpose.
+template <int D, typename T, bool INL>
+__device__ float exact_score_tail(const T* row, const float* q, double qnorm, float norm) {
+  constexpr int E = 16 / (int)sizeof(T);
+  constexpr int BYTES = D * (int)sizeof(T);
+  const char* rb = reinterpret_cast<const char*>(row);
+#pragma unroll 1
+  for (int o = 0; o < BYTES; o += 128) asm volatile("prefetch.global.L1 [%0];" ::"l"(rb + o));
+  const uint4* rv = reinterpret_cast<const uint4*>(row);
+  double dot = 0.0, n2 = 0.0;
+#pragma unroll 1
+  for (int c0 = 0; c0 < BYTES / 16; c0 += 4) {
+    uint4 v[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[i] = ld_nc16(rv + c0 + i);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const T* e = reinterpret_cast<const T*>(&v[i]);
+#pragma unroll
+      for (int k = 0; k < E; ++k) {
+        const double c = (double)to_f(e[k]);
+        dot = fma((double)q[(c0 + i) * E + k], c, dot);
+        if constexpr (INL) n2 = fma(c, c, n2);
+      }
+    }
+  }
+  if constexpr (INL) norm = (float)sqrt(n2);
+  return (float)(dot / (qnorm * (double)norm + 1.0e-8));
+}
+
+// Final merge of the G published block lists of query q (one block, NW
+// warps): pick every row whose approximate score is within 2*margin of the
+// approximate k-th best and recompute it with the reference arithmetic, or
+// flag the exact fallback when the lists were saturated inside the margin.
+// hdr->lb is by now the best block k-th score, a lower bound of the
+// approximate k-th best, so entries below lb - 2*margin are skipped: no
+// candidate is among them.  All threads filter the entry slots into a
+// shared candidate list (independent loads), warp 0 merges it while warp 1
+// computes the reference query norm.
+template <int D, typename T, bool INL, int NW>
+__device__ __forceinline__ void final_merge(const Params<T>& p, int q, int G, float margin,
+                                            bool safe, int lane, int warp,
+                                            FinishSmem<NW, D>& sm) {
+  static_assert(NW >= 2, "final_merge needs two warps");
+  Header* hdr = p.scratch.hdr(q);
+  if (threadIdx.x == 0) sm.ncand = 0;
   __syncthreads();
-  block_merge<NW>(list, lane, warp, sh_s, sh_id);
+  const int lb = __ldcg(&hdr->lb);
+  const float fthr = lb == kOrderedNegInf ? -INFINITY : ordered_to_float(lb) - 2.0f * margin;
+  const int* counts = p.scratch.counts(q);
+  const float* floors = p.scratch.floors(q);
+  const uint2* ents = reinterpret_cast<const uint2*>(p.scratch.entries(q));
+  float fmax = -INFINITY;
+#pragma unroll 4
+  for (int i = threadIdx.x; i < G * 32; i += NW * 32) {
+    const int b = i >> 5;
+    const int cnt = __ldcg(counts + b);
+    const uint2 e = __ldcg(ents + i);
+    if (lane == 0) fmax = fmaxf(fmax, __ldcg(floors + b));
+    const float es = __uint_as_float(e.x);
+    if (lane < cnt && es >= fthr) {
+      const int slot = atomicAdd(&sm.ncand, 1);
+      if (slot < NW * 32) {
+        sm.s[slot] = es;
+        sm.id[slot] = e.y;
+      }
+    }
+  }
+  if (lane == 0) sm.floor[warp] = fmax;
+  __syncthreads();
+  if (warp == 1) {
+    if (lane == 0) sm.qn = query_norm_seq_t<D>(sm.qraw);
+    __syncwarp();
+    asm volatile("bar.sync 1, 64;" ::: "memory");
+    return;
+  }
   if (warp != 0) return;
+  const int ncand = sm.ncand;
+  const int n = min(ncand, NW * 32);
+  WarpList list;
+  list.init();
+#pragma unroll 1
+  for (int c0 = 0; c0 < n; c0 += 32) {
+    const bool ok = c0 + lane < n;
+    list.offer(ok ? sm.s[c0 + lane] : -INFINITY, ok ? sm.id[c0 + lane] : kNoRow, lane);
+  }
   float floor_max = -INFINITY;
-  for (int w = 0; w < NW; ++w) floor_max = fmaxf(floor_max, sh_floor[w]);
+#pragma unroll 1
+  for (int w = 0; w < NW; ++w) floor_max = fmaxf(floor_max, sm.floor[w]);
   const float T_k = __shfl_sync(kFull, list.s, p.topk - 1);
-  const float thr = isfinite(T_k) ? T_k - 2.0f * kMargin : -INFINITY;
+  float thr = isfinite(T_k) ? T_k - 2.0f * margin : -INFINITY;
   const float last = __shfl_sync(kFull, list.s, 31);
-  const bool overflow = (isfinite(last) && last >= thr) || (isfinite(floor_max) && floor_max >= thr);
+  bool overflow = (isfinite(last) && last >= thr) || (isfinite(floor_max) && floor_max >= thr);
+  if (ncand > NW * 32) {  // more entries inside the margin than the list holds
+    overflow = true;
+    thr = fthr;
+  }
+  __syncwarp();
+  asm volatile("bar.sync 1, 64;" ::: "memory");  // sm.qn is ready
   Result* r = p.results + q;
   const bool failed = __ldcg(&hdr->err) != 0;
   if (failed) {
@@ -306,7 +372,6 @@ __device__ __forceinline__ void scan_finish(const Params<T>& p, WarpList& list, 
       hdr->lb = kOrderedNegInf;
       hdr->done = 0;
       hdr->err = 0;
-      hdr->next = 0;
     }
     return;
   }
@@ -317,7 +382,6 @@ __device__ __forceinline__ void scan_finish(const Params<T>& p, WarpList& list, 
       r->count = 0;
       hdr->lb = kOrderedNegInf;
       hdr->done = 0;
-      hdr->next = 0;
     }
     return;
   }
@@ -325,12 +389,9 @@ __device__ __forceinline__ void scan_finish(const Params<T>& p, WarpList& list, 
   const bool cand = isfinite(list.s) && list.s >= thr;
   float es = -INFINITY;
   if (cand) {
-    const double qnorm = query_norm_seq(query, D);
     const int64_t row = list.id;
-    if constexpr (INL)
-      es = exact_score_inline_norm<T>(p.rows + row * D, D, query, qnorm);
-    else
-      es = exact_score<T>(p.rows + row * D, D, query, qnorm, __ldg(p.norms + row));
+    es = exact_score_tail<D, T, INL>(p.rows + row * D, sm.qraw, sm.qn,
+                                     INL ? 0.0f : __ldg(p.norms + row));
   }
   WarpList ex;
   ex.init();
@@ -339,8 +400,75 @@ __device__ __forceinline__ void scan_finish(const Params<T>& p, WarpList& list, 
   if (lane == 0) {
     hdr->lb = kOrderedNegInf;
     hdr->done = 0;
-    hdr->next = 0;
   }
+}
+
+// Everything after the streaming loop.  The block list is seeded with the
+// warp list whose k-th score is the largest (a copy: lists are sorted) and
+// the other warps' entries are merged with offer_margin, so the block's k-th
+// approximate score is exact while entries that cannot reach a candidate are
+// skipped.  The block publishes the entries within 2*kMargin of the best
+// block k-th score so far (hdr->lb) and a floor: the largest score a row
+// dropped for lack of room can have.  The last block to finish runs
+// final_merge.
+template <int D, typename T, bool INL, int NW>
+__device__ __forceinline__ void scan_finish(const Params<T>& p, WarpList& list, bool safe, int q,
+                                            int lane, int warp, FinishSmem<NW, D>& sm) {
+  sm.s[warp * 32 + lane] = list.s;
+  sm.id[warp * 32 + lane] = list.id;
+  const float kth_w = __shfl_sync(kFull, list.s, p.topk - 1);
+  const float last_w = __shfl_sync(kFull, list.s, 31);
+  if (lane == 0) {
+    sm.kth[warp] = kth_w;
+    sm.floor[warp] = last_w;
+  }
+  __syncthreads();
+  Header* hdr = p.scratch.hdr(q);
+  if (warp == 0) {
+    float kbest = -INFINITY, floor = -INFINITY;
+    int wbest = 0;
+#pragma unroll 1
+    for (int w = 0; w < NW; ++w) {
+      const float kw = sm.kth[w];
+      if (kw > kbest) {
+        kbest = kw;
+        wbest = w;
+      }
+      floor = fmaxf(floor, sm.floor[w]);
+    }
+    WarpList m;
+    m.s = sm.s[wbest * 32 + lane];
+    m.id = sm.id[wbest * 32 + lane];
+#pragma unroll 1
+    for (int w = 0; w < NW; ++w)
+      if (w != wbest)
+        m.offer_margin(sm.s[w * 32 + lane], sm.id[w * 32 + lane], lane, p.topk, 2.0f * kMargin);
+    const float kth = __shfl_sync(kFull, m.s, p.topk - 1);
+    int lb_now = 0;
+    if (lane == 0) {
+      const int enc = isfinite(kth) ? float_to_ordered(kth) : kOrderedNegInf;
+      const int old = atomicMax(&hdr->lb, enc);
+      lb_now = old > enc ? old : enc;
+    }
+    lb_now = __shfl_sync(kFull, lb_now, 0);
+    const float wthr =
+        lb_now == kOrderedNegInf ? -INFINITY : ordered_to_float(lb_now) - 2.0f * kMargin;
+    floor = fmaxf(floor, __shfl_sync(kFull, m.s, 31));
+    const int cnt = __popc(__ballot_sync(kFull, isfinite(m.s) && m.s >= wthr));
+    Entry* ent = p.scratch.entries(q) + (int64_t)blockIdx.x * 32;
+    if (lane < cnt) ent[lane] = Entry{m.s, m.id};
+    if (lane == 0) {
+      p.scratch.counts(q)[blockIdx.x] = cnt;
+      p.scratch.floors(q)[blockIdx.x] = isfinite(floor) ? floor : -INFINITY;
+      __threadfence();
+      const unsigned ticket = atomicAdd(&hdr->done, 1u);
+      sm.last = (ticket == gridDim.x - 1);
+    }
+  }
+  __syncthreads();
+  if (!sm.last) return;
+  __threadfence();
+  final_merge<D, T, INL, NW>(p, q, (int)gridDim.x, kMargin, safe, lane, warp, sm);
 }
 
 // Approximate streaming pass (one launch per batch of queries: grid.y = query).
@@ -356,14 +484,11 @@ __global__ void __launch_bounds__(kThreads) mla_scan_kernel(const __grid_constan
   constexpr int CPL = CPR >= 32 ? CPR / 32 : 1;
   constexpr int SLOTS = L;
 
-  __shared__ float sh_s[kWarps * 32];
-  __shared__ uint32_t sh_id[kWarps * 32];
+  __shared__ FinishSmem<kWarps, D> fsm;
   __shared__ float sh_q[D];
   __shared__ float sh_eq;
   __shared__ int sh_safe;
-  __shared__ int sh_last;
   __shared__ int sh_next;
-  __shared__ float sh_floor[kWarps];
 
   const int q = blockIdx.y;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -382,7 +507,11 @@ __global__ void __launch_bounds__(kThreads) mla_scan_kernel(const __grid_constan
     const double qn = sqrt(acc);
     const bool safe = isfinite(qn) && qn > kSafeLo && qn < kSafeHi;
     const float inv = safe ? (float)(1.0 / qn) : 0.0f;
-    for (int d = lane; d < D; d += 32) sh_q[d] = query[d] * inv;
+    for (int d = lane; d < D; d += 32) {
+      const float v = query[d];
+      fsm.qraw[d] = v;
+      sh_q[d] = v * inv;
+    }
     if (lane == 0) {
       sh_safe = safe;
       sh_eq = safe ? (float)(1.0e-8 / qn) : 0.0f;
@@ -470,7 +599,7 @@ __global__ void __launch_bounds__(kThreads) mla_scan_kernel(const __grid_constan
         const float nrm = INL ? sqrtf(n2) : nrm_pre;
         if (isfinite(nrm)) s = dot * __frcp_rn(nrm + e_q);
       }
-      list.offer(s, (uint32_t)my_row, lane);
+      list.offer_margin(s, (uint32_t)my_row, lane, p.topk, 2.0f * kMargin);
       int nxt = 0;
       if (lane == 0) nxt = atomicAdd(&sh_next, 1);
       g = g_begin + __shfl_sync(kFull, nxt, 0);
@@ -479,8 +608,7 @@ __global__ void __launch_bounds__(kThreads) mla_scan_kernel(const __grid_constan
   // The resolve kernel may be scheduled as blocks leave the streaming loop;
   // it waits for this whole grid before reading anything (griddepcontrol.wait).
   asm volatile("griddepcontrol.launch_dependents;");
-  scan_finish<D, T, INL, kWarps>(p, list, safe, query, q, lane, warp, sh_s, sh_id, sh_floor,
-                                 &sh_last);
+  scan_finish<D, T, INL, kWarps>(p, list, safe, q, lane, warp, fsm);
 }
 
 // Packed fp32x2 FMA (sm_100 FFMA2): d = a * b + c on both lanes of a float2.
@@ -527,14 +655,10 @@ __global__ void __launch_bounds__(kBulkWarps * 32, 1)
 
   extern __shared__ __align__(128) unsigned char dsmem[];
   __shared__ __align__(8) uint64_t sh_bar[NW][2];
-  __shared__ float sh_s[NW * 32];
-  __shared__ uint32_t sh_id[NW * 32];
+  __shared__ FinishSmem<NW, D> fsm;
   __shared__ float sh_q[D];
   __shared__ float sh_eq;
   __shared__ int sh_safe;
-  __shared__ int sh_last;
-  __shared__ int sh_next;
-  __shared__ float sh_floor[NW];
 
   const int q = blockIdx.y;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -551,11 +675,14 @@ __global__ void __launch_bounds__(kBulkWarps * 32, 1)
     const double qn = sqrt(acc);
     const bool safe = isfinite(qn) && qn > kSafeLo && qn < kSafeHi;
     const float inv = safe ? (float)(1.0 / qn) : 0.0f;
-    for (int d = lane; d < D; d += 32) sh_q[d] = query[d] * inv;
+    for (int d = lane; d < D; d += 32) {
+      const float v = query[d];
+      fsm.qraw[d] = v;
+      sh_q[d] = v * inv;
+    }
     if (lane == 0) {
       sh_safe = safe;
       sh_eq = safe ? (float)(1.0e-8 / qn) : 0.0f;
-      sh_next = NW;
     }
   }
   if (lane == 0) {
@@ -573,18 +700,11 @@ __global__ void __launch_bounds__(kBulkWarps * 32, 1)
 
   unsigned char* const buf0 = dsmem + (warp * 2) * kHalfBytes;
   const int64_t groups = ceil_div64(p.nodes, 32);
-  // Groups come from one work queue per query (hdr->next), so every SM keeps
-  // streaming until the bank is exhausted; each warp asks one group ahead so
-  // the atomic's latency hides behind a group's arithmetic.
-  unsigned* const queue = &p.scratch.hdr(q)->next;
-  // Lane 0 holds the ticket of the group after next in a register; it is
-  // broadcast one iteration later, so the atomic's round trip overlaps a
-  // group's arithmetic instead of stalling the warp.
-  unsigned ticket = 0u;
-  auto request = [&]() {
-    if (lane == 0) ticket = atomicAdd(queue, 1u);
-  };
-  auto take = [&]() -> int64_t { return (int64_t)__shfl_sync(kFull, ticket, 0); };
+  // Static interleaved assignment: warp w of block b takes groups
+  // b*NW + w, then every gridDim.x*NW-th group after it, so the warps of the
+  // whole grid sweep the bank front to back together.
+  const int64_t gstride = (int64_t)gridDim.x * NW;
+  const uint64_t l2_stream = l2_evict_first_policy();
   // half h of group g -> buffer h (lane 0 only)
   auto issue = [&](int64_t g, int h) {
     const int64_t r0 = g * 32 + 16 * h;
@@ -595,7 +715,7 @@ __global__ void __launch_bounds__(kBulkWarps * 32, 1)
       return;
     }
     mbar_arrive_expect_tx(&sh_bar[warp][h], bytes);
-    bulk_g2s(buf0 + h * kHalfBytes, p.rows + r0 * D, bytes, &sh_bar[warp][h]);
+    bulk_g2s_hint(buf0 + h * kHalfBytes, p.rows + r0 * D, bytes, &sh_bar[warp][h], l2_stream);
   };
 
   WarpList list;
@@ -604,11 +724,8 @@ __global__ void __launch_bounds__(kBulkWarps * 32, 1)
   unsigned phase_bits = 0u;    // bit h: parity of the next phase to wait for on buffer h
   unsigned pending_bits = 0u;  // bit h: a copy into buffer h is in flight
   if (safe) {
-    request();
-    int64_t g = take();
-    request();
-    int64_t gn = take();
-    request();                                   // the group after gn, taken next iteration
+    int64_t g = (int64_t)blockIdx.x * NW + warp;
+    int64_t gn = g + gstride;
     if (g < groups) {
       if (lane == 0) {
         issue(g, 0);
@@ -617,8 +734,6 @@ __global__ void __launch_bounds__(kBulkWarps * 32, 1)
       pending_bits = 3u;
     }
     while (g < groups) {
-      const int64_t gnn = take();                // requested one iteration ago
-      request();
       const int64_t row0 = g * 32;
       const int64_t my_row = row0 + (lane % L) * R + lane / L;
       const float nrm_pre = my_row < p.nodes ? __ldg(p.norms + my_row) : 0.0f;
@@ -664,9 +779,9 @@ __global__ void __launch_bounds__(kBulkWarps * 32, 1)
       const float dot = reduce_scatter<SLOTS>(part, lane);
       float s = -INFINITY;
       if (my_row < p.nodes && isfinite(nrm_pre)) s = dot * __frcp_rn(nrm_pre + e_q);
-      list.offer(s, (uint32_t)my_row, lane);
+      list.offer_margin(s, (uint32_t)my_row, lane, p.topk, 2.0f * kMargin);
       g = gn;
-      gn = gnn;
+      gn += gstride;
     }
     if (failed) {
       // drain this warp's copies still in flight before the block can exit
@@ -677,8 +792,7 @@ __global__ void __launch_bounds__(kBulkWarps * 32, 1)
     }
   }
   asm volatile("griddepcontrol.launch_dependents;");
-  scan_finish<D, T, false, NW>(p, list, safe, query, q, lane, warp, sh_s, sh_id, sh_floor,
-                               &sh_last);
+  scan_finish<D, T, false, NW>(p, list, safe, q, lane, warp, fsm);
 }
 
 // Exact fallback: for each query whose approximate pass reported kOverflow,
@@ -709,6 +823,7 @@ __global__ void __launch_bounds__(kThreads) mla_exact_kernel(const __grid_consta
   if (threadIdx.x == 0) {
     const int st = p.force_all ? (int)kUnsafe : __ldcg(&r->status);
     sh_mode = st;
+    if (st != kOk && blockIdx.x == 0 && p.fallback_count) atomicAdd(p.fallback_count, 1ull);
     if (st != kOk) {
       const double qn = query_norm_seq(query, dim);
       sh_qnorm = qn;
@@ -839,7 +954,6 @@ __global__ void __launch_bounds__(kThreads) mla_exact_kernel(const __grid_consta
   if (lane == 0) {
     hdr->lb = kOrderedNegInf;
     hdr->done = 0;
-    hdr->next = 0;
   }
 }
 
@@ -875,7 +989,6 @@ __global__ void scratch_init_kernel(unsigned char* base, size_t stride, int quer
     h->lb = kOrderedNegInf;
     h->done = 0;
     h->err = 0;
-    h->next = 0;
   }
 }
 
@@ -907,7 +1020,8 @@ struct grm_b200_mla_bank {
   cudaEvent_t ev0 = nullptr, ev1 = nullptr;
   std::mutex mu;
   ErrorSlot err;
-  uint64_t routes = 0, fallbacks = 0;
+  uint64_t routes = 0;
+  unsigned long long* d_fallbacks = nullptr;  // counted by the exact kernel
 };
 
 namespace {
@@ -1032,6 +1146,7 @@ Params<T> make_params(grm_b200_mla_bank* b, const float* dq, int topk) {
   p.out_scores = nullptr;
   p.id_offset = 0;
   p.force_all = b->exact_only ? 1 : 0;
+  p.fallback_count = b->d_fallbacks;
   return p;
 }
 
@@ -1098,7 +1213,6 @@ int run_chunk(grm_b200_mla_bank* b, const float* dq, const float* q_host, int nq
     }
   }
   if (need_exact) {
-    b->fallbacks += 1;
     rc = launch_exact<T>(b, p, nq, b->stream);
     if (rc) return b->err.set(rc, "MLA exact pass launch failed");
     cudaError_t e = cudaStreamSynchronize(b->stream);
@@ -1150,6 +1264,9 @@ int bank_finish_create(grm_b200_mla_bank* b) {
   if (e == cudaSuccess) e = cudaEventCreate(&b->ev0);
   if (e == cudaSuccess) e = cudaEventCreate(&b->ev1);
   if (e == cudaSuccess) e = cudaMalloc(&b->d_norms, sizeof(float) * (size_t)b->nodes);
+  if (e == cudaSuccess) e = cudaMalloc(&b->d_fallbacks, sizeof(unsigned long long));
+  if (e == cudaSuccess)
+    e = cudaMemsetAsync(b->d_fallbacks, 0, sizeof(unsigned long long), b->stream);
   if (e != cudaSuccess) return cuda_status(e);
   unsigned* d_special = nullptr;
   e = cudaMalloc(&d_special, sizeof(unsigned));
@@ -1184,6 +1301,7 @@ void bank_free(grm_b200_mla_bank* b) {
   if (b->stream) cudaStreamSynchronize(b->stream);
   if (b->d_rows) cudaFree(b->d_rows);
   if (b->d_norms) cudaFree(b->d_norms);
+  if (b->d_fallbacks) cudaFree(b->d_fallbacks);
   if (b->d_scratch) cudaFree(b->d_scratch);
   if (b->d_results) cudaFree(b->d_results);
   if (b->h_results) cudaFreeHost(b->h_results);
@@ -1374,8 +1492,15 @@ const float* grm_b200_mla_row_norms_device(grm_b200_mla_bank* bank) {
 
 int grm_b200_mla_stats(grm_b200_mla_bank* bank, uint64_t* routes, uint64_t* fallbacks) {
   if (!bank) return GRM_B200_EINVAL;
+  std::lock_guard<std::mutex> lock(bank->mu);
   if (routes) *routes = bank->routes;
-  if (fallbacks) *fallbacks = bank->fallbacks;
+  if (fallbacks) {
+    unsigned long long n = 0;
+    cudaError_t e = cudaSetDevice(bank->device);
+    if (e == cudaSuccess) e = cudaMemcpy(&n, bank->d_fallbacks, sizeof(n), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return bank->err.set(cuda_status(e), "MLA stats read failed");
+    *fallbacks = n;
+  }
   return 0;
 }
 
@@ -1535,6 +1660,7 @@ extern "C" int grm_b200_mla_route_noalloc(const void* rows_device, int64_t nodes
   p.out_scores = out_scores_device;
   p.id_offset = 0;
   p.force_all = 0;
+  p.fallback_count = nullptr;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   scratch_init_kernel<<<(query_count + 127) / 128, 128, 0, s>>>(base + results_bytes, stride,
                                                                  query_count);

@@ -125,9 +125,11 @@ const char* grm_b200_mla_last_error(grm_b200_mla_bank* bank);
  * that keep their own bank copy. */
 const float* grm_b200_mla_row_norms_device(grm_b200_mla_bank* bank);
 
-/* Counters of the exactness machinery since bank creation: routes that needed
- * the exact fallback pass (margin saturated by near-ties, or a query outside
- * the fast path's safe range). */
+/* Counters of the exactness machinery since bank creation: queries routed,
+ * and queries that took the exact fallback pass (margin saturated by
+ * near-ties, a query outside the fast path's safe range, or a bank outside it),
+ * counted on the device and read here with a blocking copy, so queries still
+ * in flight on other streams may not be counted yet. */
 int grm_b200_mla_stats(grm_b200_mla_bank* bank, uint64_t* routes, uint64_t* fallbacks);
 
 /* Allocation-free MLA route.  No counterpart in the reference.  For callers
