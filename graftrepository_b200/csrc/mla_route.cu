@@ -53,7 +53,10 @@ struct Header {
   int lb;          // ordered float: best block k-th approximate score so far
   unsigned done;   // blocks finished in this launch
   int err;         // a bounded device wait gave up in this launch
-  int pad[13];
+  unsigned nent;   // entries appended to the published list in this launch
+  int floor;       // ordered float: largest score a block dropped for lack of room
+  unsigned next;   // next group of the bulk scan's dynamic tail
+  int pad[10];
 };
 
 struct Entry {
@@ -72,10 +75,16 @@ struct Scratch {
   __device__ int* counts(int q) const {
     return reinterpret_cast<int*>(base + stride * q + sizeof(Header) + sizeof(Entry) * 32 * blocks);
   }
-  __device__ float* floors(int q) const {
-    return reinterpret_cast<float*>(counts(q) + blocks);
-  }
 };
+
+// Back to the state a launch starts from (err is cleared by whoever reports it).
+__device__ __forceinline__ void reset_header(Header* h) {
+  h->lb = kOrderedNegInf;
+  h->done = 0;
+  h->nent = 0;
+  h->floor = kOrderedNegInf;
+  h->next = 0;
+}
 
 inline size_t scratch_stride(int blocks) {
   size_t b = sizeof(Header) + sizeof(Entry) * 32 * (size_t)blocks + 8 * (size_t)blocks;
@@ -294,83 +303,135 @@ __device__ float exact_score_tail(const T* row, const float* q, double qnorm, fl
   return (float)(dot / (qnorm * (double)norm + 1.0e-8));
 }
 
-// Final merge of the G published block lists of query q (one block, NW
-// warps): pick every row whose approximate score is within 2*margin of the
-// approximate k-th best and recompute it with the reference arithmetic, or
-// flag the exact fallback when the lists were saturated inside the margin.
+// Largest entry (score desc, id asc) among the R values each lane holds, over
+// the warp; returns it in every lane.
+template <int R>
+__device__ __forceinline__ void warp_best(const float (&v)[R], const uint32_t (&id)[R], float& bs,
+                                          uint32_t& bid) {
+  bs = v[0];
+  bid = id[0];
+#pragma unroll
+  for (int r = 1; r < R; ++r)
+    if (better(v[r], id[r], bs, bid)) {
+      bs = v[r];
+      bid = id[r];
+    }
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) {
+    const float os = __shfl_xor_sync(kFull, bs, o);
+    const uint32_t oid = __shfl_xor_sync(kFull, bid, o);
+    if (better(os, oid, bs, bid)) {
+      bs = os;
+      bid = oid;
+    }
+  }
+}
+
+constexpr int kSelR = 4;  // candidates per lane in the final selection (128 per warp)
+
+// Final merge of query q (one block, NW warps), after every block published.
 // hdr->lb is by now the best block k-th score, a lower bound of the
-// approximate k-th best, so entries below lb - 2*margin are skipped: no
-// candidate is among them.  All threads filter the entry slots into a
-// shared candidate list (independent loads), warp 0 merges it while warp 1
-// computes the reference query norm.
+// approximate k-th best T_k, so entries below lb - 2*margin are skipped: no
+// candidate is among them.  Warps 0..NW-2 filter the appended entries into a
+// shared list (one load each; candidate rows are prefetched) while warp
+// NW-1 computes the reference query norm.  Warp 0 then takes the best 128
+// (all of them, or the first 128 after a rank sort when more passed), finds
+// T_k by k rounds of warp arg-max, and recomputes every entry >= T_k -
+// 2*margin with the reference arithmetic.  When 32 or more entries, or a
+// block's dropped rows (hdr->floor), reach that threshold, the exact
+// fallback kernel is flagged instead.
 template <int D, typename T, bool INL, int NW>
-__device__ __forceinline__ void final_merge(const Params<T>& p, int q, int G, float margin,
-                                            bool safe, int lane, int warp,
-                                            FinishSmem<NW, D>& sm) {
+__device__ __forceinline__ void final_merge(const Params<T>& p, int q, float margin, bool safe,
+                                            int lane, int warp, FinishSmem<NW, D>& sm) {
   static_assert(NW >= 2, "final_merge needs two warps");
   Header* hdr = p.scratch.hdr(q);
   if (threadIdx.x == 0) sm.ncand = 0;
   __syncthreads();
   const int lb = __ldcg(&hdr->lb);
   const float fthr = lb == kOrderedNegInf ? -INFINITY : ordered_to_float(lb) - 2.0f * margin;
-  const int* counts = p.scratch.counts(q);
-  const float* floors = p.scratch.floors(q);
+  const int nent = min((int)__ldcg(&hdr->nent), p.scratch.blocks * 32);
   const uint2* ents = reinterpret_cast<const uint2*>(p.scratch.entries(q));
-  float fmax = -INFINITY;
-#pragma unroll 4
-  for (int i = threadIdx.x; i < G * 32; i += NW * 32) {
-    const int b = i >> 5;
-    const int cnt = __ldcg(counts + b);
-    const uint2 e = __ldcg(ents + i);
-    if (lane == 0) fmax = fmaxf(fmax, __ldcg(floors + b));
-    const float es = __uint_as_float(e.x);
-    if (lane < cnt && es >= fthr) {
-      const int slot = atomicAdd(&sm.ncand, 1);
-      if (slot < NW * 32) {
-        sm.s[slot] = es;
-        sm.id[slot] = e.y;
+  if (warp == NW - 1) {
+    if (lane == 0) sm.qn = query_norm_seq_t<D>(sm.qraw);
+  } else {
+#pragma unroll 2
+    for (int i = threadIdx.x; i < nent; i += (NW - 1) * 32) {
+      const uint2 e = __ldcg(ents + i);
+      const float es = __uint_as_float(e.x);
+      if (es >= fthr) {
+        const int slot = atomicAdd(&sm.ncand, 1);
+        if (slot < NW * 32) {
+          sm.s[slot] = es;
+          sm.id[slot] = e.y;
+        }
+        const char* rb = reinterpret_cast<const char*>(p.rows + (int64_t)e.y * D);
+#pragma unroll 1
+        for (int o = 0; o < D * (int)sizeof(T); o += 128)
+          asm volatile("prefetch.global.L1 [%0];" ::"l"(rb + o));
       }
     }
   }
-  if (lane == 0) sm.floor[warp] = fmax;
   __syncthreads();
-  if (warp == 1) {
-    if (lane == 0) sm.qn = query_norm_seq_t<D>(sm.qraw);
-    __syncwarp();
-    asm volatile("bar.sync 1, 64;" ::: "memory");
-    return;
-  }
-  if (warp != 0) return;
   const int ncand = sm.ncand;
   const int n = min(ncand, NW * 32);
-  WarpList list;
-  list.init();
+  if (n > 32 * kSelR) {  // rare: rank sort so the best 32*kSelR come first
+    float cs = -INFINITY;
+    uint32_t ci = kNoRow;
+    int rank = 0;
+    if ((int)threadIdx.x < n) {
+      cs = sm.s[threadIdx.x];
+      ci = sm.id[threadIdx.x];
 #pragma unroll 1
-  for (int c0 = 0; c0 < n; c0 += 32) {
-    const bool ok = c0 + lane < n;
-    list.offer(ok ? sm.s[c0 + lane] : -INFINITY, ok ? sm.id[c0 + lane] : kNoRow, lane);
+      for (int j = 0; j < n; ++j) rank += better(sm.s[j], sm.id[j], cs, ci) ? 1 : 0;
+    }
+    __syncthreads();
+    if ((int)threadIdx.x < n) {
+      sm.s[rank] = cs;  // the ranks are a permutation of [0, n)
+      sm.id[rank] = ci;
+    }
+    __syncthreads();
   }
-  float floor_max = -INFINITY;
+  if (warp != 0) return;
+  const int m = min(n, 32 * kSelR);
+  float v[kSelR], w[kSelR];
+  uint32_t vid[kSelR];
+#pragma unroll
+  for (int r = 0; r < kSelR; ++r) {
+    const int i = r * 32 + lane;
+    v[r] = i < m ? sm.s[i] : -INFINITY;
+    vid[r] = i < m ? sm.id[i] : kNoRow;
+    w[r] = v[r];
+  }
+  // T_k: remove the best entry k-1 times, then take the best.
+  float T_k = -INFINITY;
 #pragma unroll 1
-  for (int w = 0; w < NW; ++w) floor_max = fmaxf(floor_max, sm.floor[w]);
-  const float T_k = __shfl_sync(kFull, list.s, p.topk - 1);
+  for (int t = 0; t < p.topk; ++t) {
+    float bs;
+    uint32_t bid;
+    warp_best<kSelR>(w, vid, bs, bid);
+    T_k = bs;
+#pragma unroll
+    for (int r = 0; r < kSelR; ++r)
+      if (vid[r] == bid && w[r] == bs) w[r] = -INFINITY;
+  }
   float thr = isfinite(T_k) ? T_k - 2.0f * margin : -INFINITY;
-  const float last = __shfl_sync(kFull, list.s, 31);
-  bool overflow = (isfinite(last) && last >= thr) || (isfinite(floor_max) && floor_max >= thr);
-  if (ncand > NW * 32) {  // more entries inside the margin than the list holds
+  int above = 0;
+#pragma unroll
+  for (int r = 0; r < kSelR; ++r) above += __popc(__ballot_sync(kFull, isfinite(v[r]) && v[r] >= thr));
+  const int fl = __ldcg(&hdr->floor);
+  const float floor_max = fl == kOrderedNegInf ? -INFINITY : ordered_to_float(fl);
+  bool overflow = above >= 32 || (isfinite(floor_max) && floor_max >= thr);
+  if (ncand > NW * 32) {  // more entries inside the margin than the shared list holds
     overflow = true;
     thr = fthr;
   }
-  __syncwarp();
-  asm volatile("bar.sync 1, 64;" ::: "memory");  // sm.qn is ready
   Result* r = p.results + q;
   const bool failed = __ldcg(&hdr->err) != 0;
   if (failed) {
     if (lane == 0) {
       r->status = kError;
       r->count = 0;
-      hdr->lb = kOrderedNegInf;
-      hdr->done = 0;
+      reset_header(hdr);
       hdr->err = 0;
     }
     return;
@@ -380,37 +441,48 @@ __device__ __forceinline__ void final_merge(const Params<T>& p, int q, int G, fl
       r->status = safe ? kOverflow : kUnsafe;
       r->thr = thr;
       r->count = 0;
-      hdr->lb = kOrderedNegInf;
-      hdr->done = 0;
+      reset_header(hdr);
     }
     return;
   }
-  // Exact refine of the candidates (sorted approximate list, prefix >= thr).
-  const bool cand = isfinite(list.s) && list.s >= thr;
+  // Candidates (fewer than 32): compacted through shared memory, one per
+  // lane, and recomputed exactly.
+  __syncwarp();
+  int base = 0;
+#pragma unroll
+  for (int r = 0; r < kSelR; ++r) {
+    const bool c = isfinite(v[r]) && v[r] >= thr;
+    const unsigned bal = __ballot_sync(kFull, c);
+    if (c) {
+      const int pos = base + __popc(bal & ((1u << lane) - 1u));
+      sm.s[pos] = v[r];
+      sm.id[pos] = vid[r];
+    }
+    base += __popc(bal);
+  }
+  __syncwarp();
+  const float cs = lane < base ? sm.s[lane] : -INFINITY;
+  const uint32_t ci = lane < base ? sm.id[lane] : kNoRow;
   float es = -INFINITY;
-  if (cand) {
-    const int64_t row = list.id;
-    es = exact_score_tail<D, T, INL>(p.rows + row * D, sm.qraw, sm.qn,
-                                     INL ? 0.0f : __ldg(p.norms + row));
+  if (isfinite(cs)) {
+    es = exact_score_tail<D, T, INL>(p.rows + (int64_t)ci * D, sm.qraw, sm.qn,
+                                     INL ? 0.0f : __ldg(p.norms + ci));
   }
   WarpList ex;
   ex.init();
-  ex.offer(es, list.id, lane);
+  ex.offer(es, ci, lane);
   write_result(p, q, ex, lane);
-  if (lane == 0) {
-    hdr->lb = kOrderedNegInf;
-    hdr->done = 0;
-  }
+  if (lane == 0) reset_header(hdr);
 }
 
 // Everything after the streaming loop.  The block list is seeded with the
 // warp list whose k-th score is the largest (a copy: lists are sorted) and
 // the other warps' entries are merged with offer_margin, so the block's k-th
 // approximate score is exact while entries that cannot reach a candidate are
-// skipped.  The block publishes the entries within 2*kMargin of the best
-// block k-th score so far (hdr->lb) and a floor: the largest score a row
-// dropped for lack of room can have.  The last block to finish runs
-// final_merge.
+// skipped.  The block appends the entries within 2*kMargin of the best
+// block k-th score so far (hdr->lb) to the query's published list and raises
+// hdr->floor to the largest score a row it dropped for lack of room can
+// have.  The last block to finish runs final_merge.
 template <int D, typename T, bool INL, int NW>
 __device__ __forceinline__ void scan_finish(const Params<T>& p, WarpList& list, bool safe, int q,
                                             int lane, int warp, FinishSmem<NW, D>& sm) {
@@ -455,11 +527,15 @@ __device__ __forceinline__ void scan_finish(const Params<T>& p, WarpList& list, 
         lb_now == kOrderedNegInf ? -INFINITY : ordered_to_float(lb_now) - 2.0f * kMargin;
     floor = fmaxf(floor, __shfl_sync(kFull, m.s, 31));
     const int cnt = __popc(__ballot_sync(kFull, isfinite(m.s) && m.s >= wthr));
-    Entry* ent = p.scratch.entries(q) + (int64_t)blockIdx.x * 32;
-    if (lane < cnt) ent[lane] = Entry{m.s, m.id};
+    unsigned at = 0;
     if (lane == 0) {
-      p.scratch.counts(q)[blockIdx.x] = cnt;
-      p.scratch.floors(q)[blockIdx.x] = isfinite(floor) ? floor : -INFINITY;
+      if (cnt) at = atomicAdd(&hdr->nent, (unsigned)cnt);
+      if (isfinite(floor)) atomicMax(&hdr->floor, float_to_ordered(floor));
+    }
+    at = __shfl_sync(kFull, at, 0);
+    if (lane < cnt) p.scratch.entries(q)[at + lane] = Entry{m.s, m.id};
+    __syncwarp();
+    if (lane == 0) {
       __threadfence();
       const unsigned ticket = atomicAdd(&hdr->done, 1u);
       sm.last = (ticket == gridDim.x - 1);
@@ -468,7 +544,7 @@ __device__ __forceinline__ void scan_finish(const Params<T>& p, WarpList& list, 
   __syncthreads();
   if (!sm.last) return;
   __threadfence();
-  final_merge<D, T, INL, NW>(p, q, (int)gridDim.x, kMargin, safe, lane, warp, sm);
+  final_merge<D, T, INL, NW>(p, q, kMargin, safe, lane, warp, sm);
 }
 
 // Approximate streaming pass (one launch per batch of queries: grid.y = query).
@@ -702,8 +778,13 @@ __global__ void __launch_bounds__(kBulkWarps * 32, 1)
   const int64_t groups = ceil_div64(p.nodes, 32);
   // Static interleaved assignment: warp w of block b takes groups
   // b*NW + w, then every gridDim.x*NW-th group after it, so the warps of the
-  // whole grid sweep the bank front to back together.
+  // whole grid sweep the bank front to back together.  The last two rounds
+  // (dyn0 onwards) are handed out one group at a time through hdr->next, so
+  // SMs that stream faster take more of the tail; each ticket is requested a
+  // full group ahead of its use.
   const int64_t gstride = (int64_t)gridDim.x * NW;
+  const int64_t dyn0 = groups >= 4 * gstride ? (groups / gstride - 2) * gstride : groups;
+  unsigned* const next = &p.scratch.hdr(q)->next;
   const uint64_t l2_stream = l2_evict_first_policy();
   // half h of group g -> buffer h (lane 0 only)
   auto issue = [&](int64_t g, int h) {
@@ -734,6 +815,11 @@ __global__ void __launch_bounds__(kBulkWarps * 32, 1)
       pending_bits = 3u;
     }
     while (g < groups) {
+      // the group after gn: static, or a ticket whose atomic completes while
+      // this group is processed
+      const bool ticket = gn < groups && (gn >= dyn0 || gn + gstride >= dyn0);
+      unsigned tk = 0;
+      if (ticket && lane == 0) tk = atomicAdd(next, 1u);
       const int64_t row0 = g * 32;
       const int64_t my_row = row0 + (lane % L) * R + lane / L;
       const float nrm_pre = my_row < p.nodes ? __ldg(p.norms + my_row) : 0.0f;
@@ -781,7 +867,7 @@ __global__ void __launch_bounds__(kBulkWarps * 32, 1)
       if (my_row < p.nodes && isfinite(nrm_pre)) s = dot * __frcp_rn(nrm_pre + e_q);
       list.offer_margin(s, (uint32_t)my_row, lane, p.topk, 2.0f * kMargin);
       g = gn;
-      gn += gstride;
+      gn = ticket ? dyn0 + (int64_t)__shfl_sync(kFull, tk, 0) : gn + gstride;
     }
     if (failed) {
       // drain this warp's copies still in flight before the block can exit
@@ -951,10 +1037,7 @@ __global__ void __launch_bounds__(kThreads) mla_exact_kernel(const __grid_consta
   block_merge(list, lane, warp, sh_s, sh_id);
   if (warp != 0) return;
   write_result(p, q, list, lane);
-  if (lane == 0) {
-    hdr->lb = kOrderedNegInf;
-    hdr->done = 0;
-  }
+  if (lane == 0) reset_header(hdr);
 }
 
 template <typename T>
@@ -986,8 +1069,7 @@ __global__ void scratch_init_kernel(unsigned char* base, size_t stride, int quer
   const int q = blockIdx.x * blockDim.x + threadIdx.x;
   if (q < queries) {
     Header* h = reinterpret_cast<Header*>(base + stride * q);
-    h->lb = kOrderedNegInf;
-    h->done = 0;
+    reset_header(h);
     h->err = 0;
   }
 }
@@ -1086,6 +1168,16 @@ int pick_grid(grm_b200_mla_bank* b) {
     const void* fn = b->dtype == GRM_B200_F16 ? (const void*)scan_bulk_fn<__half>(b->dim)
                                               : (const void*)scan_bulk_fn<float>(b->dim);
     e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kBulkSmem);
+    // The resolve kernel follows every scan: give both the same shared-memory
+    // carveout so the SMs need no reconfiguration between them.
+    const void* xfn = b->dtype == GRM_B200_F16 ? (const void*)exact_fn<__half>(b->dim)
+                                               : (const void*)exact_fn<float>(b->dim);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout,
+                               cudaSharedmemCarveoutMaxShared);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(xfn, cudaFuncAttributePreferredSharedMemoryCarveout,
+                               cudaSharedmemCarveoutMaxShared);
     if (e == cudaSuccess)
       e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, kBulkWarps * 32, kBulkSmem);
   } else if (b->dtype == GRM_B200_F16) {
