@@ -307,7 +307,14 @@ def run_ours(args):
             flush.zero_()
         step(i, None)
     torch.cuda.synchronize()
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(args.steps)]
+    # Without an L2 flush the K steps run back to back between one event pair
+    # (routes chain through programmatic dependent launch, as in serving); with
+    # a flush each step is bracketed by its own events so the flush is not
+    # timed.  A second pass with per-step events gives the step distribution.
+    n_dist = min(args.steps, 1000)
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(2)]
+           for _ in range(args.steps if flush is not None else n_dist)]
+    ev_all = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
     n_scan = min(args.steps, 1000)
     sevs = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(n_scan)]
     fb0 = bank.stats()[1]
@@ -316,15 +323,26 @@ def run_ours(args):
             dist.barrier()
         torch.cuda.synchronize()
         wall0 = time.perf_counter()
-        for i in range(args.steps):
-            if flush is not None:
+        if flush is None:
+            ev_all[0].record(stream)
+            for i in range(args.steps):
+                step(args.warmup + i, None)
+            ev_all[1].record(stream)
+        else:
+            for i in range(args.steps):
                 flush.zero_()
-            step(args.warmup + i, evs[i])
+                step(args.warmup + i, evs[i])
         torch.cuda.synchronize()
         wall = time.perf_counter() - wall0
         fallbacks = bank.stats()[1] - fb0
         if world > 1:
             dist.barrier()
+        if flush is None:
+            for i in range(n_dist):
+                step(args.warmup + i, evs[i])
+            torch.cuda.synchronize()
+            if world > 1:
+                dist.barrier()
         for i in range(n_scan):
             if flush is not None:
                 flush.zero_()
@@ -332,7 +350,8 @@ def run_ours(args):
         torch.cuda.synchronize()
     step_ms = [e[0].elapsed_time(e[1]) for e in evs]
     scan_ms = [e[0].elapsed_time(e[1]) for e in sevs]
-    tot = torch.tensor([sum(step_ms)], dtype=torch.float64, device="cuda")
+    timed_ms = ev_all[0].elapsed_time(ev_all[1]) if flush is None else sum(step_ms)
+    tot = torch.tensor([timed_ms], dtype=torch.float64, device="cuda")
     if world > 1:
         dist.all_reduce(tot, op=dist.ReduceOp.MAX)
     total_ms = float(tot.item())
@@ -407,6 +426,8 @@ def run_ours(args):
                 "d2h_bytes_per_step": d2h, "steps": e2e_steps,
                 "api": "CudaMLARouteBank.route_topk" if world == 1 else "ShardedMLARoute.route"},
         "gpu_launches": args.steps * (2 if world == 1 else 3),
+        "timing": ("one event pair around the K back-to-back steps" if flush is None else
+                   "per-step event pairs, L2 flush between steps outside them"),
         "roofline_launches": n_scan,
         "clocks": clocks,
         "wall_s_timed_region": wall,

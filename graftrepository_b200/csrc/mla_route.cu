@@ -270,26 +270,26 @@ __device__ __forceinline__ double query_norm_seq_t(const float* q) {
   return sqrt(acc);
 }
 
-// exact_score / exact_score_inline_norm for the final refine: the row's
-// cache lines are prefetched first, then read 64 bytes per step in a short
-// loop.  The final merge runs in a single block right after the bank stream
-// has flushed L2, so its code is fetched cold: it is kept small on purpose.
+// exact_score / exact_score_inline_norm for the final refine: the row is read
+// in rounds of up to 16 vectors (256 bytes) issued together, so a 512-byte
+// row costs two memory round trips.  The final merge runs in a single block
+// right after the bank stream, so its code is fetched cold: the loop over
+// rounds is kept rolled on purpose.
 template <int D, typename T, bool INL>
 __device__ float exact_score_tail(const T* row, const float* q, double qnorm, float norm) {
   constexpr int E = 16 / (int)sizeof(T);
-  constexpr int BYTES = D * (int)sizeof(T);
-  const char* rb = reinterpret_cast<const char*>(row);
-#pragma unroll 1
-  for (int o = 0; o < BYTES; o += 128) asm volatile("prefetch.global.L1 [%0];" ::"l"(rb + o));
+  constexpr int NV = D / E;
+  constexpr int CH = NV < 16 ? NV : 16;
+  static_assert(NV % CH == 0, "a row splits into whole rounds");
   const uint4* rv = reinterpret_cast<const uint4*>(row);
   double dot = 0.0, n2 = 0.0;
 #pragma unroll 1
-  for (int c0 = 0; c0 < BYTES / 16; c0 += 4) {
-    uint4 v[4];
+  for (int c0 = 0; c0 < NV; c0 += CH) {
+    uint4 v[CH];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) v[i] = ld_nc16(rv + c0 + i);
+    for (int i = 0; i < CH; ++i) v[i] = ld_nc16(rv + c0 + i);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < CH; ++i) {
       const T* e = reinterpret_cast<const T*>(&v[i]);
 #pragma unroll
       for (int k = 0; k < E; ++k) {
@@ -479,10 +479,10 @@ __device__ __forceinline__ void final_merge(const Params<T>& p, int q, float mar
 // warp list whose k-th score is the largest (a copy: lists are sorted) and
 // the other warps' entries are merged with offer_margin, so the block's k-th
 // approximate score is exact while entries that cannot reach a candidate are
-// skipped.  The block appends the entries within 2*kMargin of the best
-// block k-th score so far (hdr->lb) to the query's published list and raises
-// hdr->floor to the largest score a row it dropped for lack of room can
-// have.  The last block to finish runs final_merge.
+// skipped.  The block appends its entries within 2*kMargin of its k-th score
+// to the query's published list, raises hdr->lb to that k-th score and
+// hdr->floor to the largest score a row it dropped for lack of room can have.
+// The last block to finish runs final_merge.
 template <int D, typename T, bool INL, int NW>
 __device__ __forceinline__ void scan_finish(const Params<T>& p, WarpList& list, bool safe, int q,
                                             int lane, int warp, FinishSmem<NW, D>& sm) {
@@ -516,34 +516,32 @@ __device__ __forceinline__ void scan_finish(const Params<T>& p, WarpList& list, 
       if (w != wbest)
         m.offer_margin(sm.s[w * 32 + lane], sm.id[w * 32 + lane], lane, p.topk, 2.0f * kMargin);
     const float kth = __shfl_sync(kFull, m.s, p.topk - 1);
-    int lb_now = 0;
-    if (lane == 0) {
-      const int enc = isfinite(kth) ? float_to_ordered(kth) : kOrderedNegInf;
-      const int old = atomicMax(&hdr->lb, enc);
-      lb_now = old > enc ? old : enc;
-    }
-    lb_now = __shfl_sync(kFull, lb_now, 0);
-    const float wthr =
-        lb_now == kOrderedNegInf ? -INFINITY : ordered_to_float(lb_now) - 2.0f * kMargin;
+    const float wthr = isfinite(kth) ? kth - 2.0f * kMargin : -INFINITY;
     floor = fmaxf(floor, __shfl_sync(kFull, m.s, 31));
     const int cnt = __popc(__ballot_sync(kFull, isfinite(m.s) && m.s >= wthr));
     unsigned at = 0;
-    if (lane == 0) {
-      if (cnt) at = atomicAdd(&hdr->nent, (unsigned)cnt);
+    if (lane == 0) {  // the two maxima need no reply; only the append offset does
+      if (isfinite(kth)) atomicMax(&hdr->lb, float_to_ordered(kth));
       if (isfinite(floor)) atomicMax(&hdr->floor, float_to_ordered(floor));
+      if (cnt) at = atomicAdd(&hdr->nent, (unsigned)cnt);
     }
     at = __shfl_sync(kFull, at, 0);
     if (lane < cnt) p.scratch.entries(q)[at + lane] = Entry{m.s, m.id};
     __syncwarp();
     if (lane == 0) {
-      __threadfence();
-      const unsigned ticket = atomicAdd(&hdr->done, 1u);
+      // acq_rel: releases this warp's entries (ordered before by __syncwarp)
+      // to the block that draws the last ticket, and acquires every other
+      // block's when this one does; __syncthreads passes that on to the block.
+      unsigned ticket;
+      asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;"
+                   : "=r"(ticket)
+                   : "l"(&hdr->done)
+                   : "memory");
       sm.last = (ticket == gridDim.x - 1);
     }
   }
   __syncthreads();
   if (!sm.last) return;
-  __threadfence();
   final_merge<D, T, INL, NW>(p, q, kMargin, safe, lane, warp, sm);
 }
 
@@ -566,6 +564,9 @@ __global__ void __launch_bounds__(kThreads) mla_scan_kernel(const __grid_constan
   __shared__ int sh_safe;
   __shared__ int sh_next;
 
+  // May be launched as a programmatic dependent of the previous route's
+  // resolve kernel: wait for it (and for the query's producer) first.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int q = blockIdx.y;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const float* query = query_ptr(p, q, D);
@@ -736,6 +737,9 @@ __global__ void __launch_bounds__(kBulkWarps * 32, 1)
   __shared__ float sh_eq;
   __shared__ int sh_safe;
 
+  // May be launched as a programmatic dependent of the previous route's
+  // resolve kernel: wait for it (and for the query's producer) first.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int q = blockIdx.y;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const float* query = query_ptr(p, q, D);
@@ -899,7 +903,9 @@ __global__ void __launch_bounds__(kThreads) mla_exact_kernel(const __grid_consta
 
   // Launched with programmatic dependent launch after the scan: wait until the
   // scan grid has completed and its writes are visible (no-op otherwise).
+  // The next route's scan may then be scheduled; it waits for this grid in turn.
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;");
   const int q = blockIdx.y;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int dim = D > 0 ? D : p.dim;
@@ -1037,7 +1043,10 @@ __global__ void __launch_bounds__(kThreads) mla_exact_kernel(const __grid_consta
   block_merge(list, lane, warp, sh_s, sh_id);
   if (warp != 0) return;
   write_result(p, q, list, lane);
-  if (lane == 0) reset_header(hdr);
+  if (lane == 0) {  // the scan's final merge already reset the rest of the header
+    hdr->lb = kOrderedNegInf;
+    hdr->done = 0;
+  }
 }
 
 template <typename T>
@@ -1242,12 +1251,30 @@ Params<T> make_params(grm_b200_mla_bank* b, const float* dq, int topk) {
   return p;
 }
 
+// pdl: launch as a programmatic dependent of the preceding kernel on `s` (the
+// previous route's resolve kernel), so this launch overlaps its tail; the scan
+// waits for it (griddepcontrol.wait) before reading anything.
 template <typename T>
-int launch_scan(grm_b200_mla_bank* b, const Params<T>& p, int nq, cudaStream_t s) {
+int launch_scan(grm_b200_mla_bank* b, const Params<T>& p, int nq, cudaStream_t s,
+                bool pdl = false) {
   dim3 grid(b->grid_x, nq);
   if (b->bulk) {
-    scan_bulk_fn<T>(b->dim)<<<grid, kBulkWarps * 32, kBulkSmem, s>>>(p);
-    return cuda_status(cudaGetLastError());
+    auto fn = scan_bulk_fn<T>(b->dim);
+    if (!pdl) {
+      fn<<<grid, kBulkWarps * 32, kBulkSmem, s>>>(p);
+      return cuda_status(cudaGetLastError());
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(kBulkWarps * 32);
+    cfg.dynamicSmemBytes = kBulkSmem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cuda_status(cudaLaunchKernelEx(&cfg, fn, p));
   }
   if (!b->exact_only) {
     scan_fn<T>(b->dim)<<<grid, kThreads, 0, s>>>(p);
@@ -1522,14 +1549,14 @@ int route_async_phases(grm_b200_mla_bank* bank, const float* queries_device, int
     p.out_ids = out_ids_device;
     p.out_scores = out_scores_device;
     p.id_offset = id_offset;
-    if (phase & 1) rc = launch_scan<__half>(bank, p, query_count, s);
+    if (phase & 1) rc = launch_scan<__half>(bank, p, query_count, s, true);
     if (!rc && (phase & 2)) rc = launch_exact<__half>(bank, p, query_count, s, true);
   } else {
     Params<float> p = make_params<float>(bank, queries_device, topk);
     p.out_ids = out_ids_device;
     p.out_scores = out_scores_device;
     p.id_offset = id_offset;
-    if (phase & 1) rc = launch_scan<float>(bank, p, query_count, s);
+    if (phase & 1) rc = launch_scan<float>(bank, p, query_count, s, true);
     if (!rc && (phase & 2)) rc = launch_exact<float>(bank, p, query_count, s, true);
   }
   if (rc) return bank->err.set(rc, "MLA async route launch failed");
