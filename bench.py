@@ -4,7 +4,9 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
 A step is one route of one probe over the whole 1,048,576 x 256 fp16 centroid
-bank (top-3, bit-exact ids and scores).  At N > 1 (torchrun, one process per
+bank (top-3, bit-exact ids and scores); with --workload mla_1m_b64 a step
+routes a batch of 64 probes (config 2's batch case, tensor-core path) and the
+value counts probes.  At N > 1 (torchrun, one process per
 GPU) the bank is node-range sharded: each GPU routes its 1/N of the nodes, the
 per-shard top-3 candidates are all-gathered over NCCL and merged on the device
 (strong scaling: the bank is fixed at 1M nodes).
@@ -44,7 +46,11 @@ METRIC = "1M-node MLA route throughput (1,048,576 x 256 fp16 centroids, top-3, b
 UNIT = "probes/s"
 NODES, DIM, TOPK = 1 << 20, 256, 3
 L2_BYTES = 126 * 1024 * 1024
-WORKLOAD = "mla_1m_b1"
+
+
+def batch_of(workload: str) -> int:
+    """Queries per step of an MLA workload (config 2: batch 1 and batch 64)."""
+    return 64 if workload == "mla_1m_b64" else 1
 
 
 def parse():
@@ -55,8 +61,8 @@ def parse():
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--workload", default="mla_1m_b1",
-                   choices=["mla_1m_b1", "gqa_512", "gqa_100k", "mount_int4", "mount_int6",
-                            "mount_int8", "mount_ref8"],
+                   choices=["mla_1m_b1", "mla_1m_b64", "gqa_512", "gqa_100k", "mount_int4",
+                            "mount_int6", "mount_int8", "mount_ref8"],
                    help="mla_1m_b1 is the headline (BASELINE config 2); the others measure "
                         "the GQA route (configs 3/4) and the quantised mount (config 5)")
     return p.parse_args()
@@ -70,9 +76,9 @@ def peaks():
     return 6650.0, "fallback"
 
 
-def profile_traffic():
+def profile_traffic(batch: int = 1):
     """dram bytes per scan launch from the committed ncu summary, if any."""
-    f = ROOT / "profiles" / "mla_scan_1m.md"
+    f = ROOT / "profiles" / ("mla_scan_1m.md" if batch == 1 else "mla_batch_1m_b64.md")
     if not f.exists():
         return None
     for line in f.read_text().splitlines():
@@ -218,7 +224,8 @@ def run_reference(args):
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": per_probe * 1e3, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32/f64", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "nodes": NODES, "dim": DIM, "topk": TOPK, "batch": 1,
+        "config": {"workload": args.workload, "nodes": NODES, "dim": DIM, "topk": TOPK,
+                   "batch": batch_of(args.workload),
                    "bank_dtype": "fp16 values (reference stores fp32)"},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": kind,
                          "sample": sample},
@@ -243,6 +250,7 @@ def run_ours(args):
                                 device_id=torch.device("cuda", local))
     lib = _lib.load()
 
+    B = batch_of(args.workload)   # queries per step
     rows = synth.mla_bank_device(1, NODES)
     a, b = mla_shard_range(NODES, world, rank)
     shard = rows[a:b].contiguous()
@@ -257,33 +265,39 @@ def run_ours(args):
     rows_host = rows.float().cpu().numpy() if (rank == 0 and world == 1 and
                                                not args.no_cpu_baseline) else None
     del rows
-    n_q = args.warmup + args.steps
-    qs_host = torch.from_numpy(synth.mla_queries(1, n_q)).pin_memory()
+    # distinct queries every step (a pool of batches, cycled for long runs)
+    n_q = min(args.warmup + args.steps, 4096 // B)
+    qs_host = torch.from_numpy(synth.mla_queries(1, n_q * B)).pin_memory()
     qs_dev = qs_host.cuda()
-    out_s = torch.empty((1, TOPK), dtype=torch.float32, device="cuda")
-    out_i = torch.empty((1, TOPK), dtype=torch.int64, device="cuda")
+    out_s = torch.empty((B, TOPK), dtype=torch.float32, device="cuda")
+    out_i = torch.empty((B, TOPK), dtype=torch.int64, device="cuda")
     shard_bytes = (b - a) * DIM * 2
     flush = None
     if shard_bytes < 4 * L2_BYTES:
         flush = torch.empty(2 * L2_BYTES, dtype=torch.uint8, device="cuda")
     stream = torch.cuda.current_stream()
     sptr = stream.cuda_stream
-    gs = torch.empty((world, TOPK), dtype=torch.float32, device="cuda")
-    gi = torch.empty((world, TOPK), dtype=torch.int64, device="cuda")
-    ms_s = torch.empty((1, TOPK), dtype=torch.float32, device="cuda")
-    ms_i = torch.empty((1, TOPK), dtype=torch.int64, device="cuda")
+    gs = torch.empty((world, B, TOPK), dtype=torch.float32, device="cuda")
+    gi = torch.empty((world, B, TOPK), dtype=torch.int64, device="cuda")
+    ms_s = torch.empty((B, TOPK), dtype=torch.float32, device="cuda")
+    ms_i = torch.empty((B, TOPK), dtype=torch.int64, device="cuda")
+
+    def batch(i):
+        j = i % n_q
+        return qs_dev[j * B:(j + 1) * B]
 
     def step(i, ev):
-        """One route: scan + resolve (programmatic dependent launch) [+ gather + merge]."""
-        q = qs_dev[i:i + 1]
+        """One route of B queries: scan + resolve (programmatic dependent launch)
+        [+ gather + merge]."""
+        q = batch(i)
         if ev:
             ev[0].record(stream)
-        rc = lib.grm_b200_mla_route_async(bank._h, q.data_ptr(), 1, TOPK, a, out_i.data_ptr(),
+        rc = lib.grm_b200_mla_route_async(bank._h, q.data_ptr(), B, TOPK, a, out_i.data_ptr(),
                                           out_s.data_ptr(), sptr)
         if world > 1:
-            dist.all_gather_into_tensor(gs, out_s.view(-1))
-            dist.all_gather_into_tensor(gi, out_i.view(-1))
-            rc |= lib.grm_b200_merge_topk(gs.data_ptr(), gi.data_ptr(), 1, world, TOPK, TOPK,
+            dist.all_gather_into_tensor(gs.view(world * B, TOPK), out_s)
+            dist.all_gather_into_tensor(gi.view(world * B, TOPK), out_i)
+            rc |= lib.grm_b200_merge_topk(gs.data_ptr(), gi.data_ptr(), B, world, TOPK, TOPK,
                                           ms_s.data_ptr(), ms_i.data_ptr(), sptr)
         if ev:
             ev[1].record(stream)
@@ -291,13 +305,13 @@ def run_ours(args):
             raise RuntimeError("route launch failed")
 
     def scan_only(i, ev):
-        """The dominant kernel alone, event-timed on its stream (roofline)."""
-        q = qs_dev[i:i + 1]
+        """The scan phase alone, event-timed on its stream (roofline)."""
+        q = batch(i)
         ev[0].record(stream)
-        rc = lib.grm_b200_mla_scan_async(bank._h, q.data_ptr(), 1, TOPK, a, out_i.data_ptr(),
+        rc = lib.grm_b200_mla_scan_async(bank._h, q.data_ptr(), B, TOPK, a, out_i.data_ptr(),
                                          out_s.data_ptr(), sptr)
         ev[1].record(stream)
-        rc |= lib.grm_b200_mla_resolve_async(bank._h, q.data_ptr(), 1, TOPK, a,
+        rc |= lib.grm_b200_mla_resolve_async(bank._h, q.data_ptr(), B, TOPK, a,
                                              out_i.data_ptr(), out_s.data_ptr(), sptr)
         if rc:
             raise RuntimeError("scan launch failed")
@@ -355,45 +369,47 @@ def run_ours(args):
     if world > 1:
         dist.all_reduce(tot, op=dist.ReduceOp.MAX)
     total_ms = float(tot.item())
-    value = args.steps / (total_ms / 1e3)
+    value = args.steps * B / (total_ms / 1e3)
 
     # correctness of the timed steps: the last route equals a fresh exact route
     # (the full parity suite lives in tests/)
     # e2e: the public API with host buffers every step
     e2e_steps = min(args.steps, 500)
     if world == 1:
-        qn = qs_host.numpy()
+        qn = qs_host.numpy().reshape(n_q, B, DIM)
         for i in range(5):
-            bank.route_topk(qn[i], topk=TOPK)
+            bank.route_topk(qn[i % n_q], topk=TOPK)
         t0 = time.perf_counter()
         for i in range(e2e_steps):
             bank.route_topk(qn[(args.warmup + i) % n_q], topk=TOPK)
         e2e_s = time.perf_counter() - t0
-        h2d, d2h = DIM * 4, 400
+        h2d, d2h = B * DIM * 4, B * TOPK * 12
     else:
-        qbuf = torch.empty((1, DIM), dtype=torch.float32, device="cuda")
+        qbuf = torch.empty((B, DIM), dtype=torch.float32, device="cuda")
         for i in range(5):
-            qbuf.copy_(qs_host[i:i + 1], non_blocking=True)
+            j = i % n_q
+            qbuf.copy_(qs_host[j * B:(j + 1) * B], non_blocking=True)
             ids, sc = route.route(qbuf, TOPK)
             ids.cpu(), sc.cpu()
         dist.barrier()
         t0 = time.perf_counter()
         for i in range(e2e_steps):
-            qbuf.copy_(qs_host[(args.warmup + i) % n_q:(args.warmup + i) % n_q + 1],
-                       non_blocking=True)
+            j = (args.warmup + i) % n_q
+            qbuf.copy_(qs_host[j * B:(j + 1) * B], non_blocking=True)
             ids, sc = route.route(qbuf, TOPK)
             ids.cpu(), sc.cpu()
         e2e_s = time.perf_counter() - t0
         t = torch.tensor([e2e_s], dtype=torch.float64, device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_s = float(t.item())
-        h2d, d2h = DIM * 4, TOPK * 12
-    e2e_value = e2e_steps / e2e_s
+        h2d, d2h = B * DIM * 4, B * TOPK * 12
+    e2e_value = e2e_steps * B / e2e_s
 
     peak, peak_kind = peaks()
     scan_mean = statistics.mean(scan_ms)
-    bytes_per_launch = shard_bytes + DIM * 4
+    bytes_per_launch = shard_bytes + B * DIM * 4
     achieved = bytes_per_launch / (scan_mean / 1e3) / 1e9
+    flops_per_launch = 2 * (b - a) * DIM * B
     cpu = None
     if rank == 0 and world == 1 and rows_host is not None:
         cpu = cpu_reference_full(rows_host, synth.mla_queries(1, 64))
@@ -405,18 +421,22 @@ def run_ours(args):
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "f16 bank, f32 scan, f64 exact refine",
+        "scaling": "strong", "vs_baseline": None, "dtype": ("f16 bank, f32 scan, f64 exact refine" if B == 1 else
+                  "f16 bank x f16 queries on tensor cores (f32 accumulate), f64 exact refine"),
         "data": "synthetic",
-        "config": {"workload": WORKLOAD, "nodes": NODES, "dim": DIM, "topk": TOPK, "batch": 1,
+        "config": {"workload": args.workload, "nodes": NODES, "dim": DIM, "topk": TOPK, "batch": B,
                    "bank_dtype": "fp16", "shard_nodes": b - a,
                    "parallelism": f"node-sharded x{world}" if world > 1 else "single GPU",
                    "l2": ("bank shard larger than 4x L2, no flush" if flush is None else
                           "256 MB L2 flush before every step, outside the timed events")},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "peak_kind": peak_kind,
-                     "kernel": "mla_scan_bulk_kernel<256, half>",
+                     "kernel": ("mla_scan_bulk_kernel<256, half>" if B == 1 else
+                                "mla_batch_kernel<256> (timed with its prep and merge kernels)"),
                      "algorithmic_bytes_per_launch": bytes_per_launch,
-                     "traffic": profile_traffic(),
+                     "traffic": profile_traffic(B),
+                     "tensor_tflops": (flops_per_launch / (scan_mean / 1e3) / 1e12
+                                       if B > 1 else None),
                      "scan_us_mean": scan_mean * 1e3,
                      "step_us_median": statistics.median(step_ms) * 1e3,
                      "step_us_p99": sorted(step_ms)[int(0.99 * (len(step_ms) - 1))] * 1e3},
@@ -425,7 +445,7 @@ def run_ours(args):
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "steps": e2e_steps,
                 "api": "CudaMLARouteBank.route_topk" if world == 1 else "ShardedMLARoute.route"},
-        "gpu_launches": args.steps * (2 if world == 1 else 3),
+        "gpu_launches": args.steps * ((2 if B == 1 else 4) + (0 if world == 1 else 1)),
         "timing": ("one event pair around the K back-to-back steps" if flush is None else
                    "per-step event pairs, L2 flush between steps outside them"),
         "roofline_launches": n_scan,

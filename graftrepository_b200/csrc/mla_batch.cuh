@@ -1,0 +1,559 @@
+// mla_batch.cuh -- batched MLA route on the 5th-generation tensor cores.
+//
+// Included by mla_route.cu inside namespace grm_b200::mla.  A batch of up to
+// kBQ queries reads the bank once: the approximate scores are the product
+// Qs x bank^T, computed with tcgen05.mma (M = 128 query rows of which the first
+// kBQ are the batch and the rest zero, N = 128 bank rows, K = 16 per
+// instruction, fp16 operands, fp32 accumulators in tensor memory), so a
+// 64-query batch costs one pass over HBM instead of 64.  Queries on the M side
+// put one query in each tensor-memory lane: an epilogue thread reads its
+// query's scores for consecutive bank rows and filters them against its own
+// threshold in registers.
+//
+// Operands.  The bank tile is loaded by TMA (2D tensor map, 128-byte swizzle,
+// box 64 elements x 128 rows, one box per 128-byte K atom) into a ring of
+// kBStages shared-memory stages.  The query matrix is built once per batch by
+// batch_prep_kernel: q' = q / |q| (fp64 norm), scaled by 2^8 (no fp16
+// subnormals) and rounded to fp16, written in the same K-major swizzled layout
+// and copied into shared memory with one bulk copy.
+//
+// Roles (one CTA per SM, persistent over 128-row tiles b, b + grid, ...):
+//   warps 0, 1, 4, 5   epilogue: warp w reads tensor-memory lanes 32*(w % 4)..
+//                      (32 queries, one per thread) and 64 of the tile's 128
+//                      bank rows; each thread keeps its query's sorted top-32
+//                      in registers (inserts are per thread: no warp traffic).
+//   warp 2, one lane   TMA producer (bounded waits on the stage ring)
+//   warp 3             tensor-memory allocation; one lane issues the MMAs
+// (tensor-memory lanes 64..127 hold the zero query rows and are not read.)
+// Six warps keep two per scheduler partition at most, so an epilogue thread
+// may use up to 255 registers.
+// Two 128-column accumulator buffers let the MMAs of tile i+1 run while the
+// epilogue reads tile i.
+//
+// Error bound of the approximate score s~ = acc * 2^-8 / norm against the
+// reference score s (|q'| = 1):
+//   fp16 rounding of 256 q'_d: |sum_d c_d (q'_d - h_d)| <= 2^-11 sum |c_d q'_d|
+//                               <= 2^-11 |c|;
+//   products c_d h_d are exact in fp32 (11 x 11 significant bits); fp32
+//   accumulation of <= 512 terms: <= 2^-14 |c| even with truncation;
+//   fp16 bank subnormals, should the tensor core flush them: <= 16 * 2^-14 / |c|
+//   relative, <= 2^-9 for rows with |c| >= 1/2 (banks with smaller rows are not
+//   batched);
+//   dropping the reference's 1e-8 / |q| term: <= 2^-16 for |q| >= 2^-8 (smaller
+//   queries take the exact path).
+// Total < 2^-8.5; kBMargin = 2^-8.  Candidates within 2 * kBMargin of the
+// approximate k-th best are recomputed with the reference arithmetic by the
+// per-query merge (final_merge); saturated lists flag the exact fallback.
+#pragma once
+
+#include <cuda.h>
+
+namespace grm_b200 {
+namespace mla {
+
+constexpr int kBQ = 64;                    // queries per launch (of the MMA's M = 128 rows)
+constexpr int kBMq = 128;                  // MMA M: query rows (kBQ..127 are zero)
+constexpr int kBM = 128;                   // bank rows per tile (MMA N)
+constexpr int kBStages = 4;                // shared-memory stages
+constexpr int kBEpi = 4;                   // epilogue warps (0, 1, 4, 5)
+constexpr int kBThreads = 6 * 32;
+constexpr int kBProducerWarp = 2;
+constexpr int kBMmaWarp = 3;
+constexpr int kBMergeWarps = 12;           // warps of the per-query merge kernel
+constexpr float kBMargin = 0.00390625f;    // 2^-8
+constexpr float kBQScale = 256.0f;         // 2^8
+constexpr float kBMinNorm = 0.5f;          // smallest bank row norm the batch path accepts
+constexpr double kBSafeLo = 0.00390625;    // 2^-8: smaller query norms take the exact path
+constexpr uint32_t kBTmemCols = 2 * kBM;   // two accumulator buffers
+
+template <int D>
+struct BLayout {
+  static constexpr int KA = D / 64;                    // 128-byte swizzle atoms along K
+  static constexpr int SA = KA >= 2 ? 2 : 1;           // atoms per stage
+  static constexpr int SPT = KA / SA;                  // stages per tile
+  static constexpr int kAtomT = kBM * 128;             // 16 KB: 128 bank rows x 64 halves
+  static constexpr int kAtomQ = kBMq * 128;            // 16 KB: 128 query rows x 64 halves
+  static constexpr int kStage = SA * kAtomT;
+  static constexpr int kQ = KA * kAtomQ;
+  static constexpr int kMerge = kBQ * 2 * 32 * 8;      // end-of-scan list exchange
+  static constexpr int kSmem = 1024 + kQ + kBStages * kStage;  // + alignment slack
+  static_assert(D % 64 == 0 && D <= 256, "batched dims: 64, 128, 256");
+  static_assert(kMerge <= kBStages * kStage, "the list exchange reuses the stages");
+};
+
+struct BatchParams {
+  CUtensorMap tmap;              // bank [nodes, D] fp16, box 64 x 128, 128-byte swizzle
+  const unsigned char* qmat;     // swizzled query image, BLayout<D>::kQ bytes
+  const float* rnorms;           // 2^-8 / row norm (NaN for non-finite rows)
+  int64_t nodes;
+  int64_t tiles;
+  int nq;
+  int topk;
+  Scratch scratch;
+};
+
+// ---- PTX wrappers ------------------------------------------------------------
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y,
+                                            uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      ".L2::cache_hint [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(dst)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// D[tmem] (+)= A[smem] x B[smem]^T, both K-major fp16.
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                         uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive on `bar` once every MMA issued so far by this thread has completed.
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+
+// 32 consecutive fp32 columns of this warp's 32 tensor-memory lanes; the
+// registers are valid after tmem_wait_ld().
+__device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+      "%12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, "
+      "%30, %31}, [%32];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+        "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
+        "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]),
+        "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]), "=r"(v[25]),
+        "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row atoms
+// 1024 bytes apart (stride byte offset 64 x 16 B), descriptor version 1.
+__device__ __forceinline__ uint64_t sw128_desc(const void* smem) {
+  const uint32_t a = smem_u32(smem);
+  return (uint64_t)((a >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)64 << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// Instruction descriptor: fp32 accumulator, fp16 A and B, both K-major,
+// M = kBMq query rows, N = kBM bank rows.
+constexpr uint32_t kBIdesc =
+    (1u << 4) | ((uint32_t)(kBM >> 3) << 17) | ((uint32_t)(kBMq >> 4) << 24);
+
+// Byte offset of element (query row j, dim d) in the swizzled query image.
+__host__ __device__ constexpr int qmat_offset(int j, int d) {
+  return (d / 64) * (kBMq * 128) + j * 128 + ((((d % 64) / 8) ^ (j % 8)) * 16) + (d % 8) * 2;
+}
+
+// A thread's sorted top-32 (score desc, id asc) in registers.  Inserting is
+// an unrolled compare-and-shift (no dynamic indexing, no warp traffic).
+struct LaneList {
+  float s[32];
+  uint32_t id[32];
+  __device__ __forceinline__ void init() {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      s[i] = -INFINITY;
+      id[i] = kNoRow;
+    }
+  }
+  // Insert (cs, cid) when it beats the last entry.
+  __device__ __forceinline__ void insert(float cs, uint32_t cid) {
+    if (!better(cs, cid, s[31], id[31])) return;
+#pragma unroll
+    for (int i = 31; i >= 1; --i) {
+      if (better(cs, cid, s[i - 1], id[i - 1])) {
+        s[i] = s[i - 1];
+        id[i] = id[i - 1];
+      } else if (better(cs, cid, s[i], id[i])) {
+        s[i] = cs;
+        id[i] = cid;
+      }
+    }
+    if (better(cs, cid, s[0], id[0])) {
+      s[0] = cs;
+      id[0] = cid;
+    }
+  }
+  // Score of entry k-1 (runtime 1 <= k <= 32): the list is sorted, so it is
+  // the minimum of the first k scores -- a tree reduction, which keeps the
+  // list in registers (an indexed read would move it to local memory) and
+  // needs 5 dependent steps.
+  __device__ __forceinline__ float kth(int k) const {
+    float t[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i)
+      t[i] = fminf(2 * i < k ? s[2 * i] : INFINITY, 2 * i + 1 < k ? s[2 * i + 1] : INFINITY);
+#pragma unroll
+    for (int w = 8; w >= 1; w >>= 1)
+#pragma unroll
+      for (int i = 0; i < w; ++i) t[i] = fminf(t[i], t[i + w]);
+    return t[0];
+  }
+};
+
+// v[c] for a runtime c in [0, 32), by a 5-level select tree over its bits.
+__device__ __forceinline__ float pick32(const float (&v)[32], int c) {
+  float t[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) t[i] = (c & 1) ? v[2 * i + 1] : v[2 * i];
+#pragma unroll
+  for (int lvl = 1, w = 8; w >= 1; ++lvl, w >>= 1)
+#pragma unroll
+    for (int i = 0; i < w; ++i) t[i] = ((c >> lvl) & 1) ? t[2 * i + 1] : t[2 * i];
+  return t[0];
+}
+
+// ---- kernels -----------------------------------------------------------------
+
+// One warp per query row 0..kBQ-1: unit-normalise (fp64 norm), scale by 2^8,
+// round to fp16, write the swizzled image; rows past the batch are zero (rows
+// kBQ..kBMq-1 are zeroed once when the image is allocated).  Records whether
+// the query is inside the batched path's safe range.
+template <int D>
+__global__ void __launch_bounds__(32) batch_prep_kernel(const float* queries, int nq,
+                                                        unsigned char* qmat, Scratch scratch) {
+  const int j = blockIdx.x, lane = threadIdx.x;
+  bool safe = false;
+  float inv = 0.0f;
+  if (j < nq) {
+    const float* q = queries + (int64_t)j * D;
+    double acc = 0.0;
+    for (int d = lane; d < D; d += 32) acc = fma((double)q[d], (double)q[d], acc);
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) acc += __shfl_xor_sync(kFull, acc, o);
+    const double qn = sqrt(acc);
+    safe = isfinite(qn) && qn >= kBSafeLo && qn < kSafeHi;
+    inv = safe ? (float)(1.0 / qn) : 0.0f;
+  }
+  for (int d = lane; d < D; d += 32) {
+    const float v = safe ? queries[(int64_t)j * D + d] * inv * kBQScale : 0.0f;
+    *reinterpret_cast<__half*>(qmat + qmat_offset(j, d)) = __float2half_rn(v);
+  }
+  if (j < nq && lane == 0) scratch.hdr(j)->qsafe = safe ? 1 : 0;
+}
+
+// 2^-8 / row norm for the batch epilogue (NaN for non-finite rows).
+__global__ void batch_rnorm_kernel(const float* norms, int64_t n, float* rnorms) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const float nrm = norms[i];
+    rnorms[i] = isfinite(nrm) ? (1.0f / nrm) * (1.0f / kBQScale) : __int_as_float(0x7FC00000);
+  }
+}
+
+template <int D>
+__global__ void __launch_bounds__(kBThreads, 1)
+    mla_batch_kernel(const __grid_constant__ BatchParams p) {
+  using LY = BLayout<D>;
+  extern __shared__ unsigned char bsm_raw[];
+  unsigned char* const sm = bsm_raw + ((1024u - (smem_u32(bsm_raw) & 1023u)) & 1023u);
+  unsigned char* const smQ = sm;
+  unsigned char* const smT = sm + LY::kQ;
+  __shared__ __align__(8) uint64_t full[kBStages], empty[kBStages], tfull[2], tempty[2], bq_bar,
+      mma_done;
+  __shared__ uint32_t sh_tmem;
+  __shared__ int sh_fail;
+  __shared__ unsigned sh_issued, sh_consumed;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t my_tiles =
+      (int64_t)blockIdx.x < p.tiles ? (p.tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  // epilogue warps 0, 1, 4, 5: lane quarter lq (queries 32*lq + lane), column half ch
+  const bool epi = warp == 0 || warp == 1 || warp == 4 || warp == 5;
+  const int lq = warp & 3;
+  const int ch = warp >= 4 ? 1 : 0;
+  const int qi = lq * 32 + lane;  // this thread's query
+
+  // The query image comes from batch_prep_kernel (programmatic dependent launch).
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kBStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(&tfull[0], 1);
+    mbar_init(&tfull[1], 1);
+    mbar_init(&tempty[0], kBEpi);
+    mbar_init(&tempty[1], kBEpi);
+    mbar_init(&bq_bar, 1);
+    mbar_init(&mma_done, 1);
+    sh_fail = 0;
+    sh_issued = 0;
+    sh_consumed = 0;
+    mbar_fence_init();
+  }
+  if (warp == kBMmaWarp) {
+    tmem_alloc(&sh_tmem, kBTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sh_tmem;
+
+  if (warp == kBProducerWarp) {
+    if (lane == 0) {  // TMA producer
+      const uint64_t pol = l2_evict_first_policy();
+      mbar_arrive_expect_tx(&bq_bar, LY::kQ);
+      bulk_g2s(smQ, p.qmat, LY::kQ, &bq_bar);
+      int st = 0;
+      unsigned ph = 0, issued = 0;
+      bool ok = true;
+      for (int64_t i = 0; i < my_tiles && ok; ++i) {
+        const int y = (int)(((int64_t)blockIdx.x + i * gridDim.x) * kBM);
+        for (int sp = 0; sp < LY::SPT; ++sp) {
+          if (!mbar_wait(&empty[st], ph ^ 1u, kWaitLimit)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[st], LY::kStage);
+#pragma unroll
+          for (int a = 0; a < LY::SA; ++a)
+            tma_load_2d(smT + st * LY::kStage + a * LY::kAtomT, &p.tmap, (sp * LY::SA + a) * 64,
+                        y, &full[st], pol);
+          ++issued;
+          if (++st == kBStages) {
+            st = 0;
+            ph ^= 1u;
+          }
+        }
+      }
+      sh_issued = issued;
+      if (!ok) atomicOr(&sh_fail, 1);
+    }
+  } else if (warp == kBMmaWarp) {
+    if (lane == 0) {  // MMA issuer: D[query][row] = Q x T^T
+      bool ok = mbar_wait(&bq_bar, 0, kWaitLimit);
+      int st = 0;
+      unsigned ph = 0, consumed = 0;
+      for (int64_t i = 0; i < my_tiles && ok; ++i) {
+        const int b = (int)(i & 1);
+        const unsigned u = (unsigned)(i >> 1);
+        if (!mbar_wait(&tempty[b], (u & 1u) ^ 1u, kWaitLimit)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem + (uint32_t)(b * kBM);
+        for (int sp = 0; sp < LY::SPT; ++sp) {
+          if (!mbar_wait(&full[st], ph, kWaitLimit)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          ++consumed;
+#pragma unroll
+          for (int a = 0; a < LY::SA; ++a)
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+              const uint64_t qd = sw128_desc(smQ + (sp * LY::SA + a) * LY::kAtomQ + kk * 32);
+              const uint64_t td = sw128_desc(smT + st * LY::kStage + a * LY::kAtomT + kk * 32);
+              umma_f16(d, qd, td, kBIdesc, (sp | a | kk) != 0 ? 1u : 0u);
+            }
+          umma_commit(&empty[st]);  // the stage is free once these MMAs completed
+          if (++st == kBStages) {
+            st = 0;
+            ph ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&tfull[b]);
+      }
+      // every MMA this thread issued completes before the teardown
+      umma_commit(&mma_done);
+      if (!mbar_wait(&mma_done, 0, kWaitLimit)) ok = false;
+      sh_consumed = consumed;
+      if (!ok) atomicOr(&sh_fail, 1);
+    }
+  } else if (epi) {
+    LaneList L;
+    L.init();
+    bool done_all = true;
+    const float m2 = 2.0f * kBMargin;
+    const bool active = qi < p.nq;
+    // max(entry 31, entry k-1 - 2*margin): rows below never enter
+    float thr = active ? -INFINITY : INFINITY;
+    // 2^-8 / norm of the warp's 64 rows of a tile, lane l holding rows l and
+    // 32 + l (NaN past the bank), loaded one tile ahead.
+    auto load_rn = [&](int64_t i, float& a, float& b2) {
+      const int64_t r = ((int64_t)blockIdx.x + i * gridDim.x) * kBM + ch * 64 + lane;
+      a = (i < my_tiles && r < p.nodes) ? __ldg(p.rnorms + r) : __int_as_float(0x7FC00000);
+      b2 = (i < my_tiles && r + 32 < p.nodes) ? __ldg(p.rnorms + r + 32)
+                                               : __int_as_float(0x7FC00000);
+    };
+    float rn0, rn1;
+    load_rn(0, rn0, rn1);
+    // The query's header slot lb collects every CTA's k-th approximate score
+    // (a lower bound of the final k-th best); it is read one tile ahead.
+    int* const lbq = &p.scratch.hdr(active ? qi : 0)->lb;
+    float kpub = -INFINITY;
+    for (int64_t i = 0; i < my_tiles; ++i) {
+      const int b = (int)(i & 1);
+      const unsigned u = (unsigned)(i >> 1);
+      const int64_t row0 = ((int64_t)blockIdx.x + i * gridDim.x) * kBM + ch * 64;
+      float nx0, nx1;
+      load_rn(i + 1, nx0, nx1);
+      const int lb_next = active ? __ldcg(lbq) : kOrderedNegInf;
+      if (!mbar_wait(&tfull[b], u & 1u, kWaitLimit)) {
+        if (lane == 0) atomicOr(&sh_fail, 1);
+        done_all = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t v[64];
+      const uint32_t ta = tmem + ((uint32_t)(lq * 32) << 16) + (uint32_t)(b * kBM + ch * 64);
+      tmem_ld32_nowait(ta, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
+      tmem_ld32_nowait(ta + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[b]);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const float rn = h == 0 ? rn0 : rn1;
+        // hot path: scores and a bit per row that reaches the threshold (the
+        // shuffles run in every lane; lanes past the batch have thr = +inf)
+        float sc[32];
+        uint32_t mask = 0;
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          sc[c] = __uint_as_float(v[h * 32 + c]) * __shfl_sync(kFull, rn, c);
+          mask |= (sc[c] >= thr ? 1u : 0u) << c;
+        }
+        // rare path, rolled so the insert is inlined once
+#pragma unroll 1
+        while (mask) {
+          const int c = __ffs(mask) - 1;
+          mask &= mask - 1;
+          const float x = pick32(sc, c);
+          if (x >= thr) {
+            L.insert(x, (uint32_t)(row0 + h * 32 + c));
+            const float kt = L.kth(p.topk);
+            thr = fmaxf(thr, fmaxf(L.s[31], kt - m2));
+            if (kt > kpub) {  // share this query's k-th score with every CTA
+              kpub = kt;
+              atomicMax(lbq, float_to_ordered(kt));
+            }
+          }
+        }
+      }
+      // every CTA's k-th score for this query bounds its final k-th from below
+      const int g = lb_next;
+      if (g != kOrderedNegInf) thr = fmaxf(thr, ordered_to_float(g) - m2);
+      rn0 = nx0;
+      rn1 = nx1;
+    }
+    // This warp saw the last tile: every MMA has completed and every stage
+    // load was consumed, so the stage buffers are free for the list exchange.
+    if (done_all && active) {
+      Entry* e = reinterpret_cast<Entry*>(smT) + (qi * 2 + ch) * 32;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) e[j] = Entry{L.s[j], L.id[j]};
+    }
+  }
+  __syncwarp();
+  __syncthreads();
+
+  // Teardown: every bulk load issued has landed, every MMA has completed.
+  if (warp == kBProducerWarp && lane == 0 && sh_fail) {
+    for (unsigned k = sh_consumed; k < sh_issued; ++k)
+      mbar_wait(&full[k % kBStages], (k / kBStages) & 1u, kWaitLimit);
+  }
+  __syncthreads();
+  if (warp == kBMmaWarp) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kBTmemCols);
+  }
+  asm volatile("griddepcontrol.launch_dependents;");
+
+  // Per-query block lists: each query's two column-half lists were written to
+  // shared memory by the epilogue; one warp per query merges them and appends
+  // its entries as scan_finish does.
+  Entry* const mrg = reinterpret_cast<Entry*>(smT);
+  const bool failed = sh_fail != 0;
+  for (int q = warp; q < p.nq; q += kBThreads / 32) {
+    Header* hdr = p.scratch.hdr(q);
+    if (failed) {
+      if (lane == 0) atomicOr(&hdr->err, 1);
+      continue;
+    }
+    const Entry* e = mrg + q * 2 * 32;
+    const float k0 = e[p.topk - 1].s, k1 = e[32 + p.topk - 1].s;
+    const int best = k1 > k0 ? 1 : 0;
+    float floor = fmaxf(e[31].s, e[32 + 31].s);
+    WarpList m;
+    m.s = e[best * 32 + lane].s;
+    m.id = e[best * 32 + lane].id;
+    m.offer_margin(e[(1 - best) * 32 + lane].s, e[(1 - best) * 32 + lane].id, lane, p.topk,
+                   2.0f * kBMargin);
+    const float kth = __shfl_sync(kFull, m.s, p.topk - 1);
+    const float wthr = isfinite(kth) ? kth - 2.0f * kBMargin : -INFINITY;
+    floor = fmaxf(floor, __shfl_sync(kFull, m.s, 31));
+    const int cnt = __popc(__ballot_sync(kFull, isfinite(m.s) && m.s >= wthr));
+    unsigned at = 0;
+    if (lane == 0) {
+      if (isfinite(kth)) atomicMax(&hdr->lb, float_to_ordered(kth));
+      if (isfinite(floor)) atomicMax(&hdr->floor, float_to_ordered(floor));
+      if (cnt) at = atomicAdd(&hdr->nent, (unsigned)cnt);
+    }
+    at = __shfl_sync(kFull, at, 0);
+    if (lane < cnt) p.scratch.entries(q)[at + lane] = Entry{m.s, m.id};
+  }
+}
+
+// One block per query of the batch: the final merge and exact refine of
+// final_merge, with the batch margin.  Launched as a programmatic dependent of
+// mla_batch_kernel.
+template <int D>
+__global__ void __launch_bounds__(kBMergeWarps * 32)
+    mla_batch_merge_kernel(const __grid_constant__ Params<__half> p) {
+  __shared__ FinishSmem<kBMergeWarps, D> fsm;
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;");
+  const int q = blockIdx.x;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const float* query = p.queries + (int64_t)q * D;
+  for (int d = threadIdx.x; d < D; d += blockDim.x) fsm.qraw[d] = query[d];
+  const bool safe = __ldcg(&p.scratch.hdr(q)->qsafe) != 0;
+  final_merge<D, __half, false, kBMergeWarps>(p, q, kBMargin, safe, lane, warp, fsm);
+}
+
+}  // namespace mla
+}  // namespace grm_b200

@@ -37,6 +37,7 @@ constexpr int kWarps = kThreads / 32;
 constexpr float kMargin = 1.52587890625e-05f;  // 2^-16
 constexpr double kSafeLo = 1.0e-20, kSafeHi = 1.0e20;
 constexpr int kInlineMax = 512;  // largest dim a query can travel inline
+constexpr int kBatchMin = 2;     // batches from this size on take the tensor-core route
 
 enum Status : int { kOk = 0, kOverflow = 1, kUnsafe = 2, kError = 3 };
 
@@ -56,7 +57,8 @@ struct Header {
   unsigned nent;   // entries appended to the published list in this launch
   int floor;       // ordered float: largest score a block dropped for lack of room
   unsigned next;   // next group of the bulk scan's dynamic tail
-  int pad[10];
+  int qsafe;       // batched route: the query is inside the batch path's safe range
+  int pad[9];
 };
 
 struct Entry {
@@ -253,6 +255,7 @@ struct FinishSmem {
   float kth[NW];
   float floor[NW];
   float qraw[D];
+  double qd[D];  // qraw as double, for the exact refine
   double qn;
   int last;
   int ncand;
@@ -275,8 +278,15 @@ __device__ __forceinline__ double query_norm_seq_t(const float* q) {
 // row costs two memory round trips.  The final merge runs in a single block
 // right after the bank stream, so its code is fetched cold: the loop over
 // rounds is kept rolled on purpose.
+__device__ __forceinline__ double to_d(__half h) {
+  double d;
+  asm("cvt.f64.f16 %0, %1;" : "=d"(d) : "h"(__half_as_ushort(h)));
+  return d;
+}
+__device__ __forceinline__ double to_d(float f) { return (double)f; }
+
 template <int D, typename T, bool INL>
-__device__ float exact_score_tail(const T* row, const float* q, double qnorm, float norm) {
+__device__ float exact_score_tail(const T* row, const double* q, double qnorm, float norm) {
   constexpr int E = 16 / (int)sizeof(T);
   constexpr int NV = D / E;
   constexpr int CH = NV < 16 ? NV : 16;
@@ -293,8 +303,8 @@ __device__ float exact_score_tail(const T* row, const float* q, double qnorm, fl
       const T* e = reinterpret_cast<const T*>(&v[i]);
 #pragma unroll
       for (int k = 0; k < E; ++k) {
-        const double c = (double)to_f(e[k]);
-        dot = fma((double)q[(c0 + i) * E + k], c, dot);
+        const double c = to_d(e[k]);
+        dot = fma(q[(c0 + i) * E + k], c, dot);
         if constexpr (INL) n2 = fma(c, c, n2);
       }
     }
@@ -350,8 +360,11 @@ __device__ __forceinline__ void final_merge(const Params<T>& p, int q, float mar
   const int lb = __ldcg(&hdr->lb);
   const float fthr = lb == kOrderedNegInf ? -INFINITY : ordered_to_float(lb) - 2.0f * margin;
   const int nent = min((int)__ldcg(&hdr->nent), p.scratch.blocks * 32);
+  const int fl = __ldcg(&hdr->floor);
+  const bool failed = __ldcg(&hdr->err) != 0;
   const uint2* ents = reinterpret_cast<const uint2*>(p.scratch.entries(q));
   if (warp == NW - 1) {
+    for (int d = lane; d < D; d += 32) sm.qd[d] = (double)sm.qraw[d];
     if (lane == 0) sm.qn = query_norm_seq_t<D>(sm.qraw);
   } else {
 #pragma unroll 2
@@ -418,7 +431,6 @@ __device__ __forceinline__ void final_merge(const Params<T>& p, int q, float mar
   int above = 0;
 #pragma unroll
   for (int r = 0; r < kSelR; ++r) above += __popc(__ballot_sync(kFull, isfinite(v[r]) && v[r] >= thr));
-  const int fl = __ldcg(&hdr->floor);
   const float floor_max = fl == kOrderedNegInf ? -INFINITY : ordered_to_float(fl);
   bool overflow = above >= 32 || (isfinite(floor_max) && floor_max >= thr);
   if (ncand > NW * 32) {  // more entries inside the margin than the shared list holds
@@ -426,7 +438,6 @@ __device__ __forceinline__ void final_merge(const Params<T>& p, int q, float mar
     thr = fthr;
   }
   Result* r = p.results + q;
-  const bool failed = __ldcg(&hdr->err) != 0;
   if (failed) {
     if (lane == 0) {
       r->status = kError;
@@ -465,7 +476,7 @@ __device__ __forceinline__ void final_merge(const Params<T>& p, int q, float mar
   const uint32_t ci = lane < base ? sm.id[lane] : kNoRow;
   float es = -INFINITY;
   if (isfinite(cs)) {
-    es = exact_score_tail<D, T, INL>(p.rows + (int64_t)ci * D, sm.qraw, sm.qn,
+    es = exact_score_tail<D, T, INL>(p.rows + (int64_t)ci * D, sm.qd, sm.qn,
                                      INL ? 0.0f : __ldg(p.norms + ci));
   }
   WarpList ex;
@@ -474,6 +485,14 @@ __device__ __forceinline__ void final_merge(const Params<T>& p, int q, float mar
   write_result(p, q, ex, lane);
   if (lane == 0) reset_header(hdr);
 }
+
+}  // namespace mla
+}  // namespace grm_b200
+
+#include "mla_batch.cuh"
+
+namespace grm_b200 {
+namespace mla {
 
 // Everything after the streaming loop.  The block list is seeded with the
 // warp list whose k-th score is the largest (a copy: lists are sorted) and
@@ -1069,6 +1088,8 @@ __global__ void row_norms_kernel(const T* rows, int64_t n, int dim, float* norms
       nrm = __int_as_float(0x7FC00000);  // any non-finite value: the reference score is NaN
     } else if (!isfinite(nrm) || maxabs > 1.0e30f) {
       atomicAdd(special, 1u);            // outside the fast path's proven range
+    } else if (nrm < kBMinNorm) {
+      atomicAdd(special + 1, 1u);        // outside the batched path's proven range
     }
     norms[row] = nrm;
   }
@@ -1098,6 +1119,10 @@ struct grm_b200_mla_bank {
   float* d_norms = nullptr;
   bool exact_only = false;
   bool bulk = false;         // scan with the bulk-copy kernel
+  bool batch = false;        // batches of queries go to the tensor-core route
+  unsigned char* d_qmat = nullptr;  // its swizzled query image
+  float* d_rnorms = nullptr;        // its 2^-8 / row norm table
+  CUtensorMap tmap;                 // its bank tensor map
   int grid_x = 1;
   int scratch_queries = 0;
   size_t stride = 0;
@@ -1308,6 +1333,129 @@ int launch_exact(grm_b200_mla_bank* b, const Params<T>& p, int nq, cudaStream_t 
   return cuda_status(cudaLaunchKernelEx(&cfg, fn, p));
 }
 
+// ---- batched route (tensor cores) ---------------------------------------------
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// cuTensorMapEncodeTiled from the driver, looked up once (no libcuda link).
+EncodeTiledFn encode_tiled() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &f, 12000, cudaEnableDefault,
+                                         &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(f);
+  });
+  return fn;
+}
+
+template <int D>
+int batch_smem_attr() {
+  return cuda_status(cudaFuncSetAttribute(mla_batch_kernel<D>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          BLayout<D>::kSmem));
+}
+
+// Enables the batched route for fp16 banks of dim 64/128/256 whose rows all
+// have norm >= kBMinNorm (or are non-finite); other banks batch by looping the
+// single-query scan.
+int setup_batch(grm_b200_mla_bank* b) {
+  b->batch = false;
+  if (b->dtype != GRM_B200_F16 || !(b->dim == 64 || b->dim == 128 || b->dim == 256) ||
+      b->nodes >= ((int64_t)1 << 31) || (reinterpret_cast<uintptr_t>(b->d_rows) & 15) != 0)
+    return 0;
+  EncodeTiledFn enc = encode_tiled();
+  if (!enc) return 0;
+  const cuuint64_t dims[2] = {(cuuint64_t)b->dim, (cuuint64_t)b->nodes};
+  const cuuint64_t strides[1] = {(cuuint64_t)b->dim * 2};
+  const cuuint32_t box[2] = {64, (cuuint32_t)kBM};
+  const cuuint32_t estr[2] = {1, 1};
+  if (enc(&b->tmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, b->d_rows, dims, strides, box, estr,
+          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return 0;
+  int rc = b->dim == 64 ? batch_smem_attr<64>() : b->dim == 128 ? batch_smem_attr<128>()
+                                                                 : batch_smem_attr<256>();
+  if (rc) return b->err.set(rc, "batched route setup failed");
+  const size_t qbytes = (size_t)(b->dim / 64) * kBMq * 128;
+  cudaError_t e = cudaMalloc(&b->d_qmat, qbytes);
+  if (e == cudaSuccess) e = cudaMemsetAsync(b->d_qmat, 0, qbytes, b->stream);  // zero query rows
+  if (e == cudaSuccess) e = cudaMalloc(&b->d_rnorms, sizeof(float) * (size_t)b->nodes);
+  if (e == cudaSuccess) {
+    const int grid = (int)std::min<int64_t>(ceil_div64(b->nodes, 256), 148 * 8);
+    batch_rnorm_kernel<<<grid, 256, 0, b->stream>>>(b->d_norms, b->nodes, b->d_rnorms);
+    e = cudaGetLastError();
+  }
+  if (e == cudaSuccess) e = cudaStreamSynchronize(b->stream);
+  if (e != cudaSuccess) return b->err.set(cuda_status(e), "batched route setup failed");
+  b->batch = true;
+  return 0;
+}
+
+cudaLaunchConfig_t pdl_config(dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                              cudaLaunchAttribute* attr) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cfg;
+}
+
+// Prep, scan and per-query merge of up to kBQ queries (p.queries / p.results /
+// p.out_* / p.scratch already offset to the chunk).  Statuses other than kOk
+// are resolved by the exact kernel launched after it.
+template <int D>
+int launch_batch_chunk(grm_b200_mla_bank* b, const Params<__half>& p, int nq, cudaStream_t s) {
+  batch_prep_kernel<D><<<kBQ, 32, 0, s>>>(p.queries, nq, b->d_qmat, p.scratch);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_status(e);
+  BatchParams bp;
+  bp.tmap = b->tmap;
+  bp.qmat = b->d_qmat;
+  bp.rnorms = b->d_rnorms;
+  bp.nodes = b->nodes;
+  bp.tiles = ceil_div64(b->nodes, kBM);
+  bp.nq = nq;
+  bp.topk = p.topk;
+  bp.scratch = p.scratch;
+  const int grid = (int)std::min<int64_t>(b->grid_x, bp.tiles);
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = pdl_config(dim3(grid), dim3(kBThreads), BLayout<D>::kSmem, s, attr);
+  e = cudaLaunchKernelEx(&cfg, mla_batch_kernel<D>, bp);
+  if (e != cudaSuccess) return cuda_status(e);
+  cfg = pdl_config(dim3(nq), dim3(kBMergeWarps * 32), 0, s, attr);
+  e = cudaLaunchKernelEx(&cfg, mla_batch_merge_kernel<D>, p);
+  return cuda_status(e);
+}
+
+int launch_batch(grm_b200_mla_bank* b, const Params<__half>& p0, int nq, cudaStream_t s) {
+  for (int c0 = 0; c0 < nq; c0 += kBQ) {
+    const int n = std::min(kBQ, nq - c0);
+    Params<__half> p = p0;
+    p.queries = p0.queries + (int64_t)c0 * b->dim;
+    p.results = p0.results + c0;
+    p.scratch.base = p0.scratch.base + p0.scratch.stride * (size_t)c0;
+    if (p0.out_ids) p.out_ids = p0.out_ids + (int64_t)c0 * p0.topk;
+    if (p0.out_scores) p.out_scores = p0.out_scores + (int64_t)c0 * p0.topk;
+    const int rc = b->dim == 64    ? launch_batch_chunk<64>(b, p, n, s)
+                   : b->dim == 128 ? launch_batch_chunk<128>(b, p, n, s)
+                                   : launch_batch_chunk<256>(b, p, n, s);
+    if (rc) return rc;
+  }
+  return 0;
+}
+
 // Route `nq` queries synchronously into b->h_results[0..nq).  The queries are
 // device memory (dq), or one host query carried inline in the launch
 // parameters (dq == nullptr, q_host != nullptr).  Results are written by the
@@ -1317,7 +1465,13 @@ int run_chunk(grm_b200_mla_bank* b, const float* dq, const float* q_host, int nq
   Params<T> p = make_params<T>(b, dq, topk);
   p.results = b->d_results_mapped;
   if (!dq) std::memcpy(p.qinline, q_host, sizeof(float) * (size_t)b->dim);
-  int rc = launch_scan<T>(b, p, nq, b->stream);
+  int rc;
+  if constexpr (sizeof(T) == 2) {
+    rc = (b->batch && dq && nq >= kBatchMin) ? launch_batch(b, p, nq, b->stream)
+                                             : launch_scan<T>(b, p, nq, b->stream);
+  } else {
+    rc = launch_scan<T>(b, p, nq, b->stream);
+  }
   if (rc) return b->err.set(rc, "MLA scan launch failed: %s", cudaGetErrorString(cudaGetLastError()));
   bool need_exact = b->exact_only;
   if (!b->exact_only) {
@@ -1387,9 +1541,9 @@ int bank_finish_create(grm_b200_mla_bank* b) {
   if (e == cudaSuccess)
     e = cudaMemsetAsync(b->d_fallbacks, 0, sizeof(unsigned long long), b->stream);
   if (e != cudaSuccess) return cuda_status(e);
-  unsigned* d_special = nullptr;
-  e = cudaMalloc(&d_special, sizeof(unsigned));
-  if (e == cudaSuccess) e = cudaMemsetAsync(d_special, 0, sizeof(unsigned), b->stream);
+  unsigned* d_special = nullptr;  // [0] rows outside the fast path, [1] outside the batch path
+  e = cudaMalloc(&d_special, 2 * sizeof(unsigned));
+  if (e == cudaSuccess) e = cudaMemsetAsync(d_special, 0, 2 * sizeof(unsigned), b->stream);
   if (e != cudaSuccess) return cuda_status(e);
   DeviceInfo info;
   int rc = device_info(b->device, &info);
@@ -1401,16 +1555,17 @@ int bank_finish_create(grm_b200_mla_bank* b) {
   else
     row_norms_kernel<float><<<grid, 256, 0, b->stream>>>(static_cast<const float*>(b->d_rows),
                                                          b->nodes, b->dim, b->d_norms, d_special);
-  unsigned special = 0;
+  unsigned special[2] = {0, 0};
   e = cudaGetLastError();
   if (e == cudaSuccess)
-    e = cudaMemcpyAsync(&special, d_special, sizeof(unsigned), cudaMemcpyDeviceToHost, b->stream);
+    e = cudaMemcpyAsync(special, d_special, 2 * sizeof(unsigned), cudaMemcpyDeviceToHost, b->stream);
   if (e == cudaSuccess) e = cudaStreamSynchronize(b->stream);
   cudaFree(d_special);
   if (e != cudaSuccess) return cuda_status(e);
-  b->exact_only = !fast_dim(b->dim) || special > 0;
+  b->exact_only = !fast_dim(b->dim) || special[0] > 0;
   rc = pick_grid(b);
   if (rc) return rc;
+  if (!b->exact_only && special[1] == 0 && (rc = setup_batch(b))) return rc;
   return reserve(b, 8);
 }
 
@@ -1421,6 +1576,8 @@ void bank_free(grm_b200_mla_bank* b) {
   if (b->d_rows) cudaFree(b->d_rows);
   if (b->d_norms) cudaFree(b->d_norms);
   if (b->d_fallbacks) cudaFree(b->d_fallbacks);
+  if (b->d_qmat) cudaFree(b->d_qmat);
+  if (b->d_rnorms) cudaFree(b->d_rnorms);
   if (b->d_scratch) cudaFree(b->d_scratch);
   if (b->d_results) cudaFree(b->d_results);
   if (b->h_results) cudaFreeHost(b->h_results);
@@ -1549,7 +1706,9 @@ int route_async_phases(grm_b200_mla_bank* bank, const float* queries_device, int
     p.out_ids = out_ids_device;
     p.out_scores = out_scores_device;
     p.id_offset = id_offset;
-    if (phase & 1) rc = launch_scan<__half>(bank, p, query_count, s, true);
+    if (phase & 1)
+      rc = (bank->batch && query_count >= kBatchMin) ? launch_batch(bank, p, query_count, s)
+                                                     : launch_scan<__half>(bank, p, query_count, s, true);
     if (!rc && (phase & 2)) rc = launch_exact<__half>(bank, p, query_count, s, true);
   } else {
     Params<float> p = make_params<float>(bank, queries_device, topk);
@@ -1607,6 +1766,13 @@ const char* grm_b200_mla_last_error(grm_b200_mla_bank* bank) {
 
 const float* grm_b200_mla_row_norms_device(grm_b200_mla_bank* bank) {
   return bank ? bank->d_norms : nullptr;
+}
+
+int grm_b200_mla_paths(grm_b200_mla_bank* bank, int* flags) {
+  if (!bank || !flags) return GRM_B200_EINVAL;
+  *flags = (bank->bulk ? GRM_B200_PATH_BULK : 0) | (bank->batch ? GRM_B200_PATH_BATCH : 0) |
+           (bank->exact_only ? GRM_B200_PATH_EXACT : 0);
+  return 0;
 }
 
 int grm_b200_mla_stats(grm_b200_mla_bank* bank, uint64_t* routes, uint64_t* fallbacks) {

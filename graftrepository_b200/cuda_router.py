@@ -283,6 +283,14 @@ class CudaMLARouteBank:
                    self._err)
         return int(a.value), int(b.value)
 
+    def paths(self) -> dict:
+        """Which kernels serve this bank: bulk single-query scan, tensor-core
+        batch route, or the exact kernel only."""
+        f = ctypes.c_int(0)
+        _lib.check(_lib.load().grm_b200_mla_paths(self._h, ctypes.byref(f)), self._err)
+        return {"bulk": bool(f.value & 1), "batch": bool(f.value & 2),
+                "exact_only": bool(f.value & 4)}
+
 
 class CudaMLARouteSidecar:
     """core/grm_cuda_router.py:344-405.  ``build`` loads (building in-tree if

@@ -132,6 +132,13 @@ const float* grm_b200_mla_row_norms_device(grm_b200_mla_bank* bank);
  * in flight on other streams may not be counted yet. */
 int grm_b200_mla_stats(grm_b200_mla_bank* bank, uint64_t* routes, uint64_t* fallbacks);
 
+/* Which kernels serve this bank (no reference counterpart; for tests and
+ * diagnostics): GRM_B200_PATH_* bits. */
+#define GRM_B200_PATH_BULK 1   /* single queries: bulk-copy streaming scan */
+#define GRM_B200_PATH_BATCH 2  /* batches of >= 2 queries: tensor-core route */
+#define GRM_B200_PATH_EXACT 4  /* bank outside the fast path: exact kernel only */
+int grm_b200_mla_paths(grm_b200_mla_bank* bank, int* flags);
+
 /* Allocation-free MLA route.  No counterpart in the reference.  For callers
  * that must not allocate device memory on the route path -- an engine that owns
  * all of HBM through its own pool, a route issued during CUDA-graph capture, a
