@@ -2,13 +2,14 @@
 //
 // Included by mla_route.cu inside namespace grm_b200::mla.  A batch of up to
 // kBQ queries reads the bank once: the approximate scores are the product
-// Qs x bank^T, computed with tcgen05.mma (M = 128 query rows of which the first
-// kBQ are the batch and the rest zero, N = 128 bank rows, K = 16 per
-// instruction, fp16 operands, fp32 accumulators in tensor memory), so a
-// 64-query batch costs one pass over HBM instead of 64.  Queries on the M side
-// put one query in each tensor-memory lane: an epilogue thread reads its
-// query's scores for consecutive bank rows and filters them against its own
-// threshold in registers.
+// Qs x bank^T, computed with tcgen05.mma (M = 128 query rows: the kBQ queries
+// twice, N = 128 bank rows, K = 16 per instruction, fp16 operands, fp32
+// accumulators in tensor memory), so a 64-query batch costs one pass over HBM
+// instead of 64.  Queries on the M side put one query in each tensor-memory
+// lane: an epilogue thread reads its query's scores for consecutive bank rows
+// and filters them against its own threshold in registers.  The second copy
+// of the queries fills tensor-memory lanes 64..127, so all four lane quarters
+// -- and the warps of all four scheduler partitions -- share the epilogue.
 //
 // Operands.  The bank tile is loaded by TMA (2D tensor map, 128-byte swizzle,
 // box 64 elements x 128 rows, one box per 128-byte K atom) into a ring of
@@ -18,15 +19,13 @@
 // and copied into shared memory with one bulk copy.
 //
 // Roles (one CTA per SM, persistent over 128-row tiles b, b + grid, ...):
-//   warps 0, 1, 4, 5   epilogue: warp w reads tensor-memory lanes 32*(w % 4)..
-//                      (32 queries, one per thread) and 64 of the tile's 128
-//                      bank rows; each thread keeps its query's sorted top-32
-//                      in registers (inserts are per thread: no warp traffic).
-//   warp 2, one lane   TMA producer (bounded waits on the stage ring)
-//   warp 3             tensor-memory allocation; one lane issues the MMAs
-// (tensor-memory lanes 64..127 hold the zero query rows and are not read.)
-// Six warps keep two per scheduler partition at most, so an epilogue thread
-// may use up to 255 registers.
+//   warps 0..7         epilogue: warp w reads tensor-memory lanes 32*(w % 4)..
+//                      (32 queries, one per thread) and one quarter (32) of
+//                      the tile's 128 bank rows; each thread keeps its query's
+//                      sorted top-16 in registers (inserts are per thread: no
+//                      warp traffic).  Batches ask for top-k <= 16.
+//   warp 8, one lane   TMA producer (bounded waits on the stage ring)
+//   warp 9             tensor-memory allocation; one lane issues the MMAs
 // Two 128-column accumulator buffers let the MMAs of tile i+1 run while the
 // epilogue reads tile i.
 //
@@ -51,14 +50,16 @@
 namespace grm_b200 {
 namespace mla {
 
-constexpr int kBQ = 64;                    // queries per launch (of the MMA's M = 128 rows)
-constexpr int kBMq = 128;                  // MMA M: query rows (kBQ..127 are zero)
+constexpr int kBQ = 64;                    // queries per launch
+constexpr int kBMq = 128;                  // MMA M: the kBQ queries, twice
 constexpr int kBM = 128;                   // bank rows per tile (MMA N)
 constexpr int kBStages = 4;                // shared-memory stages
-constexpr int kBEpi = 4;                   // epilogue warps (0, 1, 4, 5)
-constexpr int kBThreads = 6 * 32;
-constexpr int kBProducerWarp = 2;
-constexpr int kBMmaWarp = 3;
+constexpr int kBEpi = 8;                   // epilogue warps 0..7
+constexpr int kBThreads = 10 * 32;
+constexpr int kBProducerWarp = 8;
+constexpr int kBMmaWarp = 9;
+constexpr int kBList = 16;                 // per-thread list capacity: top-k <= 16
+constexpr int kBMaxTopk = kBList;
 constexpr int kBMergeWarps = 12;           // warps of the per-query merge kernel
 constexpr float kBMargin = 0.00390625f;    // 2^-8
 constexpr float kBQScale = 256.0f;         // 2^8
@@ -75,7 +76,7 @@ struct BLayout {
   static constexpr int kAtomQ = kBMq * 128;            // 16 KB: 128 query rows x 64 halves
   static constexpr int kStage = SA * kAtomT;
   static constexpr int kQ = KA * kAtomQ;
-  static constexpr int kMerge = kBQ * 2 * 32 * 8;      // end-of-scan list exchange
+  static constexpr int kMerge = kBQ * 4 * 32 * 8;      // end-of-scan list exchange
   static constexpr int kSmem = 1024 + kQ + kBStages * kStage;  // + alignment slack
   static_assert(D % 64 == 0 && D <= 256, "batched dims: 64, 128, 256");
   static_assert(kMerge <= kBStages * kStage, "the list exchange reuses the stages");
@@ -181,23 +182,24 @@ __host__ __device__ constexpr int qmat_offset(int j, int d) {
   return (d / 64) * (kBMq * 128) + j * 128 + ((((d % 64) / 8) ^ (j % 8)) * 16) + (d % 8) * 2;
 }
 
-// A thread's sorted top-32 (score desc, id asc) in registers.  Inserting is
+// A thread's sorted top-C (score desc, id asc) in registers.  Inserting is
 // an unrolled compare-and-shift (no dynamic indexing, no warp traffic).
+template <int C>
 struct LaneList {
-  float s[32];
-  uint32_t id[32];
+  float s[C];
+  uint32_t id[C];
   __device__ __forceinline__ void init() {
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
+    for (int i = 0; i < C; ++i) {
       s[i] = -INFINITY;
       id[i] = kNoRow;
     }
   }
   // Insert (cs, cid) when it beats the last entry.
   __device__ __forceinline__ void insert(float cs, uint32_t cid) {
-    if (!better(cs, cid, s[31], id[31])) return;
+    if (!better(cs, cid, s[C - 1], id[C - 1])) return;
 #pragma unroll
-    for (int i = 31; i >= 1; --i) {
+    for (int i = C - 1; i >= 1; --i) {
       if (better(cs, cid, s[i - 1], id[i - 1])) {
         s[i] = s[i - 1];
         id[i] = id[i - 1];
@@ -211,17 +213,16 @@ struct LaneList {
       id[0] = cid;
     }
   }
-  // Score of entry k-1 (runtime 1 <= k <= 32): the list is sorted, so it is
+  // Score of entry k-1 (runtime 1 <= k <= C): the list is sorted, so it is
   // the minimum of the first k scores -- a tree reduction, which keeps the
-  // list in registers (an indexed read would move it to local memory) and
-  // needs 5 dependent steps.
+  // list in registers (an indexed read would move it to local memory).
   __device__ __forceinline__ float kth(int k) const {
-    float t[16];
+    float t[C / 2];
 #pragma unroll
-    for (int i = 0; i < 16; ++i)
+    for (int i = 0; i < C / 2; ++i)
       t[i] = fminf(2 * i < k ? s[2 * i] : INFINITY, 2 * i + 1 < k ? s[2 * i + 1] : INFINITY);
 #pragma unroll
-    for (int w = 8; w >= 1; w >>= 1)
+    for (int w = C / 4; w >= 1; w >>= 1)
 #pragma unroll
       for (int i = 0; i < w; ++i) t[i] = fminf(t[i], t[i + w]);
     return t[0];
@@ -242,10 +243,10 @@ __device__ __forceinline__ float pick32(const float (&v)[32], int c) {
 
 // ---- kernels -----------------------------------------------------------------
 
-// One warp per query row 0..kBQ-1: unit-normalise (fp64 norm), scale by 2^8,
-// round to fp16, write the swizzled image; rows past the batch are zero (rows
-// kBQ..kBMq-1 are zeroed once when the image is allocated).  Records whether
-// the query is inside the batched path's safe range.
+// One warp per query 0..kBQ-1: unit-normalise (fp64 norm), scale by 2^8,
+// round to fp16, write the swizzled image at rows j and kBQ + j; queries past
+// the batch are zero.  Records whether the query is inside the batched path's
+// safe range.
 template <int D>
 __global__ void __launch_bounds__(32) batch_prep_kernel(const float* queries, int nq,
                                                         unsigned char* qmat, Scratch scratch) {
@@ -263,8 +264,9 @@ __global__ void __launch_bounds__(32) batch_prep_kernel(const float* queries, in
     inv = safe ? (float)(1.0 / qn) : 0.0f;
   }
   for (int d = lane; d < D; d += 32) {
-    const float v = safe ? queries[(int64_t)j * D + d] * inv * kBQScale : 0.0f;
-    *reinterpret_cast<__half*>(qmat + qmat_offset(j, d)) = __float2half_rn(v);
+    const __half h = __float2half_rn(safe ? queries[(int64_t)j * D + d] * inv * kBQScale : 0.0f);
+    *reinterpret_cast<__half*>(qmat + qmat_offset(j, d)) = h;
+    *reinterpret_cast<__half*>(qmat + qmat_offset(kBQ + j, d)) = h;  // second copy
   }
   if (j < nq && lane == 0) scratch.hdr(j)->qsafe = safe ? 1 : 0;
 }
@@ -295,11 +297,14 @@ __global__ void __launch_bounds__(kBThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t my_tiles =
       (int64_t)blockIdx.x < p.tiles ? (p.tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
-  // epilogue warps 0, 1, 4, 5: lane quarter lq (queries 32*lq + lane), column half ch
-  const bool epi = warp == 0 || warp == 1 || warp == 4 || warp == 5;
+  // epilogue warps 0..7: tensor-memory lane quarter lq holds queries
+  // 32*(lq & 1) + lane (quarters 2, 3: the second copy); the warp takes the
+  // tile's bank rows 32*cq .. 32*cq + 31
+  constexpr int C = kBList;
+  const bool epi = warp < kBEpi;
   const int lq = warp & 3;
-  const int ch = warp >= 4 ? 1 : 0;
-  const int qi = lq * 32 + lane;  // this thread's query
+  const int cq = (warp >> 2) * 2 + (lq >> 1);
+  const int qi = (lq & 1) * 32 + lane;  // this thread's query
 
   // The query image comes from batch_prep_kernel (programmatic dependent launch).
   asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -403,23 +408,20 @@ __global__ void __launch_bounds__(kBThreads, 1)
       if (!ok) atomicOr(&sh_fail, 1);
     }
   } else if (epi) {
-    LaneList L;
+    LaneList<C> L;
     L.init();
     bool done_all = true;
     const float m2 = 2.0f * kBMargin;
     const bool active = qi < p.nq;
-    // max(entry 31, entry k-1 - 2*margin): rows below never enter
+    // max(last entry, entry k-1 - 2*margin): rows below never enter
     float thr = active ? -INFINITY : INFINITY;
-    // 2^-8 / norm of the warp's 64 rows of a tile, lane l holding rows l and
-    // 32 + l (NaN past the bank), loaded one tile ahead.
-    auto load_rn = [&](int64_t i, float& a, float& b2) {
-      const int64_t r = ((int64_t)blockIdx.x + i * gridDim.x) * kBM + ch * 64 + lane;
-      a = (i < my_tiles && r < p.nodes) ? __ldg(p.rnorms + r) : __int_as_float(0x7FC00000);
-      b2 = (i < my_tiles && r + 32 < p.nodes) ? __ldg(p.rnorms + r + 32)
-                                               : __int_as_float(0x7FC00000);
+    // 2^-8 / norm of the warp's 32 rows of a tile, lane l holding row l (NaN
+    // past the bank), loaded one tile ahead.
+    auto load_rn = [&](int64_t i) -> float {
+      const int64_t r = ((int64_t)blockIdx.x + i * gridDim.x) * kBM + cq * 32 + lane;
+      return (i < my_tiles && r < p.nodes) ? __ldg(p.rnorms + r) : __int_as_float(0x7FC00000);
     };
-    float rn0, rn1;
-    load_rn(0, rn0, rn1);
+    float rn = load_rn(0);
     // The query's header slot lb collects every CTA's k-th approximate score
     // (a lower bound of the final k-th best); it is read one tile ahead.
     int* const lbq = &p.scratch.hdr(active ? qi : 0)->lb;
@@ -427,9 +429,8 @@ __global__ void __launch_bounds__(kBThreads, 1)
     for (int64_t i = 0; i < my_tiles; ++i) {
       const int b = (int)(i & 1);
       const unsigned u = (unsigned)(i >> 1);
-      const int64_t row0 = ((int64_t)blockIdx.x + i * gridDim.x) * kBM + ch * 64;
-      float nx0, nx1;
-      load_rn(i + 1, nx0, nx1);
+      const int64_t row0 = ((int64_t)blockIdx.x + i * gridDim.x) * kBM + cq * 32;
+      const float rn_next = load_rn(i + 1);
       const int lb_next = active ? __ldcg(lbq) : kOrderedNegInf;
       if (!mbar_wait(&tfull[b], u & 1u, kWaitLimit)) {
         if (lane == 0) atomicOr(&sh_fail, 1);
@@ -437,55 +438,47 @@ __global__ void __launch_bounds__(kBThreads, 1)
         break;
       }
       tc_fence_after();
-      uint32_t v[64];
-      const uint32_t ta = tmem + ((uint32_t)(lq * 32) << 16) + (uint32_t)(b * kBM + ch * 64);
-      tmem_ld32_nowait(ta, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
-      tmem_ld32_nowait(ta + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
+      uint32_t v[32];
+      tmem_ld32_nowait(tmem + ((uint32_t)(lq * 32) << 16) + (uint32_t)(b * kBM + cq * 32), v);
       tmem_wait_ld();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[b]);
+      // hot path: scores and a bit per row that reaches the threshold (the
+      // shuffles run in every lane; lanes past the batch have thr = +inf)
+      float sc[32];
+      uint32_t mask = 0;
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const float rn = h == 0 ? rn0 : rn1;
-        // hot path: scores and a bit per row that reaches the threshold (the
-        // shuffles run in every lane; lanes past the batch have thr = +inf)
-        float sc[32];
-        uint32_t mask = 0;
-#pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          sc[c] = __uint_as_float(v[h * 32 + c]) * __shfl_sync(kFull, rn, c);
-          mask |= (sc[c] >= thr ? 1u : 0u) << c;
-        }
-        // rare path, rolled so the insert is inlined once
+      for (int c = 0; c < 32; ++c) {
+        sc[c] = __uint_as_float(v[c]) * __shfl_sync(kFull, rn, c);
+        mask |= (sc[c] >= thr ? 1u : 0u) << c;
+      }
+      // rare path, rolled so the insert is inlined once
 #pragma unroll 1
-        while (mask) {
-          const int c = __ffs(mask) - 1;
-          mask &= mask - 1;
-          const float x = pick32(sc, c);
-          if (x >= thr) {
-            L.insert(x, (uint32_t)(row0 + h * 32 + c));
-            const float kt = L.kth(p.topk);
-            thr = fmaxf(thr, fmaxf(L.s[31], kt - m2));
-            if (kt > kpub) {  // share this query's k-th score with every CTA
-              kpub = kt;
-              atomicMax(lbq, float_to_ordered(kt));
-            }
+      while (mask) {
+        const int c = __ffs(mask) - 1;
+        mask &= mask - 1;
+        const float x = pick32(sc, c);
+        if (x >= thr) {
+          L.insert(x, (uint32_t)(row0 + c));
+          const float kt = L.kth(p.topk);
+          thr = fmaxf(thr, fmaxf(L.s[C - 1], kt - m2));
+          if (kt > kpub) {  // share this query's k-th score with every CTA
+            kpub = kt;
+            atomicMax(lbq, float_to_ordered(kt));
           }
         }
       }
       // every CTA's k-th score for this query bounds its final k-th from below
-      const int g = lb_next;
-      if (g != kOrderedNegInf) thr = fmaxf(thr, ordered_to_float(g) - m2);
-      rn0 = nx0;
-      rn1 = nx1;
+      if (lb_next != kOrderedNegInf) thr = fmaxf(thr, ordered_to_float(lb_next) - m2);
+      rn = rn_next;
     }
     // This warp saw the last tile: every MMA has completed and every stage
     // load was consumed, so the stage buffers are free for the list exchange.
     if (done_all && active) {
-      Entry* e = reinterpret_cast<Entry*>(smT) + (qi * 2 + ch) * 32;
+      Entry* e = reinterpret_cast<Entry*>(smT) + (qi * 4 + cq) * 32;
 #pragma unroll
-      for (int j = 0; j < 32; ++j) e[j] = Entry{L.s[j], L.id[j]};
+      for (int j = 0; j < 32; ++j) e[j] = j < C ? Entry{L.s[j], L.id[j]} : Entry{-INFINITY, kNoRow};
     }
   }
   __syncwarp();
@@ -503,7 +496,7 @@ __global__ void __launch_bounds__(kBThreads, 1)
   }
   asm volatile("griddepcontrol.launch_dependents;");
 
-  // Per-query block lists: each query's two column-half lists were written to
+  // Per-query block lists: each query's four row-quarter lists were written to
   // shared memory by the epilogue; one warp per query merges them and appends
   // its entries as scan_finish does.
   Entry* const mrg = reinterpret_cast<Entry*>(smT);
@@ -514,15 +507,25 @@ __global__ void __launch_bounds__(kBThreads, 1)
       if (lane == 0) atomicOr(&hdr->err, 1);
       continue;
     }
-    const Entry* e = mrg + q * 2 * 32;
-    const float k0 = e[p.topk - 1].s, k1 = e[32 + p.topk - 1].s;
-    const int best = k1 > k0 ? 1 : 0;
-    float floor = fmaxf(e[31].s, e[32 + 31].s);
+    const Entry* e = mrg + q * 4 * 32;
+    float kbest = -INFINITY, floor = -INFINITY;
+    int best = 0;
+#pragma unroll 1
+    for (int w = 0; w < 4; ++w) {
+      const float kw = e[w * 32 + p.topk - 1].s;
+      if (kw > kbest) {
+        kbest = kw;
+        best = w;
+      }
+      floor = fmaxf(floor, e[w * 32 + C - 1].s);
+    }
     WarpList m;
     m.s = e[best * 32 + lane].s;
     m.id = e[best * 32 + lane].id;
-    m.offer_margin(e[(1 - best) * 32 + lane].s, e[(1 - best) * 32 + lane].id, lane, p.topk,
-                   2.0f * kBMargin);
+#pragma unroll 1
+    for (int w = 0; w < 4; ++w)
+      if (w != best)
+        m.offer_margin(e[w * 32 + lane].s, e[w * 32 + lane].id, lane, p.topk, 2.0f * kBMargin);
     const float kth = __shfl_sync(kFull, m.s, p.topk - 1);
     const float wthr = isfinite(kth) ? kth - 2.0f * kBMargin : -INFINITY;
     floor = fmaxf(floor, __shfl_sync(kFull, m.s, 31));

@@ -37,7 +37,7 @@ constexpr int kWarps = kThreads / 32;
 constexpr float kMargin = 1.52587890625e-05f;  // 2^-16
 constexpr double kSafeLo = 1.0e-20, kSafeHi = 1.0e20;
 constexpr int kInlineMax = 512;  // largest dim a query can travel inline
-constexpr int kBatchMin = 2;     // batches from this size on take the tensor-core route
+constexpr int kBatchMin = 2;     // batches from this size on (top-k <= 16) take the tensor-core route
 
 enum Status : int { kOk = 0, kOverflow = 1, kUnsafe = 2, kError = 3 };
 
@@ -1467,8 +1467,9 @@ int run_chunk(grm_b200_mla_bank* b, const float* dq, const float* q_host, int nq
   if (!dq) std::memcpy(p.qinline, q_host, sizeof(float) * (size_t)b->dim);
   int rc;
   if constexpr (sizeof(T) == 2) {
-    rc = (b->batch && dq && nq >= kBatchMin) ? launch_batch(b, p, nq, b->stream)
-                                             : launch_scan<T>(b, p, nq, b->stream);
+    rc = (b->batch && dq && nq >= kBatchMin && topk <= kBMaxTopk)
+             ? launch_batch(b, p, nq, b->stream)
+             : launch_scan<T>(b, p, nq, b->stream);
   } else {
     rc = launch_scan<T>(b, p, nq, b->stream);
   }
@@ -1707,8 +1708,9 @@ int route_async_phases(grm_b200_mla_bank* bank, const float* queries_device, int
     p.out_scores = out_scores_device;
     p.id_offset = id_offset;
     if (phase & 1)
-      rc = (bank->batch && query_count >= kBatchMin) ? launch_batch(bank, p, query_count, s)
-                                                     : launch_scan<__half>(bank, p, query_count, s, true);
+      rc = (bank->batch && query_count >= kBatchMin && topk <= kBMaxTopk)
+               ? launch_batch(bank, p, query_count, s)
+               : launch_scan<__half>(bank, p, query_count, s, true);
     if (!rc && (phase & 2)) rc = launch_exact<__half>(bank, p, query_count, s, true);
   } else {
     Params<float> p = make_params<float>(bank, queries_device, topk);

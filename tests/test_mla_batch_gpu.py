@@ -1,7 +1,8 @@
-"""Batched MLA route (tensor-core path) parity on the GPU, through the C ABI,
-against the CPU oracle: ids and scores bit-exact for batches of 2..130 queries,
-including chunking past 64 queries, queries outside the batch path's safe range,
-margin-saturating ties, banks that cannot be batched and the async entry."""
+"""Batched MLA route (tensor-core path, top-k <= 16) parity on the GPU, through
+the C ABI, against the CPU oracle: ids and scores bit-exact for batches of
+2..130 queries, including chunking past 64 queries, queries outside the batch
+path's safe range, margin-saturating ties, banks that cannot be batched and the
+async entry."""
 
 import numpy as np
 import pytest
@@ -96,18 +97,22 @@ def test_small_norm_rows_disable_the_batch_path(sidecar):
     bank.close()
 
 
-def test_batch_nan_rows_and_sentinels(sidecar):
-    rows = synth.mla_bank(36, 40).astype(np.float32)
+@pytest.mark.parametrize("n,k,valid", [(40, 32, 32), (12, 16, 10)])
+def test_batch_nan_rows_and_sentinels(sidecar, n, k, valid):
+    """k <= 16 runs on the tensor-core path, k = 32 loops the single-query scan."""
+    rows = synth.mla_bank(36, n).astype(np.float32)
     rows[3, 1] = np.nan
     rows[9, 0] = np.inf
     qs = synth.mla_queries(37, 3)
     bank = sidecar.create_bank(rows)
     assert bank.paths()["batch"]
-    ids, _ = raw_route(bank, qs, 32)
+    ids, scores = raw_route(bank, qs, k)
     for i, q in enumerate(qs):
-        want, _ = O.mla_route(rows, q, 32)
+        want, want_s = O.mla_route(rows, q, k)
         assert np.array_equal(ids[i], want)
-        assert np.sum(ids[i] != U64MAX) == 32
+        assert np.sum(ids[i] != U64MAX) == valid
+        fin = want != U64MAX
+        assert np.array_equal(scores[i][fin], want_s[fin])
     bank.close()
 
 
