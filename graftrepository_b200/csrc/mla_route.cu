@@ -107,6 +107,7 @@ struct Params {
   float* out_scores;
   uint64_t id_offset;
   int force_all;         // exact kernel: score every row (bank outside the fast path)
+  int nq;                // exact kernel: queries in this launch
   unsigned long long* fallback_count;  // queries that took the exact pass (optional)
   // A single query may travel inside the launch parameters (queries == nullptr):
   // the synchronous host entry then needs no host-to-device copy.
@@ -904,47 +905,40 @@ __global__ void __launch_bounds__(kBulkWarps * 32, 1)
   scan_finish<D, T, false, NW>(p, list, safe, q, lane, warp, fsm);
 }
 
-// Exact fallback: for each query whose approximate pass reported kOverflow,
-// compute exact scores for every row whose approximate score reaches the
-// threshold; for kUnsafe (or force_all) compute exact scores for all rows.
-// Queries whose status is kOk exit at once.  D == 0 means runtime dim
-// (force_all only).  INL: row norms computed inline (see mla_scan_kernel).
-template <int D, typename T, bool INL = false>
-__global__ void __launch_bounds__(kThreads) mla_exact_kernel(const __grid_constant__ Params<T> p) {
-  __shared__ float sh_s[kWarps * 32];
-  __shared__ uint32_t sh_id[kWarps * 32];
-  __shared__ double sh_qnorm;
-  __shared__ float sh_eq;
-  __shared__ int sh_mode;
-  __shared__ int sh_last;
-  constexpr int DMAX = D > 0 ? D : 1;
-  __shared__ float sh_q[DMAX];
+constexpr int kExactQ = 64;  // queries per block row of the exact kernel
 
-  // Launched with programmatic dependent launch after the scan: wait until the
-  // scan grid has completed and its writes are visible (no-op otherwise).
-  // The next route's scan may then be scheduled; it waits for this grid in turn.
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-  asm volatile("griddepcontrol.launch_dependents;");
-  const int q = blockIdx.y;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+// Shared memory of the exact pass.
+template <int D>
+struct ExactSmem {
+  float s[kWarps * 32];
+  uint32_t id[kWarps * 32];
+  float q[D > 0 ? D : 1];
+  double qnorm;
+  float eq;
+  int last;
+  int work[kExactQ];
+  int nwork;
+};
+
+// The exact pass of one query (every thread of the block calls it).  kOverflow:
+// exact scores for every row whose approximate score reaches the threshold;
+// kUnsafe (or force_all): exact scores for every row.
+template <int D, typename T, bool INL>
+__device__ __forceinline__ void exact_one(const Params<T>& p, int q, int lane, int warp,
+                                          ExactSmem<D>& sm) {
   const int dim = D > 0 ? D : p.dim;
   const float* query = query_ptr(p, q, dim);
   Result* r = p.results + q;
-
+  __syncthreads();  // sm is reused from the previous query
   if (threadIdx.x == 0) {
-    const int st = p.force_all ? (int)kUnsafe : __ldcg(&r->status);
-    sh_mode = st;
-    if (st != kOk && blockIdx.x == 0 && p.fallback_count) atomicAdd(p.fallback_count, 1ull);
-    if (st != kOk) {
-      const double qn = query_norm_seq(query, dim);
-      sh_qnorm = qn;
-      sh_eq = (float)(1.0e-8 / qn);
-    }
+    const double qn = query_norm_seq(query, dim);
+    sm.qnorm = qn;
+    sm.eq = (float)(1.0e-8 / qn);
+    if (blockIdx.x == 0 && p.fallback_count) atomicAdd(p.fallback_count, 1ull);
   }
   __syncthreads();
-  const int mode = sh_mode;
-  if (mode == kOk || mode == kError) return;
-  const double qnorm = sh_qnorm;
+  const int mode = p.force_all ? (int)kUnsafe : __ldcg(&r->status);
+  const double qnorm = sm.qnorm;
 
   WarpList list;
   list.init();
@@ -972,10 +966,10 @@ __global__ void __launch_bounds__(kThreads) mla_exact_kernel(const __grid_consta
     constexpr int CPL = CPR >= 32 ? CPR / 32 : 1;
     constexpr int SLOTS = L;
     const float thr = __ldcg(&r->thr);
-    const float e_q = sh_eq;
+    const float e_q = sm.eq;
     if (warp == 0) {
       const float inv = (float)(1.0 / qnorm);
-      for (int d = lane; d < D; d += 32) sh_q[d] = query[d] * inv;
+      for (int d = lane; d < D; d += 32) sm.q[d] = query[d] * inv;
     }
     __syncthreads();
     float qr[CPL * E];
@@ -983,7 +977,7 @@ __global__ void __launch_bounds__(kThreads) mla_exact_kernel(const __grid_consta
     for (int i = 0; i < CPL; ++i) {
       const int c = (CPR >= 32) ? lane + 32 * i : lane % L;
 #pragma unroll
-      for (int e = 0; e < E; ++e) qr[i * E + e] = sh_q[c * E + e];
+      for (int e = 0; e < E; ++e) qr[i * E + e] = sm.q[c * E + e];
     }
     const int64_t groups = ceil_div64(p.nodes, 32);
     for (int64_t g = (int64_t)blockIdx.x * kWarps + warp; g < groups;
@@ -1029,7 +1023,7 @@ __global__ void __launch_bounds__(kThreads) mla_exact_kernel(const __grid_consta
     }
   }
 
-  block_merge(list, lane, warp, sh_s, sh_id);
+  block_merge(list, lane, warp, sm.s, sm.id);
   Header* hdr = p.scratch.hdr(q);
   if (warp == 0) {
     const bool keep = lane < p.topk && isfinite(list.s);
@@ -1040,11 +1034,11 @@ __global__ void __launch_bounds__(kThreads) mla_exact_kernel(const __grid_consta
       p.scratch.counts(q)[blockIdx.x] = cnt;
       __threadfence();
       const unsigned ticket = atomicAdd(&hdr->done, 1u);
-      sh_last = (ticket == gridDim.x - 1);
+      sm.last = (ticket == gridDim.x - 1);
     }
   }
   __syncthreads();
-  if (!sh_last) return;
+  if (!sm.last) return;
   __threadfence();
   list.init();
   for (int b = warp; b < (int)gridDim.x; b += kWarps) {
@@ -1058,14 +1052,42 @@ __global__ void __launch_bounds__(kThreads) mla_exact_kernel(const __grid_consta
     }
     list.offer(s, id, lane);
   }
-  __syncthreads();
-  block_merge(list, lane, warp, sh_s, sh_id);
-  if (warp != 0) return;
-  write_result(p, q, list, lane);
-  if (lane == 0) {  // the scan's final merge already reset the rest of the header
-    hdr->lb = kOrderedNegInf;
-    hdr->done = 0;
+  block_merge(list, lane, warp, sm.s, sm.id);
+  if (warp == 0) {
+    write_result(p, q, list, lane);
+    if (lane == 0) {  // the scan's final merge already reset the rest of the header
+      hdr->lb = kOrderedNegInf;
+      hdr->done = 0;
+    }
   }
+}
+
+// Exact fallback (the resolve phase after every scan).  Block row y covers
+// queries [64y, 64y + 64): the block reads their statuses in one pass and
+// runs exact_one for those whose approximate pass reported kOverflow or
+// kUnsafe (all of them under force_all); queries with kOk (or kError) cost
+// nothing more.  D == 0 means runtime dim (force_all only).  INL: row norms
+// computed inline (see mla_scan_kernel).
+template <int D, typename T, bool INL = false>
+__global__ void __launch_bounds__(kThreads) mla_exact_kernel(const __grid_constant__ Params<T> p) {
+  __shared__ ExactSmem<D> sm;
+  // Launched with programmatic dependent launch after the scan: wait until the
+  // scan grid has completed and its writes are visible (no-op otherwise).
+  // The next route's scan may then be scheduled; it waits for this grid in turn.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;");
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int q0 = (int)blockIdx.y * kExactQ;
+  const int nq = min(kExactQ, p.nq - q0);
+  if (threadIdx.x == 0) sm.nwork = 0;
+  __syncthreads();
+  for (int t = threadIdx.x; t < nq; t += blockDim.x) {
+    const int st = p.force_all ? (int)kUnsafe : __ldcg(&p.results[q0 + t].status);
+    if (st == kOverflow || st == kUnsafe) sm.work[atomicAdd(&sm.nwork, 1)] = q0 + t;
+  }
+  __syncthreads();
+  const int nwork = sm.nwork;
+  for (int w = 0; w < nwork; ++w) exact_one<D, T, INL>(p, sm.work[w], lane, warp, sm);
 }
 
 template <typename T>
@@ -1272,6 +1294,7 @@ Params<T> make_params(grm_b200_mla_bank* b, const float* dq, int topk) {
   p.out_scores = nullptr;
   p.id_offset = 0;
   p.force_all = b->exact_only ? 1 : 0;
+  p.nq = 0;
   p.fallback_count = b->d_fallbacks;
   return p;
 }
@@ -1312,9 +1335,11 @@ int launch_scan(grm_b200_mla_bank* b, const Params<T>& p, int nq, cudaStream_t s
 // pdl: launch as a programmatic dependent of the preceding scan on `s`, so the
 // launch overlaps the scan's tail instead of following it.
 template <typename T>
-int launch_exact(grm_b200_mla_bank* b, const Params<T>& p, int nq, cudaStream_t s,
+int launch_exact(grm_b200_mla_bank* b, const Params<T>& p0, int nq, cudaStream_t s,
                  bool pdl = false) {
-  dim3 grid(b->grid_x, nq);
+  Params<T> p = p0;
+  p.nq = nq;
+  dim3 grid(b->grid_x, (unsigned)ceil_div64(nq, kExactQ));
   auto fn = exact_fn<T>(b->exact_only ? 0 : b->dim);
   if (!pdl || b->exact_only) {
     fn<<<grid, kThreads, 0, s>>>(p);
@@ -1947,13 +1972,15 @@ extern "C" int grm_b200_mla_route_noalloc(const void* rows_device, int64_t nodes
   p.out_scores = out_scores_device;
   p.id_offset = 0;
   p.force_all = 0;
+  p.nq = query_count;
   p.fallback_count = nullptr;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   scratch_init_kernel<<<(query_count + 127) / 128, 128, 0, s>>>(base + results_bytes, stride,
                                                                  query_count);
   dim3 grid(grid_x, query_count);
   scan_fn_inline(dim)<<<grid, kThreads, 0, s>>>(p);
-  exact_fn_inline(dim)<<<grid, kThreads, 0, s>>>(p);
+  exact_fn_inline(dim)<<<dim3(grid_x, (unsigned)ceil_div64(query_count, kExactQ)), kThreads, 0,
+                         s>>>(p);
   e = cudaGetLastError();
   if (e != cudaSuccess) {
     set_thread_error("allocation-free MLA route launch failed: %s", cudaGetErrorString(e));
