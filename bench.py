@@ -60,6 +60,9 @@ def parse():
     p.add_argument("--warmup", type=int, default=20)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--gqa-prefix-gb", type=float, default=150.0,
+                   help="gqa_100k on one GPU: size of the resident node prefix (the whole "
+                        "216.5 GB bank does not fit one B200)")
     p.add_argument("--workload", default="mla_1m_b1",
                    choices=["mla_1m_b1", "mla_1m_b64", "gqa_512", "gqa_100k", "mount_int4",
                             "mount_int6", "mount_int8", "mount_ref8"],
@@ -269,16 +272,22 @@ def run_ours(args):
     n_q = min(args.warmup + args.steps, 4096 // B)
     qs_host = torch.from_numpy(synth.mla_queries(1, n_q * B)).pin_memory()
     qs_dev = qs_host.cuda()
-    out_s = torch.empty((B, TOPK), dtype=torch.float32, device="cuda")
-    out_i = torch.empty((B, TOPK), dtype=torch.int64, device="cuda")
+    # route results go straight into one packed block per rank (ids, scores,
+    # padding: 16 B per entry), so the exchange is a single all-gather
+    n_out = B * TOPK
+    blk = torch.empty(16 * n_out, dtype=torch.uint8, device="cuda")
+    out_i = blk[:8 * n_out].view(torch.int64).view(B, TOPK)
+    out_s = blk[8 * n_out:12 * n_out].view(torch.float32).view(B, TOPK)
+    gblk = torch.empty(world * 16 * n_out, dtype=torch.uint8, device="cuda")
+    gv = gblk.view(world, 16 * n_out)
     shard_bytes = (b - a) * DIM * 2
     flush = None
-    if shard_bytes < 4 * L2_BYTES:
+    if shard_bytes <= L2_BYTES:   # a shard larger than L2 cannot stay resident between steps
         flush = torch.empty(2 * L2_BYTES, dtype=torch.uint8, device="cuda")
     stream = torch.cuda.current_stream()
     sptr = stream.cuda_stream
-    gs = torch.empty((world, B, TOPK), dtype=torch.float32, device="cuda")
-    gi = torch.empty((world, B, TOPK), dtype=torch.int64, device="cuda")
+    gi = gv[:, :8 * n_out].view(torch.int64)
+    gs = gv[:, 8 * n_out:12 * n_out].view(torch.float32)
     ms_s = torch.empty((B, TOPK), dtype=torch.float32, device="cuda")
     ms_i = torch.empty((B, TOPK), dtype=torch.int64, device="cuda")
 
@@ -295,10 +304,10 @@ def run_ours(args):
         rc = lib.grm_b200_mla_route_async(bank._h, q.data_ptr(), B, TOPK, a, out_i.data_ptr(),
                                           out_s.data_ptr(), sptr)
         if world > 1:
-            dist.all_gather_into_tensor(gs.view(world * B, TOPK), out_s)
-            dist.all_gather_into_tensor(gi.view(world * B, TOPK), out_i)
-            rc |= lib.grm_b200_merge_topk(gs.data_ptr(), gi.data_ptr(), B, world, TOPK, TOPK,
-                                          ms_s.data_ptr(), ms_i.data_ptr(), sptr)
+            dist.all_gather_into_tensor(gblk, blk)
+            rc |= lib.grm_b200_merge_topk_strided(gs.data_ptr(), gs.stride(0), gi.data_ptr(),
+                                                  gi.stride(0), B, world, TOPK, TOPK,
+                                                  ms_s.data_ptr(), ms_i.data_ptr(), sptr)
         if ev:
             ev[1].record(stream)
         if rc:
@@ -427,7 +436,7 @@ def run_ours(args):
         "config": {"workload": args.workload, "nodes": NODES, "dim": DIM, "topk": TOPK, "batch": B,
                    "bank_dtype": "fp16", "shard_nodes": b - a,
                    "parallelism": f"node-sharded x{world}" if world > 1 else "single GPU",
-                   "l2": ("bank shard larger than 4x L2, no flush" if flush is None else
+                   "l2": ("bank shard larger than L2, no flush" if flush is None else
                           "256 MB L2 flush before every step, outside the timed events")},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "peak_kind": peak_kind,
@@ -498,7 +507,7 @@ def run_gqa(args):
     a, b = gqa_shard_range(off_all, world, rank)
     prefix_note = None
     if world == 1 and args.workload == "gqa_100k":
-        cap_tokens = int(150e9 // (KH * D * 2))           # largest resident prefix: 150 GB
+        cap_tokens = int(args.gqa_prefix_gb * 1e9 // (KH * D * 2))  # resident prefix
         b = int(np.searchsorted(off_all, cap_tokens, side="right")) - 1
         prefix_note = f"resident prefix of {b} of 100000 nodes ({int(off_all[b])} tokens)"
     sub_len = lengths[a:b]
@@ -512,10 +521,12 @@ def run_gqa(args):
     qs_host = torch.from_numpy(synth.gqa_query(seed, count=n_q)).pin_memory()
     qs_dev = qs_host.cuda()
     k = TOPK
-    out_s = torch.empty((1, k), dtype=torch.float32, device="cuda")
-    out_i = torch.empty((1, k), dtype=torch.int64, device="cuda")
-    gs = torch.empty((world, k), dtype=torch.float32, device="cuda")
-    gi = torch.empty((world, k), dtype=torch.int64, device="cuda")
+    blk = torch.empty(16 * k, dtype=torch.uint8, device="cuda")   # ids, scores, padding
+    out_i = blk[:8 * k].view(torch.int64).view(1, k)
+    out_s = blk[8 * k:12 * k].view(torch.float32).view(1, k)
+    gblk = torch.empty(world * 16 * k, dtype=torch.uint8, device="cuda")
+    gi = gblk.view(world, 16 * k)[:, :8 * k].view(torch.int64)
+    gs = gblk.view(world, 16 * k)[:, 8 * k:12 * k].view(torch.float32)
     ms_s = torch.empty((1, k), dtype=torch.float32, device="cuda")
     ms_i = torch.empty((1, k), dtype=torch.int64, device="cuda")
     stream = torch.cuda.current_stream()
@@ -525,10 +536,10 @@ def run_gqa(args):
         rc = lib.grm_b200_gqa_route_async(bank._h, qs_dev[i].data_ptr(), 1, H, 1, k, a,
                                           out_i.data_ptr(), out_s.data_ptr(), stream.cuda_stream)
         if world > 1:
-            dist.all_gather_into_tensor(gs, out_s.view(-1))
-            dist.all_gather_into_tensor(gi, out_i.view(-1))
-            rc |= lib.grm_b200_merge_topk(gs.data_ptr(), gi.data_ptr(), 1, world, k, k,
-                                          ms_s.data_ptr(), ms_i.data_ptr(), stream.cuda_stream)
+            dist.all_gather_into_tensor(gblk, blk)
+            rc |= lib.grm_b200_merge_topk_strided(gs.data_ptr(), gs.stride(0), gi.data_ptr(),
+                                                  gi.stride(0), 1, world, k, k, ms_s.data_ptr(),
+                                                  ms_i.data_ptr(), stream.cuda_stream)
         if rc:
             raise RuntimeError(bank._err())
 
@@ -569,10 +580,10 @@ def run_gqa(args):
             qbuf.copy_(qs_host[(args.warmup + i) % n_q], non_blocking=True)
             lib.grm_b200_gqa_route_async(bank._h, qbuf.data_ptr(), 1, H, 1, k, a,
                                          out_i.data_ptr(), out_s.data_ptr(), stream.cuda_stream)
-            dist.all_gather_into_tensor(gs, out_s.view(-1))
-            dist.all_gather_into_tensor(gi, out_i.view(-1))
-            lib.grm_b200_merge_topk(gs.data_ptr(), gi.data_ptr(), 1, world, k, k,
-                                    ms_s.data_ptr(), ms_i.data_ptr(), stream.cuda_stream)
+            dist.all_gather_into_tensor(gblk, blk)
+            lib.grm_b200_merge_topk_strided(gs.data_ptr(), gs.stride(0), gi.data_ptr(),
+                                            gi.stride(0), 1, world, k, k, ms_s.data_ptr(),
+                                            ms_i.data_ptr(), stream.cuda_stream)
             ms_i.cpu(), ms_s.cpu()
         e2e_s = time.perf_counter() - t0
         t = torch.tensor([e2e_s], dtype=torch.float64, device="cuda")

@@ -39,8 +39,9 @@ int device_info(int device, DeviceInfo* out) {
 // Merge `lists` sorted-or-unsorted candidate lists per query into the best
 // `topk` (score desc, id asc; non-finite and UINT64_MAX entries dropped).
 // One warp per query; ids are 64-bit global node rows here.
-__global__ void merge_topk_kernel(const float* scores, const uint64_t* ids, int queries, int lists,
-                                  int per_list, int topk, float* out_scores, uint64_t* out_ids) {
+__global__ void merge_topk_kernel(const float* scores, const uint64_t* ids, int64_t sstride,
+                                  int64_t istride, int queries, int lists, int per_list, int topk,
+                                  float* out_scores, uint64_t* out_ids) {
   const int q = blockIdx.x;
   const int lane = threadIdx.x;
   if (q >= queries) return;
@@ -54,8 +55,8 @@ __global__ void merge_topk_kernel(const float* scores, const uint64_t* ids, int 
     uint64_t cid = UINT64_MAX;
     if (i < n) {
       const int l = i / per_list, j = i % per_list;
-      cs = scores[((int64_t)l * queries + q) * per_list + j];
-      cid = ids[((int64_t)l * queries + q) * per_list + j];
+      cs = scores[l * sstride + (int64_t)q * per_list + j];
+      cid = ids[l * istride + (int64_t)q * per_list + j];
       if (cid == UINT64_MAX) cs = -INFINITY;
     }
     auto better64 = [](float sa, uint64_t ia, float sb, uint64_t ib) {
@@ -125,22 +126,34 @@ int grm_b200_free_device_ptr(void* device) {
   return cuda_status(cudaFree(device));
 }
 
-int grm_b200_merge_topk(const float* scores_device, const uint64_t* ids_device, int queries,
-                        int lists, int per_list, int topk, float* out_scores_device,
-                        uint64_t* out_ids_device, void* stream) {
+int grm_b200_merge_topk_strided(const float* scores_device, int64_t scores_list_stride,
+                                const uint64_t* ids_device, int64_t ids_list_stride, int queries,
+                                int lists, int per_list, int topk, float* out_scores_device,
+                                uint64_t* out_ids_device, void* stream) {
   if (!scores_device || !ids_device || !out_scores_device || !out_ids_device || queries <= 0 ||
-      lists <= 0 || per_list <= 0 || topk <= 0 || topk > GRM_B200_MAX_TOPK) {
+      lists <= 0 || per_list <= 0 || topk <= 0 || topk > GRM_B200_MAX_TOPK ||
+      scores_list_stride < (int64_t)queries * per_list ||
+      ids_list_stride < (int64_t)queries * per_list) {
     set_thread_error("invalid merge_topk arguments");
     return GRM_B200_EINVAL;
   }
   merge_topk_kernel<<<queries, 32, 0, static_cast<cudaStream_t>(stream)>>>(
-      scores_device, ids_device, queries, lists, per_list, topk, out_scores_device, out_ids_device);
+      scores_device, ids_device, scores_list_stride, ids_list_stride, queries, lists, per_list,
+      topk, out_scores_device, out_ids_device);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     set_thread_error("merge_topk launch failed: %s", cudaGetErrorString(e));
     return cuda_status(e);
   }
   return 0;
+}
+
+int grm_b200_merge_topk(const float* scores_device, const uint64_t* ids_device, int queries,
+                        int lists, int per_list, int topk, float* out_scores_device,
+                        uint64_t* out_ids_device, void* stream) {
+  const int64_t stride = (int64_t)queries * per_list;
+  return grm_b200_merge_topk_strided(scores_device, stride, ids_device, stride, queries, lists,
+                                     per_list, topk, out_scores_device, out_ids_device, stream);
 }
 
 }  // extern "C"

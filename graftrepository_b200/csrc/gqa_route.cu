@@ -190,6 +190,7 @@ struct RouteParams {
   int topk;
   int fast;                    // 1 = approximate pass available for this bank
   Result* result;
+  unsigned long long* refined_total;  // nodes recomputed exactly, all routes (device counter)
   int qt4;                     // reference query_tokens == 4 path
   uint64_t* out_ids;           // optional device outputs (topk entries of this query)
   float* out_scores;
@@ -623,6 +624,7 @@ __global__ void finalize_kernel(RouteParams p) {
   if (lane == 0) {
     p.result->count = __popc(m);
     p.result->cands = count;
+    if (p.refined_total) atomicAdd(p.refined_total, (unsigned long long)count);
     *p.cand_count = 0;
   }
 }
@@ -670,7 +672,8 @@ struct grm_b200_gqa_bank {
   cudaEvent_t ev0 = nullptr, ev1 = nullptr;
   std::mutex mu;
   ErrorSlot err;
-  uint64_t routes = 0, refined = 0;
+  uint64_t routes = 0;
+  unsigned long long* d_refined = nullptr;  // counted by finalize_kernel
 };
 
 namespace {
@@ -812,6 +815,7 @@ int route_one(grm_b200_gqa_bank* b, const float* dq, int heads, int qt, int topk
   p.topk = topk;
   p.fast = fast ? 1 : 0;
   p.result = b->d_result;
+  p.refined_total = b->d_refined;
   p.qt4 = (qt == 4) ? 1 : 0;
   p.out_ids = out_ids;
   p.out_scores = out_scores;
@@ -865,7 +869,6 @@ int route_device_queries(grm_b200_gqa_bank* b, const float* dq, int qc, int head
     e = cudaMemcpyAsync(b->h_result, b->d_result, sizeof(Result), cudaMemcpyDeviceToHost, b->stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(b->stream);
     if (e != cudaSuccess) return b->err.set(cuda_status(e), "GQA route failed: %s", cudaGetErrorString(e));
-    b->refined += (uint64_t)b->h_result->cands;
     for (int j = 0; j < topk; ++j) {
       out_ids[(int64_t)i * topk + j] = b->h_result->ids[j];
       if (out_scores) out_scores[(int64_t)i * topk + j] = b->h_result->scores[j];
@@ -888,7 +891,7 @@ void bank_free(grm_b200_gqa_bank* b) {
   if (b->owns_keys && b->d_keys) cudaFree(b->d_keys);
   void* ptrs[] = {b->d_off, b->d_items, b->d_kmax, b->d_key_bad, b->d_headmax, b->d_lo, b->d_hi,
                   b->d_cand, b->d_cand_count, b->d_frag, b->d_qnorm, b->d_qinfo, b->d_result,
-                  b->d_queries, b->d_qparts, b->d_qcount};
+                  b->d_queries, b->d_qparts, b->d_qcount, b->d_refined};
   for (void* q : ptrs)
     if (q) cudaFree(q);
   if (b->h_result) cudaFreeHost(b->h_result);
@@ -921,6 +924,9 @@ int finish_create(grm_b200_gqa_bank* b) {
   if (e == cudaSuccess) e = cudaMemsetAsync(b->d_qcount, 0, sizeof(unsigned), b->stream);
   if (e == cudaSuccess) e = cudaMalloc(&b->d_result, sizeof(Result));
   if (e == cudaSuccess) e = cudaMallocHost(&b->h_result, sizeof(Result));
+  if (e == cudaSuccess) e = cudaMalloc(&b->d_refined, sizeof(unsigned long long));
+  if (e == cudaSuccess)
+    e = cudaMemsetAsync(b->d_refined, 0, sizeof(unsigned long long), b->stream);
   if (e != cudaSuccess) return cuda_status(e);
   DeviceInfo info;
   int rc = device_info(b->device, &info);
@@ -1140,8 +1146,15 @@ const char* grm_b200_gqa_last_error(grm_b200_gqa_bank* bank) {
 
 int grm_b200_gqa_stats(grm_b200_gqa_bank* bank, uint64_t* routes, uint64_t* refined_nodes) {
   if (!bank) return GRM_B200_EINVAL;
+  std::lock_guard<std::mutex> lock(bank->mu);
   if (routes) *routes = bank->routes;
-  if (refined_nodes) *refined_nodes = bank->refined;
+  if (refined_nodes) {
+    unsigned long long n = 0;
+    cudaError_t e = cudaSetDevice(bank->device);
+    if (e == cudaSuccess) e = cudaMemcpy(&n, bank->d_refined, sizeof(n), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return bank->err.set(cuda_status(e), "GQA stats read failed");
+    *refined_nodes = n;
+  }
   return 0;
 }
 

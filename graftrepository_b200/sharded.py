@@ -67,13 +67,19 @@ def merge_topk_host(scores: np.ndarray, ids: np.ndarray, k: int) -> tuple[np.nda
 
 
 class ShardedRoute:
-    """Local route -> all-gather of (score, global row) candidates -> merge.
+    """Local route -> one all-gather of (score, global row) candidates -> merge.
 
-    ``local_route(queries) -> (scores [Q, k] float32, ids [Q, k] int64)`` (torch
+    ``local_route(queries, k) -> (scores [Q, k] float32, ids [Q, k] int64)`` (torch
     tensors on the process group's device; ids already global, UINT64_MAX as
     -1 for empty slots); ``merge(gathered_scores [W, Q, k], gathered_ids) ->
-    (ids, scores)``.
+    (ids, scores)`` (the gathered views may be strided along W).  Scores and
+    ids of a rank travel in one packed block of 16 bytes per entry (ids, then
+    scores, then padding), so a route costs a single collective.  Subclasses
+    may set ``local_into(queries, k, scores_out, ids_out)`` to write straight
+    into the block.
     """
+
+    local_into = None
 
     def __init__(self, group, local_route: Callable, merge: Callable):
         import torch.distributed as dist
@@ -88,18 +94,26 @@ class ShardedRoute:
     def route(self, queries, k: int):
         import torch
 
-        scores, ids = self.local_route(queries, k)
-        Q = scores.shape[0]
-        # output concatenated on dim 0 ([W*Q, k]) is accepted by every backend
-        gs = torch.empty((self.world * Q, k), dtype=scores.dtype, device=scores.device)
-        gi = torch.empty((self.world * Q, k), dtype=ids.dtype, device=ids.device)
-        if self.world == 1:
-            gs.copy_(scores)
-            gi.copy_(ids)
+        Q = queries.shape[0]
+        n = Q * k
+        blk = torch.empty(16 * n, dtype=torch.uint8, device=queries.device)
+        bi = blk[:8 * n].view(torch.int64).view(Q, k)
+        bs = blk[8 * n:12 * n].view(torch.float32).view(Q, k)
+        if self.local_into is not None:
+            self.local_into(queries, k, bs, bi)
         else:
-            self.dist.all_gather_into_tensor(gs, scores.contiguous(), group=self.group)
-            self.dist.all_gather_into_tensor(gi, ids.contiguous(), group=self.group)
-        return self.merge(gs.view(self.world, Q, k), gi.view(self.world, Q, k), k)
+            scores, ids = self.local_route(queries, k)
+            bs.copy_(scores)
+            bi.copy_(ids)
+        g = torch.empty(self.world * 16 * n, dtype=torch.uint8, device=queries.device)
+        if self.world == 1:
+            g.copy_(blk)
+        else:
+            self.dist.all_gather_into_tensor(g, blk, group=self.group)
+        g2 = g.view(self.world, 16 * n)
+        gi = g2[:, :8 * n].view(torch.int64).view(self.world, Q, k)
+        gs = g2[:, 8 * n:12 * n].view(torch.float32).view(self.world, Q, k)
+        return self.merge(gs, gi, k)
 
 
 class ShardedMLARoute(ShardedRoute):
@@ -131,17 +145,21 @@ class ShardedMLARoute(ShardedRoute):
         Q = queries.shape[0]
         s = torch.empty((Q, k), dtype=torch.float32, device=queries.device)
         i = torch.empty((Q, k), dtype=torch.int64, device=queries.device)
-        self.bank.route_async(queries.data_ptr(), Q, k, i.data_ptr(), s.data_ptr(),
-                              self._stream(), self.first_row)
+        self.local_into(queries, k, s, i)
         return s, i
+
+    def local_into(self, queries, k: int, s, i):
+        self.bank.route_async(queries.data_ptr(), queries.shape[0], k, i.data_ptr(), s.data_ptr(),
+                              self._stream(), self.first_row)
 
     def _merge(self, gs, gi, k: int):
         torch = self.torch
         W, Q, P = gs.shape
         out_s = torch.empty((Q, k), dtype=torch.float32, device=gs.device)
         out_i = torch.empty((Q, k), dtype=torch.int64, device=gs.device)
-        rc = self._lib.grm_b200_merge_topk(gs.data_ptr(), gi.data_ptr(), Q, W, P, k,
-                                           out_s.data_ptr(), out_i.data_ptr(), self._stream())
+        rc = self._lib.grm_b200_merge_topk_strided(gs.data_ptr(), gs.stride(0), gi.data_ptr(),
+                                                   gi.stride(0), Q, W, P, k, out_s.data_ptr(),
+                                                   out_i.data_ptr(), self._stream())
         if rc != 0:
             raise RuntimeError("merge_topk failed")
         return out_i, out_s
@@ -177,15 +195,19 @@ class ShardedGQARoute(ShardedRoute):
     def _local(self, queries, k: int):
         """queries: device fp32 [Q, H, qt, D]."""
         torch = self.torch
-        Q, H, qt, _ = queries.shape
+        Q = queries.shape[0]
         s = torch.empty((Q, k), dtype=torch.float32, device=queries.device)
         i = torch.empty((Q, k), dtype=torch.int64, device=queries.device)
+        self.local_into(queries, k, s, i)
+        return s, i
+
+    def local_into(self, queries, k: int, s, i):
+        Q, H, qt, _ = queries.shape
         rc = self._lib.grm_b200_gqa_route_async(self.bank._h, queries.data_ptr(), Q, H, qt, k,
                                                 self.first_row, i.data_ptr(), s.data_ptr(),
                                                 self._stream())
         if rc != 0:
             raise RuntimeError(self.bank._err())
-        return s, i
 
     _merge = ShardedMLARoute._merge
 

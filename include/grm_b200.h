@@ -265,6 +265,15 @@ int grm_b200_merge_topk(const float* scores_device, const uint64_t* ids_device, 
                         int lists, int per_list, int topk, float* out_scores_device,
                         uint64_t* out_ids_device, void* stream);
 
+/* The same merge with list l's entries at scores_device + l * scores_list_stride
+ * and ids_device + l * ids_list_stride (elements; each stride >= queries *
+ * per_list), so the scores and ids of every rank can travel in one all-gather
+ * of a packed per-rank block.  No reference counterpart. */
+int grm_b200_merge_topk_strided(const float* scores_device, int64_t scores_list_stride,
+                                const uint64_t* ids_device, int64_t ids_list_stride, int queries,
+                                int lists, int per_list, int topk, float* out_scores_device,
+                                uint64_t* out_ids_device, void* stream);
+
 /* ----------------------------------------------------------------- helpers */
 
 /* Upload a host buffer to a fresh device allocation on the current device.
