@@ -33,6 +33,8 @@
 #include <type_traits>
 #include <vector>
 
+#include <cuda.h>
+
 #include "common.cuh"
 
 namespace grm_b200 {
@@ -65,7 +67,8 @@ static_assert(sizeof(Item) == 16, "one 16-byte load per item");
 struct QueryInfo {
   int finite;      // every query value finite
   int fast_ok;     // the query fits the fast path (|q| range)
-  float pad[2];
+  int err;         // a bounded device wait gave up during this route
+  float pad;
 };
 
 // ---------------------------------------------------------------- helpers
@@ -197,11 +200,19 @@ struct RouteParams {
   uint64_t id_offset;          // added to returned node rows (first row of this shard)
 };
 
+// K permutation shared by the query fragments and the scan kernels: thread
+// c (lane & 3) holds, for each key row, the 16-byte chunks w = 0 .. D/32-1 at
+// dims chunk_dim(c, w) .. +7: chunks 2c and 2c+1 of every 64-dim half.  With
+// the 128-byte swizzle of the staged key tiles, the 8 threads of a quarter
+// warp then read 8 different 16-byte bank groups.  k-step s takes halves
+// 4*(s % 2) .. +3 of chunk s / 2.
+__host__ __device__ constexpr int chunk_dim(int c, int w) { return (w / 2) * 64 + 16 * c + 8 * (w % 2); }
+
 // Query preparation, one block per kv head: hi/lo fragments in mma B layout,
 // the norms of that kv head's query heads, and the finite / range flags of
 // its query values.  The last block to finish combines the flags into
 // p.qinfo (and re-arms the counter).  K permutation: k-step s, slot (c, j)
-// <-> dim (D/4)*c + 4*s + j.
+// <-> dim chunk_dim(c, s / 2) + 4 * (s % 2) + j.
 template <typename KT, int D, int NT>
 __global__ void __launch_bounds__(128) query_prep_kernel(RouteParams p) {
   constexpr int KSTEPS = D / 16;
@@ -251,7 +262,7 @@ __global__ void __launch_bounds__(128) query_prep_kernel(RouteParams p) {
         const int lh = vi / p.qt, qi = vi % p.qt;
         const int h = kh * p.group + lh;
         const float* q = p.query + ((int64_t)h * p.qt + qi) * D;
-        const int d0 = (D / 4) * c + 4 * s;
+        const int d0 = chunk_dim(c, s / 2) + 4 * (s % 2);
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           const float x = q[d0 + j];
@@ -274,6 +285,7 @@ __global__ void __launch_bounds__(128) query_prep_kernel(RouteParams p) {
       for (int k = 0; k < (int)gridDim.x; ++k) flags |= __ldcg(p.qparts + k);
       p.qinfo->finite = !(flags & 1);
       p.qinfo->fast_ok = !flags;
+      p.qinfo->err = 0;
       *p.qcount = 0u;
     }
   }
@@ -315,7 +327,7 @@ __global__ void __launch_bounds__(kThreads) gqa_scan_kernel(RouteParams p) {
     float mx[NT][2];
 #pragma unroll
     for (int t = 0; t < NT; ++t) mx[t][0] = mx[t][1] = 0.0f;
-    // 16 key tokens x this thread's (D/4) contiguous dims of rows g and g+8:
+    // 16 key tokens x this thread's D/4 dims (chunk_dim) of rows g and g+8:
     // 8 MMAs per n-tile, then hi + lo and |.| max over the two rows.
     auto tile = [&](const uint32_t (&ra)[2 * KSTEPS], const uint32_t (&rb)[2 * KSTEPS]) {
       float acc[NT][4];
@@ -352,13 +364,14 @@ __global__ void __launch_bounds__(kThreads) gqa_scan_kernel(RouteParams p) {
     // full pairs of tiles: 4 rows x W unchecked 16-byte loads in flight per thread
     for (; tt + 32 <= tend; tt += 32) {
       uint32_t ra0[2 * KSTEPS], rb0[2 * KSTEPS], ra1[2 * KSTEPS], rb1[2 * KSTEPS];
-      const KT* p0 = base + (tt + g) * D + (D / 4) * c;
+      const KT* p0 = base + (tt + g) * D;
 #pragma unroll
       for (int w = 0; w < W; ++w) {
-        put(ra0 + 4 * w, ld_nc16(p0 + 8 * w));
-        put(rb0 + 4 * w, ld_nc16(p0 + 8 * D + 8 * w));
-        put(ra1 + 4 * w, ld_nc16(p0 + 16 * D + 8 * w));
-        put(rb1 + 4 * w, ld_nc16(p0 + 24 * D + 8 * w));
+        const int d = chunk_dim(c, w);
+        put(ra0 + 4 * w, ld_nc16(p0 + d));
+        put(rb0 + 4 * w, ld_nc16(p0 + 8 * D + d));
+        put(ra1 + 4 * w, ld_nc16(p0 + 16 * D + d));
+        put(rb1 + 4 * w, ld_nc16(p0 + 24 * D + d));
       }
       tile(ra0, rb0);
       tile(ra1, rb1);
@@ -369,8 +382,8 @@ __global__ void __launch_bounds__(kThreads) gqa_scan_kernel(RouteParams p) {
 #pragma unroll
       for (int w = 0; w < W; ++w) {
         uint4 va = make_uint4(0, 0, 0, 0), vb = make_uint4(0, 0, 0, 0);
-        if (r0 < tend) va = ld_nc16(base + r0 * D + (D / 4) * c + 8 * w);
-        if (r1 < tend) vb = ld_nc16(base + r1 * D + (D / 4) * c + 8 * w);
+        if (r0 < tend) va = ld_nc16(base + r0 * D + chunk_dim(c, w));
+        if (r1 < tend) vb = ld_nc16(base + r1 * D + chunk_dim(c, w));
         put(ra + 4 * w, va);
         put(rb + 4 * w, vb);
       }
@@ -405,6 +418,230 @@ __global__ void __launch_bounds__(kThreads) gqa_scan_kernel(RouteParams p) {
       }
     }
     (void)NVP;
+  }
+}
+
+// TMA-staged approximate pass.  The keys are viewed as one 2D tensor
+// [rows, D] (rows = every (node, kv head, token)); each of the kTmaWarps warps
+// of a CTA walks its work items (wid, wid + nw, ...) as 32-token sub-chunks
+// and streams them through two shared-memory buffers with TMA box loads
+// (64 dims x 32 rows, 128-byte swizzle, L2 evict-first), the next sub-chunk
+// always in flight.  Fragments are read from shared memory in the chunk_dim
+// permutation (conflict-free under the swizzle); the MMA and epilogue are
+// those of gqa_scan_kernel.  Rows past an item's last token (the next kv
+// head's rows, or zero fill past the tensor) are masked.  Every wait is
+// bounded: a wait that gives up drains this warp's loads and sets qinfo->err.
+constexpr int kTmaWarps = 12;
+constexpr int kSubRows = 32;
+
+template <int D>
+struct TmaLayout {
+  static constexpr int kBoxes = D / 64;
+  static constexpr int kBox = kSubRows * 128;          // 4 KB: 32 rows x 64 dims
+  static constexpr int kBuf = kBoxes * kBox;           // one sub-chunk
+  static constexpr int kSmem = 1024 + kTmaWarps * 2 * kBuf;
+};
+
+__device__ __forceinline__ void tma_load_2d_g(void* dst, const CUtensorMap* map, int x, int y,
+                                              uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      ".L2::cache_hint [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+template <typename KT, int D, int NT>
+__global__ void __launch_bounds__(kTmaWarps * 32, 1)
+    gqa_scan_tma_kernel(const __grid_constant__ CUtensorMap tmap, RouteParams p) {
+  using LY = TmaLayout<D>;
+  constexpr int KSTEPS = D / 16;
+  constexpr int W = D / 32;
+  extern __shared__ unsigned char gsm_raw[];
+  unsigned char* const gsm = gsm_raw + ((1024u - (smem_u32(gsm_raw) & 1023u)) & 1023u);
+  __shared__ __align__(8) uint64_t bar[kTmaWarps][2];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (!p.qinfo->fast_ok) return;
+  const int g = lane >> 2, c = lane & 3;
+  if (lane == 0) {
+    mbar_init(&bar[warp][0], 1);
+    mbar_init(&bar[warp][1], 1);
+    mbar_fence_init();
+  }
+  __syncwarp();
+  unsigned char* const buf0 = gsm + warp * 2 * LY::kBuf;
+  const int64_t nw = (int64_t)gridDim.x * kTmaWarps;
+  const uint64_t pol = l2_evict_first_policy();
+
+  // the warp's sequence of sub-chunks: (item, sub) in item order
+  struct Pos {
+    int64_t it;
+    int sub;
+    uint64_t row;   // tensor row of the sub-chunk's first token
+    int ntok;       // tokens of the item
+  };
+  auto item_at = [&](int64_t it, Pos& ps) {
+    ps.it = it;
+    ps.sub = 0;
+    if (it < p.n_items) {
+      const uint4 raw = __ldg(reinterpret_cast<const uint4*>(p.items + it));
+      const uint64_t base_off = (uint64_t)raw.x | ((uint64_t)raw.y << 32);
+      ps.row = base_off / D;
+      ps.ntok = (int)(raw.w >> 16);
+    } else {
+      ps.row = 0;
+      ps.ntok = 0;
+    }
+  };
+  auto advance = [&](Pos& ps) {
+    if ((ps.sub + 1) * kSubRows < ps.ntok) {
+      ++ps.sub;
+    } else {
+      item_at(ps.it + nw, ps);
+    }
+  };
+  auto issue = [&](const Pos& ps, int b) {  // lane 0
+    unsigned char* dst = buf0 + b * LY::kBuf;
+    mbar_arrive_expect_tx(&bar[warp][b], LY::kBuf);
+    const int y = (int)(ps.row + (uint64_t)ps.sub * kSubRows);
+#pragma unroll
+    for (int x = 0; x < LY::kBoxes; ++x)
+      tma_load_2d_g(dst + x * LY::kBox, &tmap, 64 * x, y, &bar[warp][b], pol);
+  };
+
+  Pos cur, nxt;
+  item_at((int64_t)blockIdx.x * kTmaWarps + warp, cur);
+  nxt = cur;
+  advance(nxt);
+  unsigned phase_bits = 0u, pending_bits = 0u;
+  if (cur.it < p.n_items) {
+    if (lane == 0) issue(cur, 0);
+    pending_bits |= 1u;
+    if (nxt.it < p.n_items) {
+      if (lane == 0) issue(nxt, 1);
+      pending_bits |= 2u;
+    }
+  }
+  bool failed = false;
+  int b = 0;
+  uint32_t bq[NT][2 * KSTEPS];
+  float mx[NT][2];
+  int64_t item_node = 0;
+  int item_kh = 0;
+  while (cur.it < p.n_items) {
+    if (cur.sub == 0) {  // a new item: its kv head's query fragments, fresh maxima
+      const uint4 raw = __ldg(reinterpret_cast<const uint4*>(p.items + cur.it));
+      item_node = (int64_t)raw.z;
+      item_kh = (int)(raw.w & 0xFFFF);
+      const uint32_t* fsrc = p.frag + ((int64_t)item_kh * NT * 32 + lane) * (2 * KSTEPS);
+#pragma unroll
+      for (int t = 0; t < NT; ++t)
+#pragma unroll
+        for (int w = 0; w < 2 * KSTEPS; ++w)
+          bq[t][w] = __ldg(fsrc + (int64_t)t * 32 * 2 * KSTEPS + w);
+#pragma unroll
+      for (int t = 0; t < NT; ++t) mx[t][0] = mx[t][1] = 0.0f;
+    }
+    if (!mbar_wait(&bar[warp][b], (phase_bits >> b) & 1u, kWaitLimit)) {
+      failed = true;
+      break;
+    }
+    phase_bits ^= 1u << b;
+    pending_bits &= ~(1u << b);
+    const unsigned char* sb = buf0 + b * LY::kBuf;
+    const int valid = min(kSubRows, cur.ntok - cur.sub * kSubRows);
+    // two 16-row tiles of this sub-chunk
+#pragma unroll
+    for (int tl = 0; tl < 2; ++tl) {
+      uint32_t ra[2 * KSTEPS], rb[2 * KSTEPS];
+      const int r0 = tl * 16 + g, r1 = r0 + 8;
+#pragma unroll
+      for (int w = 0; w < W; ++w) {
+        const int box = w / 2, chunk = 2 * c + (w % 2);
+        const uint4 va = *reinterpret_cast<const uint4*>(
+            sb + box * LY::kBox + r0 * 128 + ((chunk ^ (r0 & 7)) * 16));
+        const uint4 vb = *reinterpret_cast<const uint4*>(
+            sb + box * LY::kBox + r1 * 128 + ((chunk ^ (r1 & 7)) * 16));
+        const uint4 z = make_uint4(0, 0, 0, 0);
+        const uint4 a = r0 < valid ? va : z;
+        const uint4 bb = r1 < valid ? vb : z;
+        ra[4 * w] = a.x; ra[4 * w + 1] = a.y; ra[4 * w + 2] = a.z; ra[4 * w + 3] = a.w;
+        rb[4 * w] = bb.x; rb[4 * w + 1] = bb.y; rb[4 * w + 2] = bb.z; rb[4 * w + 3] = bb.w;
+      }
+      float acc[NT][4];
+#pragma unroll
+      for (int t = 0; t < NT; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.0f;
+#pragma unroll
+      for (int s2 = 0; s2 < KSTEPS; ++s2) {
+        const uint32_t a[4] = {ra[2 * s2], rb[2 * s2], ra[2 * s2 + 1], rb[2 * s2 + 1]};
+#pragma unroll
+        for (int t = 0; t < NT; ++t) mma16816<KT>(acc[t], a, bq[t][2 * s2], bq[t][2 * s2 + 1]);
+      }
+      if constexpr (NT == 1) {
+        float o[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) o[j] = acc[0][j] + __shfl_xor_sync(kFull, acc[0][j], 2);
+        mx[0][0] = fmaxf(mx[0][0], fmaxf(fabsf(o[0]), fabsf(o[2])));
+        mx[0][1] = fmaxf(mx[0][1], fmaxf(fabsf(o[1]), fabsf(o[3])));
+      } else {
+#pragma unroll
+        for (int t = 0; t < NT / 2; ++t) {
+          const float o0 = acc[t][0] + acc[t + NT / 2][0];
+          const float o1 = acc[t][1] + acc[t + NT / 2][1];
+          const float o2 = acc[t][2] + acc[t + NT / 2][2];
+          const float o3 = acc[t][3] + acc[t + NT / 2][3];
+          mx[t][0] = fmaxf(mx[t][0], fmaxf(fabsf(o0), fabsf(o2)));
+          mx[t][1] = fmaxf(mx[t][1], fmaxf(fabsf(o1), fabsf(o3)));
+        }
+      }
+    }
+    // buffer b is read: start the sub-chunk after nxt in it
+    __syncwarp();
+    fence_proxy_async_smem();
+    Pos after = nxt;
+    advance(after);
+    if (after.it < p.n_items) {
+      if (lane == 0) issue(after, b);
+      pending_bits |= 1u << b;
+    }
+    const bool item_done = (cur.sub + 1) * kSubRows >= cur.ntok;
+    if (item_done) {  // max across the 8 row groups, then one atomic per (node, head)
+#pragma unroll
+      for (int t = 0; t < NT; ++t)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          float v = mx[t][e];
+          v = fmaxf(v, __shfl_xor_sync(kFull, v, 4));
+          v = fmaxf(v, __shfl_xor_sync(kFull, v, 8));
+          v = fmaxf(v, __shfl_xor_sync(kFull, v, 16));
+          mx[t][e] = v;
+        }
+      if (g == 0) {
+        const int tiles = (NT == 1) ? 1 : NT / 2;
+        const int cmax = (NT == 1) ? 2 : 4;
+        if (c < cmax) {
+#pragma unroll
+          for (int t = 0; t < tiles; ++t)
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const int vi = t * 8 + 2 * c + e;
+              if (vi < p.nv) {
+                const int h = item_kh * p.group + vi / p.qt;
+                atomicMax(p.headmax + item_node * p.heads + h,
+                          __float_as_uint(mx[t][e] * p.inv_denom));
+              }
+            }
+        }
+      }
+    }
+    cur = nxt;
+    nxt = after;
+    b ^= 1;
+  }
+  if (failed) {
+    for (int k = 0; k < 2; ++k)
+      if ((pending_bits >> k) & 1u) mbar_wait(&bar[warp][k], (phase_bits >> k) & 1u, kWaitLimit);
+    if (lane == 0) atomicOr(&p.qinfo->err, 1);
   }
 }
 
@@ -611,7 +848,8 @@ __global__ void finalize_kernel(RouteParams p) {
     }
     list.offer(score, node, lane);
   }
-  const bool ok = lane < p.topk && isfinite(list.s) && list.id != kNoRow;
+  const bool failed = p.qinfo->err != 0;  // a bounded wait of the scan gave up
+  const bool ok = !failed && lane < p.topk && isfinite(list.s) && list.id != kNoRow;
   const unsigned m = __ballot_sync(kFull, ok);
   if (lane < p.topk) {
     const uint64_t id = ok ? (uint64_t)list.id + p.id_offset : UINT64_MAX;
@@ -622,7 +860,7 @@ __global__ void finalize_kernel(RouteParams p) {
     if (p.out_scores) p.out_scores[lane] = sc;
   }
   if (lane == 0) {
-    p.result->count = __popc(m);
+    p.result->count = failed ? -1 : __popc(m);
     p.result->cands = count;
     if (p.refined_total) atomicAdd(p.refined_total, (unsigned long long)count);
     *p.cand_count = 0;
@@ -667,6 +905,9 @@ struct grm_b200_gqa_bank {
   float* d_queries = nullptr;
   size_t dq_cap = 0;
   int grid_scan = 1;
+  bool tma = false;          // scan with gqa_scan_tma_kernel
+  int grid_tma = 1;
+  CUtensorMap tmap;          // keys as a 2D tensor [rows, dim]
   int sms = 1;
   cudaStream_t stream = nullptr;
   cudaEvent_t ev0 = nullptr, ev1 = nullptr;
@@ -687,8 +928,74 @@ int nt_for(int nv) { return nv <= 4 ? 1 : (nv <= 8 ? 2 : (nv <= 16 ? 4 : 0)); }
 template <typename KT, int D, int NT>
 void launch_fast(grm_b200_gqa_bank* b, const RouteParams& p) {
   query_prep_kernel<KT, D, NT><<<b->kh_n, 128, 0, b->stream>>>(p);
-  if (b->n_items > 0)
+  if (b->n_items <= 0) return;
+  if (b->tma)
+    gqa_scan_tma_kernel<KT, D, NT>
+        <<<b->grid_tma, kTmaWarps * 32, TmaLayout<D>::kSmem, b->stream>>>(b->tmap, p);
+  else
     gqa_scan_kernel<KT, D, NT><<<b->grid_scan, kThreads, 0, b->stream>>>(p);
+}
+
+template <typename KT, int D>
+cudaError_t tma_smem_attr() {
+  cudaError_t e = cudaSuccess;
+  for (auto fn : {gqa_scan_tma_kernel<KT, D, 1>, gqa_scan_tma_kernel<KT, D, 2>,
+                  gqa_scan_tma_kernel<KT, D, 4>})
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               TmaLayout<D>::kSmem);
+  return e;
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_tiled_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &f, 12000, cudaEnableDefault,
+                                         &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(f);
+  });
+  return fn;
+}
+
+// The TMA-staged scan for 16-bit banks of dim 64/128 whose row count fits a
+// tensor-map coordinate; otherwise the direct-load scan stays in use.
+int setup_tma(grm_b200_gqa_bank* b, int sms) {
+  b->tma = false;
+  if (!(b->dtype == GRM_B200_BF16 || b->dtype == GRM_B200_F16) ||
+      !(b->dim == 64 || b->dim == 128) || b->n_items <= 0)
+    return 0;
+  const uint64_t rows = b->h_off[b->nodes] * (uint64_t)b->kh_n;
+  if (rows >= ((uint64_t)1 << 31) || (reinterpret_cast<uintptr_t>(b->d_keys) & 15) != 0) return 0;
+  EncodeTiledFn enc = encode_tiled_fn();
+  if (!enc) return 0;
+  const cuuint64_t dims[2] = {(cuuint64_t)b->dim, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)b->dim * 2};
+  const cuuint32_t box[2] = {64, (cuuint32_t)kSubRows};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUtensorMapDataType dt =
+      b->dtype == GRM_B200_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  if (enc(&b->tmap, dt, 2, b->d_keys, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return 0;
+  cudaError_t e;
+  if (b->dtype == GRM_B200_BF16)
+    e = b->dim == 128 ? tma_smem_attr<__nv_bfloat16, 128>() : tma_smem_attr<__nv_bfloat16, 64>();
+  else
+    e = b->dim == 128 ? tma_smem_attr<__half, 128>() : tma_smem_attr<__half, 64>();
+  if (e != cudaSuccess) return cuda_status(e);
+  b->grid_tma = (int)std::max<int64_t>(1, std::min<int64_t>(sms, ceil_div64(b->n_items, kTmaWarps)));
+  b->tma = true;
+  return 0;
 }
 
 template <typename KT>
@@ -869,6 +1176,8 @@ int route_device_queries(grm_b200_gqa_bank* b, const float* dq, int qc, int head
     e = cudaMemcpyAsync(b->h_result, b->d_result, sizeof(Result), cudaMemcpyDeviceToHost, b->stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(b->stream);
     if (e != cudaSuccess) return b->err.set(cuda_status(e), "GQA route failed: %s", cudaGetErrorString(e));
+    if (b->h_result->count < 0)
+      return b->err.set(GRM_B200_KERNEL_BASE + 1, "GQA scan: a bounded device wait gave up (query %d)", i);
     for (int j = 0; j < topk; ++j) {
       out_ids[(int64_t)i * topk + j] = b->h_result->ids[j];
       if (out_scores) out_scores[(int64_t)i * topk + j] = b->h_result->scores[j];
@@ -990,7 +1299,7 @@ int finish_create(grm_b200_gqa_bank* b) {
   }
   const int64_t want = ceil_div64(std::max<int64_t>(b->n_items, 1), kWarps);
   b->grid_scan = (int)std::max<int64_t>(1, std::min<int64_t>((int64_t)info.sms * std::max(occ, 1), want));
-  return 0;
+  return setup_tma(b, info.sms);
 }
 
 int create_common(const void* keys, bool host, int dtype, const uint64_t* off, int64_t nodes,
@@ -1142,6 +1451,12 @@ int grm_b200_gqa_bank_destroy(grm_b200_gqa_bank* bank) {
 
 const char* grm_b200_gqa_last_error(grm_b200_gqa_bank* bank) {
   return bank ? bank->err.text.c_str() : grm_b200_last_error();
+}
+
+int grm_b200_gqa_paths(grm_b200_gqa_bank* bank, int* flags) {
+  if (!bank || !flags) return GRM_B200_EINVAL;
+  *flags = (fast_bank(bank) ? GRM_B200_GQA_PATH_FAST : 0) | (bank->tma ? GRM_B200_GQA_PATH_TMA : 0);
+  return 0;
 }
 
 int grm_b200_gqa_stats(grm_b200_gqa_bank* bank, uint64_t* routes, uint64_t* refined_nodes) {

@@ -493,6 +493,13 @@ class CudaGQARouteBank:
                    self._err)
         return int(a.value), int(b.value)
 
+    def paths(self) -> dict:
+        """Which scan serves this bank: the tensor-core approximate pass, and
+        whether its key tiles are TMA-staged."""
+        f = ctypes.c_int(0)
+        _lib.check(_lib.load().grm_b200_gqa_paths(self._h, ctypes.byref(f)), self._err)
+        return {"fast": bool(f.value & 1), "tma": bool(f.value & 2)}
+
 
 class CudaGQARouteSidecar:
     """core/grm_cuda_router.py:87-156."""

@@ -208,6 +208,12 @@ int grm_b200_gqa_bank_destroy(grm_b200_gqa_bank* bank);
 const char* grm_b200_gqa_last_error(grm_b200_gqa_bank* bank);
 int grm_b200_gqa_stats(grm_b200_gqa_bank* bank, uint64_t* routes, uint64_t* refined_nodes);
 
+/* Which scan serves this bank (no reference counterpart; for tests and
+ * diagnostics): GRM_B200_GQA_PATH_* bits. */
+#define GRM_B200_GQA_PATH_FAST 1  /* tensor-core approximate pass + exact refine */
+#define GRM_B200_GQA_PATH_TMA 2   /* ... with TMA-staged key tiles */
+int grm_b200_gqa_paths(grm_b200_gqa_bank* bank, int* flags);
+
 /* ------------------------------------------------------------------- mount */
 
 /* Fused dequantise + scatter of routed grafts into a preallocated bf16 arena

@@ -75,6 +75,7 @@ def test_random_ragged(sidecar, group, qt):
     keys, off = _ragged(group * 10 + qt, 70, kh, d, 150, zero_nodes=(3, 40), nan_node=9,
                         dup=(30, 50))
     bank = sidecar.create_bank_csr(keys, off, kh, d, dtype="bf16")
+    assert bank.paths() == {"fast": True, "tma": True}
     rng = np.random.default_rng(qt)
     qs = rng.standard_normal((3, kh * group, qt, d), dtype=np.float32)
     for k in (1, 3, 16):
