@@ -31,120 +31,129 @@ __device__ __forceinline__ uint32_t bf16x2_bits(float a, float b) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
-// Reference format: int8 codes, groups of 32, fp32 scales; output
-// bf16(fp16(code * scale)).  Grid: x strides 16-value chunks of one
-// (graft, layer) slice, y = slice.  Each thread handles kU consecutive chunks
-// with all loads issued before any store; consecutive threads write
-// consecutive 32-byte pieces, so a warp stores 1 KB contiguously.
-constexpr int kU = 2;
+// Packed format, warp tiles: a warp takes tiles of kTV values of one
+// (graft, layer) slice, loads the tile's codes with coalesced 16-byte loads
+// into its shared-memory buffer, and writes the output as 8 rounds in which
+// lane l dequantises values 256*i + 8*l .. +7, so every store instruction
+// writes 512 contiguous bytes.  The grid is persistent (SMs x 8 blocks).
+constexpr int kTV = 2048;
 
-__device__ __forceinline__ void store_bf16x16(uint16_t* dst, const float (&f)[16]) {
-  uint32_t o[8];
+template <int BITS>
+__device__ __forceinline__ void codes8(const uint32_t* sw, int v, int (&code)[8]) {
+  const int b0 = v * BITS;  // bit offset of the piece (v is a multiple of 8)
+  const int w = b0 >> 5, sh = b0 & 31;
+  const uint64_t x = (((uint64_t)sw[w + 1] << 32) | sw[w]) >> sh;
 #pragma unroll
-  for (int j = 0; j < 8; ++j) o[j] = bf16x2_bits(f[2 * j], f[2 * j + 1]);
-  reinterpret_cast<uint4*>(dst)[0] = make_uint4(o[0], o[1], o[2], o[3]);
-  reinterpret_cast<uint4*>(dst)[1] = make_uint4(o[4], o[5], o[6], o[7]);
-}
-
-__global__ void __launch_bounds__(256) mount_ref_kernel(const int8_t* __restrict__ codes,
-                                                        const float* __restrict__ scales,
-                                                        int64_t layers, int64_t vals, int64_t width,
-                                                        Seats seats, uint16_t* __restrict__ arena,
-                                                        int64_t arena_seats) {
-  const int64_t slice = blockIdx.y;
-  const int64_t g = slice / layers, l = slice - g * layers;
-  const int64_t chunks = vals / 16;
-  const int8_t* src = codes + slice * vals;
-  const float* sc = scales + slice * (vals / 32);
-  uint16_t* dst = arena + (l * arena_seats + seats.seat[g]) * width;
-  for (int64_t c0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * kU; c0 < chunks;
-       c0 += (int64_t)gridDim.x * blockDim.x * kU) {
-    uint4 v[kU];
-    float s[kU];
-#pragma unroll
-    for (int u = 0; u < kU; ++u) {
-      if (c0 + u < chunks) {
-        v[u] = ld_stream(src + (c0 + u) * 16);
-        s[u] = __ldg(sc + ((c0 + u) * 16) / 32);
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < kU; ++u) {
-      if (c0 + u >= chunks) break;
-      const int8_t* cb = reinterpret_cast<const int8_t*>(&v[u]);
-      float f[16];
-#pragma unroll
-      for (int j = 0; j < 16; ++j)  // fp16 first (dequantize_symmetric_group32), then bf16
-        f[j] = __half2float(__float2half_rn((float)cb[j] * s[u]));
-      store_bf16x16(dst + (c0 + u) * 16, f);
-    }
+  for (int j = 0; j < 8; ++j) {
+    const uint32_t c = (uint32_t)(x >> (BITS * j)) & ((1u << BITS) - 1u);
+    code[j] = (int)(c << (32 - BITS)) >> (32 - BITS);  // sign-extend
   }
 }
 
-// 16 codes of one chunk from the chunk's little-endian bit stream.
 template <int BITS>
-struct Chunk {
-  static constexpr int kWords = 16 * BITS / 32;  // 4 / 3 / 2 words
-  uint32_t w[kWords];
-  __device__ __forceinline__ void load(const uint8_t* p) {
-    if constexpr (BITS == 8) {
-      const uint4 v = ld_stream(p);
-      w[0] = v.x; w[1] = v.y; w[2] = v.z; w[3] = v.w;
-    } else if constexpr (BITS == 4) {
-      const uint2 v = __ldg(reinterpret_cast<const uint2*>(p));
-      w[0] = v.x; w[1] = v.y;
-    } else {
-      const uint32_t* q = reinterpret_cast<const uint32_t*>(p);
-      w[0] = __ldg(q); w[1] = __ldg(q + 1); w[2] = __ldg(q + 2);
-    }
-  }
-  __device__ __forceinline__ int code(int j) const {
-    if constexpr (BITS == 8) {
-      return (int)(int8_t)((w[j >> 2] >> (8 * (j & 3))) & 0xFF);
-    } else if constexpr (BITS == 4) {
-      return (int)(((w[j >> 3] >> (4 * (j & 7))) & 0xF) << 28) >> 28;
-    } else {
-      const int bit = 6 * j, word = bit >> 5, sh = bit & 31;
-      uint32_t v = w[word] >> sh;
-      if (sh > 26) v |= w[word + 1] << (32 - sh);
-      return (int)((v & 0x3F) << 26) >> 26;
-    }
-  }
-};
-
-// Packed format: `BITS`-bit codes, groups of 64 values, fp16 scales; output
-// bf16(code * scale).  Same grid shape as mount_ref_kernel.
-template <int BITS>
-__global__ void __launch_bounds__(256) mount_packed_kernel(const uint8_t* __restrict__ codes,
-                                                           const __half* __restrict__ scales,
-                                                           int64_t layers, int64_t vals,
-                                                           int64_t width, Seats seats,
-                                                           uint16_t* __restrict__ arena,
-                                                           int64_t arena_seats) {
-  const int64_t slice = blockIdx.y;
-  const int64_t g = slice / layers, l = slice - g * layers;
-  const int64_t chunks = vals / 16;
-  const uint8_t* src = codes + slice * (vals * BITS / 8);
-  const __half* sc = scales + slice * (vals / 64);
-  uint16_t* dst = arena + (l * arena_seats + seats.seat[g]) * width;
-  for (int64_t c0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * kU; c0 < chunks;
-       c0 += (int64_t)gridDim.x * blockDim.x * kU) {
-    Chunk<BITS> ch[kU];
-    float s[kU];
+__global__ void __launch_bounds__(256) mount_packed_tiled_kernel(
+    const uint8_t* __restrict__ codes, const __half* __restrict__ scales, int64_t slices,
+    int64_t layers, int64_t vals, int64_t width, Seats seats, uint16_t* __restrict__ arena,
+    int64_t arena_seats) {
+  constexpr int TB = kTV * BITS / 8;      // code bytes of a full tile: 1024 / 1536 / 2048
+  constexpr int NL = TB / (16 * 32);      // 16-byte loads per lane: 2 / 3 / 4
+  __shared__ uint4 sbuf[8][TB / 16 + 1];  // +1: the 64-bit window of the last piece
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t tps = ceil_div64(vals, kTV);
+  const int64_t total = slices * tps;
+  const uint32_t* sw = reinterpret_cast<const uint32_t*>(sbuf[warp]);
+  for (int64_t t = (int64_t)blockIdx.x * 8 + warp; t < total; t += (int64_t)gridDim.x * 8) {
+    const int64_t slice = t / tps, tile = t - slice * tps;
+    const int64_t g = slice / layers, l = slice - g * layers;
+    const int64_t v0 = tile * kTV;
+    const int nv = (int)min((int64_t)kTV, vals - v0);  // a multiple of 64
+    const uint8_t* src = codes + slice * (vals * BITS / 8) + v0 * BITS / 8;
+    const int nb16 = nv * BITS / 128;
+    uint4 r[NL];
 #pragma unroll
-    for (int u = 0; u < kU; ++u) {
-      if (c0 + u < chunks) {
-        ch[u].load(src + (c0 + u) * (2 * BITS));  // 16 codes = 2*BITS bytes
-        s[u] = __half2float(sc[(c0 + u) >> 2]);
+    for (int j = 0; j < NL; ++j) {
+      const int u = j * 32 + lane;
+      r[j] = u < nb16 ? ld_stream(src + (int64_t)u * 16) : make_uint4(0, 0, 0, 0);
+    }
+    const __half* sc = scales + slice * (vals / 64) + v0 / 64;
+    const float s_lane = lane < nv / 64 ? __half2float(sc[lane]) : 0.0f;
+    __syncwarp();  // the previous tile's reads of the buffer are done
+#pragma unroll
+    for (int j = 0; j < NL; ++j) sbuf[warp][j * 32 + lane] = r[j];
+    __syncwarp();
+    uint16_t* dst = arena + (l * arena_seats + seats.seat[g]) * width + v0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int v = i * 256 + 8 * lane;
+      const float s = __shfl_sync(kFull, s_lane, (v >> 6) & 31);
+      if (v < nv) {
+        int code[8];
+        codes8<BITS>(sw, v, code);
+        uint4 o;
+        o.x = bf16x2_bits((float)code[0] * s, (float)code[1] * s);
+        o.y = bf16x2_bits((float)code[2] * s, (float)code[3] * s);
+        o.z = bf16x2_bits((float)code[4] * s, (float)code[5] * s);
+        o.w = bf16x2_bits((float)code[6] * s, (float)code[7] * s);
+        *reinterpret_cast<uint4*>(dst + v) = o;
       }
     }
+  }
+}
+
+// Reference format, warp tiles (the tiling of mount_packed_tiled_kernel):
+// int8 codes, one fp32 scale per 32 values (lane l holds the tile's scales l
+// and 32 + l), output bf16(fp16(code * scale)).
+__global__ void __launch_bounds__(256) mount_ref_tiled_kernel(
+    const int8_t* __restrict__ codes, const float* __restrict__ scales, int64_t slices,
+    int64_t layers, int64_t vals, int64_t width, Seats seats, uint16_t* __restrict__ arena,
+    int64_t arena_seats) {
+  constexpr int NL = kTV / (16 * 32);  // 4 16-byte loads per lane
+  __shared__ uint4 sbuf[8][kTV / 16];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t tps = ceil_div64(vals, kTV);
+  const int64_t total = slices * tps;
+  const uint2* sw = reinterpret_cast<const uint2*>(sbuf[warp]);
+  for (int64_t t = (int64_t)blockIdx.x * 8 + warp; t < total; t += (int64_t)gridDim.x * 8) {
+    const int64_t slice = t / tps, tile = t - slice * tps;
+    const int64_t g = slice / layers, l = slice - g * layers;
+    const int64_t v0 = tile * kTV;
+    const int nv = (int)min((int64_t)kTV, vals - v0);  // a multiple of 32
+    const int8_t* src = codes + slice * vals + v0;
+    const int nb16 = nv / 16;
+    uint4 r[NL];
 #pragma unroll
-    for (int u = 0; u < kU; ++u) {
-      if (c0 + u >= chunks) break;
-      float f[16];
+    for (int j = 0; j < NL; ++j) {
+      const int u = j * 32 + lane;
+      r[j] = u < nb16 ? ld_stream(src + (int64_t)u * 16) : make_uint4(0, 0, 0, 0);
+    }
+    const float* sc = scales + slice * (vals / 32) + v0 / 32;
+    const int ng = nv / 32;
+    const float s_lo = lane < ng ? __ldg(sc + lane) : 0.0f;
+    const float s_hi = 32 + lane < ng ? __ldg(sc + 32 + lane) : 0.0f;
+    __syncwarp();
 #pragma unroll
-      for (int j = 0; j < 16; ++j) f[j] = (float)ch[u].code(j) * s[u];
-      store_bf16x16(dst + (c0 + u) * 16, f);
+    for (int j = 0; j < NL; ++j) sbuf[warp][j * 32 + lane] = r[j];
+    __syncwarp();
+    uint16_t* dst = arena + (l * arena_seats + seats.seat[g]) * width + v0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int v = i * 256 + 8 * lane;
+      const int grp = v >> 5;  // 8*i + lane/4
+      const float s = __shfl_sync(kFull, i < 4 ? s_lo : s_hi, grp & 31);
+      if (v < nv) {
+        const uint2 w = sw[v >> 3];
+        const int8_t* cb = reinterpret_cast<const int8_t*>(&w);
+        float f[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j)  // fp16 first (dequantize_symmetric_group32), then bf16
+          f[j] = __half2float(__float2half_rn((float)cb[j] * s));
+        uint4 o;
+        o.x = bf16x2_bits(f[0], f[1]);
+        o.y = bf16x2_bits(f[2], f[3]);
+        o.z = bf16x2_bits(f[4], f[5]);
+        o.w = bf16x2_bits(f[6], f[7]);
+        *reinterpret_cast<uint4*>(dst + v) = o;
+      }
     }
   }
 }
@@ -180,13 +189,6 @@ int grid_for(int64_t work) {
   return (int)std::max<int64_t>(1, std::min<int64_t>(ceil_div64(work, 256), (int64_t)info.sms * 8));
 }
 
-// x: enough 256-thread blocks for kU chunks per thread of one slice (capped,
-// then grid-strided); y: one row of blocks per (graft, layer) slice.
-dim3 slice_grid(int64_t slices, int64_t chunks) {
-  const int64_t per = ceil_div64(chunks, 256 * kU);
-  return dim3((unsigned)std::max<int64_t>(1, std::min<int64_t>(per, 1024)), (unsigned)slices);
-}
-
 bool seats_ok(const int64_t* seats, int64_t n, int64_t tokens, int64_t arena_seats, Seats* out) {
   if (!seats || n <= 0 || n > kMaxGrafts) return false;
   for (int64_t g = 0; g < n; ++g) {
@@ -215,9 +217,15 @@ int grm_b200_mount_ref(const int8_t* codes_device, const float* scales_device, i
     return GRM_B200_EINVAL;
   }
   const int64_t vals = tokens * width;
-  const dim3 grid = slice_grid(n_grafts * layers, vals / 16);
-  mount_ref_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      codes_device, scales_device, layers, vals, width, seats, arena_device, arena_seats);
+  const int64_t slices = n_grafts * layers;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  DeviceInfo info;
+  if (device_info(dev, &info) != 0) info.sms = 148;
+  const int grid = (int)std::max<int64_t>(
+      1, std::min<int64_t>((int64_t)info.sms * 8, ceil_div64(slices * ceil_div64(vals, kTV), 8)));
+  mount_ref_tiled_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      codes_device, scales_device, slices, layers, vals, width, seats, arena_device, arena_seats);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     set_thread_error("mount_ref launch failed: %s", cudaGetErrorString(e));
@@ -240,18 +248,24 @@ int grm_b200_mount_packed(const uint8_t* codes_device, const uint16_t* scales_de
                      (long long)width);
     return GRM_B200_EINVAL;
   }
-  const dim3 grid = slice_grid(n_grafts * layers, vals / 16);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const __half* sc = reinterpret_cast<const __half*>(scales_device);
+  const int64_t slices = n_grafts * layers;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  DeviceInfo info;
+  if (device_info(dev, &info) != 0) info.sms = 148;
+  const int grid = (int)std::max<int64_t>(
+      1, std::min<int64_t>((int64_t)info.sms * 8, ceil_div64(slices * ceil_div64(vals, kTV), 8)));
   if (bits == 8)
-    mount_packed_kernel<8><<<grid, 256, 0, s>>>(codes_device, sc, layers, vals, width, seats,
-                                                arena_device, arena_seats);
+    mount_packed_tiled_kernel<8><<<grid, 256, 0, s>>>(codes_device, sc, slices, layers, vals, width,
+                                                      seats, arena_device, arena_seats);
   else if (bits == 6)
-    mount_packed_kernel<6><<<grid, 256, 0, s>>>(codes_device, sc, layers, vals, width, seats,
-                                                arena_device, arena_seats);
+    mount_packed_tiled_kernel<6><<<grid, 256, 0, s>>>(codes_device, sc, slices, layers, vals, width,
+                                                      seats, arena_device, arena_seats);
   else
-    mount_packed_kernel<4><<<grid, 256, 0, s>>>(codes_device, sc, layers, vals, width, seats,
-                                                arena_device, arena_seats);
+    mount_packed_tiled_kernel<4><<<grid, 256, 0, s>>>(codes_device, sc, slices, layers, vals, width,
+                                                      seats, arena_device, arena_seats);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     set_thread_error("mount_packed launch failed: %s", cudaGetErrorString(e));
