@@ -65,7 +65,8 @@ def parse():
                         "216.5 GB bank does not fit one B200)")
     p.add_argument("--workload", default="mla_1m_b1",
                    choices=["mla_1m_b1", "mla_1m_b64", "gqa_512", "gqa_100k", "mount_int4",
-                            "mount_int6", "mount_int8", "mount_ref8"],
+                            "mount_int6", "mount_int8", "mount_ref8", "mount_int4_rope",
+                            "mount_ref8_rope"],
                    help="mla_1m_b1 is the headline (BASELINE config 2); the others measure "
                         "the GQA route (configs 3/4) and the quantised mount (config 5)")
     return p.parse_args()
@@ -661,7 +662,9 @@ def cpu_gqa_baseline(keys_dev, off, q, KH, D, max_tokens=40_000, budget_s=8.0):
 def run_mount(args):
     """Config 5: 3 grafts x 62 layers x 2048 tokens x 288 values, quantised,
     dequantised + scattered into a bf16 arena [62, 8192, 288].  A step is one
-    mount of all three grafts.  Replicas only at N > 1 (no collective)."""
+    mount of all three grafts.  `_rope` workloads also re-RoPE the 32-wide
+    k_pe columns (256..287) at the arena seats in the same kernel.  Replicas
+    only at N > 1 (no collective)."""
     import torch
     import torch.distributed as dist
 
@@ -675,20 +678,30 @@ def run_mount(args):
     arena = graft_mount.ArenaMount(L, S, W, device=f"cuda:{local}", fill=0x7F81)
     stream = torch.cuda.current_stream()
     V = G * L * T * W
-    if args.workload == "mount_ref8":
+    base = args.workload.removesuffix("_rope")
+    rope = None
+    if base != args.workload:
+        rc, rs = graft_mount.rope_tables(S, 32)
+        rope = graft_mount.RopeSpec(torch.from_numpy(rc).cuda(), torch.from_numpy(rs).cuda(),
+                                    256, 32)
+    if base == "mount_ref8":
         c, sc = O.quant_ref(vals, 8)              # graft_quant format (group 32, fp32 scales)
         codes = torch.from_numpy(c.reshape(G, L, -1)).cuda()
         scales = torch.from_numpy(sc.reshape(G, L, -1)).cuda()
         bytes_per = V + V // 32 * 4 + 2 * V
-        fn = lambda: arena.mount_ref(codes, scales, seats, T, stream=stream)  # noqa: E731
+        fn = lambda: arena.mount_ref(codes, scales, seats, T, rope=rope,  # noqa: E731
+                                     stream=stream)
         bits = 8
     else:
-        bits = int(args.workload[-1])
+        bits = int(base[-1])
         c, sc = graft_mount.quantize_packed(vals.reshape(G, L, -1), bits)
         codes = torch.from_numpy(c).cuda()
         scales = torch.from_numpy(sc.view(np.uint16)).cuda()
         bytes_per = V * bits // 8 + V // 64 * 2 + 2 * V
-        fn = lambda: arena.mount_packed(codes, scales, seats, T, bits, stream=stream)  # noqa: E731
+        fn = lambda: arena.mount_packed(codes, scales, seats, T, bits, rope=rope,  # noqa: E731
+                                        stream=stream)
+    if rope is not None:
+        bytes_per += G * T * 32 * 4 * 2            # the cos/sin rows of the mounted seats
     flush = torch.empty(2 * L2_BYTES, dtype=torch.uint8, device="cuda")
     for _ in range(args.warmup):
         fn()
@@ -716,7 +729,7 @@ def run_mount(args):
     e2e_s = time.perf_counter() - t0
     cpu = None
     if rank == 0 and not args.no_cpu_baseline:
-        cpu = cpu_mount_baseline(vals, bits, args.workload)
+        cpu = cpu_mount_baseline(vals, bits, args.workload, rope is not None)
     peak, peak_kind = peaks()
     achieved = bytes_per / (statistics.mean(ms) / 1e3) / 1e9
     if world > 1:
@@ -733,8 +746,9 @@ def run_mount(args):
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "peak_kind": peak_kind,
                      "algorithmic_bytes_per_launch": bytes_per, "traffic": None,
-                     "kernel": "mount_ref_kernel" if bits == 8 and args.workload == "mount_ref8"
-                     else f"mount_packed_kernel<{bits}>"},
+                     "kernel": ("mount_ref_tiled_kernel" if base == "mount_ref8"
+                                else f"mount_packed_tiled_kernel<{bits}>")
+                     + (" (rope)" if rope is not None else "")},
         "cpu_baseline": cpu,
         "e2e": {"value": e2e_steps / e2e_s, "unit": "mounts/s",
                 "h2d_bytes_per_step": int(c.nbytes + sc.nbytes), "d2h_bytes_per_step": 16,
@@ -743,25 +757,34 @@ def run_mount(args):
     }), flush=True)
 
 
-def cpu_mount_baseline(vals, bits, workload):
+def cpu_mount_baseline(vals, bits, workload, rope=False):
     """The reference's CPU dequant (core/graft_quant.dequantize_symmetric_group32
     restated by the oracle, group 32, fp32 scales) + the bf16 cast, per mount,
     on one graft layer scaled to the 3 x 62 layers (the reference does it per
-    layer on the host, core/graft_arena.py:3485-3492)."""
+    layer on the host, core/graft_arena.py:3485-3492); with `rope`, plus the
+    re-RoPE of that layer's k_pe columns at its seats (orc_mount_rope)."""
     import oracle as O
+    from graftrepository_b200 import graft_mount
 
     one = vals[0, 0]
     c, s = O.quant_ref(one, 8 if bits == 8 else bits)
+    if rope:
+        T, W = one.shape
+        rc, rs = graft_mount.rope_tables(8192, 32)
+        layer = np.zeros((1, 8192, W), np.uint16)
     times = []
     for _ in range(5):
         t0 = time.perf_counter()
-        O.dequant_ref(c, s)
+        _, bf = O.dequant_ref(c, s)
+        if rope:
+            layer[0, 100:100 + T] = bf.reshape(T, W)
+            O.mount_rope(layer, 1, 1, T, [100], rc, rs, 256, 32)
         times.append(time.perf_counter() - t0)
     per_layer = statistics.median(times)
     layers = vals.shape[0] * vals.shape[1]
     return {"value": 1.0 / (per_layer * layers), "unit": "mounts/s", "cores":
             len(os.sched_getaffinity(0)), "kind": "port",
-            "sample": f"dequant of one [2048, 288] layer x {layers} layers "
+            "sample": f"dequant{' + re-RoPE' if rope else ''} of one [2048, 288] layer x {layers} layers "
                       f"(median {per_layer*1e3:.2f} ms/layer, OpenMP C restatement)"}
 
 

@@ -68,6 +68,9 @@ _SIGS = {
     "grm_b200_gqa_stats": (_I, [_P, _P, _P]),
     "grm_b200_mount_ref": (_I, [_P, _P, _I64, _I64, _I64, _I64, _P, _P, _I64, _P]),
     "grm_b200_mount_packed": (_I, [_P, _P, _I, _I, _I64, _I64, _I64, _I64, _P, _P, _I64, _P]),
+    "grm_b200_mount_packed_rope": (_I, [_P, _P, _I, _I, _I64, _I64, _I64, _I64, _P, _P, _I64, _P,
+                                        _P]),
+    "grm_b200_mount_ref_rope": (_I, [_P, _P, _I64, _I64, _I64, _I64, _P, _P, _I64, _P, _P]),
     "grm_b200_arena_splice": (_I, [_P, _I64, _I64, _P, _I64, _I64, _I64, _I64, _P, _P, _P]),
     "grm_b200_merge_topk": (_I, [_P, _P, _I, _I, _I, _I, _P, _P, _P]),
     "grm_b200_merge_topk_strided": (_I, [_P, ctypes.c_int64, _P, ctypes.c_int64, _I, _I, _I, _I,

@@ -6,7 +6,9 @@ Host-side mirror of the mount half of GraftRepository's per-turn step:
 then an fp16 -> bf16 upload per layer) and splices them into the arena seats
 (:1933-1995).  Here the codes and scales are uploaded as they are stored and
 one kernel dequantises and writes bf16 rows straight into the preallocated
-arena ``[layers, seats, width]``.
+arena ``[layers, seats, width]``; with a ``RopeSpec`` the same kernel also
+re-RoPEs the positional columns at their arena seats (``_graft_block``,
+core/graft_arena.py:1848-1859).
 
 Two storage formats:
 
@@ -27,7 +29,7 @@ import numpy as np
 from . import _lib
 
 __all__ = ["quantize_packed", "packed_group_bytes", "ArenaMount", "mount_ref", "mount_packed",
-           "arena_splice"]
+           "arena_splice", "RopeSpec", "rope_tables"]
 
 GROUP_PACKED = 64
 
@@ -70,6 +72,47 @@ def quantize_packed(values: np.ndarray, bits: int, group: int = GROUP_PACKED):
     return codes, scales
 
 
+class _RopeC(ctypes.Structure):
+    _fields_ = [("cos_device", ctypes.c_void_p), ("sin_device", ctypes.c_void_p),
+                ("rows", ctypes.c_int64), ("offset", ctypes.c_int64), ("dim", ctypes.c_int64),
+                ("pair_swap", ctypes.c_int)]
+
+
+class RopeSpec:
+    """Re-RoPE of mounted rows: device fp32 ``cos``/``sin`` tables ``[rows, dim]``
+    (``emb = cat([pos*inv, pos*inv])``, as the models build ``rope_cos``),
+    the first positional column ``offset`` of a row (MLA: 256, after the latent;
+    GQA: 0) and the rotary head width ``dim`` (MLA k_pe: 32; GQA: head_dim).
+    ``pair_swap`` selects the ``ROPE_PAIR_SWAP`` layout (DeepSeek)."""
+
+    def __init__(self, cos, sin, offset: int, dim: int, pair_swap: bool = False):
+        self.cos, self.sin = cos, sin
+        self.offset, self.dim, self.pair_swap = int(offset), int(dim), bool(pair_swap)
+
+    def c(self) -> _RopeC:
+        for t in (self.cos, self.sin):
+            if hasattr(t, "shape") and (tuple(t.shape[1:]) != (self.dim,) or
+                                        getattr(t, "dtype", None) is not None and
+                                        "float32" not in str(t.dtype)):
+                raise ValueError("rope tables must be fp32 [rows, dim]")
+        if hasattr(self.cos, "shape") and self.cos.shape != self.sin.shape:
+            raise ValueError("rope cos and sin tables differ in shape")
+        return _RopeC(_ptr(self.cos), _ptr(self.sin), int(self.cos.shape[0]), self.offset,
+                      self.dim, 1 if self.pair_swap else 0)
+
+
+def rope_tables(rows: int, dim: int, theta: float = 10000.0, factors=None):
+    """fp32 (cos, sin) [rows, dim] the way the reference models build them
+    (core/minicpm3_tc.py:345-355): inv = 1/theta^(2i/dim) [/ factors],
+    emb = cat([pos*inv, pos*inv])."""
+    inv = 1.0 / (theta ** (np.arange(0, dim, 2, np.float32) / dim))
+    if factors is not None:
+        inv = inv / np.asarray(factors, np.float32)
+    ang = np.arange(rows, dtype=np.float32)[:, None] * inv[None, :]
+    emb = np.concatenate([ang, ang], axis=-1)
+    return np.cos(emb).astype(np.float32), np.sin(emb).astype(np.float32)
+
+
 def _ptr(t) -> int:
     if hasattr(t, "data_ptr"):
         return int(t.data_ptr())
@@ -85,25 +128,39 @@ def _stream(stream) -> int:
 
 
 def mount_ref(codes, scales, seats, arena, *, layers: int, tokens: int, width: int,
-              stream=None) -> None:
+              rope: RopeSpec | None = None, stream=None) -> None:
     """codes int8 [G, layers, tokens*width], scales fp32 [G, layers, tokens*width/32]
     and arena bf16 [layers, seats, width] are device tensors (or pointers)."""
     st = np.ascontiguousarray(seats, dtype=np.int64)
     arena_seats = int(arena.shape[1]) if hasattr(arena, "shape") else None
     if arena_seats is None:
         raise ValueError("arena must be a tensor with a shape")
-    rc = _lib.load().grm_b200_mount_ref(_ptr(codes), _ptr(scales), st.shape[0], layers, tokens,
-                                        width, st.ctypes.data, _ptr(arena), arena_seats,
-                                        _stream(stream))
+    L = _lib.load()
+    if rope is None:
+        rc = L.grm_b200_mount_ref(_ptr(codes), _ptr(scales), st.shape[0], layers, tokens, width,
+                                  st.ctypes.data, _ptr(arena), arena_seats, _stream(stream))
+    else:
+        spec = rope.c()
+        rc = L.grm_b200_mount_ref_rope(_ptr(codes), _ptr(scales), st.shape[0], layers, tokens,
+                                       width, st.ctypes.data, _ptr(arena), arena_seats,
+                                       ctypes.addressof(spec), _stream(stream))
     _lib.check(rc, _lib.thread_error)
 
 
 def mount_packed(codes, scales, seats, arena, *, bits: int, layers: int, tokens: int, width: int,
-                 group: int = GROUP_PACKED, stream=None) -> None:
+                 group: int = GROUP_PACKED, rope: RopeSpec | None = None, stream=None) -> None:
     st = np.ascontiguousarray(seats, dtype=np.int64)
-    rc = _lib.load().grm_b200_mount_packed(_ptr(codes), _ptr(scales), bits, group, st.shape[0],
-                                           layers, tokens, width, st.ctypes.data, _ptr(arena),
-                                           int(arena.shape[1]), _stream(stream))
+    L = _lib.load()
+    if rope is None:
+        rc = L.grm_b200_mount_packed(_ptr(codes), _ptr(scales), bits, group, st.shape[0], layers,
+                                     tokens, width, st.ctypes.data, _ptr(arena),
+                                     int(arena.shape[1]), _stream(stream))
+    else:
+        spec = rope.c()
+        rc = L.grm_b200_mount_packed_rope(_ptr(codes), _ptr(scales), bits, group, st.shape[0],
+                                          layers, tokens, width, st.ctypes.data, _ptr(arena),
+                                          int(arena.shape[1]), ctypes.addressof(spec),
+                                          _stream(stream))
     _lib.check(rc, _lib.thread_error)
 
 
@@ -130,10 +187,12 @@ class ArenaMount:
         if fill is not None:
             self.arena.view(torch.int16).fill_(int(np.uint16(fill).view(np.int16)))
 
-    def mount_ref(self, codes, scales, seats, tokens: int, stream=None) -> None:
+    def mount_ref(self, codes, scales, seats, tokens: int, rope: RopeSpec | None = None,
+                  stream=None) -> None:
         mount_ref(codes, scales, seats, self.arena, layers=self.layers, tokens=tokens,
-                  width=self.width, stream=stream)
+                  width=self.width, rope=rope, stream=stream)
 
-    def mount_packed(self, codes, scales, seats, tokens: int, bits: int, stream=None) -> None:
+    def mount_packed(self, codes, scales, seats, tokens: int, bits: int,
+                     rope: RopeSpec | None = None, stream=None) -> None:
         mount_packed(codes, scales, seats, self.arena, bits=bits, layers=self.layers,
-                     tokens=tokens, width=self.width, stream=stream)
+                     tokens=tokens, width=self.width, rope=rope, stream=stream)

@@ -248,6 +248,42 @@ int grm_b200_mount_packed(const uint8_t* codes_device, const uint16_t* scales_de
                           int64_t tokens, int64_t width, const int64_t* seats_host,
                           uint16_t* arena_device, int64_t arena_seats, void* stream);
 
+/* Re-RoPE of the positional part of the mounted rows, fused into the mount
+ * (core/graft_arena.py:344-367 `_rope_tensor`, applied by `_graft_block`
+ * :1848-1859 at the mount seats; the reference runs it through tensor_cuda's
+ * rope_apply, which is not vendored).  Columns [offset, width) of every
+ * mounted row are heads of `dim` values (MLA: the 32-d k_pe after the 256-d
+ * latent, offset 256; GQA: offset 0, dim = head_dim).  Head element j of the
+ * row at arena seat p becomes x'_j * cos[p][j] + r_j * sin[p][j] with x' the
+ * stored bf16 values (pair-swapped [x0 x2 .. x1 x3 ..] when pair_swap, the
+ * `ROPE_PAIR_SWAP` layout), r = rotate_half(x'); fp32 products and add, one
+ * bf16 rounding.  cos/sin: device fp32 [rows, dim], rows > every seat + tokens - 1;
+ * offset % 8 == 0, dim % 16 == 0.  With dim a power of two <= 256, offset a
+ * multiple of dim and 16-byte aligned tables (every MLA k_pe and GQA head
+ * layout) the partner values come from the same warp's registers; other
+ * layouts re-read them from the codes. */
+typedef struct grm_b200_rope_spec {
+  const float* cos_device;
+  const float* sin_device;
+  int64_t rows;
+  int64_t offset;
+  int64_t dim;
+  int pair_swap;
+} grm_b200_rope_spec;
+
+int grm_b200_mount_packed_rope(const uint8_t* codes_device, const uint16_t* scales_device,
+                               int bits, int group, int64_t n_grafts, int64_t layers,
+                               int64_t tokens, int64_t width, const int64_t* seats_host,
+                               uint16_t* arena_device, int64_t arena_seats,
+                               const grm_b200_rope_spec* rope, void* stream);
+
+/* The reference format with the same fused re-RoPE (on the bf16(fp16(code *
+ * scale)) values the plain mount stores). */
+int grm_b200_mount_ref_rope(const int8_t* codes_device, const float* scales_device,
+                            int64_t n_grafts, int64_t layers, int64_t tokens, int64_t width,
+                            const int64_t* seats_host, uint16_t* arena_device,
+                            int64_t arena_seats, const grm_b200_rope_spec* rope, void* stream);
+
 /* Device byte splice out = old[:sink] | mount | old[tail_start:] per outer row,
  * tail_start = min(sink + old_mount_tokens, input_tokens).  old[outer,
  * input_tokens, row_bytes], mount[outer, mount_tokens, row_bytes], out[outer,

@@ -69,6 +69,9 @@ ORC_API float orc_f16_to_f32(uint16_t h) {
   return bits_f32(sign | ((e + 112u) << 23) | (m << 13));
 }
 
+/* bf16 -> fp32 (exact). */
+ORC_API float orc_bf16_to_f32(uint16_t b) { return bits_f32((uint32_t)b << 16); }
+
 /* fp32 -> bf16, round to nearest even. */
 ORC_API uint16_t orc_f32_to_bf16(float f) {
   const uint32_t u = f32_bits(f);
@@ -407,6 +410,53 @@ ORC_API int orc_mount_scatter(const uint16_t* values, int64_t grafts, int64_t la
       memcpy(arena + (l * arena_seats + seats[g]) * width,
              values + ((g * layers + l) * tokens) * width,
              (size_t)(tokens * width) * sizeof(uint16_t));
+  return 0;
+}
+
+/* Re-RoPE of the positional part of mounted rows, at their arena seats
+ * (core/graft_arena.py:344-367 `_rope_tensor` / `_rope_block_at`, called from
+ * `_graft_block` :1848-1859 with pos0 = the first mounted seat).  For graft
+ * g, layer l, token t at arena row p = seat[g] + t, every rope head (columns
+ * offset + h*dim .. +dim, h = 0 .. (width-offset)/dim - 1) of the stored bf16
+ * row becomes apply_rotary at position p, as the reference's fallback path
+ * computes it on the uploaded tensor: x' = pair_swap ? [x0 x2 x4 ... x1 x3 ...]
+ * (`_pair_swap_last`) : x; out_j = x'_j*cos[p][j] + r_j*sin[p][j] with
+ * r_j = -x'_{j+dim/2} for j < dim/2 and x'_{j-dim/2} otherwise (rotate_half;
+ * the tables hold cat([pos*inv, pos*inv])).  fp32 arithmetic: two products,
+ * then one add (no fused multiply-add), one rounding to bf16.  tensor_cuda's
+ * rope_apply, which the reference prefers, is not vendored: parity of this
+ * step is unpinned. */
+ORC_API int orc_mount_rope(uint16_t* arena, int64_t grafts, int64_t layers, int64_t tokens,
+                           int64_t width, const int64_t* seats, int64_t arena_seats,
+                           const float* cos_t, const float* sin_t, int64_t rows, int64_t offset,
+                           int64_t dim, int pair_swap) {
+  if (dim <= 0 || dim % 2 || dim > 1024 || offset < 0 || offset > width ||
+      (width - offset) % dim)
+    return -1;
+  for (int64_t g = 0; g < grafts; ++g)
+    if (seats[g] < 0 || seats[g] + tokens > arena_seats || seats[g] + tokens > rows) return -1;
+  const int64_t heads = (width - offset) / dim, half = dim / 2;
+#pragma omp parallel for collapse(2) schedule(static)
+  for (int64_t g = 0; g < grafts; ++g)
+    for (int64_t l = 0; l < layers; ++l) {
+      float x[1024], xp[1024];
+      for (int64_t t = 0; t < tokens; ++t) {
+        const int64_t pos = seats[g] + t;
+        uint16_t* row = arena + (l * arena_seats + pos) * width;
+        for (int64_t h = 0; h < heads; ++h) {
+          uint16_t* hp = row + offset + h * dim;
+          for (int64_t j = 0; j < dim; ++j) x[j] = orc_bf16_to_f32(hp[j]);
+          for (int64_t j = 0; j < dim; ++j)
+            xp[j] = pair_swap ? (j < half ? x[2 * j] : x[2 * (j - half) + 1]) : x[j];
+          for (int64_t j = 0; j < dim; ++j) {
+            const float r = j < half ? -xp[j + half] : xp[j - half];
+            const float a = xp[j] * cos_t[pos * dim + j];
+            const float b = r * sin_t[pos * dim + j];
+            hp[j] = orc_f32_to_bf16(a + b);
+          }
+        }
+      }
+    }
   return 0;
 }
 

@@ -26,7 +26,7 @@ __all__ = [
     "mla_row_norms", "mla_scores", "mla_route", "topk",
     "gqa_scores", "gqa_route",
     "quant_ref", "dequant_ref", "quant_packed", "dequant_packed", "packed_group_bytes",
-    "mount_scatter", "swap_splice",
+    "mount_scatter", "mount_rope", "swap_splice",
 ]
 
 _P = ctypes.c_void_p
@@ -41,7 +41,9 @@ def ensure_built(ref_root: str | os.PathLike | None = None, with_ref: bool = Fal
         root = Path(ref_root or os.environ.get("GRM_REFERENCE_ROOT", "/root/reference"))
         if (root / "cpp" / "grm_runtime.cpp").is_file():
             targets.append("ref")
-    need = (not LIB_PATH.exists()) or (
+    src = HERE / "grm_oracle.c"
+    stale = LIB_PATH.exists() and src.exists() and src.stat().st_mtime > LIB_PATH.stat().st_mtime
+    need = (not LIB_PATH.exists()) or stale or (
         "ref" in targets and not (REF_LIB_PATH.exists() and REF_OMP_LIB_PATH.exists()))
     if not need:
         return
@@ -85,6 +87,9 @@ def lib() -> ctypes.CDLL:
         L.orc_dequant_packed.restype = ctypes.c_int
         L.orc_mount_scatter.argtypes = [_P, _I64, _I64, _I64, _I64, _P, _P, _I64]
         L.orc_mount_scatter.restype = ctypes.c_int
+        L.orc_mount_rope.argtypes = [_P, _I64, _I64, _I64, _I64, _P, _I64, _P, _P, _I64, _I64,
+                                     _I64, ctypes.c_int]
+        L.orc_mount_rope.restype = ctypes.c_int
         L.orc_swap_splice.argtypes = [_P, _I64, _I64, _P, _I64, _I64, _I64, _I64, _P,
                                       ctypes.POINTER(_I64)]
         L.orc_swap_splice.restype = ctypes.c_int
@@ -240,6 +245,22 @@ def mount_scatter(values_bf16, seats, arena_bf16) -> np.ndarray:
     rc = lib().orc_mount_scatter(_ptr(v), G, L, T, W, _ptr(st), _ptr(a), a.shape[1])
     if rc != 0:
         raise ValueError("seat out of range")
+    return a
+
+
+def mount_rope(arena_bf16, grafts: int, layers: int, tokens: int, seats, cos, sin, offset: int,
+               dim: int, pair_swap: bool = False) -> np.ndarray:
+    """Re-RoPE of the mounted rows' rope heads at their seats (orc_mount_rope).
+    arena [L, S, W] bf16 bits (modified copy); cos/sin [rows, dim] fp32."""
+    a = np.array(arena_bf16, dtype=np.uint16, copy=True, order="C")
+    L, S, W = a.shape
+    st = np.ascontiguousarray(seats, dtype=np.int64)
+    c = np.ascontiguousarray(cos, dtype=np.float32)
+    sn = np.ascontiguousarray(sin, dtype=np.float32)
+    rc = lib().orc_mount_rope(_ptr(a), grafts, layers, tokens, W, _ptr(st), S, _ptr(c), _ptr(sn),
+                              c.shape[0], offset, dim, 1 if pair_swap else 0)
+    if rc != 0:
+        raise ValueError("bad rope arguments")
     return a
 
 

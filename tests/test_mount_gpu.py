@@ -116,3 +116,75 @@ def test_splice_golden(golden):
         got = out.cpu().numpy().view(np.uint16)[:, :, :inner]
         assert np.array_equal(got, exp), i
         i += 1
+
+
+def _rope_dev(rows, dim):
+    import torch
+
+    c, s = graft_mount.rope_tables(rows, dim)
+    return c, s, torch.from_numpy(c).cuda(), torch.from_numpy(s).cuda()
+
+
+@pytest.mark.parametrize("bits", [8, 6, 4, 0])
+@pytest.mark.parametrize("W,offset,dim,pair_swap", [(288, 256, 32, False), (288, 256, 32, True),
+                                                    (256, 0, 128, False), (192, 64, 64, True),
+                                                    (288, 32, 64, False), (288, 96, 96, True)])
+def test_rope_mount_matches_oracle(bits, W, offset, dim, pair_swap):
+    """Dequant + scatter + re-RoPE of the positional columns at the arena seats
+    in one kernel == oracle mount followed by orc_mount_rope, bit-exact
+    (bits 0: the reference format)."""
+    import torch
+
+    G, L, T, S = 3, 4, 96, 700
+    vals = synth.grafts(60 + bits + dim, G, L, T, W)
+    seats = synth.seat_offsets(bits + W, G, T, S)
+    c, s, dc, ds = _rope_dev(S, dim)
+    rope = graft_mount.RopeSpec(dc, ds, offset, dim, pair_swap)
+    m = graft_mount.ArenaMount(L, S, W, fill=SENTINEL)
+    if bits:
+        codes, scales = graft_mount.quantize_packed(vals.reshape(G, L, -1), bits)
+        m.mount_packed(torch.from_numpy(codes).cuda(),
+                       torch.from_numpy(scales.view(np.uint16)).cuda(), seats, T, bits,
+                       rope=rope)
+        deq = O.dequant_packed(codes.reshape(-1), scales.view(np.uint16).reshape(-1), bits)
+    else:
+        c32, s32 = O.quant_ref(vals, 8)
+        m.mount_ref(torch.from_numpy(c32.reshape(G, L, -1)).cuda(),
+                    torch.from_numpy(s32.reshape(G, L, -1)).cuda(), seats, T, rope=rope)
+        _, deq = O.dequant_ref(c32, s32)
+    want = O.mount_scatter(deq.reshape(G, L, T, W), seats,
+                           np.full((L, S, W), SENTINEL, np.uint16))
+    want = O.mount_rope(want, G, L, T, seats, c, s, offset, dim, pair_swap)
+    assert np.array_equal(_u16(m.arena), want)
+
+
+def test_rope_mount_full_size_config5_int4():
+    """3 grafts x 62 layers x 2048 tokens x 288 values (k_pe 32 at column 256)
+    re-RoPEd at arena seats up to 8192."""
+    import torch
+
+    vals = synth.grafts(4)
+    seats = synth.seat_offsets(4, 3, 2048, 8192)
+    c, s, dc, ds = _rope_dev(8192, 32)
+    codes, scales = graft_mount.quantize_packed(vals.reshape(3, 62, -1), 4)
+    m = graft_mount.ArenaMount(62, 8192, 288, fill=SENTINEL)
+    m.mount_packed(torch.from_numpy(codes).cuda(), torch.from_numpy(scales.view(np.uint16)).cuda(),
+                   seats, 2048, 4, rope=graft_mount.RopeSpec(dc, ds, 256, 32))
+    deq = O.dequant_packed(codes.reshape(-1), scales.view(np.uint16).reshape(-1), 4)
+    want = O.mount_scatter(deq.reshape(3, 62, 2048, 288), seats,
+                           np.full((62, 8192, 288), SENTINEL, np.uint16))
+    want = O.mount_rope(want, 3, 62, 2048, seats, c, s, 256, 32)
+    assert np.array_equal(_u16(m.arena), want)
+
+
+@pytest.mark.parametrize("offset,dim,rows", [(250, 32, 700), (256, 24, 700), (256, 32, 100)])
+def test_rope_mount_rejects_bad_specs(offset, dim, rows):
+    import torch
+
+    codes = torch.zeros(8 * 288 // 2, dtype=torch.uint8, device="cuda")
+    scales = torch.zeros(8 * 288 // 64, dtype=torch.int16, device="cuda")
+    arena = torch.zeros((1, 700, 288), dtype=torch.bfloat16, device="cuda")
+    c = torch.zeros((rows, dim), dtype=torch.float32, device="cuda")
+    with pytest.raises(GrmB200Error):
+        graft_mount.mount_packed(codes, scales, [200], arena, bits=4, layers=1, tokens=8,
+                                 width=288, rope=graft_mount.RopeSpec(c, c, offset, dim))
