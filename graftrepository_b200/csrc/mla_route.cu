@@ -28,6 +28,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "route_policy.cuh"
 
 namespace grm_b200 {
 namespace mla {
@@ -109,6 +110,7 @@ struct Params {
   int force_all;         // exact kernel: score every row (bank outside the fast path)
   int nq;                // exact kernel: queries in this launch
   unsigned long long* fallback_count;  // queries that took the exact pass (optional)
+  const uint32_t* allow;  // route filters: bitmap of the rows that may be routed (nullptr: all)
   // A single query may travel inside the launch parameters (queries == nullptr):
   // the synchronous host entry then needs no host-to-device copy.
   float qinline[kInlineMax];
@@ -692,7 +694,7 @@ __global__ void __launch_bounds__(kThreads) mla_scan_kernel(const __grid_constan
       float n2 = 0.0f;
       if constexpr (INL) n2 = reduce_scatter<SLOTS>(sq, lane);
       float s = -INFINITY;
-      if (my_row < p.nodes) {
+      if (my_row < p.nodes && policy::row_allowed(p.allow, my_row)) {
         const float nrm = INL ? sqrtf(n2) : nrm_pre;
         if (isfinite(nrm)) s = dot * __frcp_rn(nrm + e_q);
       }
@@ -888,7 +890,8 @@ __global__ void __launch_bounds__(kBulkWarps * 32, 1)
       if (failed) break;
       const float dot = reduce_scatter<SLOTS>(part, lane);
       float s = -INFINITY;
-      if (my_row < p.nodes && isfinite(nrm_pre)) s = dot * __frcp_rn(nrm_pre + e_q);
+      if (my_row < p.nodes && isfinite(nrm_pre) && policy::row_allowed(p.allow, my_row))
+        s = dot * __frcp_rn(nrm_pre + e_q);
       list.offer_margin(s, (uint32_t)my_row, lane, p.topk, 2.0f * kMargin);
       g = gn;
       gn = ticket ? dyn0 + (int64_t)__shfl_sync(kFull, tk, 0) : gn + gstride;
@@ -948,7 +951,7 @@ __device__ __forceinline__ void exact_one(const Params<T>& p, int q, int lane, i
          row0 += (int64_t)gridDim.x * kWarps * 32) {
       const int64_t row = row0 + lane;
       float es = -INFINITY;
-      if (row < p.nodes) {
+      if (row < p.nodes && policy::row_allowed(p.allow, row)) {
         if constexpr (INL) {
           es = exact_score_inline_norm<T>(p.rows + row * dim, dim, query, qnorm);
         } else {
@@ -1007,7 +1010,7 @@ __device__ __forceinline__ void exact_one(const Params<T>& p, int q, int lane, i
       if constexpr (INL) n2 = reduce_scatter<SLOTS>(sq, lane);
       const int64_t row = row0 + (lane % L) * R + lane / L;
       float es = -INFINITY;
-      if (row < p.nodes) {
+      if (row < p.nodes && policy::row_allowed(p.allow, row)) {
         const float nrm = INL ? sqrtf(n2) : __ldg(p.norms + row);
         if (isfinite(nrm)) {
           const float s = dot * __frcp_rn(nrm + e_q);
@@ -1117,6 +1120,36 @@ __global__ void row_norms_kernel(const T* rows, int64_t n, int dim, float* norms
   }
 }
 
+// Lexical channel of route_mla_arena (cpp/grm_runtime.cpp:4339-4350): every
+// allowed node with lexical hits gets S = exact score + hits / m (fp32 divide,
+// fp32 add), one thread per node (the exact score is one sequential fp64
+// chain); non-finite S is dropped by the merge.
+template <typename T>
+__global__ void mla_lex_score_kernel(const T* __restrict__ rows, const float* __restrict__ norms,
+                                     int dim, const float* __restrict__ query,
+                                     const uint2* __restrict__ list,
+                                     const uint32_t* __restrict__ counter,
+                                     const uint32_t* __restrict__ allow, int m,
+                                     float* __restrict__ cand_s, uint32_t* __restrict__ cand_id) {
+  __shared__ double qn;
+  if (threadIdx.x == 0) qn = query_norm_seq(query, dim);
+  __syncthreads();
+  const uint32_t n = *counter;
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const uint2 h = list[i];
+    float S = -INFINITY;
+    if (policy::row_allowed(allow, h.x)) {
+      const float nrm = __ldg(norms + h.x);
+      if (isfinite(nrm)) {
+        const float es = exact_score<T>(rows + (int64_t)h.x * dim, dim, query, qn, nrm);
+        S = es + __fdiv_rn((float)h.y, (float)m);
+      }
+    }
+    cand_s[i] = S;
+    cand_id[i] = h.x;
+  }
+}
+
 __global__ void scratch_init_kernel(unsigned char* base, size_t stride, int queries) {
   const int q = blockIdx.x * blockDim.x + threadIdx.x;
   if (q < queries) {
@@ -1160,6 +1193,8 @@ struct grm_b200_mla_bank {
   ErrorSlot err;
   uint64_t routes = 0;
   unsigned long long* d_fallbacks = nullptr;  // counted by the exact kernel
+  grm_b200::policy::Policy pol;               // lexical keys, filter codes, active flags
+  const uint32_t* cur_allow = nullptr;        // filter bitmap of the route in progress
 };
 
 namespace {
@@ -1296,6 +1331,7 @@ Params<T> make_params(grm_b200_mla_bank* b, const float* dq, int topk) {
   p.force_all = b->exact_only ? 1 : 0;
   p.nq = 0;
   p.fallback_count = b->d_fallbacks;
+  p.allow = b->cur_allow;
   return p;
 }
 
@@ -1492,7 +1528,7 @@ int run_chunk(grm_b200_mla_bank* b, const float* dq, const float* q_host, int nq
   if (!dq) std::memcpy(p.qinline, q_host, sizeof(float) * (size_t)b->dim);
   int rc;
   if constexpr (sizeof(T) == 2) {
-    rc = (b->batch && dq && nq >= kBatchMin && topk <= kBMaxTopk)
+    rc = (b->batch && dq && nq >= kBatchMin && topk <= kBMaxTopk && !p.allow)
              ? launch_batch(b, p, nq, b->stream)
              : launch_scan<T>(b, p, nq, b->stream);
   } else {
@@ -1608,6 +1644,7 @@ void bank_free(grm_b200_mla_bank* b) {
   if (b->d_results) cudaFree(b->d_results);
   if (b->h_results) cudaFreeHost(b->h_results);
   if (b->d_queries) cudaFree(b->d_queries);
+  grm_b200::policy::policy_free(b->pol);
   if (b->ev0) cudaEventDestroy(b->ev0);
   if (b->ev1) cudaEventDestroy(b->ev1);
   if (b->stream) cudaStreamDestroy(b->stream);
@@ -1795,6 +1832,109 @@ const float* grm_b200_mla_row_norms_device(grm_b200_mla_bank* bank) {
   return bank ? bank->d_norms : nullptr;
 }
 
+int grm_b200_mla_bank_set_policy(grm_b200_mla_bank* bank, const char* const* lexical_keys,
+                                 const char* const* kinds, const char* const* scopes,
+                                 const char* const* durabilities,
+                                 const char* const* mutabilities, const uint8_t* active) {
+  if (!bank) return GRM_B200_EINVAL;
+  std::lock_guard<std::mutex> lock(bank->mu);
+  cudaError_t e = cudaSetDevice(bank->device);
+  if (e != cudaSuccess) return bank->err.set(cuda_status(e), "cudaSetDevice failed");
+  cudaStreamSynchronize(bank->stream);
+  const char* const* cats[policy::kCats] = {kinds, scopes, durabilities, mutabilities};
+  return policy::policy_set(bank->pol, bank->nodes, lexical_keys, cats, active, bank->err);
+}
+
+int grm_b200_mla_route_policy(grm_b200_mla_bank* bank, const float* queries_host, int query_count,
+                              int dim, int topk, const char* const* lexical_keys,
+                              const char* kind_filters, const char* scope_filters,
+                              const char* durability_filters, const char* mutability_filters,
+                              uint64_t* out_ids_host, float* out_scores_host, float* elapsed_ms) {
+  if (!bank) return GRM_B200_EINVAL;
+  std::lock_guard<std::mutex> lock(bank->mu);
+  if (!queries_host || query_count <= 0 || dim != bank->dim || !out_ids_host || topk <= 0 ||
+      topk > GRM_B200_MAX_TOPK)
+    return bank->err.set(GRM_B200_EINVAL, "invalid MLA policy route arguments (queries=%d dim=%d topk=%d)",
+                         query_count, dim, topk);
+  bool any_lex = false;
+  for (int i = 0; lexical_keys && i < query_count; ++i)
+    any_lex = any_lex || !policy::split_keys(lexical_keys[i]).empty();
+  cudaError_t e = cudaSetDevice(bank->device);
+  if (e != cudaSuccess) return bank->err.set(cuda_status(e), "cudaSetDevice failed");
+  int rc = reserve(bank, query_count);
+  if (rc) return rc;
+  if (!bank->pol.set) {  // every node keeps the reference's defaults: no keys, active
+    const char* const* cats[policy::kCats] = {nullptr, nullptr, nullptr, nullptr};
+    cudaStreamSynchronize(bank->stream);
+    if ((rc = policy::policy_set(bank->pol, bank->nodes, nullptr, cats, nullptr, bank->err)))
+      return rc;
+  }
+  const size_t need = (size_t)query_count * dim;
+  if (need > bank->dq_cap) {
+    if (bank->d_queries) cudaFree(bank->d_queries);
+    bank->d_queries = nullptr;
+    bank->dq_cap = 0;
+    e = cudaMalloc(&bank->d_queries, need * sizeof(float));
+    if (e != cudaSuccess) return bank->err.set(cuda_status(e), "MLA query buffer allocation failed");
+    bank->dq_cap = need;
+  }
+  e = cudaMemcpyAsync(bank->d_queries, queries_host, need * sizeof(float), cudaMemcpyHostToDevice,
+                      bank->stream);
+  if (e != cudaSuccess) return bank->err.set(cuda_status(e), "MLA query upload failed");
+  DeviceInfo info;
+  if (device_info(bank->device, &info) != 0) info.sms = 148;
+  cudaEventRecord(bank->ev0, bank->stream);
+  const char* const filters[policy::kCats] = {kind_filters, scope_filters, durability_filters,
+                                              mutability_filters};
+  const uint32_t* allow = nullptr;
+  if ((rc = policy::policy_allow(bank->pol, filters, info.sms, bank->stream, &allow, bank->err)))
+    return rc;
+  bank->cur_allow = allow;
+  rc = (bank->dtype == GRM_B200_F16)
+           ? run_chunk<__half>(bank, bank->d_queries, nullptr, query_count, topk)
+           : run_chunk<float>(bank, bank->d_queries, nullptr, query_count, topk);
+  bank->cur_allow = nullptr;
+  if (rc) return rc;
+  for (int q = 0; any_lex && q < query_count; ++q) {
+    int m = 0;
+    if ((rc = policy::policy_collect(bank->pol, lexical_keys[q], info.sms, bank->stream, &m,
+                                     bank->err)))
+      return rc;
+    if (m == 0) continue;
+    const float* dq = bank->d_queries + (int64_t)q * dim;
+    const int grid = info.sms * 2;
+    if (bank->dtype == GRM_B200_F16)
+      mla_lex_score_kernel<__half><<<grid, 128, 0, bank->stream>>>(
+          static_cast<const __half*>(bank->d_rows), bank->d_norms, dim, dq, bank->pol.d_hitlist,
+          bank->pol.d_counter, allow, m, bank->pol.d_cand_s, bank->pol.d_cand_id);
+    else
+      mla_lex_score_kernel<float><<<grid, 128, 0, bank->stream>>>(
+          static_cast<const float*>(bank->d_rows), bank->d_norms, dim, dq, bank->pol.d_hitlist,
+          bank->pol.d_counter, allow, m, bank->pol.d_cand_s, bank->pol.d_cand_id);
+    Result* r = bank->d_results_mapped + q;
+    policy::lex_merge_kernel<<<1, policy::kMergeWarps * 32, 0, bank->stream>>>(
+        r->ids, r->scores, &r->count, topk, 0, bank->pol.d_cand_s, bank->pol.d_cand_id,
+        bank->pol.d_counter);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return bank->err.set(cuda_status(e), "MLA lexical kernels launch failed");
+  }
+  cudaEventRecord(bank->ev1, bank->stream);
+  e = cudaEventSynchronize(bank->ev1);
+  float ms = 0.0f;
+  if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, bank->ev0, bank->ev1);
+  if (e != cudaSuccess) return bank->err.set(cuda_status(e), "MLA policy route failed: %s", cudaGetErrorString(e));
+  for (int q = 0; q < query_count; ++q) {
+    const Result& r = bank->h_results[q];
+    for (int j = 0; j < topk; ++j) {
+      out_ids_host[(int64_t)q * topk + j] = r.ids[j];
+      if (out_scores_host) out_scores_host[(int64_t)q * topk + j] = r.scores[j];
+    }
+  }
+  if (elapsed_ms) *elapsed_ms = ms;
+  bank->routes += (uint64_t)query_count;
+  return 0;
+}
+
 int grm_b200_mla_paths(grm_b200_mla_bank* bank, int* flags) {
   if (!bank || !flags) return GRM_B200_EINVAL;
   *flags = (bank->bulk ? GRM_B200_PATH_BULK : 0) | (bank->batch ? GRM_B200_PATH_BATCH : 0) |
@@ -1974,6 +2114,7 @@ extern "C" int grm_b200_mla_route_noalloc(const void* rows_device, int64_t nodes
   p.force_all = 0;
   p.nq = query_count;
   p.fallback_count = nullptr;
+  p.allow = nullptr;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   scratch_init_kernel<<<(query_count + 127) / 128, 128, 0, s>>>(base + results_bytes, stride,
                                                                  query_count);

@@ -121,6 +121,37 @@ def _device_ptr(device_queries) -> int:
     return int(h.value if isinstance(h, ctypes.c_void_p) else h)
 
 
+_U64MAX = np.uint64(np.iinfo(np.uint64).max)
+
+
+def _blob(values) -> bytes:
+    """A '\\n'-joined filter or key blob (core/grm_native.py:1367-1381)."""
+    if values is None:
+        return b""
+    if isinstance(values, (str, bytes)):
+        values = (values,)
+    vals = [v.decode() if isinstance(v, bytes) else str(v) for v in values
+            if v is not None and str(v) != ""]
+    return "\n".join(vals).encode("utf-8")
+
+
+def _c_strings(values, n: int, *, join: bool = False):
+    """A (char* [n]) array for per-row / per-query strings; None -> NULL."""
+    if values is None:
+        return None
+    if len(values) != n:
+        raise ValueError(f"expected {n} entries, got {len(values)}")
+    arr = (ctypes.c_char_p * n)()
+    for i, v in enumerate(values):
+        if v is None:
+            arr[i] = None
+        elif join and not isinstance(v, (str, bytes)):
+            arr[i] = _blob(v)
+        else:
+            arr[i] = v if isinstance(v, bytes) else str(v).encode("utf-8")
+    return arr
+
+
 def _fits(values: np.ndarray, dtype) -> bool:
     """True when every value survives a round trip through `dtype` bit-exactly
     (NaN payloads aside), so a narrower bank keeps the reference's values."""
@@ -282,6 +313,72 @@ class CudaMLARouteBank:
         _lib.check(_lib.load().grm_b200_mla_stats(self._h, ctypes.byref(a), ctypes.byref(b)),
                    self._err)
         return int(a.value), int(b.value)
+
+    def set_route_policy(self, *, lexical_keys=None, kinds=None, scopes=None,
+                         durabilities=None, mutabilities=None, active=None) -> None:
+        """Per-row route policy data (RouterIndex::Entry lexical_keys, kind,
+        scope, durability, mutability, active; cpp/grm_runtime.hpp:483-494),
+        one entry per bank row.  lexical_keys[i]: a sequence of keys or a
+        '\n'-joined string; None values keep the reference's defaults."""
+        n = self.nodes
+        arrays = [_c_strings(lexical_keys, n, join=True)]
+        arrays += [_c_strings(v, n) for v in (kinds, scopes, durabilities, mutabilities)]
+        act = None
+        if active is not None:
+            act = np.ascontiguousarray(active, dtype=np.uint8).reshape(-1)
+            if act.shape[0] != n:
+                raise ValueError("active must have one entry per bank row")
+        rc = _lib.load().grm_b200_mla_bank_set_policy(
+            self._h, *[None if a is None else ctypes.addressof(a) for a in arrays],
+            None if act is None else act.ctypes.data)
+        _lib.check(rc, self._err)
+        self._policy_rows = n
+
+    def route_policy_topk(self, queries, *, topk: int, lexical_keys=None, kinds=(), scopes=(),
+                          durabilities=(), mutabilities=()):
+        """route_mla_arena with its lexical bonus and filters
+        (cpp/grm_runtime.cpp:4299-4361) on the device: (node ids [Q, topk],
+        policy scores [Q, topk]); lexical_keys: one key list per query (or
+        one list for a single query)."""
+        if self._h is None:
+            raise RuntimeError("CUDA MLA route bank is closed")
+        q = np.ascontiguousarray(queries, dtype=np.float32)
+        if q.ndim == 1:
+            q = q[None, ...]
+        if q.ndim != 2 or q.shape[1] != self.dim:
+            raise ValueError("query dim does not match rows")
+        if not 0 < int(topk) <= MAX_TOPK:
+            raise ValueError(f"topk must be in 1..{MAX_TOPK}")
+        count = q.shape[0]
+        lex = lexical_keys
+        if lex is not None and count == 1 and (isinstance(lex, str) or (
+                len(lex) > 0 and all(isinstance(x, str) for x in lex))):
+            lex = [lex]
+        lex_arr = _c_strings(lex, count, join=True)
+        out = np.empty((count, int(topk)), dtype=np.uint64)
+        scores = np.empty((count, int(topk)), dtype=np.float32)
+        elapsed = ctypes.c_float(0.0)
+        rc = _lib.load().grm_b200_mla_route_policy(
+            self._h, q.ctypes.data, count, self.dim, int(topk),
+            None if lex_arr is None else ctypes.addressof(lex_arr), _blob(kinds), _blob(scopes),
+            _blob(durabilities), _blob(mutabilities), out.ctypes.data, scores.ctypes.data,
+            ctypes.byref(elapsed))
+        _lib.check(rc, self._err)
+        self.last_scores = scores
+        if np.any((out != _U64MAX) & (out >= self.node_ids.shape[0])):
+            raise RuntimeError("CUDA MLA route returned an out-of-range row ID")
+        mapped = np.where(out == _U64MAX, _U64MAX, self.node_ids[np.minimum(out, self.nodes - 1)])
+        return mapped, scores
+
+    def route(self, query, lexical_keys=(), topk=3, kinds=(), scopes=(), durabilities=(),
+              mutabilities=()) -> list[int]:
+        """NativeGraftStore.route's signature (core/grm_native.py:1446-1469):
+        the ranked node ids of one query, lexical bonus and filters applied."""
+        ids, _ = self.route_policy_topk(np.asarray(query, dtype=np.float32).reshape(1, -1),
+                                        topk=int(topk), lexical_keys=[list(lexical_keys or ())],
+                                        kinds=kinds, scopes=scopes, durabilities=durabilities,
+                                        mutabilities=mutabilities)
+        return [int(x) for x in ids[0] if x != _U64MAX]
 
     def paths(self) -> dict:
         """Which kernels serve this bank: bulk single-query scan, tensor-core

@@ -132,6 +132,38 @@ const float* grm_b200_mla_row_norms_device(grm_b200_mla_bank* bank);
  * in flight on other streams may not be counted yet. */
 int grm_b200_mla_stats(grm_b200_mla_bank* bank, uint64_t* routes, uint64_t* fallbacks);
 
+/* Route policy data of the bank's nodes (RouterIndex::Entry lexical_keys,
+ * kind, scope, durability, mutability, active; set through
+ * grm_store_set_route_list's lexical blob, grm_store_set_route_metadata and
+ * grm_store_set_active, cpp/grm_runtime_c.h:162-184, :394-400).
+ * lexical_keys[i]: node i's '\n'-separated keys (NULL array or entry: none);
+ * kinds/scopes/durabilities/mutabilities[i]: node i's values (NULL array or
+ * entry, or "": the reference's defaults "turn" / "conversation" / "session" /
+ * "ephemeral", cpp/grm_runtime.hpp:488-492); active[i] != 0 (NULL: all
+ * active).  Replaces the previous policy data; at most 255 distinct values
+ * per category are filterable. */
+int grm_b200_mla_bank_set_policy(grm_b200_mla_bank* bank, const char* const* lexical_keys,
+                                 const char* const* kinds, const char* const* scopes,
+                                 const char* const* durabilities,
+                                 const char* const* mutabilities, const uint8_t* active);
+
+/* route_mla_arena with its policy channels (cpp/grm_runtime.cpp:4299-4361),
+ * replacing grm_store_route / grm_store_route_filtered
+ * (cpp/grm_runtime_c.h:403-422) for an MLA store: only active nodes whose
+ * values pass every non-empty filter list are routed; a node's score is its
+ * exact MLA score plus hits / m, where m is the number of the query's lexical
+ * keys and hits how many of them the node carries (lexical_hit_count /
+ * lexical_bonus, :3107-3167).  lexical_keys[q]: query q's '\n'-separated keys
+ * (NULL array or entry: none); filters: '\n'-separated value lists, NULL or
+ * "" = no constraint (split as split_lexical_keys, :5196-5208).  Output as
+ * grm_b200_mla_route (scores are the policy scores). */
+int grm_b200_mla_route_policy(grm_b200_mla_bank* bank, const float* queries_host,
+                              int query_count, int dim, int topk,
+                              const char* const* lexical_keys, const char* kind_filters,
+                              const char* scope_filters, const char* durability_filters,
+                              const char* mutability_filters, uint64_t* out_ids_host,
+                              float* out_scores_host, float* elapsed_ms);
+
 /* Which kernels serve this bank (no reference counterpart; for tests and
  * diagnostics): GRM_B200_PATH_* bits. */
 #define GRM_B200_PATH_BULK 1   /* single queries: bulk-copy streaming scan */

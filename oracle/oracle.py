@@ -27,6 +27,7 @@ __all__ = [
     "gqa_scores", "gqa_route",
     "quant_ref", "dequant_ref", "quant_packed", "dequant_packed", "packed_group_bytes",
     "mount_scatter", "mount_rope", "swap_splice",
+    "ROUTE_DEFAULTS", "split_keys", "route_allowed", "lexical_hits", "mla_route_policy",
 ]
 
 _P = ctypes.c_void_p
@@ -159,6 +160,70 @@ def mla_route(rows, query, k: int, norms=None) -> tuple[np.ndarray, np.ndarray]:
     """Exact reference MLA route: (ids uint64[k] with UINT64_MAX fill, scores)."""
     ids, s, _ = topk(mla_scores(rows, query, norms), k)
     return ids, s
+
+
+# ------------------------------------------------------------ route policy
+
+# RouterIndex::Entry defaults (cpp/grm_runtime.hpp:488-492): kind, scope,
+# durability, mutability of a node whose metadata was never set.
+ROUTE_DEFAULTS = ("turn", "conversation", "session", "ephemeral")
+
+
+def split_keys(blob) -> list[str]:
+    """split_lexical_keys (cpp/grm_runtime.cpp:5196-5208): '\n'-separated,
+    empty items dropped.  A list/tuple is taken as already split (empties
+    dropped the same way)."""
+    if blob is None:
+        return []
+    if isinstance(blob, (list, tuple)):
+        return [str(x) for x in blob if str(x) != ""]
+    return [x for x in str(blob).split("\n") if x != ""]
+
+
+def route_allowed(n: int, cats=None, active=None, filters=None) -> np.ndarray:
+    """entry_allowed (cpp/grm_runtime.cpp:3056-3105): active and, for every
+    category with a non-empty filter list, the node's value is in the list.
+    cats: 4 sequences of per-node values (None entries / arrays: defaults)."""
+    ok = np.ones(n, dtype=bool) if active is None else np.asarray(active, dtype=bool).copy()
+    for k in range(4):
+        f = split_keys(filters[k]) if filters is not None else []
+        if not f:
+            continue
+        fs = set(f)
+        col = cats[k] if cats is not None else None
+        for i in range(n):
+            v = col[i] if col is not None and col[i] else ROUTE_DEFAULTS[k]
+            if v not in fs:
+                ok[i] = False
+    return ok
+
+
+def lexical_hits(query_keys, node_keys) -> int:
+    """lexical_hit_count (cpp/grm_runtime.cpp:3107-3150): query keys counted
+    with multiplicity, each hit when the node carries it."""
+    ks = set(split_keys(node_keys))
+    return sum(1 for q in split_keys(query_keys) if q in ks)
+
+
+def mla_route_policy(rows, query, k: int, *, node_lexical=None, cats=None, active=None,
+                     query_lexical=None, filters=None, norms=None):
+    """route_mla_arena with its lexical and filter channels
+    (cpp/grm_runtime.cpp:4299-4361): S = exact score + float(hits)/float(m)
+    in fp32 for allowed nodes; non-finite dropped; (S desc, id asc)."""
+    r = np.ascontiguousarray(rows, dtype=np.float32)
+    n = r.shape[0]
+    s = mla_scores(r, query, norms)
+    qk = split_keys(query_lexical)
+    m = len(qk)
+    if m:
+        hits = np.array([lexical_hits(qk, node_lexical[i] if node_lexical is not None else None)
+                         for i in range(n)], dtype=np.float32)
+        s = (s + hits / np.float32(m)).astype(np.float32)
+    else:
+        s = (s + np.float32(0.0)).astype(np.float32)
+    s[~route_allowed(n, cats, active, filters)] = np.nan
+    ids, sc, _ = topk(s, k)
+    return ids, sc
 
 
 # --------------------------------------------------------------------- GQA
@@ -306,6 +371,11 @@ class RefStore:
             L.refd_mla_create.argtypes = [_P, ctypes.c_uint64, ctypes.c_uint64]
             L.refd_mla_route.restype = ctypes.c_int
             L.refd_mla_route.argtypes = [_P, _P, ctypes.c_uint64, ctypes.c_uint64, _P, _P]
+            L.refd_mla_create_policy.restype = _P
+            L.refd_mla_create_policy.argtypes = [_P, ctypes.c_uint64, ctypes.c_uint64] + [_P] * 6
+            L.refd_mla_route_policy.restype = ctypes.c_int
+            L.refd_mla_route_policy.argtypes = [_P, _P, ctypes.c_uint64] + [ctypes.c_char_p] * 5 + [
+                ctypes.c_uint64, _P, _P]
             L.refd_gqa_create.restype = _P
             L.refd_gqa_create.argtypes = [_P, _P, ctypes.c_uint64, ctypes.c_uint64,
                                           ctypes.c_uint64]
@@ -334,6 +404,51 @@ class RefStore:
         self._h, self.kind, self.dim = h, "mla", r.shape[1]
         del self._keep
         return self
+
+    def load_mla_policy(self, rows, node_lexical=None, cats=None, active=None) -> "RefStore":
+        """MLA store with per-node lexical keys, route metadata and active flags."""
+        r = np.ascontiguousarray(rows, dtype=np.float32)
+        n = r.shape[0]
+
+        def carr(vals):
+            if vals is None:
+                return None
+            a = (ctypes.c_char_p * n)()
+            for i, v in enumerate(vals):
+                if isinstance(v, (list, tuple)):
+                    v = "\n".join(v)
+                a[i] = None if v is None else str(v).encode()
+            return a
+
+        lex = carr(node_lexical)
+        cs = [carr(cats[k]) if cats is not None else None for k in range(4)]
+        act = None if active is None else np.ascontiguousarray(active, dtype=np.uint8)
+        self._keep_c = (lex, cs, act)
+        h = self._L.refd_mla_create_policy(_ptr(r), n, r.shape[1], lex, cs[0], cs[1], cs[2],
+                                           cs[3], None if act is None else _ptr(act))
+        if not h:
+            raise RuntimeError("reference MLA store load failed")
+        self._h, self.kind, self.dim = h, "mla", r.shape[1]
+        return self
+
+    def route_policy(self, query, k: int, lexical=None, filters=None) -> list[int]:
+        """grm_store_route_filtered with '\n'-joined blobs."""
+        def blob(v):
+            if v is None:
+                return b""
+            if isinstance(v, (list, tuple)):
+                v = "\n".join(str(x) for x in v)
+            return str(v).encode()
+        f = list(filters) if filters is not None else [None] * 4
+        out = np.zeros(k, dtype=np.uint64)
+        cnt = ctypes.c_uint64(0)
+        q = np.ascontiguousarray(query, dtype=np.float32)
+        rc = self._L.refd_mla_route_policy(self._h, _ptr(q), q.size, blob(lexical), blob(f[0]),
+                                           blob(f[1]), blob(f[2]), blob(f[3]), k, _ptr(out),
+                                           ctypes.addressof(cnt))
+        if rc != 0:
+            raise RuntimeError(self._L.refd_last_error(self._h).decode())
+        return [int(x) for x in out[: cnt.value]]
 
     def load_gqa(self, keys_bf16, token_offsets, kv_heads: int, head_dim: int) -> "RefStore":
         k = np.ascontiguousarray(keys_bf16, dtype=np.uint16).reshape(-1)

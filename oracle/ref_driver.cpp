@@ -33,6 +33,49 @@ grm_store_handle* refd_mla_create(const float* rows, uint64_t n, uint64_t dim) {
   return h;
 }
 
+// MLA store with route policy data per node: lexical keys through
+// grm_store_set_route_list's blob, kind/scope/durability/mutability through
+// grm_store_set_route_metadata and the active flag through grm_store_set_active
+// (cpp/grm_runtime_c.h:162-184, :394-400).  NULL arrays or entries leave the
+// reference's defaults.
+grm_store_handle* refd_mla_create_policy(const float* rows, uint64_t n, uint64_t dim,
+                                         const char* const* lexical, const char* const* kinds,
+                                         const char* const* scopes,
+                                         const char* const* durabilities,
+                                         const char* const* mutabilities,
+                                         const uint8_t* active) {
+  grm_store_handle* h = grm_store_create_mla("RefDriverMLA", 1, 2048, 576, 0, 512, 64);
+  if (!h) return nullptr;
+  const uint64_t offs[2] = {0, dim};
+  auto at = [](const char* const* a, uint64_t i) -> const char* { return a ? a[i] : nullptr; };
+  for (uint64_t i = 0; i < n; ++i) {
+    uint64_t id = 0;
+    const char* lex = at(lexical, i);
+    int rc = grm_store_add_node(h, "", 1, nullptr, 0, &id);
+    if (rc == 0 && id != i) rc = -1;
+    if (rc == 0) rc = grm_store_set_route_list(h, id, rows + i * dim, dim, offs, 1, lex ? lex : "");
+    if (rc == 0 && (kinds || scopes || durabilities || mutabilities))
+      rc = grm_store_set_route_metadata(h, id, at(kinds, i), at(scopes, i), at(durabilities, i),
+                                        at(mutabilities, i));
+    if (rc == 0 && active && !active[i]) rc = grm_store_set_active(h, id, 0);
+    if (rc != 0) {
+      grm_store_destroy(h);
+      return nullptr;
+    }
+  }
+  return h;
+}
+
+// grm_store_route_filtered (cpp/grm_runtime_c.h:411-422).
+int refd_mla_route_policy(grm_store_handle* h, const float* q, uint64_t dim, const char* lexical,
+                          const char* kinds, const char* scopes, const char* durabilities,
+                          const char* mutabilities, uint64_t topk, uint64_t* out,
+                          uint64_t* out_count) {
+  return grm_store_route_filtered(h, q, dim, lexical ? lexical : "", kinds ? kinds : "",
+                                  scopes ? scopes : "", durabilities ? durabilities : "",
+                                  mutabilities ? mutabilities : "", topk, out, topk, out_count);
+}
+
 // grm_store_route (cpp/grm_runtime_c.h:403-410).
 int refd_mla_route(grm_store_handle* h, const float* q, uint64_t dim, uint64_t topk,
                    uint64_t* out, uint64_t* out_count) {

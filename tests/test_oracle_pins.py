@@ -42,3 +42,46 @@ def test_gqa_restatement_equals_reference_runtime(qt, kv, h):
         want = st.route(q, 12)
     got = [int(x) for x in ids if x != np.iinfo(np.uint64).max]
     assert got == want
+
+
+def _policy_case(seed, n, dim):
+    rng = np.random.default_rng(seed)
+    rows = rng.standard_normal((n, dim)).astype(np.float32)
+    rows[::53] = rows[7]                          # tie groups
+    vocab = [f"tok{i}" for i in range(60)] + ["common"]
+    lex = []
+    for i in range(n):
+        keys = list(rng.choice(vocab[:-1], rng.integers(0, 4), replace=False))
+        if i % 3 == 0:
+            keys.append("common")
+        lex.append(keys if keys else None)
+    kinds = [str(rng.choice(["turn", "doc", "fact", "custom", ""])) for _ in range(n)]
+    scopes = [str(rng.choice(["conversation", "project", "user", "odd scope"])) for _ in range(n)]
+    active = rng.random(n) > 0.08
+    return rows, lex, [kinds, scopes, None, None], active, rng
+
+
+@pytest.mark.parametrize("seed,n,dim", [(21, 900, 64), (22, 1500, 128), (23, 400, 16)])
+def test_mla_policy_restatement_equals_reference_runtime(seed, n, dim):
+    """Lexical bonus, filters (known, unknown and default values) and
+    inactive nodes: route_mla_arena through grm_store_route_filtered."""
+    rows, lex, cats, active, rng = _policy_case(seed, n, dim)
+    cases = [
+        ([], None),
+        (["tok1", "tok2"], None),
+        (["common"], None),
+        (["tok3", "tok3", "nosuchkey"], [["doc", "custom"], None, None, None]),
+        (["tok4", "common"], [["turn"], ["project", "user"], None, None]),
+        ([], [None, ["odd scope"], ["session"], None]),
+        (["tok5"], [None, None, ["permanent"], None]),      # excludes every node
+        (["tok6"], [None, None, None, ["ephemeral", "stable"]]),
+    ]
+    with O.RefStore().load_mla_policy(rows, lex, cats, active) as st:
+        for qlex, filt in cases:
+            q = rng.standard_normal(dim).astype(np.float32)
+            for k in (1, 5, 16):
+                want = st.route_policy(q, k, qlex, filt)
+                ids, _ = O.mla_route_policy(rows, q, k, node_lexical=lex, cats=cats,
+                                            active=active, query_lexical=qlex, filters=filt)
+                got = [int(x) for x in ids if x != np.iinfo(np.uint64).max]
+                assert got == want, (qlex, filt, k)
