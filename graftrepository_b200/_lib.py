@@ -61,6 +61,10 @@ _SIGS = {
                                        ctypes.c_char_p, ctypes.c_char_p, ctypes.c_char_p,
                                        _P, _P, _P]),
     "grm_b200_gqa_paths": (_I, [_P, _P]),
+    "grm_b200_gqa_bank_set_policy": (_I, [_P, _P, _P, _P, _P, _P, _P]),
+    "grm_b200_gqa_route_policy": (_I, [_P, _P, _I, _I, _I, _I, _P, ctypes.c_char_p,
+                                       ctypes.c_char_p, ctypes.c_char_p, ctypes.c_char_p,
+                                       _P, _P, _P]),
     "grm_b200_mla_route_noalloc": (_I, [_P, _I64, _I, _P, _I, _I, _P, _P, _P]),
     "grm_b200_gqa_bank_create": (_I, [_P, _I, _P, _I64, _I, _I, _I, _P]),
     "grm_b200_gqa_bank_create_device": (_I, [_P, _I, _P, _I64, _I, _I, _P]),

@@ -36,6 +36,7 @@
 #include <cuda.h>
 
 #include "common.cuh"
+#include "route_policy.cuh"
 
 namespace grm_b200 {
 namespace gqa {
@@ -198,6 +199,10 @@ struct RouteParams {
   uint64_t* out_ids;           // optional device outputs (topk entries of this query)
   float* out_scores;
   uint64_t id_offset;          // added to returned node rows (first row of this shard)
+  // route policy (lexical bonus and filters, cpp/grm_runtime.cpp:4498-4867)
+  const uint32_t* allow;       // bitmap of routable nodes (nullptr: all)
+  const uint32_t* hits;        // [N] lexical hits of this query (lexical routes)
+  int lex_m;                   // query lexical keys; > 0 selects the normalised lexical law
 };
 
 // K permutation shared by the query fragments and the scan kernels: thread
@@ -676,7 +681,9 @@ __global__ void node_bounds_kernel(RouteParams p, float eps_abs) {
     forced = __any_sync(kFull, forced);
     if (lane == 0) {
       float l, u;
-      if (T == 0) {
+      if (!policy::row_allowed(p.allow, node)) {
+        l = u = __int_as_float(0x7FC00000);                 // filtered out: never scored
+      } else if (T == 0) {
         l = u = 0.0f;                                       // exact: the reference returns 0
       } else if (!qfinite || p.key_bad[node]) {
         l = u = __int_as_float(0x7FC00000);                 // NaN: dropped
@@ -723,10 +730,15 @@ __global__ void __launch_bounds__(1024) select_kernel(RouteParams p) {
     if (lane == 0) sh_L = L;
   }
   __syncthreads();
-  const float L = sh_L;
+  // Lexical routes order by raw / (max raw + 1e-8) + bonus: a node without
+  // hits can reach the final top-k only if its raw is within a rounding of
+  // that division (2^-23 relative) of the k-th raw, so the threshold drops by
+  // 2^-21 relative; every allowed node with hits is a candidate as well.
+  const float L = p.lex_m ? sh_L - fabsf(sh_L) * 4.76837158203125e-07f : sh_L;
   for (int64_t n = threadIdx.x; n < p.nodes; n += blockDim.x) {
     const float u = p.hi[n];
-    if (u == u && u >= L) {  // not NaN
+    const bool hit = p.lex_m && p.hits[n] && policy::row_allowed(p.allow, n);
+    if ((u == u && u >= L) || hit) {  // not NaN
       const int slot = atomicAdd(p.cand_count, 1);
       p.cand[slot] = (uint32_t)n;
     }
@@ -821,12 +833,17 @@ __global__ void __launch_bounds__(256) refine_kernel(RouteParams p) {
 }
 
 // Final scores of the candidates (sequential fp32 head sum, as the reference)
-// and the exact top-k.  One warp.
+// and the exact top-k.  One warp.  Lexical routes (lex_m > 0) rank by the
+// reference's S = raw / (max raw + 1e-8) + hits / m instead
+// (cpp/grm_runtime.cpp:4840-4867): the raws are kept in lo[node] by the first
+// pass and the maximum over the candidates (which contain the top raw) sets
+// the norm.
 __global__ void finalize_kernel(RouteParams p) {
   const int lane = threadIdx.x;
   const int count = *p.cand_count;
   WarpList list;
   list.init();
+  float max_abs = 0.0f;
   for (int base = 0; base < count; base += 32) {
     const int ci = base + lane;
     float score = -INFINITY;
@@ -845,8 +862,29 @@ __global__ void finalize_kernel(RouteParams p) {
         score = __fdiv_rn(total, (float)p.heads);
       }
       for (int h = 0; h < p.heads; ++h) best[h] = 0u;
+      if (p.lex_m) {
+        p.lo[node] = score;
+        if (isfinite(score)) max_abs = fmaxf(max_abs, fabsf(score));
+      }
     }
-    list.offer(score, node, lane);
+    if (!p.lex_m) list.offer(score, node, lane);
+  }
+  if (p.lex_m) {
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) max_abs = fmaxf(max_abs, __shfl_xor_sync(kFull, max_abs, o));
+    const float norm = __fadd_rn(max_abs, 1.0e-8f);
+    for (int base = 0; base < count; base += 32) {
+      const int ci = base + lane;
+      float S = -INFINITY;
+      uint32_t node = kNoRow;
+      if (ci < count) {
+        node = p.cand[ci];
+        const float raw = p.lo[node];
+        if (isfinite(raw))
+          S = __fadd_rn(__fdiv_rn(raw, norm), __fdiv_rn((float)p.hits[node], (float)p.lex_m));
+      }
+      list.offer(S, node, lane);
+    }
   }
   const bool failed = p.qinfo->err != 0;  // a bounded wait of the scan gave up
   const bool ok = !failed && lane < p.topk && isfinite(list.s) && list.id != kNoRow;
@@ -915,6 +953,7 @@ struct grm_b200_gqa_bank {
   ErrorSlot err;
   uint64_t routes = 0;
   unsigned long long* d_refined = nullptr;  // counted by finalize_kernel
+  grm_b200::policy::Policy pol;             // lexical keys, filter codes, active flags
 };
 
 namespace {
@@ -1082,10 +1121,12 @@ int ensure_heads(grm_b200_gqa_bank* b, int heads, int nt) {
 
 // `use_bank_stream`: launch on the bank's private stream (synchronous entry
 // points); otherwise on `stream`, where 0 is the legacy default stream.
+// `allow`, `hits`, `lex_m`: route policy inputs (see RouteParams).
 int route_one(grm_b200_gqa_bank* b, const float* dq, int heads, int qt, int topk,
               bool use_bank_stream = true, cudaStream_t stream = nullptr,
               uint64_t* out_ids = nullptr, float* out_scores = nullptr,
-              uint64_t id_offset = 0) {
+              uint64_t id_offset = 0, const uint32_t* allow = nullptr,
+              const uint32_t* hits = nullptr, int lex_m = 0) {
   if (use_bank_stream) stream = b->stream;
   const int group = heads / b->kh_n;
   const int nv = group * qt;
@@ -1127,6 +1168,9 @@ int route_one(grm_b200_gqa_bank* b, const float* dq, int heads, int qt, int topk
   p.out_ids = out_ids;
   p.out_scores = out_scores;
   p.id_offset = id_offset;
+  p.allow = allow;
+  p.hits = hits;
+  p.lex_m = lex_m;
   cudaStream_t saved = b->stream;
   b->stream = stream;  // every launch below goes to the caller's stream
   struct Restore {
@@ -1204,6 +1248,7 @@ void bank_free(grm_b200_gqa_bank* b) {
   for (void* q : ptrs)
     if (q) cudaFree(q);
   if (b->h_result) cudaFreeHost(b->h_result);
+  grm_b200::policy::policy_free(b->pol);
   if (b->ev0) cudaEventDestroy(b->ev0);
   if (b->ev1) cudaEventDestroy(b->ev1);
   if (b->stream) cudaStreamDestroy(b->stream);
@@ -1440,6 +1485,90 @@ int grm_b200_gqa_route_async(grm_b200_gqa_bank* bank, const float* queries_devic
                              out_scores_device + (int64_t)i * topk, id_offset);
     if (rc) return rc;
   }
+  bank->routes += (uint64_t)query_count;
+  return 0;
+}
+
+int grm_b200_gqa_bank_set_policy(grm_b200_gqa_bank* bank, const char* const* lexical_keys,
+                                 const char* const* kinds, const char* const* scopes,
+                                 const char* const* durabilities,
+                                 const char* const* mutabilities, const uint8_t* active) {
+  if (!bank) return GRM_B200_EINVAL;
+  std::lock_guard<std::mutex> lock(bank->mu);
+  cudaError_t e = cudaSetDevice(bank->device);
+  if (e != cudaSuccess) return bank->err.set(cuda_status(e), "cudaSetDevice failed");
+  cudaStreamSynchronize(bank->stream);
+  const char* const* cats[policy::kCats] = {kinds, scopes, durabilities, mutabilities};
+  return policy::policy_set(bank->pol, bank->nodes, lexical_keys, cats, active, bank->err);
+}
+
+int grm_b200_gqa_route_policy(grm_b200_gqa_bank* bank, const float* queries_host, int query_count,
+                              int query_heads, int query_tokens, int topk,
+                              const char* const* lexical_keys, const char* kind_filters,
+                              const char* scope_filters, const char* durability_filters,
+                              const char* mutability_filters, uint64_t* out_ids_host,
+                              float* out_scores_host, float* elapsed_ms) {
+  if (!bank) return GRM_B200_EINVAL;
+  std::lock_guard<std::mutex> lock(bank->mu);
+  if (!queries_host || query_count <= 0 || query_heads <= 0 || query_tokens <= 0 ||
+      query_heads % bank->kh_n != 0 || !out_ids_host || topk <= 0 || topk > GRM_B200_MAX_TOPK)
+    return bank->err.set(GRM_B200_EINVAL, "invalid GQA policy route arguments");
+  cudaError_t e = cudaSetDevice(bank->device);
+  if (e != cudaSuccess) return bank->err.set(cuda_status(e), "cudaSetDevice failed");
+  int rc = 0;
+  if (!bank->pol.set) {  // every node keeps the reference's defaults: no keys, active
+    const char* const* cats[policy::kCats] = {nullptr, nullptr, nullptr, nullptr};
+    cudaStreamSynchronize(bank->stream);
+    if ((rc = policy::policy_set(bank->pol, bank->nodes, nullptr, cats, nullptr, bank->err)))
+      return rc;
+  }
+  const size_t qsize = (size_t)query_heads * query_tokens * bank->dim;
+  const size_t need = (size_t)query_count * qsize;
+  if (need > bank->dq_cap) {
+    if (bank->d_queries) cudaFree(bank->d_queries);
+    bank->d_queries = nullptr;
+    bank->dq_cap = 0;
+    e = cudaMalloc(&bank->d_queries, need * sizeof(float));
+    if (e != cudaSuccess) return bank->err.set(cuda_status(e), "GQA query buffer allocation failed");
+    bank->dq_cap = need;
+  }
+  e = cudaMemcpyAsync(bank->d_queries, queries_host, need * sizeof(float), cudaMemcpyHostToDevice,
+                      bank->stream);
+  if (e != cudaSuccess) return bank->err.set(cuda_status(e), "GQA query upload failed");
+  cudaEventRecord(bank->ev0, bank->stream);
+  const char* const filters[policy::kCats] = {kind_filters, scope_filters, durability_filters,
+                                              mutability_filters};
+  const uint32_t* allow = nullptr;
+  if ((rc = policy::policy_allow(bank->pol, filters, bank->sms, bank->stream, &allow, bank->err)))
+    return rc;
+  for (int q = 0; q < query_count; ++q) {
+    int m = 0;
+    const policy::Ranges ranges =
+        policy::policy_ranges(bank->pol, lexical_keys ? lexical_keys[q] : nullptr, &m);
+    if (m && (rc = policy::policy_pass(bank->pol, ranges, 0, bank->sms, bank->stream, bank->err)))
+      return rc;
+    rc = route_one(bank, bank->d_queries + q * qsize, query_heads, query_tokens, topk, true,
+                   nullptr, nullptr, nullptr, 0, allow, bank->pol.d_hits, m);
+    if (rc) return rc;
+    if (m && (rc = policy::policy_pass(bank->pol, ranges, 1, bank->sms, bank->stream, bank->err)))
+      return rc;  // leaves hits zero for the next query
+    e = cudaMemcpyAsync(bank->h_result, bank->d_result, sizeof(Result), cudaMemcpyDeviceToHost,
+                        bank->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(bank->stream);
+    if (e != cudaSuccess) return bank->err.set(cuda_status(e), "GQA policy route failed: %s", cudaGetErrorString(e));
+    if (bank->h_result->count < 0)
+      return bank->err.set(GRM_B200_KERNEL_BASE + 1, "GQA scan: a bounded device wait gave up (query %d)", q);
+    for (int j = 0; j < topk; ++j) {
+      out_ids_host[(int64_t)q * topk + j] = bank->h_result->ids[j];
+      if (out_scores_host) out_scores_host[(int64_t)q * topk + j] = bank->h_result->scores[j];
+    }
+  }
+  cudaEventRecord(bank->ev1, bank->stream);
+  e = cudaEventSynchronize(bank->ev1);
+  float ms = 0.0f;
+  if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, bank->ev0, bank->ev1);
+  if (e != cudaSuccess) return bank->err.set(cuda_status(e), "GQA route timing failed");
+  if (elapsed_ms) *elapsed_ms = ms;
   bank->routes += (uint64_t)query_count;
   return 0;
 }

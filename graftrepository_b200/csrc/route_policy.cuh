@@ -109,7 +109,7 @@ __device__ __forceinline__ bool row_allowed(const uint32_t* allow, int64_t row) 
 }
 
 // allow word w covers rows 32w .. 32w+31: lane l tests row 32w + l.
-__global__ void allow_kernel(const uint32_t* __restrict__ codes, const uint32_t* __restrict__ active,
+static __global__ void allow_kernel(const uint32_t* __restrict__ codes, const uint32_t* __restrict__ active,
                              int64_t nodes, AllowSets sets, uint32_t* __restrict__ allow) {
   const int lane = threadIdx.x & 31;
   const int64_t words = (nodes + 31) / 32;
@@ -138,7 +138,7 @@ __device__ __forceinline__ uint32_t posting_node(const ItemRanges& r, const uint
 }
 
 // Every posting of every query key: hits[node] += 1.
-__global__ void lex_count_kernel(ItemRanges r, const uint32_t* __restrict__ post,
+static __global__ void lex_count_kernel(ItemRanges r, const uint32_t* __restrict__ post,
                                  uint32_t* __restrict__ hits) {
   const uint32_t total = r.start[r.n];
   for (uint32_t j = blockIdx.x * blockDim.x + threadIdx.x; j < total; j += gridDim.x * blockDim.x)
@@ -147,7 +147,7 @@ __global__ void lex_count_kernel(ItemRanges r, const uint32_t* __restrict__ post
 
 // The first posting thread to reach a node takes its count (and leaves 0
 // behind for the next route) and appends (node, hits).
-__global__ void lex_collect_kernel(ItemRanges r, const uint32_t* __restrict__ post,
+static __global__ void lex_collect_kernel(ItemRanges r, const uint32_t* __restrict__ post,
                                    uint32_t* __restrict__ hits, uint2* __restrict__ list,
                                    uint32_t* __restrict__ counter) {
   const uint32_t total = r.start[r.n];
@@ -165,7 +165,7 @@ __global__ void lex_collect_kernel(ItemRanges r, const uint32_t* __restrict__ po
 // first; non-finite S dropped.  One block of kMergeWarps warps.
 constexpr int kMergeWarps = 8;
 
-__global__ void __launch_bounds__(kMergeWarps * 32) lex_merge_kernel(
+static __global__ void __launch_bounds__(kMergeWarps * 32) lex_merge_kernel(
     uint64_t* ids, float* scores, int* count, int topk, uint64_t id_offset,
     const float* __restrict__ cand_s, const uint32_t* __restrict__ cand_id,
     const uint32_t* __restrict__ counter) {
@@ -349,47 +349,64 @@ inline int policy_allow(Policy& P, const char* const filters[kCats], int sms, cu
   return 0;
 }
 
-// Launch the count + collect kernels for one query's lexical keys.  *m_out =
-// the number of query keys (the bonus denominator, unknown keys included).
-// Returns 0 with *m_out == 0 when the query has no keys.
-inline int policy_collect(Policy& P, const char* blob, int sms, cudaStream_t s, int* m_out,
-                          ErrorSlot& err) {
+// The posting ranges of one query's lexical keys (keys absent from the
+// bank's dictionary have none).  *m_out = the number of query keys, the
+// bonus denominator (unknown keys included).
+using Ranges = std::vector<std::pair<uint32_t, uint32_t>>;
+
+inline Ranges policy_ranges(const Policy& P, const char* blob, int* m_out) {
   const auto keys = split_keys(blob);
   *m_out = (int)keys.size();
-  if (keys.empty()) return 0;
-  cudaError_t e = cudaMemsetAsync(P.d_counter, 0, sizeof(uint32_t), s);
-  if (e != cudaSuccess) return err.set(cuda_status(e), "lexical counter reset failed");
-  std::vector<std::pair<uint32_t, uint32_t>> ranges;
+  Ranges ranges;
   for (const auto& k : keys) {
     auto it = P.lex_dict.find(k);
     if (it == P.lex_dict.end()) continue;
     const uint32_t off = P.h_post_off[it->second], end = P.h_post_off[it->second + 1];
     if (end > off) ranges.emplace_back(off, end - off);
   }
-  for (int pass = 0; pass < 2; ++pass) {
-    for (size_t c0 = 0; c0 < ranges.size(); c0 += kItemsPerLaunch) {
-      ItemRanges r;
-      std::memset(&r, 0, sizeof(r));
-      r.n = (int)std::min<size_t>(kItemsPerLaunch, ranges.size() - c0);
-      uint64_t acc = 0;
-      for (int i = 0; i < r.n; ++i) {
-        r.off[i] = ranges[c0 + i].first;
-        r.len[i] = ranges[c0 + i].second;
-        r.start[i] = (uint32_t)acc;
-        acc += r.len[i];
-      }
-      if (acc > 0xFFFFFFFFull) return err.set(GRM_B200_EINVAL, "lexical postings exceed 2^32");
-      r.start[r.n] = (uint32_t)acc;
-      const int grid = (int)std::max<uint64_t>(1, std::min<uint64_t>((uint64_t)sms * 8, (acc + 255) / 256));
-      if (pass == 0)
-        lex_count_kernel<<<grid, 256, 0, s>>>(r, P.d_post, P.d_hits);
-      else
-        lex_collect_kernel<<<grid, 256, 0, s>>>(r, P.d_post, P.d_hits, P.d_hitlist, P.d_counter);
+  return ranges;
+}
+
+// pass 0: hits[node] += 1 over every posting; pass 1: take the counts into
+// the hit list (and leave hits zero).
+inline int policy_pass(Policy& P, const Ranges& ranges, int pass, int sms, cudaStream_t s,
+                       ErrorSlot& err) {
+  for (size_t c0 = 0; c0 < ranges.size(); c0 += kItemsPerLaunch) {
+    ItemRanges r;
+    std::memset(&r, 0, sizeof(r));
+    r.n = (int)std::min<size_t>(kItemsPerLaunch, ranges.size() - c0);
+    uint64_t acc = 0;
+    for (int i = 0; i < r.n; ++i) {
+      r.off[i] = ranges[c0 + i].first;
+      r.len[i] = ranges[c0 + i].second;
+      r.start[i] = (uint32_t)acc;
+      acc += r.len[i];
     }
+    if (acc > 0xFFFFFFFFull) return err.set(GRM_B200_EINVAL, "lexical postings exceed 2^32");
+    r.start[r.n] = (uint32_t)acc;
+    const int grid = (int)std::max<uint64_t>(1, std::min<uint64_t>((uint64_t)sms * 8, (acc + 255) / 256));
+    if (pass == 0)
+      lex_count_kernel<<<grid, 256, 0, s>>>(r, P.d_post, P.d_hits);
+    else
+      lex_collect_kernel<<<grid, 256, 0, s>>>(r, P.d_post, P.d_hits, P.d_hitlist, P.d_counter);
   }
-  e = cudaGetLastError();
+  cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return err.set(cuda_status(e), "lexical kernels launch failed");
   return 0;
+}
+
+// Count + collect for one query: the hit list (node, hits) in d_hitlist,
+// its length in d_counter.  Returns 0 with *m_out == 0 when the query has no
+// keys.
+inline int policy_collect(Policy& P, const char* blob, int sms, cudaStream_t s, int* m_out,
+                          ErrorSlot& err) {
+  const Ranges ranges = policy_ranges(P, blob, m_out);
+  if (*m_out == 0) return 0;
+  cudaError_t e = cudaMemsetAsync(P.d_counter, 0, sizeof(uint32_t), s);
+  if (e != cudaSuccess) return err.set(cuda_status(e), "lexical counter reset failed");
+  int rc = policy_pass(P, ranges, 0, sms, s, err);
+  if (!rc) rc = policy_pass(P, ranges, 1, sms, s, err);
+  return rc;
 }
 
 }  // namespace policy

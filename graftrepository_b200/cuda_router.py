@@ -152,6 +152,29 @@ def _c_strings(values, n: int, *, join: bool = False):
     return arr
 
 
+def _set_policy(fn, handle, err, n, lexical_keys, kinds, scopes, durabilities, mutabilities,
+                active) -> None:
+    arrays = [_c_strings(lexical_keys, n, join=True)]
+    arrays += [_c_strings(v, n) for v in (kinds, scopes, durabilities, mutabilities)]
+    act = None
+    if active is not None:
+        act = np.ascontiguousarray(active, dtype=np.uint8).reshape(-1)
+        if act.shape[0] != n:
+            raise ValueError("active must have one entry per bank row")
+    rc = fn(handle, *[None if a is None else ctypes.addressof(a) for a in arrays],
+            None if act is None else act.ctypes.data)
+    _lib.check(rc, err)
+
+
+def _query_lexical(lexical_keys, count: int):
+    """One key list per query; a single list (or blob) for a single query."""
+    lex = lexical_keys
+    if lex is not None and count == 1 and (isinstance(lex, str) or (
+            len(lex) > 0 and all(isinstance(x, str) for x in lex))):
+        lex = [lex]
+    return _c_strings(lex, count, join=True)
+
+
 def _fits(values: np.ndarray, dtype) -> bool:
     """True when every value survives a round trip through `dtype` bit-exactly
     (NaN payloads aside), so a narrower bank keeps the reference's values."""
@@ -320,19 +343,8 @@ class CudaMLARouteBank:
         scope, durability, mutability, active; cpp/grm_runtime.hpp:483-494),
         one entry per bank row.  lexical_keys[i]: a sequence of keys or a
         '\n'-joined string; None values keep the reference's defaults."""
-        n = self.nodes
-        arrays = [_c_strings(lexical_keys, n, join=True)]
-        arrays += [_c_strings(v, n) for v in (kinds, scopes, durabilities, mutabilities)]
-        act = None
-        if active is not None:
-            act = np.ascontiguousarray(active, dtype=np.uint8).reshape(-1)
-            if act.shape[0] != n:
-                raise ValueError("active must have one entry per bank row")
-        rc = _lib.load().grm_b200_mla_bank_set_policy(
-            self._h, *[None if a is None else ctypes.addressof(a) for a in arrays],
-            None if act is None else act.ctypes.data)
-        _lib.check(rc, self._err)
-        self._policy_rows = n
+        _set_policy(_lib.load().grm_b200_mla_bank_set_policy, self._h, self._err, self.nodes,
+                    lexical_keys, kinds, scopes, durabilities, mutabilities, active)
 
     def route_policy_topk(self, queries, *, topk: int, lexical_keys=None, kinds=(), scopes=(),
                           durabilities=(), mutabilities=()):
@@ -350,11 +362,7 @@ class CudaMLARouteBank:
         if not 0 < int(topk) <= MAX_TOPK:
             raise ValueError(f"topk must be in 1..{MAX_TOPK}")
         count = q.shape[0]
-        lex = lexical_keys
-        if lex is not None and count == 1 and (isinstance(lex, str) or (
-                len(lex) > 0 and all(isinstance(x, str) for x in lex))):
-            lex = [lex]
-        lex_arr = _c_strings(lex, count, join=True)
+        lex_arr = _query_lexical(lexical_keys, count)
         out = np.empty((count, int(topk)), dtype=np.uint64)
         scores = np.empty((count, int(topk)), dtype=np.float32)
         elapsed = ctypes.c_float(0.0)
@@ -564,6 +572,57 @@ class CudaGQARouteBank:
             walls.append(wall)
             devs.append(dev)
         return self._finish(rows, scores, walls, devs, q.shape[0], warmup, repeats)
+
+    def set_route_policy(self, *, lexical_keys=None, kinds=None, scopes=None,
+                         durabilities=None, mutabilities=None, active=None) -> None:
+        """Per-node route policy data, as CudaMLARouteBank.set_route_policy."""
+        _set_policy(_lib.load().grm_b200_gqa_bank_set_policy, self._h, self._err,
+                    int(self.node_ids.shape[0]), lexical_keys, kinds, scopes, durabilities,
+                    mutabilities, active)
+
+    def route_policy_topk(self, queries, *, topk: int, lexical_keys=None, kinds=(), scopes=(),
+                          durabilities=(), mutabilities=()):
+        """route_gqa_raw with its lexical bonus and filters
+        (cpp/grm_runtime.cpp:4498-4867) on the device: (node ids [Q, topk],
+        scores [Q, topk]: S with lexical keys, raw without)."""
+        if self._h is None:
+            raise RuntimeError("CUDA GQA route bank is closed")
+        q = np.ascontiguousarray(queries, dtype=np.float32)
+        if q.ndim == 3:
+            q = q[None, ...]
+        if q.ndim != 4 or q.shape[3] != self.head_dim:
+            raise ValueError("GQA queries must have shape (queries, heads, tokens, head_dim)")
+        if not 0 < int(topk) <= MAX_TOPK:
+            raise ValueError(f"topk must be in 1..{MAX_TOPK}")
+        count = q.shape[0]
+        lex_arr = _query_lexical(lexical_keys, count)
+        out = np.empty((count, int(topk)), dtype=np.uint64)
+        scores = np.empty((count, int(topk)), dtype=np.float32)
+        elapsed = ctypes.c_float(0.0)
+        rc = _lib.load().grm_b200_gqa_route_policy(
+            self._h, q.ctypes.data, count, q.shape[1], q.shape[2], int(topk),
+            None if lex_arr is None else ctypes.addressof(lex_arr), _blob(kinds), _blob(scopes),
+            _blob(durabilities), _blob(mutabilities), out.ctypes.data, scores.ctypes.data,
+            ctypes.byref(elapsed))
+        _lib.check(rc, self._err)
+        self.last_scores = scores
+        n = self.node_ids.shape[0]
+        if np.any((out != _U64MAX) & (out >= n)):
+            raise RuntimeError("CUDA GQA route returned an out-of-range row ID")
+        mapped = np.where(out == _U64MAX, _U64MAX, self.node_ids[np.minimum(out, n - 1)])
+        return mapped, scores
+
+    def route_gqa(self, query, lexical_keys=(), topk=3, kinds=(), scopes=(), durabilities=(),
+                  mutabilities=()) -> list[int]:
+        """NativeGraftStore.route_gqa's signature (core/grm_native.py:1471-1496)."""
+        q = np.asarray(query, dtype=np.float32)
+        if q.ndim != 3:
+            raise ValueError("GQA query must have shape (heads, tokens, dim)")
+        ids, _ = self.route_policy_topk(q[None], topk=int(topk),
+                                        lexical_keys=[list(lexical_keys or ())], kinds=kinds,
+                                        scopes=scopes, durabilities=durabilities,
+                                        mutabilities=mutabilities)
+        return [int(x) for x in ids[0] if x != _U64MAX]
 
     def route_topk_device(self, device_queries, *, topk: int, warmup: int = 0,
                           route_repeats: int = 1):

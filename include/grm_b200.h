@@ -246,6 +246,25 @@ int grm_b200_gqa_stats(grm_b200_gqa_bank* bank, uint64_t* routes, uint64_t* refi
 #define GRM_B200_GQA_PATH_TMA 2   /* ... with TMA-staged key tiles */
 int grm_b200_gqa_paths(grm_b200_gqa_bank* bank, int* flags);
 
+/* Route policy data of the GQA bank's nodes: as grm_b200_mla_bank_set_policy. */
+int grm_b200_gqa_bank_set_policy(grm_b200_gqa_bank* bank, const char* const* lexical_keys,
+                                 const char* const* kinds, const char* const* scopes,
+                                 const char* const* durabilities,
+                                 const char* const* mutabilities, const uint8_t* active);
+
+/* route_gqa_raw with its policy channels (cpp/grm_runtime.cpp:4498-4867),
+ * replacing grm_store_route_gqa with lexical keys or filters
+ * (cpp/grm_runtime_c.h:423-436): filters as grm_b200_mla_route_policy; with
+ * lexical keys the order is S = raw / (max raw + 1e-8) + hits / m over the
+ * allowed nodes (the normalised law of :4840-4867), without them the raw
+ * order.  Scores returned are S (lexical) or raw. */
+int grm_b200_gqa_route_policy(grm_b200_gqa_bank* bank, const float* queries_host,
+                              int query_count, int query_heads, int query_tokens, int topk,
+                              const char* const* lexical_keys, const char* kind_filters,
+                              const char* scope_filters, const char* durability_filters,
+                              const char* mutability_filters, uint64_t* out_ids_host,
+                              float* out_scores_host, float* elapsed_ms);
+
 /* ------------------------------------------------------------------- mount */
 
 /* Fused dequantise + scatter of routed grafts into a preallocated bf16 arena

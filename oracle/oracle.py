@@ -28,6 +28,7 @@ __all__ = [
     "quant_ref", "dequant_ref", "quant_packed", "dequant_packed", "packed_group_bytes",
     "mount_scatter", "mount_rope", "swap_splice",
     "ROUTE_DEFAULTS", "split_keys", "route_allowed", "lexical_hits", "mla_route_policy",
+    "gqa_route_policy",
 ]
 
 _P = ctypes.c_void_p
@@ -248,6 +249,32 @@ def gqa_route(keys_bf16, token_offsets, kv_heads, head_dim, query, k: int):
     return ids, s
 
 
+def gqa_route_policy(keys_bf16, token_offsets, kv_heads: int, head_dim: int, query, k: int, *,
+                     node_lexical=None, cats=None, active=None, query_lexical=None,
+                     filters=None):
+    """route_gqa_raw with its lexical and filter channels
+    (cpp/grm_runtime.cpp:4498-4867).  Without lexical keys: raw order over
+    the allowed nodes.  With them: norm = max |raw| + 1e-8 (fp32) over the
+    allowed nodes with a finite raw, S = raw / norm + float(hits)/float(m)."""
+    raw = gqa_scores(keys_bf16, token_offsets, kv_heads, head_dim, query)
+    n = raw.shape[0]
+    have = route_allowed(n, cats, active, filters) & np.isfinite(raw)
+    qk = split_keys(query_lexical)
+    m = len(qk)
+    if m == 0:
+        s = raw.copy()
+    else:
+        max_abs = np.float32(np.max(np.abs(raw[have]), initial=np.float32(0.0)))
+        norm = np.float32(max_abs + np.float32(1.0e-8))
+        hits = np.array([lexical_hits(qk, node_lexical[i] if node_lexical is not None else None)
+                         for i in range(n)], dtype=np.float32)
+        with np.errstate(invalid="ignore"):
+            s = ((raw / norm).astype(np.float32) + hits / np.float32(m)).astype(np.float32)
+    s[~have] = np.nan
+    ids, sc, _ = topk(s, k)
+    return ids, sc
+
+
 # ------------------------------------------------------------------- quant
 
 def quant_ref(x, bits: int, group: int = 32) -> tuple[np.ndarray, np.ndarray]:
@@ -354,6 +381,18 @@ def ref_available(omp: bool = False) -> bool:
     return (REF_OMP_LIB_PATH if omp else REF_LIB_PATH).exists()
 
 
+def _c_array(vals, n: int):
+    """(char* [n]) of per-node strings; lists are '\n'-joined; None -> NULL."""
+    if vals is None:
+        return None
+    a = (ctypes.c_char_p * n)()
+    for i, v in enumerate(vals):
+        if isinstance(v, (list, tuple)):
+            v = "\n".join(v)
+        a[i] = None if v is None else str(v).encode()
+    return a
+
+
 class RefStore:
     """A reference ``grm_store_handle`` loaded with one route bank, driven
     through the reference's C ABI (``cpp/grm_runtime_c.h``)."""
@@ -376,6 +415,12 @@ class RefStore:
             L.refd_mla_route_policy.restype = ctypes.c_int
             L.refd_mla_route_policy.argtypes = [_P, _P, ctypes.c_uint64] + [ctypes.c_char_p] * 5 + [
                 ctypes.c_uint64, _P, _P]
+            L.refd_gqa_create_policy.restype = _P
+            L.refd_gqa_create_policy.argtypes = [_P, _P, ctypes.c_uint64, ctypes.c_uint64,
+                                                 ctypes.c_uint64] + [_P] * 6
+            L.refd_gqa_route_policy.restype = ctypes.c_int
+            L.refd_gqa_route_policy.argtypes = [_P, _P] + [ctypes.c_uint64] * 3 + [
+                ctypes.c_char_p] * 5 + [ctypes.c_uint64, _P, _P]
             L.refd_gqa_create.restype = _P
             L.refd_gqa_create.argtypes = [_P, _P, ctypes.c_uint64, ctypes.c_uint64,
                                           ctypes.c_uint64]
@@ -409,19 +454,8 @@ class RefStore:
         """MLA store with per-node lexical keys, route metadata and active flags."""
         r = np.ascontiguousarray(rows, dtype=np.float32)
         n = r.shape[0]
-
-        def carr(vals):
-            if vals is None:
-                return None
-            a = (ctypes.c_char_p * n)()
-            for i, v in enumerate(vals):
-                if isinstance(v, (list, tuple)):
-                    v = "\n".join(v)
-                a[i] = None if v is None else str(v).encode()
-            return a
-
-        lex = carr(node_lexical)
-        cs = [carr(cats[k]) if cats is not None else None for k in range(4)]
+        lex = _c_array(node_lexical, n)
+        cs = [_c_array(cats[k], n) if cats is not None else None for k in range(4)]
         act = None if active is None else np.ascontiguousarray(active, dtype=np.uint8)
         self._keep_c = (lex, cs, act)
         h = self._L.refd_mla_create_policy(_ptr(r), n, r.shape[1], lex, cs[0], cs[1], cs[2],
@@ -443,12 +477,38 @@ class RefStore:
         out = np.zeros(k, dtype=np.uint64)
         cnt = ctypes.c_uint64(0)
         q = np.ascontiguousarray(query, dtype=np.float32)
-        rc = self._L.refd_mla_route_policy(self._h, _ptr(q), q.size, blob(lexical), blob(f[0]),
-                                           blob(f[1]), blob(f[2]), blob(f[3]), k, _ptr(out),
-                                           ctypes.addressof(cnt))
+        if self.kind == "mla":
+            rc = self._L.refd_mla_route_policy(self._h, _ptr(q), q.size, blob(lexical),
+                                               blob(f[0]), blob(f[1]), blob(f[2]), blob(f[3]), k,
+                                               _ptr(out), ctypes.addressof(cnt))
+        else:
+            if q.ndim == 2:
+                q = np.ascontiguousarray(q[:, None, :])
+            rc = self._L.refd_gqa_route_policy(self._h, _ptr(q), q.shape[0], q.shape[1],
+                                               q.shape[2], blob(lexical), blob(f[0]), blob(f[1]),
+                                               blob(f[2]), blob(f[3]), k, _ptr(out),
+                                               ctypes.addressof(cnt))
         if rc != 0:
             raise RuntimeError(self._L.refd_last_error(self._h).decode())
         return [int(x) for x in out[: cnt.value]]
+
+    def load_gqa_policy(self, keys_bf16, token_offsets, kv_heads: int, head_dim: int,
+                        node_lexical=None, cats=None, active=None) -> "RefStore":
+        """GQA store with per-node lexical keys, route metadata and active flags."""
+        k = np.ascontiguousarray(keys_bf16, dtype=np.uint16).reshape(-1)
+        off = np.ascontiguousarray(token_offsets, dtype=np.uint64)
+        n = off.shape[0] - 1
+        lex = _c_array(node_lexical, n)
+        cs = [_c_array(cats[j], n) if cats is not None else None for j in range(4)]
+        act = None if active is None else np.ascontiguousarray(active, dtype=np.uint8)
+        self._keep_c = (lex, cs, act)
+        h = self._L.refd_gqa_create_policy(_ptr(k), _ptr(off), n, kv_heads, head_dim, lex, cs[0],
+                                           cs[1], cs[2], cs[3],
+                                           None if act is None else _ptr(act))
+        if not h:
+            raise RuntimeError("reference GQA store load failed")
+        self._h, self.kind, self.dim = h, "gqa", head_dim
+        return self
 
     def load_gqa(self, keys_bf16, token_offsets, kv_heads: int, head_dim: int) -> "RefStore":
         k = np.ascontiguousarray(keys_bf16, dtype=np.uint16).reshape(-1)

@@ -115,6 +115,57 @@ grm_store_handle* refd_gqa_create(const uint16_t* keys_bf16, const uint64_t* tok
   return h;
 }
 
+// GQA store with route policy data per node (as refd_mla_create_policy).
+grm_store_handle* refd_gqa_create_policy(const uint16_t* keys_bf16, const uint64_t* tok_off,
+                                         uint64_t n, uint64_t kv_heads, uint64_t head_dim,
+                                         const char* const* lexical, const char* const* kinds,
+                                         const char* const* scopes,
+                                         const char* const* durabilities,
+                                         const char* const* mutabilities,
+                                         const uint8_t* active) {
+  grm_store_handle* h = grm_store_create_gqa(
+      "RefDriverGQA", 36, 2560, 2048, 0, static_cast<int>(kv_heads),
+      static_cast<int>(head_dim));
+  if (!h) return nullptr;
+  auto at = [](const char* const* a, uint64_t i) -> const char* { return a ? a[i] : nullptr; };
+  std::vector<float> buf;
+  for (uint64_t i = 0; i < n; ++i) {
+    uint64_t id = 0;
+    int rc = grm_store_add_node(h, "", 1, nullptr, 0, &id);
+    if (rc == 0 && id != i) rc = -1;
+    const uint64_t T = tok_off[i + 1] - tok_off[i];
+    const uint64_t nv = kv_heads * T * head_dim;
+    buf.resize(nv);
+    const uint16_t* src = keys_bf16 + tok_off[i] * kv_heads * head_dim;
+    for (uint64_t v = 0; v < nv; ++v) {
+      const uint32_t u = static_cast<uint32_t>(src[v]) << 16;
+      std::memcpy(&buf[v], &u, 4);
+    }
+    const uint64_t offs[2] = {0, nv};
+    const char* lex = at(lexical, i);
+    if (rc == 0) rc = grm_store_set_route_list(h, id, buf.data(), nv, offs, 1, lex ? lex : "");
+    if (rc == 0 && (kinds || scopes || durabilities || mutabilities))
+      rc = grm_store_set_route_metadata(h, id, at(kinds, i), at(scopes, i), at(durabilities, i),
+                                        at(mutabilities, i));
+    if (rc == 0 && active && !active[i]) rc = grm_store_set_active(h, id, 0);
+    if (rc != 0) {
+      grm_store_destroy(h);
+      return nullptr;
+    }
+  }
+  return h;
+}
+
+int refd_gqa_route_policy(grm_store_handle* h, const float* q, uint64_t q_heads, uint64_t q_tokens,
+                          uint64_t head_dim, const char* lexical, const char* kinds,
+                          const char* scopes, const char* durabilities, const char* mutabilities,
+                          uint64_t topk, uint64_t* out, uint64_t* out_count) {
+  return grm_store_route_gqa(h, q, q_heads, q_tokens, head_dim, lexical ? lexical : "",
+                             kinds ? kinds : "", scopes ? scopes : "",
+                             durabilities ? durabilities : "", mutabilities ? mutabilities : "",
+                             topk, out, topk, out_count);
+}
+
 // grm_store_route_gqa (cpp/grm_runtime_c.h:423-436), no lexical/filter policy.
 int refd_gqa_route(grm_store_handle* h, const float* q, uint64_t q_heads, uint64_t q_tokens,
                    uint64_t head_dim, uint64_t topk, uint64_t* out, uint64_t* out_count) {

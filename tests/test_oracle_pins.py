@@ -85,3 +85,34 @@ def test_mla_policy_restatement_equals_reference_runtime(seed, n, dim):
                                             active=active, query_lexical=qlex, filters=filt)
                 got = [int(x) for x in ids if x != np.iinfo(np.uint64).max]
                 assert got == want, (qlex, filt, k)
+
+
+@pytest.mark.parametrize("seed,qt", [(31, 1), (32, 4), (33, 2)])
+def test_gqa_policy_restatement_equals_reference_runtime(seed, qt):
+    """The GQA lexical law (raw / (max raw + 1e-8) + hits / m), filters and
+    inactive nodes through grm_store_route_gqa."""
+    rng = np.random.default_rng(seed)
+    n, kv, d, h = 70, 4, 32, 16
+    T = rng.integers(0, 30, n)
+    T[0] = T[9] = 0
+    off = np.zeros(n + 1, np.uint64)
+    off[1:] = np.cumsum(T)
+    keys = O.f32_to_bf16_bits(rng.standard_normal(int(off[-1]) * kv * d).astype(np.float32))
+    vocab = [f"t{i}" for i in range(15)]
+    lex = [list(rng.choice(vocab, rng.integers(0, 3), replace=False)) for _ in range(n)]
+    kinds = [str(rng.choice(["turn", "doc", "custom", ""])) for _ in range(n)]
+    muts = [str(rng.choice(["ephemeral", "stable", "weird"])) for _ in range(n)]
+    active = rng.random(n) > 0.1
+    cats = [kinds, None, None, muts]
+    with O.RefStore().load_gqa_policy(keys, off, kv, d, lex, cats, active) as st:
+        for t in range(12):
+            q = rng.standard_normal((h, qt, d)).astype(np.float32)
+            qlex = list(rng.choice(vocab + ["absent"], rng.integers(0, 4)))
+            filt = [[None] * 4, [["doc", "custom"], None, None, None],
+                    [None, None, None, ["weird", "stable"]], [["turn"], None, None, ["x"]]][t % 4]
+            for k in (1, 7):
+                want = st.route_policy(q, k, qlex, filt)
+                ids, _ = O.gqa_route_policy(keys, off, kv, d, q, k, node_lexical=lex, cats=cats,
+                                            active=active, query_lexical=qlex, filters=filt)
+                got = [int(x) for x in ids if x != np.iinfo(np.uint64).max]
+                assert got == want, (t, qlex, filt, k)

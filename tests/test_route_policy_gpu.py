@@ -121,3 +121,52 @@ def test_nan_rows_and_queries_under_policy(sidecar):
     qlex = [["hot"], ["hot"], ["hot"]]
     check(bank, rows, qs, 6, lex, None, None, qlex, [None] * 4)
     bank.close()
+
+
+# ----------------------------------------------------------------------- GQA
+
+def gqa_bank(seed, n, kv=8, d=128, tmax=300):
+    rng = np.random.default_rng(seed)
+    T = rng.integers(0, tmax, n)
+    T[::17] = 0
+    off = np.zeros(n + 1, np.uint64)
+    off[1:] = np.cumsum(T)
+    keys = O.f32_to_bf16_bits(rng.standard_normal(int(off[-1]) * kv * d).astype(np.float32))
+    return keys, off, rng
+
+
+@pytest.mark.parametrize("qt", [1, 4])
+def test_gqa_lexical_and_filters_match_oracle(qt):
+    from graftrepository_b200.cuda_router import CudaGQARouteSidecar
+
+    n, kv, d, h = 600, 8, 128, 32
+    keys, off, rng = gqa_bank(50 + qt, n, kv, d)
+    vocab = [f"g{i}" for i in range(40)]
+    lex = [list(rng.choice(vocab, rng.integers(0, 4), replace=False)) + (["hot"] if i % 5 == 0 else [])
+           for i in range(n)]
+    kinds = [str(rng.choice(["turn", "doc", "fact"])) for _ in range(n)]
+    durs = [str(rng.choice(["session", "permanent"])) for _ in range(n)]
+    active = rng.random(n) > 0.07
+    cats = [kinds, None, durs, None]
+    side = CudaGQARouteSidecar(device=0)
+    bank = side.create_bank_csr(keys.view(np.uint16), off, kv, d)
+    bank.set_route_policy(lexical_keys=lex, kinds=kinds, durabilities=durs, active=active)
+    qs = rng.standard_normal((4, h, qt, d)).astype(np.float32)
+    qlex = [[], ["hot"], [vocab[1], vocab[2], "absent"], [vocab[3], vocab[3]]]
+    for filt in ([None] * 4, [["doc", "fact"], None, None, None],
+                 [None, None, ["permanent"], None], [["era"], None, None, None]):
+        for k in (1, 5, 16):
+            ids, sc = bank.route_policy_topk(qs, topk=k, lexical_keys=qlex,
+                                             kinds=filt[0] or (), durabilities=filt[2] or ())
+            for i in range(4):
+                want, want_s = O.gqa_route_policy(keys, off, kv, d, qs[i], k, node_lexical=lex,
+                                                  cats=cats, active=active,
+                                                  query_lexical=qlex[i], filters=filt)
+                assert np.array_equal(ids[i], want), (filt, k, i, ids[i], want)
+                fin = want != U64MAX
+                assert np.array_equal(sc[i][fin], want_s[fin])
+    assert bank.route_gqa(qs[1][:, :, :], ["hot"], 5) == [
+        int(x) for x in O.gqa_route_policy(keys, off, kv, d, qs[1], 5, node_lexical=lex,
+                                           cats=cats, active=active, query_lexical=["hot"])[0]
+        if x != U64MAX]
+    bank.close()
