@@ -66,7 +66,7 @@ def parse():
     p.add_argument("--workload", default="mla_1m_b1",
                    choices=["mla_1m_b1", "mla_1m_b64", "gqa_512", "gqa_100k", "mount_int4",
                             "mount_int6", "mount_int8", "mount_ref8", "mount_int4_rope",
-                            "mount_ref8_rope"],
+                            "mount_ref8_rope", "mla_1m_policy"],
                    help="mla_1m_b1 is the headline (BASELINE config 2); the others measure "
                         "the GQA route (configs 3/4) and the quantised mount (config 5)")
     return p.parse_args()
@@ -788,6 +788,99 @@ def cpu_mount_baseline(vals, bits, workload, rope=False):
                       f"(median {per_layer*1e3:.2f} ms/layer, OpenMP C restatement)"}
 
 
+def run_policy(args):
+    """The 1M-node MLA route with its policy channels on: every probe carries
+    three lexical keys (two that nodes carry, one the bank lacks) and a kind
+    filter of three kinds, over a bank whose nodes carry two Zipf-drawn keys,
+    a kind and an active flag (1 % inactive).  A step is one probe through
+    the public policy route (host query in, host ids out); the value is the
+    route's device time (query upload excluded, the filter bitmap, scan,
+    exact pass and lexical kernels included), e2e its wall time."""
+    import torch
+
+    import oracle as O
+    from graftrepository_b200 import synth
+    from graftrepository_b200.cuda_router import CudaMLARouteSidecar
+
+    world, rank, local = _dist_setup()
+    rows16 = synth.mla_bank(1, NODES)
+    lexical, kinds, active = synth.route_policy(1, NODES)
+    side = CudaMLARouteSidecar(device=local)
+    bank = side.create_bank_raw(rows16, 1)
+    t0 = time.perf_counter()
+    bank.set_route_policy(lexical_keys=lexical, kinds=kinds, active=active)
+    attach_s = time.perf_counter() - t0
+    qs = synth.mla_queries(1, max(4, args.steps + args.warmup))
+    qkeys = [synth.route_policy_query(i) for i in range(qs.shape[0])]
+    kind_filter = ["turn", "doc", "fact"]
+    from graftrepository_b200 import _lib
+    L = _lib.load()
+    flush = torch.empty(2 * L2_BYTES, dtype=torch.uint8, device=f"cuda:{local}")
+
+    def one(i):
+        ids, _ = bank.route_policy_topk(qs[i], topk=TOPK, lexical_keys=[qkeys[i]],
+                                        kinds=kind_filter)
+        return ids
+
+    for i in range(args.warmup):
+        one(i)
+    dev_ms, walls = [], []
+    with ClockSampler(local) as clk:
+        for j in range(args.steps):
+            i = args.warmup + j
+            flush.zero_()
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            one(i)
+            walls.append(time.perf_counter() - t0)
+            dev_ms.append(float(bank._last_elapsed_ms))
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline and O.ref_available(omp=True):
+        per = NODES // 32
+        rows = rows16.astype(np.float32)
+        with O.RefStore(omp=True).load_mla_policy(rows[:per], lexical[:per],
+                                                  [kinds[:per], None, None, None],
+                                                  active[:per]) as st:
+            st.route_policy(qs[0], TOPK, qkeys[0], [kind_filter, None, None, None])
+            ts = []
+            for i in range(min(20, qs.shape[0])):
+                t0 = time.perf_counter()
+                st.route_policy(qs[i], TOPK, qkeys[i], [kind_filter, None, None, None])
+                ts.append(time.perf_counter() - t0)
+        per_probe = statistics.median(ts) * 32
+        cpu = {"value": 1.0 / per_probe, "unit": UNIT, "cores": len(os.sched_getaffinity(0)),
+               "kind": "reference",
+               "sample": f"grm_store_route_filtered over a {per}-node slice (1/32) of the bank "
+                         f"with the same policy data, median of {len(ts)} probes "
+                         f"({statistics.median(ts)*1e3:.2f} ms), x32"}
+    bank.close()
+    peak, peak_kind = peaks()
+    mean_ms = statistics.mean(dev_ms)
+    achieved = NODES * DIM * 2 / (mean_ms / 1e3) / 1e9
+    if rank != 0:
+        return
+    print(json.dumps({
+        "metric": "1M-node MLA route with lexical bonus + kind filter (policy channels on device)",
+        "value": 1.0 / (mean_ms / 1e3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": mean_ms, "higher_is_better": True,
+        "scaling": "replicas", "vs_baseline": None, "dtype": "f16 bank, f32/f64 exact",
+        "data": "synthetic",
+        "config": {"workload": "mla_1m_policy", "nodes": NODES, "dim": DIM, "topk": TOPK,
+                   "query_keys": 3, "node_keys": 2, "kind_filter": kind_filter,
+                   "policy_attach_s": attach_s,
+                   "l2": "256 MB L2 flush before every step, outside the route"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "peak_kind": peak_kind,
+                     "algorithmic_bytes_per_launch": NODES * DIM * 2, "traffic": None,
+                     "note": "bank bytes over the whole policy route's device time"},
+        "cpu_baseline": cpu,
+        "e2e": {"value": len(walls) / sum(walls), "unit": UNIT,
+                "h2d_bytes_per_step": DIM * 4, "d2h_bytes_per_step": TOPK * 12},
+        "step_ms_p50": statistics.median(dev_ms), "gpu_launches": None,
+        "clocks": clk.summary(),
+    }), flush=True)
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -796,6 +889,8 @@ def main():
         run_gqa(args)
     elif args.workload.startswith("mount"):
         run_mount(args)
+    elif args.workload == "mla_1m_policy":
+        run_policy(args)
     else:
         run_ours(args)
 

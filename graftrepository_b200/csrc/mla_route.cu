@@ -1122,31 +1122,63 @@ __global__ void row_norms_kernel(const T* rows, int64_t n, int dim, float* norms
 
 // Lexical channel of route_mla_arena (cpp/grm_runtime.cpp:4339-4350): every
 // allowed node with lexical hits gets S = exact score + hits / m (fp32 divide,
-// fp32 add), one thread per node (the exact score is one sequential fp64
-// chain); non-finite S is dropped by the merge.
+// fp32 add); non-finite S is dropped by the merge.  A warp per hit node: the
+// lanes load the row with independent strided loads into shared memory, then
+// lane 0 runs the reference's sequential fp64 dot over it (one memory round
+// trip per node instead of one per unrolled slice of the chain).
+constexpr int kLexWarps = 4;
+constexpr int kLexMaxDim = 1024;
+
 template <typename T>
-__global__ void mla_lex_score_kernel(const T* __restrict__ rows, const float* __restrict__ norms,
-                                     int dim, const float* __restrict__ query,
-                                     const uint2* __restrict__ list,
-                                     const uint32_t* __restrict__ counter,
-                                     const uint32_t* __restrict__ allow, int m,
-                                     float* __restrict__ cand_s, uint32_t* __restrict__ cand_id) {
+__global__ void __launch_bounds__(kLexWarps * 32) mla_lex_score_kernel(
+    const T* __restrict__ rows, const float* __restrict__ norms, int dim,
+    const float* __restrict__ query, const uint2* __restrict__ list,
+    const uint32_t* __restrict__ counter, const uint32_t* __restrict__ allow, int m,
+    float* __restrict__ cand_s, uint32_t* __restrict__ cand_id) {
+  __shared__ float qs[kLexMaxDim];
+  __shared__ float rowbuf[kLexWarps][kLexMaxDim];
   __shared__ double qn;
-  if (threadIdx.x == 0) qn = query_norm_seq(query, dim);
-  __syncthreads();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int d = threadIdx.x; d < dim; d += blockDim.x) qs[d] = query[d];
   const uint32_t n = *counter;
-  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
-    const uint2 h = list[i];
-    float S = -INFINITY;
-    if (policy::row_allowed(allow, h.x)) {
-      const float nrm = __ldg(norms + h.x);
-      if (isfinite(nrm)) {
-        const float es = exact_score<T>(rows + (int64_t)h.x * dim, dim, query, qn, nrm);
+  const uint32_t nw = gridDim.x * kLexWarps;
+  bool first = true;
+  for (uint32_t i = blockIdx.x * kLexWarps + warp; i < n || first; i += nw) {
+    const bool live = i < n;
+    const uint2 h = live ? list[i] : make_uint2(0u, 0u);
+    const bool ok = live && policy::row_allowed(allow, h.x);
+    float nrm = 0.0f;
+    if (ok) {  // the row's loads go out before the query norm's chain
+      const T* row = rows + (int64_t)h.x * dim;
+      for (int d = lane; d < dim; d += 32) rowbuf[warp][d] = to_f(__ldg(row + d));
+      nrm = __ldg(norms + h.x);
+    }
+    if (first) {  // the reference's query norm (sequential fp64), once per block
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        double acc = 0.0;
+#pragma unroll 8
+        for (int d = 0; d < dim; ++d) acc += (double)qs[d] * (double)qs[d];
+        qn = sqrt(acc);
+      }
+      __syncthreads();
+      first = false;
+      if (!live) break;
+    }
+    __syncwarp();
+    if (lane == 0) {
+      float S = -INFINITY;
+      if (ok && isfinite(nrm)) {
+        double dot = 0.0;
+#pragma unroll 8
+        for (int d = 0; d < dim; ++d) dot = fma((double)qs[d], (double)rowbuf[warp][d], dot);
+        const float es = (float)(dot / (qn * (double)nrm + 1.0e-8));
         S = es + __fdiv_rn((float)h.y, (float)m);
       }
+      cand_s[i] = S;
+      cand_id[i] = h.x;
     }
-    cand_s[i] = S;
-    cand_id[i] = h.x;
+    __syncwarp();
   }
 }
 
@@ -1195,6 +1227,8 @@ struct grm_b200_mla_bank {
   unsigned long long* d_fallbacks = nullptr;  // counted by the exact kernel
   grm_b200::policy::Policy pol;               // lexical keys, filter codes, active flags
   const uint32_t* cur_allow = nullptr;        // filter bitmap of the route in progress
+  cudaStream_t lex_stream = nullptr;          // single-query lexical pass beside the scan
+  cudaEvent_t ev_fork = nullptr, ev_lex = nullptr;
 };
 
 namespace {
@@ -1645,6 +1679,10 @@ void bank_free(grm_b200_mla_bank* b) {
   if (b->h_results) cudaFreeHost(b->h_results);
   if (b->d_queries) cudaFree(b->d_queries);
   grm_b200::policy::policy_free(b->pol);
+  if (b->lex_stream) cudaStreamSynchronize(b->lex_stream);
+  if (b->ev_fork) cudaEventDestroy(b->ev_fork);
+  if (b->ev_lex) cudaEventDestroy(b->ev_lex);
+  if (b->lex_stream) cudaStreamDestroy(b->lex_stream);
   if (b->ev0) cudaEventDestroy(b->ev0);
   if (b->ev1) cudaEventDestroy(b->ev1);
   if (b->stream) cudaStreamDestroy(b->stream);
@@ -1859,6 +1897,9 @@ int grm_b200_mla_route_policy(grm_b200_mla_bank* bank, const float* queries_host
   bool any_lex = false;
   for (int i = 0; lexical_keys && i < query_count; ++i)
     any_lex = any_lex || !policy::split_keys(lexical_keys[i]).empty();
+  if (any_lex && dim > kLexMaxDim)
+    return bank->err.set(GRM_B200_EINVAL, "lexical keys on banks of dim > %d are not supported",
+                         kLexMaxDim);
   cudaError_t e = cudaSetDevice(bank->device);
   if (e != cudaSuccess) return bank->err.set(cuda_status(e), "cudaSetDevice failed");
   int rc = reserve(bank, query_count);
@@ -1889,40 +1930,89 @@ int grm_b200_mla_route_policy(grm_b200_mla_bank* bank, const float* queries_host
   const uint32_t* allow = nullptr;
   if ((rc = policy::policy_allow(bank->pol, filters, info.sms, bank->stream, &allow, bank->err)))
     return rc;
-  bank->cur_allow = allow;
-  rc = (bank->dtype == GRM_B200_F16)
-           ? run_chunk<__half>(bank, bank->d_queries, nullptr, query_count, topk)
-           : run_chunk<float>(bank, bank->d_queries, nullptr, query_count, topk);
-  bank->cur_allow = nullptr;
-  if (rc) return rc;
-  for (int q = 0; any_lex && q < query_count; ++q) {
-    int m = 0;
-    if ((rc = policy::policy_collect(bank->pol, lexical_keys[q], info.sms, bank->stream, &m,
-                                     bank->err)))
-      return rc;
-    if (m == 0) continue;
+  // Stream-ordered from here to the final event: scan and exact pass chained
+  // as in the async route (the exact kernel reads the statuses on the
+  // device), the lexical kernels per query, one host wait at the end.  A
+  // single query's lexical pass (postings, hit scores) does not depend on the
+  // scan: it runs on a side stream launched first, and only the merge waits
+  // for both.
+  auto lex_pass = [&](int q, cudaStream_t st, int* m) -> int {
+    uint64_t postings = 0;  // bounds the hit nodes: one warp each at most
+    int r = policy::policy_collect(bank->pol, lexical_keys[q], info.sms, st, m, bank->err,
+                                   &postings);
+    if (r || *m == 0) return r;
     const float* dq = bank->d_queries + (int64_t)q * dim;
-    const int grid = info.sms * 2;
+    const int grid = (int)std::max<uint64_t>(
+        1, std::min<uint64_t>((uint64_t)info.sms * 2, (postings + kLexWarps - 1) / kLexWarps));
     if (bank->dtype == GRM_B200_F16)
-      mla_lex_score_kernel<__half><<<grid, 128, 0, bank->stream>>>(
+      mla_lex_score_kernel<__half><<<grid, kLexWarps * 32, 0, st>>>(
           static_cast<const __half*>(bank->d_rows), bank->d_norms, dim, dq, bank->pol.d_hitlist,
-          bank->pol.d_counter, allow, m, bank->pol.d_cand_s, bank->pol.d_cand_id);
+          bank->pol.d_counter, allow, *m, bank->pol.d_cand_s, bank->pol.d_cand_id);
     else
-      mla_lex_score_kernel<float><<<grid, 128, 0, bank->stream>>>(
+      mla_lex_score_kernel<float><<<grid, kLexWarps * 32, 0, st>>>(
           static_cast<const float*>(bank->d_rows), bank->d_norms, dim, dq, bank->pol.d_hitlist,
-          bank->pol.d_counter, allow, m, bank->pol.d_cand_s, bank->pol.d_cand_id);
-    Result* r = bank->d_results_mapped + q;
-    policy::lex_merge_kernel<<<1, policy::kMergeWarps * 32, 0, bank->stream>>>(
+          bank->pol.d_counter, allow, *m, bank->pol.d_cand_s, bank->pol.d_cand_id);
+    cudaError_t le = cudaGetLastError();
+    return le == cudaSuccess ? 0 : bank->err.set(cuda_status(le), "MLA lexical kernels launch failed");
+  };
+  auto merge = [&](int q, cudaStream_t st) -> int {
+    Result* r = bank->d_results + q;
+    policy::lex_merge_kernel<<<1, policy::kMergeWarps * 32, 0, st>>>(
         r->ids, r->scores, &r->count, topk, 0, bank->pol.d_cand_s, bank->pol.d_cand_id,
         bank->pol.d_counter);
-    e = cudaGetLastError();
-    if (e != cudaSuccess) return bank->err.set(cuda_status(e), "MLA lexical kernels launch failed");
+    cudaError_t le = cudaGetLastError();
+    return le == cudaSuccess ? 0 : bank->err.set(cuda_status(le), "MLA lexical merge launch failed");
+  };
+  int m0 = 0;
+  const bool side = any_lex && query_count == 1;
+  if (side) {
+    if (!bank->lex_stream) {
+      e = cudaStreamCreateWithFlags(&bank->lex_stream, cudaStreamNonBlocking);
+      if (e == cudaSuccess) e = cudaEventCreateWithFlags(&bank->ev_fork, cudaEventDisableTiming);
+      if (e == cudaSuccess) e = cudaEventCreateWithFlags(&bank->ev_lex, cudaEventDisableTiming);
+      if (e != cudaSuccess) return bank->err.set(cuda_status(e), "lexical stream setup failed");
+    }
+    cudaEventRecord(bank->ev_fork, bank->stream);  // queries uploaded, allow built
+    cudaStreamWaitEvent(bank->lex_stream, bank->ev_fork, 0);
+    if ((rc = lex_pass(0, bank->lex_stream, &m0))) return rc;
+    cudaEventRecord(bank->ev_lex, bank->lex_stream);
   }
+  bank->cur_allow = allow;
+  if (bank->dtype == GRM_B200_F16) {
+    Params<__half> p = make_params<__half>(bank, bank->d_queries, topk);  // device results
+    rc = (bank->batch && !allow && query_count >= kBatchMin && topk <= kBMaxTopk)
+             ? launch_batch(bank, p, query_count, bank->stream)
+             : launch_scan<__half>(bank, p, query_count, bank->stream, true);
+    if (!rc) rc = launch_exact<__half>(bank, p, query_count, bank->stream, true);
+  } else {
+    Params<float> p = make_params<float>(bank, bank->d_queries, topk);
+    rc = launch_scan<float>(bank, p, query_count, bank->stream, true);
+    if (!rc) rc = launch_exact<float>(bank, p, query_count, bank->stream, true);
+  }
+  bank->cur_allow = nullptr;
+  if (rc) return bank->err.set(rc, "MLA policy route launch failed");
+  if (side) {
+    cudaStreamWaitEvent(bank->stream, bank->ev_lex, 0);
+    if (m0 && (rc = merge(0, bank->stream))) return rc;
+  } else {
+    for (int q = 0; any_lex && q < query_count; ++q) {
+      int m = 0;
+      if ((rc = lex_pass(q, bank->stream, &m))) return rc;
+      if (m && (rc = merge(q, bank->stream))) return rc;
+    }
+  }
+  e = cudaMemcpyAsync(bank->h_results, bank->d_results, sizeof(Result) * query_count,
+                      cudaMemcpyDeviceToHost, bank->stream);
+  if (e != cudaSuccess) return bank->err.set(cuda_status(e), "MLA policy result copy failed");
   cudaEventRecord(bank->ev1, bank->stream);
   e = cudaEventSynchronize(bank->ev1);
   float ms = 0.0f;
   if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, bank->ev0, bank->ev1);
   if (e != cudaSuccess) return bank->err.set(cuda_status(e), "MLA policy route failed: %s", cudaGetErrorString(e));
+  for (int q = 0; q < query_count; ++q)
+    if (((volatile Result*)bank->h_results)[q].status == kError)
+      return bank->err.set(GRM_B200_KERNEL_BASE + 1,
+                           "MLA scan: a bounded device wait gave up (query %d)", q);
   for (int q = 0; q < query_count; ++q) {
     const Result& r = bank->h_results[q];
     for (int j = 0; j < topk; ++j) {

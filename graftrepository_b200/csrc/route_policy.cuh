@@ -192,21 +192,25 @@ static __global__ void __launch_bounds__(kMergeWarps * 32) lex_merge_kernel(
   __syncthreads();
   WarpList list;
   list.init();
+  // only the first topk entries of each list matter: candidates below the
+  // list's k-th are skipped (that k-th only grows)
   for (uint32_t i0 = (uint32_t)warp * 32; i0 < n; i0 += blockDim.x) {
     const uint32_t i = i0 + lane;
     const float s = i < n ? cand_s[i] : -INFINITY;
     const uint32_t id = i < n ? cand_id[i] : kNoRow;
-    list.offer(s, id, lane);
+    list.offer_margin(s, id, lane, topk, 0.0f);
   }
   if (warp == 0) {
     const bool keep = lane < bc && !((superseded >> lane) & 1u);
-    list.offer(keep ? base_s[lane] : -INFINITY, keep ? base_id[lane] : kNoRow, lane);
+    list.offer_margin(keep ? base_s[lane] : -INFINITY, keep ? base_id[lane] : kNoRow, lane, topk,
+                      0.0f);
   }
   sh_s[warp * 32 + lane] = list.s;
   sh_id[warp * 32 + lane] = list.id;
   __syncthreads();
   if (warp == 0) {
-    for (int w = 1; w < kMergeWarps; ++w) list.offer(sh_s[w * 32 + lane], sh_id[w * 32 + lane], lane);
+    for (int w = 1; w < kMergeWarps; ++w)
+      list.offer_margin(sh_s[w * 32 + lane], sh_id[w * 32 + lane], lane, topk, 0.0f);
     const bool ok = lane < topk && isfinite(list.s) && list.id != kNoRow;
     const unsigned m = __ballot_sync(kFull, ok);
     if (lane < topk) {
@@ -399,8 +403,12 @@ inline int policy_pass(Policy& P, const Ranges& ranges, int pass, int sms, cudaS
 // its length in d_counter.  Returns 0 with *m_out == 0 when the query has no
 // keys.
 inline int policy_collect(Policy& P, const char* blob, int sms, cudaStream_t s, int* m_out,
-                          ErrorSlot& err) {
+                          ErrorSlot& err, uint64_t* postings = nullptr) {
   const Ranges ranges = policy_ranges(P, blob, m_out);
+  if (postings) {
+    *postings = 0;
+    for (const auto& r : ranges) *postings += r.second;
+  }
   if (*m_out == 0) return 0;
   cudaError_t e = cudaMemsetAsync(P.d_counter, 0, sizeof(uint32_t), s);
   if (e != cudaSuccess) return err.set(cuda_status(e), "lexical counter reset failed");

@@ -373,6 +373,7 @@ class CudaMLARouteBank:
             ctypes.byref(elapsed))
         _lib.check(rc, self._err)
         self.last_scores = scores
+        self._last_elapsed_ms = float(elapsed.value)
         if np.any((out != _U64MAX) & (out >= self.node_ids.shape[0])):
             raise RuntimeError("CUDA MLA route returned an out-of-range row ID")
         mapped = np.where(out == _U64MAX, _U64MAX, self.node_ids[np.minimum(out, self.nodes - 1)])

@@ -127,3 +127,28 @@ def seat_offsets(seed: int, n_grafts: int, tokens: int, arena_seats: int) -> np.
     for rank, g in enumerate(order):
         seats[g] = cuts[rank] + rank * tokens
     return seats
+
+
+ROUTE_KINDS = ("turn", "doc", "digest", "era", "fact", "task_state", "recall", "cull_span")
+
+
+def route_policy(seed: int, nodes: int, vocab: int = 100_000, keys_per_node: int = 2):
+    """Synthetic route policy data for a bank of `nodes` rows: each node
+    carries `keys_per_node` lexical keys drawn Zipf-like from a vocabulary of
+    `vocab` words ("w<rank>"), a kind cycling through the reference's known
+    kinds, and 1 % inactive nodes.  Returns (lexical key lists, kinds, active)."""
+    rng = np.random.default_rng(seed + 7)
+    ranks = np.minimum(rng.zipf(1.3, size=(nodes, keys_per_node)), vocab) - 1
+    lexical = [[f"w{r}" for r in row] for row in ranks.tolist()]
+    kinds = [ROUTE_KINDS[i % len(ROUTE_KINDS)] for i in range(nodes)]
+    active = rng.random(nodes) >= 0.01
+    return lexical, kinds, active
+
+
+def route_policy_query(seed: int, count: int = 3):
+    """Query keys for a policy route (the arena's rare query tokens):
+    `count - 1` words of Zipf rank 50..2000 (tens to a thousand nodes each at
+    1M nodes) plus one key absent from the bank."""
+    rng = np.random.default_rng(seed + 11)
+    keys = [f"w{int(r)}" for r in rng.integers(50, 2000, count - 1)]
+    return keys + ["absent-from-bank"]
