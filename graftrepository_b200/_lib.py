@@ -76,6 +76,7 @@ _SIGS = {
     "grm_b200_gqa_stats": (_I, [_P, _P, _P]),
     "grm_b200_mount_ref": (_I, [_P, _P, _I64, _I64, _I64, _I64, _P, _P, _I64, _P]),
     "grm_b200_mount_packed": (_I, [_P, _P, _I, _I, _I64, _I64, _I64, _I64, _P, _P, _I64, _P]),
+    "grm_b200_upload_rows": (_I, [_P, _P, _I, _I64, _P, _I64, _P]),
     "grm_b200_mount_packed_rope": (_I, [_P, _P, _I, _I, _I64, _I64, _I64, _I64, _P, _P, _I64, _P,
                                         _P]),
     "grm_b200_mount_ref_rope": (_I, [_P, _P, _I64, _I64, _I64, _I64, _P, _P, _I64, _P, _P]),

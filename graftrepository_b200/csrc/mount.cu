@@ -733,4 +733,44 @@ int grm_b200_arena_splice(const void* old_device, int64_t outer, int64_t input_t
   return 0;
 }
 
+int grm_b200_upload_rows(const void* const* parts_host, const int64_t* part_row_bytes, int n_parts,
+                         int64_t rows, void* dst_device, int64_t dst_row_bytes, void* stream) {
+  if (!parts_host || !part_row_bytes || n_parts <= 0 || rows < 0 || !dst_device ||
+      dst_row_bytes <= 0) {
+    set_thread_error("invalid upload_rows arguments");
+    return GRM_B200_EINVAL;
+  }
+  int64_t total = 0;
+  for (int i = 0; i < n_parts; ++i) {
+    if (!parts_host[i] || part_row_bytes[i] <= 0) {
+      set_thread_error("upload_rows: part %d is empty", i);
+      return GRM_B200_EINVAL;
+    }
+    total += part_row_bytes[i];
+  }
+  if (total > dst_row_bytes) {
+    set_thread_error("upload_rows: parts (%lld bytes per row) exceed the row (%lld)",
+                     (long long)total, (long long)dst_row_bytes);
+    return GRM_B200_EINVAL;
+  }
+  if (rows == 0) return 0;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int64_t col = 0;
+  for (int i = 0; i < n_parts; ++i) {
+    cudaError_t e = (total == dst_row_bytes && n_parts == 1)
+                        ? cudaMemcpyAsync(dst_device, parts_host[0], (size_t)(rows * total),
+                                          cudaMemcpyHostToDevice, s)
+                        : cudaMemcpy2DAsync(static_cast<char*>(dst_device) + col,
+                                            (size_t)dst_row_bytes, parts_host[i],
+                                            (size_t)part_row_bytes[i], (size_t)part_row_bytes[i],
+                                            (size_t)rows, cudaMemcpyHostToDevice, s);
+    if (e != cudaSuccess) {
+      set_thread_error("upload_rows: copy of part %d failed: %s", i, cudaGetErrorString(e));
+      return cuda_status(e);
+    }
+    col += part_row_bytes[i];
+  }
+  return 0;
+}
+
 }  // extern "C"

@@ -347,6 +347,17 @@ int grm_b200_arena_splice(const void* old_device, int64_t outer, int64_t input_t
                           int64_t sink_tokens, int64_t old_mount_tokens, void* out_device,
                           int64_t* out_tokens, void* stream);
 
+/* Host -> device upload of a packed payload's per-row parts, interleaved:
+ * device row r (dst_row_bytes) = part 0 row r | part 1 row r | ..., where
+ * part p is rows x part_row_bytes[p] contiguous bytes at parts_host[p].  This
+ * puts an MLA node's separately packed {"c", "kpe"} codes (or scales) side
+ * by side as the arena row [latent | k_pe] the mount writes, without a host
+ * copy (pack_kv_arrays fields, core/graft_quant.py:177-217; node payload
+ * core/graft_arena.py:464-477).  Stream-ordered on `stream`. */
+int grm_b200_upload_rows(const void* const* parts_host, const int64_t* part_row_bytes,
+                         int n_parts, int64_t rows, void* dst_device, int64_t dst_row_bytes,
+                         void* stream);
+
 /* ----------------------------------------------------- multi-GPU top-k merge */
 
 /* Merge `lists` candidate lists of `per_list` (score, id) entries each (device

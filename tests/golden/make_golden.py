@@ -3,7 +3,7 @@
 Run in a container that has the GraftRepository checkout (default
 /root/reference, or GRM_REFERENCE_ROOT) and a C++ compiler:
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py [fixture ...]
 
 Every expected output below is produced by the reference's own code:
 
@@ -20,6 +20,12 @@ Every expected output below is produced by the reference's own code:
   not vendored.
 * Arena splice -- DeviceArena::apply_swap_tensor (cpp/grm_runtime.cpp:4941)
   through grm_store_apply_swap_tensor.
+* Packed payloads -- pack_kv_arrays (core/graft_quant.py:177-217) of an
+  MLA-shaped node ({"c": [L, S, 256], "kpe": [L, S, 32]}, the payload of
+  core/graft_arena.py:464-477) and a GQA-shaped one ({"k": [L, H, S, D]},
+  :3459-3477), every field as pack_kv_arrays wrote it, with
+  unpack_kv_arrays's fp16 output and its bf16 cast; plus payloads that
+  unpack_kv_arrays rejects, each with the error it raised.
 
 Inputs are seeded synthetic data with the configs' shapes at small sizes, plus
 the edge cases the reference tests exercise (ties, non-finite rows, empty
@@ -147,6 +153,50 @@ def quant_case(seed: int):
     return out
 
 
+def packed_case(seed: int):
+    import torch
+    from core import graft_quant as GQ
+
+    def bf16(x16):
+        return torch.from_numpy(x16).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
+
+    rng = np.random.default_rng(seed)
+    out = {}
+    L, S = 3, 16
+    c = (rng.standard_normal((L, S, 256)) * 0.8).astype(np.float16)
+    kpe = (rng.standard_normal((L, S, 32)) * 2.5).astype(np.float16)
+    c[1, 2, 32:64] = 0
+    k = (rng.standard_normal((2, 4, 8, 64)) * 1.3).astype(np.float16)
+    for tag, arrays, bits in (("mla8", {"c": c, "kpe": kpe}, 8), ("mla4", {"c": c, "kpe": kpe}, 4),
+                              ("gqa6", {"k": k}, 6), ("gqa3", {"k": k}, 3)):
+        payload = GQ.pack_kv_arrays(arrays, bits)
+        rt = GQ.unpack_kv_arrays(payload, list(arrays))
+        for key, val in payload.items():
+            out[f"{tag}__{key}"] = np.asarray(val)
+        for name in arrays:
+            out[f"{tag}__expect_f16_{name}"] = rt[name].view(np.uint16)
+            out[f"{tag}__expect_bf16_{name}"] = bf16(rt[name])
+    # payloads unpack_kv_arrays rejects (fail-closed), with its error text
+    base = GQ.pack_kv_arrays({"k": k}, 8)
+    bad = {
+        "noversion": {kk: v for kk, v in base.items() if kk != "format_version"},
+        "version2": {**base, "format_version": np.asarray(2, dtype=np.int64)},
+        "bits16": {**base, "storage_bits": np.asarray(16, dtype=np.int64)},
+        "bits5": {**base, "storage_bits": np.asarray(5, dtype=np.int64)},
+        "noscales": {kk: v for kk, v in base.items() if kk != "k_scales"},
+        "vecversion": {**base, "format_version": np.asarray([1, 1], dtype=np.int64)},
+    }
+    for tag, payload in bad.items():
+        try:
+            GQ.unpack_kv_arrays(payload, ["k"])
+            raise AssertionError(f"{tag} was accepted")
+        except GQ.GraftQuantFormatError as exc:
+            out[f"bad_{tag}__error"] = np.asarray(str(exc))
+        for key, val in payload.items():
+            out[f"bad_{tag}__{key}"] = np.asarray(val)
+    return out
+
+
 def splice_case(seed: int):
     rng = np.random.default_rng(seed)
     out = {}
@@ -166,12 +216,20 @@ def main() -> None:
     if not (REF / "cpp" / "grm_runtime.cpp").is_file():
         raise SystemExit(f"reference checkout not found at {REF}")
     O.ensure_built(ref_root=REF, with_ref=True)
+    only = sys.argv[1:]
+    if only:  # regenerate the named fixtures only, e.g. packed_payload
+        cases = {"packed_payload": lambda: packed_case(6)}
+        for name in only:
+            np.savez_compressed(HERE / f"{name}.npz", **cases[name]())
+            print(name, (HERE / f"{name}.npz").stat().st_size)
+        return
     np.savez_compressed(HERE / "mla_d256.npz", **mla_case(0, 512, 256, 16))
     np.savez_compressed(HERE / "mla_d64.npz", **mla_case(10, 300, 64, 5))
     np.savez_compressed(HERE / "gqa_d128.npz", **gqa_case(2, 48, 2, 8, 128, 24, 16))
     np.savez_compressed(HERE / "gqa_d64_l4.npz", **gqa_case(3, 40, 8, 32, 64, 10, 8))
     np.savez_compressed(HERE / "quant_g32.npz", **quant_case(4))
     np.savez_compressed(HERE / "splice.npz", **splice_case(5))
+    np.savez_compressed(HERE / "packed_payload.npz", **packed_case(6))
     for p in sorted(HERE.glob("*.npz")):
         print(p.name, p.stat().st_size)
 

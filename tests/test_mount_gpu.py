@@ -188,3 +188,54 @@ def test_rope_mount_rejects_bad_specs(offset, dim, rows):
     with pytest.raises(GrmB200Error):
         graft_mount.mount_packed(codes, scales, [200], arena, bits=4, layers=1, tokens=8,
                                  width=288, rope=graft_mount.RopeSpec(c, c, offset, dim))
+
+
+@pytest.mark.parametrize("tag,names", [("mla8", ("c", "kpe")), ("mla4", ("c", "kpe")),
+                                       ("gqa6", ("k",)), ("gqa3", ("k",))])
+@pytest.mark.parametrize("with_rope", [False, True])
+def test_packed_payloads_mount_like_unpack_kv_arrays(golden, tag, names, with_rope):
+    """Payloads written by the reference's pack_kv_arrays, uploaded as stored
+    and mounted by the fused kernel == the reference's unpack_kv_arrays
+    output cast to bf16, rows [c | kpe] (MLA) or L*H slices (GQA), scattered
+    to the seats; with rope, then re-RoPEd (oracle) at the seats."""
+    from graftrepository_b200 import packed
+
+    g = golden("packed_payload.npz")
+    pre = f"{tag}__"
+    pl = {k[len(pre):]: g[k] for k in g if k.startswith(pre)}
+    shapes = {n: tuple(int(x) for x in pl[f"{n}_shape"]) for n in names}
+    lead = shapes[names[0]][:-1]
+    slices, tokens = int(np.prod(lead[:-1])), lead[-1]
+    width = sum(shapes[n][-1] for n in names)
+    # two nodes: the payload and a copy with its codes negated
+    pl2 = dict(pl)
+    for n in names:
+        pl2[f"{n}_codes"] = (-pl[f"{n}_codes"].astype(np.int16)).clip(-128, 127).astype(np.int8)
+    S = 3 * tokens + 5
+    seats = np.array([tokens + 2, 0], dtype=np.int64)
+    m = graft_mount.ArenaMount(slices, S, width, fill=SENTINEL)
+    rope = None
+    if with_rope:
+        off, dim = (256, 32) if names == ("c", "kpe") else (0, width)
+        c_tab, s_tab = graft_mount.rope_tables(S, dim)
+        import torch
+        rope = graft_mount.RopeSpec(torch.from_numpy(c_tab).cuda(), torch.from_numpy(s_tab).cuda(),
+                                    off, dim, pair_swap=(tag == "mla4"))
+    packed.mount_payloads(m, [pl, pl2], seats, names, rope=rope)
+    vals = []
+    for p in (pl, pl2):
+        parts = []
+        for n in names:
+            _, bf = O.dequant_ref(p[f"{n}_codes"].reshape(-1), p[f"{n}_scales"].reshape(-1))
+            parts.append(bf.reshape(slices, tokens, shapes[n][-1]))
+        vals.append(np.concatenate(parts, axis=-1))
+    want = O.mount_scatter(np.stack(vals), seats, np.full((slices, S, width), SENTINEL, np.uint16))
+    if with_rope:
+        want = O.mount_rope(want, 2, slices, tokens, seats, c_tab, s_tab, off, dim,
+                            pair_swap=(tag == "mla4"))
+    assert np.array_equal(_u16(m.arena), want)
+    # node 1 of the payload is exactly the reference's own output
+    if not with_rope:
+        ref = np.concatenate([pl[f"expect_bf16_{n}"].reshape(slices, tokens, -1) for n in names],
+                             axis=-1)
+        assert np.array_equal(_u16(m.arena)[:, seats[0]:seats[0] + tokens], ref)
