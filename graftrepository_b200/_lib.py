@@ -45,6 +45,7 @@ class GrmB200Error(RuntimeError):
 _SIGS = {
     "grm_b200_mla_bank_create": (_I, [_P, _I, _I64, _I, _I, _P]),
     "grm_b200_mla_bank_create_device": (_I, [_P, _I, _I64, _I, _P]),
+    "grm_b200_mla_bank_create_multi": (_I, [_P, _I, _I64, _I, _P, _I64, _I, _P]),
     "grm_b200_mla_route": (_I, [_P, _P, _I, _I, _I, _I, _P, _P, _P]),
     "grm_b200_mla_route_device": (_I, [_P, _P, _I, _I, _I, _I, _P, _P, _P]),
     "grm_b200_mla_route_async": (_I, [_P, _P, _I, _I, _U64, _P, _P, _P]),

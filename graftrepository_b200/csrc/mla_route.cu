@@ -111,6 +111,11 @@ struct Params {
   int nq;                // exact kernel: queries in this launch
   unsigned long long* fallback_count;  // queries that took the exact pass (optional)
   const uint32_t* allow;  // route filters: bitmap of the rows that may be routed (nullptr: all)
+  // multi-row entries (entry score = max over its rows): the scan folds row
+  // scores into entry_best[entry_of_row[row]] instead of keeping row lists
+  const uint32_t* entry_of_row;
+  int* entry_best;        // [entries] ordered float, reset to -inf by the collect step
+  int* multi_unsafe;      // [Q] the query is outside the approximate pass's safe range
   // A single query may travel inside the launch parameters (queries == nullptr):
   // the synchronous host entry then needs no host-to-device copy.
   float qinline[kInlineMax];
@@ -571,7 +576,7 @@ __device__ __forceinline__ void scan_finish(const Params<T>& p, WarpList& list, 
 // INL: no precomputed norms -- the approximate row norm is accumulated from
 // the same loads (fp32, <= 8 ulp relative, inside the margin) and the exact
 // refine recomputes the reference norm.
-template <int D, typename T, bool INL = false>
+template <int D, typename T, bool INL = false, bool MULTI = false>
 __global__ void __launch_bounds__(kThreads) mla_scan_kernel(const __grid_constant__ Params<T> p) {
   constexpr int E = 16 / (int)sizeof(T);
   constexpr int CPR = D / E;
@@ -693,21 +698,170 @@ __global__ void __launch_bounds__(kThreads) mla_scan_kernel(const __grid_constan
       const float dot = reduce_scatter<SLOTS>(part, lane);
       float n2 = 0.0f;
       if constexpr (INL) n2 = reduce_scatter<SLOTS>(sq, lane);
-      float s = -INFINITY;
-      if (my_row < p.nodes && policy::row_allowed(p.allow, my_row)) {
-        const float nrm = INL ? sqrtf(n2) : nrm_pre;
-        if (isfinite(nrm)) s = dot * __frcp_rn(nrm + e_q);
+      if constexpr (MULTI) {
+        if (my_row < p.nodes) {
+          const uint32_t ent = __ldg(p.entry_of_row + my_row);
+          if (policy::row_allowed(p.allow, ent) && isfinite(nrm_pre)) {
+            const float s = dot * __frcp_rn(nrm_pre + e_q);
+            if (isfinite(s)) atomicMax(p.entry_best + ent, float_to_ordered(s));
+          }
+        }
+      } else {
+        float s = -INFINITY;
+        if (my_row < p.nodes && policy::row_allowed(p.allow, my_row)) {
+          const float nrm = INL ? sqrtf(n2) : nrm_pre;
+          if (isfinite(nrm)) s = dot * __frcp_rn(nrm + e_q);
+        }
+        list.offer_margin(s, (uint32_t)my_row, lane, p.topk, 2.0f * kMargin);
       }
-      list.offer_margin(s, (uint32_t)my_row, lane, p.topk, 2.0f * kMargin);
       int nxt = 0;
       if (lane == 0) nxt = atomicAdd(&sh_next, 1);
       g = g_begin + __shfl_sync(kFull, nxt, 0);
     }
   }
+  if constexpr (MULTI) {
+    if (blockIdx.x == 0 && threadIdx.x == 0) p.multi_unsafe[q] = safe ? 0 : 1;
+    return;
+  }
   // The resolve kernel may be scheduled as blocks leave the streaming loop;
   // it waits for this whole grid before reading anything (griddepcontrol.wait).
   asm volatile("griddepcontrol.launch_dependents;");
   scan_finish<D, T, INL, kWarps>(p, list, safe, q, lane, warp, fsm);
+}
+
+// ------------------------------------------------------ multi-row entries
+// RouterIndex::exact_mla_entry_score over several rows
+// (cpp/grm_runtime.cpp:3518-3545): an entry scores the max of its finite row
+// scores, NaN (dropped) if none.  After the streaming pass has folded the
+// approximate row scores into entry_best, the entries are selected like the
+// single rows: L = the k-th best approximate entry score, candidates = the
+// entries within 2*kMargin of it (every row score is within kMargin of its
+// exact value, so is their max), refined exactly, top-k by (score, entry).
+
+constexpr int kEntryWarps = 8;
+
+// Per block: the approximate top-32 entries of a strided share.
+__global__ void __launch_bounds__(kEntryWarps * 32) entry_top_kernel(
+    const int* __restrict__ entry_best, int64_t entries, float* __restrict__ blk_s,
+    uint32_t* __restrict__ blk_id) {
+  __shared__ float sh_s[kEntryWarps * 32];
+  __shared__ uint32_t sh_id[kEntryWarps * 32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  WarpList list;
+  list.init();
+  for (int64_t e0 = ((int64_t)blockIdx.x * kEntryWarps + warp) * 32; e0 < entries;
+       e0 += (int64_t)gridDim.x * kEntryWarps * 32) {
+    const int64_t e = e0 + lane;
+    const float v = e < entries ? ordered_to_float(__ldcg(entry_best + e)) : -INFINITY;
+    list.offer(v, (uint32_t)e, lane);
+  }
+  sh_s[warp * 32 + lane] = list.s;
+  sh_id[warp * 32 + lane] = list.id;
+  __syncthreads();
+  if (warp == 0) {
+    for (int w = 1; w < kEntryWarps; ++w) list.offer(sh_s[w * 32 + lane], sh_id[w * 32 + lane], lane);
+    blk_s[blockIdx.x * 32 + lane] = list.s;
+    blk_id[blockIdx.x * 32 + lane] = list.id;
+  }
+}
+
+// One warp: the k-th best over the block lists -> the candidate threshold.
+__global__ void entry_threshold_kernel(const float* __restrict__ blk_s,
+                                       const uint32_t* __restrict__ blk_id, int nblk, int topk,
+                                       float* __restrict__ thr) {
+  const int lane = threadIdx.x;
+  WarpList list;
+  list.init();
+  for (int b = 0; b < nblk; ++b) list.offer(blk_s[b * 32 + lane], blk_id[b * 32 + lane], lane);
+  const float kth = __shfl_sync(kFull, list.s, topk - 1);
+  if (lane == 0) *thr = isfinite(kth) ? kth - 2.0f * kMargin : -INFINITY;
+}
+
+// Candidates: entries at or above the threshold (every entry with rows when
+// the query is outside the safe range or the bank outside the fast path);
+// entry_best is reset for the next query on the way.
+__global__ void entry_collect_kernel(int* __restrict__ entry_best, const uint64_t* __restrict__ off,
+                                     int64_t entries, const float* __restrict__ thr,
+                                     const int* __restrict__ unsafe, int force_all,
+                                     uint32_t* __restrict__ cand, unsigned* __restrict__ count) {
+  const float t = *thr;
+  const bool all = force_all || *unsafe;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < entries;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const float v = ordered_to_float(entry_best[e]);
+    entry_best[e] = kOrderedNegInf;
+    const bool pick = all ? off[e + 1] > off[e] : (v >= t && v > -INFINITY);
+    if (pick) cand[atomicAdd(count, 1u)] = (uint32_t)e;
+  }
+}
+
+// Exact entry scores of the candidates: a warp per entry, a lane per row
+// (the reference's sequential fp64 dot each), max over the finite ones.
+template <typename T>
+__global__ void __launch_bounds__(kEntryWarps * 32) entry_refine_kernel(
+    const T* __restrict__ rows, const float* __restrict__ norms, int dim,
+    const float* __restrict__ query, const uint64_t* __restrict__ off,
+    const uint32_t* __restrict__ cand, const unsigned* __restrict__ count,
+    const uint32_t* __restrict__ allow, float* __restrict__ cand_s) {
+  __shared__ double qn;
+  if (threadIdx.x == 0) qn = query_norm_seq(query, dim);
+  __syncthreads();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const unsigned n = *count;
+  for (unsigned i = blockIdx.x * kEntryWarps + warp; i < n; i += gridDim.x * kEntryWarps) {
+    const uint32_t e = cand[i];
+    float best = -INFINITY;
+    if (policy::row_allowed(allow, e)) {
+      for (uint64_t r = off[e] + lane; r < off[e + 1]; r += 32) {
+        const float nrm = __ldg(norms + r);
+        if (!isfinite(nrm)) continue;
+        const float sc = exact_score<T>(rows + r * dim, dim, query, qn, nrm);
+        if (isfinite(sc)) best = fmaxf(best, sc);
+      }
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) best = fmaxf(best, __shfl_xor_sync(kFull, best, o));
+    if (lane == 0) cand_s[i] = best;  // -inf: no finite row (dropped)
+  }
+}
+
+// Top-k of the scored candidates into the query's Result.
+__global__ void __launch_bounds__(kEntryWarps * 32) entry_finalize_kernel(
+    const uint32_t* __restrict__ cand, const float* __restrict__ cand_s,
+    unsigned* __restrict__ count, int topk, uint64_t id_offset, Result* __restrict__ r,
+    uint64_t* out_ids, float* out_scores) {
+  __shared__ float sh_s[kEntryWarps * 32];
+  __shared__ uint32_t sh_id[kEntryWarps * 32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const unsigned n = *count;
+  WarpList list;
+  list.init();
+  for (unsigned i0 = warp * 32; i0 < n; i0 += blockDim.x) {
+    const unsigned i = i0 + lane;
+    list.offer_margin(i < n ? cand_s[i] : -INFINITY, i < n ? cand[i] : kNoRow, lane, topk, 0.0f);
+  }
+  sh_s[warp * 32 + lane] = list.s;
+  sh_id[warp * 32 + lane] = list.id;
+  __syncthreads();
+  if (warp == 0) {
+    for (int w = 1; w < kEntryWarps; ++w)
+      list.offer_margin(sh_s[w * 32 + lane], sh_id[w * 32 + lane], lane, topk, 0.0f);
+    const bool ok = lane < topk && isfinite(list.s) && list.id != kNoRow;
+    const unsigned m = __ballot_sync(kFull, ok);
+    if (lane < topk) {
+      const uint64_t id = ok ? (uint64_t)list.id + id_offset : UINT64_MAX;
+      const float sc = ok ? list.s : __int_as_float(0x7FC00000);
+      r->ids[lane] = id;
+      r->scores[lane] = sc;
+      if (out_ids) out_ids[lane] = id;
+      if (out_scores) out_scores[lane] = sc;
+    }
+    if (lane == 0) {
+      r->count = __popc(m);
+      r->status = kOk;
+      *count = 0u;
+    }
+  }
 }
 
 // Packed fp32x2 FMA (sm_100 FFMA2): d = a * b + c on both lanes of a float2.
@@ -1134,51 +1288,48 @@ __global__ void __launch_bounds__(kLexWarps * 32) mla_lex_score_kernel(
     const T* __restrict__ rows, const float* __restrict__ norms, int dim,
     const float* __restrict__ query, const uint2* __restrict__ list,
     const uint32_t* __restrict__ counter, const uint32_t* __restrict__ allow, int m,
-    float* __restrict__ cand_s, uint32_t* __restrict__ cand_id) {
+    const uint64_t* __restrict__ entry_off, float* __restrict__ cand_s,
+    uint32_t* __restrict__ cand_id) {
   __shared__ float qs[kLexMaxDim];
   __shared__ float rowbuf[kLexWarps][kLexMaxDim];
   __shared__ double qn;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   for (int d = threadIdx.x; d < dim; d += blockDim.x) qs[d] = query[d];
+  __syncthreads();
+  if (threadIdx.x == 0) {  // the reference's query norm (sequential fp64)
+    double acc = 0.0;
+#pragma unroll 8
+    for (int d = 0; d < dim; ++d) acc += (double)qs[d] * (double)qs[d];
+    qn = sqrt(acc);
+  }
+  __syncthreads();
   const uint32_t n = *counter;
   const uint32_t nw = gridDim.x * kLexWarps;
-  bool first = true;
-  for (uint32_t i = blockIdx.x * kLexWarps + warp; i < n || first; i += nw) {
-    const bool live = i < n;
-    const uint2 h = live ? list[i] : make_uint2(0u, 0u);
-    const bool ok = live && policy::row_allowed(allow, h.x);
-    float nrm = 0.0f;
-    if (ok) {  // the row's loads go out before the query norm's chain
-      const T* row = rows + (int64_t)h.x * dim;
+  for (uint32_t i = blockIdx.x * kLexWarps + warp; i < n; i += nw) {
+    const uint2 h = list[i];
+    const bool ok = policy::row_allowed(allow, h.x);
+    // a node's rows: itself, or its entry's rows in a multi-row bank (max)
+    const uint64_t r0 = entry_off ? entry_off[h.x] : h.x;
+    const uint64_t r1 = entry_off ? entry_off[h.x + 1] : (uint64_t)h.x + 1;
+    float best = -INFINITY;
+    for (uint64_t r = r0; ok && r < r1; ++r) {
+      const T* row = rows + (int64_t)r * dim;
       for (int d = lane; d < dim; d += 32) rowbuf[warp][d] = to_f(__ldg(row + d));
-      nrm = __ldg(norms + h.x);
-    }
-    if (first) {  // the reference's query norm (sequential fp64), once per block
-      __syncthreads();
-      if (threadIdx.x == 0) {
-        double acc = 0.0;
-#pragma unroll 8
-        for (int d = 0; d < dim; ++d) acc += (double)qs[d] * (double)qs[d];
-        qn = sqrt(acc);
-      }
-      __syncthreads();
-      first = false;
-      if (!live) break;
-    }
-    __syncwarp();
-    if (lane == 0) {
-      float S = -INFINITY;
-      if (ok && isfinite(nrm)) {
+      const float nrm = __ldg(norms + r);
+      __syncwarp();
+      if (lane == 0 && isfinite(nrm)) {
         double dot = 0.0;
 #pragma unroll 8
         for (int d = 0; d < dim; ++d) dot = fma((double)qs[d], (double)rowbuf[warp][d], dot);
         const float es = (float)(dot / (qn * (double)nrm + 1.0e-8));
-        S = es + __fdiv_rn((float)h.y, (float)m);
+        if (isfinite(es)) best = fmaxf(best, es);
       }
-      cand_s[i] = S;
+      __syncwarp();
+    }
+    if (lane == 0) {
+      cand_s[i] = best > -INFINITY ? best + __fdiv_rn((float)h.y, (float)m) : -INFINITY;
       cand_id[i] = h.x;
     }
-    __syncwarp();
   }
 }
 
@@ -1229,6 +1380,20 @@ struct grm_b200_mla_bank {
   const uint32_t* cur_allow = nullptr;        // filter bitmap of the route in progress
   cudaStream_t lex_stream = nullptr;          // single-query lexical pass beside the scan
   cudaEvent_t ev_fork = nullptr, ev_lex = nullptr;
+  // multi-row entries: `nodes` counts rows, `entries` the routed entries
+  bool multi = false;
+  int64_t entries = 0;
+  uint64_t* d_entry_off = nullptr;     // [entries + 1] row offsets
+  uint32_t* d_entry_of_row = nullptr;  // [rows]
+  int* d_entry_best = nullptr;         // [entries] ordered approximate maxima
+  float* d_blk_s = nullptr;            // [entry_blocks * 32]
+  uint32_t* d_blk_id = nullptr;
+  float* d_thr = nullptr;
+  int* d_unsafe = nullptr;
+  uint32_t* d_cand = nullptr;          // [entries]
+  float* d_cand_s = nullptr;
+  unsigned* d_cand_count = nullptr;
+  int entry_blocks = 1;
 };
 
 namespace {
@@ -1267,6 +1432,17 @@ ScanFn<T> scan_fn(int dim) {
     case 128: return mla_scan_kernel<128, T>;
     case 256: return mla_scan_kernel<256, T>;
     case 512: return mla_scan_kernel<512, T>;
+  }
+  return nullptr;
+}
+
+template <typename T>
+ScanFn<T> scan_multi_fn(int dim) {
+  switch (dim) {
+    case 64: return mla_scan_kernel<64, T, false, true>;
+    case 128: return mla_scan_kernel<128, T, false, true>;
+    case 256: return mla_scan_kernel<256, T, false, true>;
+    case 512: return mla_scan_kernel<512, T, false, true>;
   }
   return nullptr;
 }
@@ -1366,6 +1542,9 @@ Params<T> make_params(grm_b200_mla_bank* b, const float* dq, int topk) {
   p.nq = 0;
   p.fallback_count = b->d_fallbacks;
   p.allow = b->cur_allow;
+  p.entry_of_row = b->d_entry_of_row;
+  p.entry_best = b->d_entry_best;
+  p.multi_unsafe = b->d_unsafe;
   return p;
 }
 
@@ -1556,7 +1735,54 @@ int launch_batch(grm_b200_mla_bank* b, const Params<__half>& p0, int nq, cudaStr
 // parameters (dq == nullptr, q_host != nullptr).  Results are written by the
 // kernels straight into mapped pinned host memory (no copy-back call).
 template <typename T>
+int run_chunk(grm_b200_mla_bank* b, const float* dq, const float* q_host, int nq, int topk);
+
+// Multi-row bank, stream-ordered: per query the folding scan, the entry
+// threshold and candidates, their exact scores and the top-k into
+// results[q] (and the optional device outputs).
+template <typename T>
+int launch_multi(grm_b200_mla_bank* b, const float* dq, int nq, int topk, Result* results,
+                 cudaStream_t s, uint64_t* out_ids = nullptr, float* out_scores = nullptr,
+                 uint64_t id_offset = 0) {
+  DeviceInfo info;
+  if (device_info(b->device, &info) != 0) info.sms = 148;
+  for (int q = 0; q < nq; ++q) {
+    const float* qp = dq + (int64_t)q * b->dim;
+    Params<T> p = make_params<T>(b, qp, topk);
+    if (!b->exact_only) {
+      scan_multi_fn<T>(b->dim)<<<dim3(b->grid_x, 1), kThreads, 0, s>>>(p);
+      entry_top_kernel<<<b->entry_blocks, kEntryWarps * 32, 0, s>>>(b->d_entry_best, b->entries,
+                                                                     b->d_blk_s, b->d_blk_id);
+      entry_threshold_kernel<<<1, 32, 0, s>>>(b->d_blk_s, b->d_blk_id, b->entry_blocks, topk,
+                                              b->d_thr);
+    }
+    const int cg = (int)std::max<int64_t>(1, std::min<int64_t>((int64_t)info.sms * 4,
+                                                                ceil_div64(b->entries, 256)));
+    entry_collect_kernel<<<cg, 256, 0, s>>>(b->d_entry_best, b->d_entry_off, b->entries, b->d_thr,
+                                            b->d_unsafe, b->exact_only ? 1 : 0, b->d_cand,
+                                            b->d_cand_count);
+    entry_refine_kernel<T><<<info.sms * 2, kEntryWarps * 32, 0, s>>>(
+        static_cast<const T*>(b->d_rows), b->d_norms, b->dim, qp, b->d_entry_off, b->d_cand,
+        b->d_cand_count, b->cur_allow, b->d_cand_s);
+    entry_finalize_kernel<<<1, kEntryWarps * 32, 0, s>>>(
+        b->d_cand, b->d_cand_s, b->d_cand_count, topk, id_offset, results + q,
+        out_ids ? out_ids + (int64_t)q * topk : nullptr,
+        out_scores ? out_scores + (int64_t)q * topk : nullptr);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_status(e);
+  }
+  return 0;
+}
+
+template <typename T>
 int run_chunk(grm_b200_mla_bank* b, const float* dq, const float* q_host, int nq, int topk) {
+  if (b->multi) {
+    int rc = launch_multi<T>(b, dq, nq, topk, b->d_results_mapped, b->stream);
+    if (rc) return b->err.set(rc, "MLA multi-row route launch failed");
+    cudaError_t e = cudaStreamSynchronize(b->stream);
+    if (e != cudaSuccess) return b->err.set(cuda_status(e), "MLA multi-row route failed: %s", cudaGetErrorString(e));
+    return 0;
+  }
   Params<T> p = make_params<T>(b, dq, topk);
   p.results = b->d_results_mapped;
   if (!dq) std::memcpy(p.qinline, q_host, sizeof(float) * (size_t)b->dim);
@@ -1680,6 +1906,10 @@ void bank_free(grm_b200_mla_bank* b) {
   if (b->d_queries) cudaFree(b->d_queries);
   grm_b200::policy::policy_free(b->pol);
   if (b->lex_stream) cudaStreamSynchronize(b->lex_stream);
+  void* mptrs[] = {b->d_entry_off, b->d_entry_of_row, b->d_entry_best, b->d_blk_s, b->d_blk_id,
+                   b->d_thr, b->d_unsafe, b->d_cand, b->d_cand_s, b->d_cand_count};
+  for (void* m : mptrs)
+    if (m) cudaFree(m);
   if (b->ev_fork) cudaEventDestroy(b->ev_fork);
   if (b->ev_lex) cudaEventDestroy(b->ev_lex);
   if (b->lex_stream) cudaStreamDestroy(b->lex_stream);
@@ -1727,9 +1957,97 @@ int create_common(const void* rows, bool host, int dtype, int64_t nodes, int dim
   return 0;
 }
 
+__global__ void fill_int_kernel(int* p, int64_t n, int v) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    p[i] = v;
+}
+
+// Turn a row bank into a bank of multi-row entries: entry e owns rows
+// off[e] .. off[e+1]-1 (RouterIndex's entry_row_offsets, cpp/grm_runtime.cpp:3219-3260).
+int make_multi(grm_b200_mla_bank* b, const uint64_t* off, int64_t entries) {
+  b->multi = true;
+  b->batch = false;
+  b->bulk = false;
+  b->entries = entries;
+  DeviceInfo info;
+  int rc = device_info(b->device, &info);
+  if (rc) return rc;
+  int occ = 1;
+  cudaError_t e = cudaSuccess;
+  if (!b->exact_only) {
+    const void* fn = b->dtype == GRM_B200_F16 ? (const void*)scan_multi_fn<__half>(b->dim)
+                                              : (const void*)scan_multi_fn<float>(b->dim);
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, kThreads, 0);
+    if (e != cudaSuccess) return cuda_status(e);
+  }
+  b->grid_x = (int)std::max<int64_t>(
+      1, std::min<int64_t>((int64_t)info.sms * std::max(occ, 1), ceil_div64(ceil_div64(b->nodes, 32), kWarps)));
+  b->entry_blocks = (int)std::max<int64_t>(
+      1, std::min<int64_t>((int64_t)info.sms * 2, ceil_div64(entries, kEntryWarps * 32)));
+  std::vector<uint32_t> eor((size_t)b->nodes);
+  for (int64_t en = 0; en < entries; ++en)
+    for (uint64_t r = off[en]; r < off[en + 1]; ++r) eor[(size_t)r] = (uint32_t)en;
+  auto alloc = [&](void** ptr, size_t bytes) {
+    if (e == cudaSuccess) e = cudaMalloc(ptr, std::max<size_t>(bytes, 16));
+  };
+  alloc((void**)&b->d_entry_off, sizeof(uint64_t) * (size_t)(entries + 1));
+  alloc((void**)&b->d_entry_of_row, sizeof(uint32_t) * (size_t)b->nodes);
+  alloc((void**)&b->d_entry_best, sizeof(int) * (size_t)entries);
+  alloc((void**)&b->d_blk_s, sizeof(float) * 32 * (size_t)b->entry_blocks);
+  alloc((void**)&b->d_blk_id, sizeof(uint32_t) * 32 * (size_t)b->entry_blocks);
+  alloc((void**)&b->d_thr, sizeof(float));
+  alloc((void**)&b->d_unsafe, sizeof(int) * 64);
+  alloc((void**)&b->d_cand, sizeof(uint32_t) * (size_t)entries);
+  alloc((void**)&b->d_cand_s, sizeof(float) * (size_t)entries);
+  alloc((void**)&b->d_cand_count, sizeof(unsigned));
+  if (e == cudaSuccess)
+    e = cudaMemcpy(b->d_entry_off, off, sizeof(uint64_t) * (size_t)(entries + 1),
+                   cudaMemcpyHostToDevice);
+  if (e == cudaSuccess)
+    e = cudaMemcpy(b->d_entry_of_row, eor.data(), sizeof(uint32_t) * eor.size(),
+                   cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemset(b->d_cand_count, 0, sizeof(unsigned));
+  if (e == cudaSuccess) e = cudaMemset(b->d_unsafe, 0, sizeof(int) * 64);
+  if (e == cudaSuccess) {
+    fill_int_kernel<<<info.sms * 4, 256, 0, b->stream>>>(b->d_entry_best, entries, kOrderedNegInf);
+    e = cudaGetLastError();
+  }
+  if (e == cudaSuccess) e = cudaStreamSynchronize(b->stream);
+  return cuda_status(e);
+}
+
 }  // namespace
 
 extern "C" {
+
+int grm_b200_mla_bank_create_multi(const void* rows_host, int dtype, int64_t rows, int dim,
+                                   const uint64_t* entry_row_offsets, int64_t entries, int device,
+                                   grm_b200_mla_bank** out_bank) {
+  if (!out_bank) return GRM_B200_EINVAL;
+  *out_bank = nullptr;
+  if (!entry_row_offsets || entries <= 0 || entries >= (int64_t)0xFFFFFFFF ||
+      entry_row_offsets[0] != 0 || entry_row_offsets[entries] != (uint64_t)rows) {
+    set_thread_error("invalid entry_row_offsets (entries=%lld rows=%lld)", (long long)entries,
+                     (long long)rows);
+    return GRM_B200_EINVAL;
+  }
+  for (int64_t i = 0; i < entries; ++i)
+    if (entry_row_offsets[i + 1] < entry_row_offsets[i]) {
+      set_thread_error("entry_row_offsets must be non-decreasing (entry %lld)", (long long)i);
+      return GRM_B200_EINVAL;
+    }
+  grm_b200_mla_bank* b = nullptr;
+  int rc = create_common(rows_host, true, dtype, rows, dim, device, &b);
+  if (rc) return rc;
+  if ((rc = make_multi(b, entry_row_offsets, entries))) {
+    set_thread_error("MLA multi-row bank setup failed (%d)", rc);
+    bank_free(b);
+    return rc;
+  }
+  *out_bank = b;
+  return 0;
+}
 
 int grm_b200_mla_bank_create(const void* rows_host, int dtype, int64_t nodes, int dim, int device,
                              grm_b200_mla_bank** out_bank) {
@@ -1752,7 +2070,7 @@ int grm_b200_mla_route(grm_b200_mla_bank* bank, const float* queries_host, int q
     return bank->err.set(GRM_B200_EINVAL, "invalid MLA route arguments (dim=%d, bank dim=%d)", dim,
                          bank->dim);
   cudaError_t e = cudaSetDevice(bank->device);
-  if (e == cudaSuccess && query_count == 1 && dim <= kInlineMax)
+  if (e == cudaSuccess && query_count == 1 && dim <= kInlineMax && !bank->multi)
     return route_device_queries(bank, nullptr, 1, warmup, topk, out_ids_host, out_scores_host,
                                 elapsed_ms, queries_host);
   const size_t need = (size_t)query_count * dim;
@@ -1802,6 +2120,18 @@ int route_async_phases(grm_b200_mla_bank* bank, const float* queries_device, int
                          query_count, bank->scratch_queries);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   int rc = 0;
+  if (bank->multi) {  // one stream-ordered pipeline: both phases at once
+    if (phase & 1) {
+      rc = (bank->dtype == GRM_B200_F16)
+               ? launch_multi<__half>(bank, queries_device, query_count, topk, bank->d_results, s,
+                                      out_ids_device, out_scores_device, id_offset)
+               : launch_multi<float>(bank, queries_device, query_count, topk, bank->d_results, s,
+                                     out_ids_device, out_scores_device, id_offset);
+      if (rc) return bank->err.set(rc, "MLA multi-row async route launch failed");
+      bank->routes += (uint64_t)query_count;
+    }
+    return 0;
+  }
   if (bank->dtype == GRM_B200_F16) {
     Params<__half> p = make_params<__half>(bank, queries_device, topk);
     p.out_ids = out_ids_device;
@@ -1880,7 +2210,8 @@ int grm_b200_mla_bank_set_policy(grm_b200_mla_bank* bank, const char* const* lex
   if (e != cudaSuccess) return bank->err.set(cuda_status(e), "cudaSetDevice failed");
   cudaStreamSynchronize(bank->stream);
   const char* const* cats[policy::kCats] = {kinds, scopes, durabilities, mutabilities};
-  return policy::policy_set(bank->pol, bank->nodes, lexical_keys, cats, active, bank->err);
+  return policy::policy_set(bank->pol, bank->multi ? bank->entries : bank->nodes, lexical_keys,
+                            cats, active, bank->err);
 }
 
 int grm_b200_mla_route_policy(grm_b200_mla_bank* bank, const float* queries_host, int query_count,
@@ -1907,7 +2238,8 @@ int grm_b200_mla_route_policy(grm_b200_mla_bank* bank, const float* queries_host
   if (!bank->pol.set) {  // every node keeps the reference's defaults: no keys, active
     const char* const* cats[policy::kCats] = {nullptr, nullptr, nullptr, nullptr};
     cudaStreamSynchronize(bank->stream);
-    if ((rc = policy::policy_set(bank->pol, bank->nodes, nullptr, cats, nullptr, bank->err)))
+    if ((rc = policy::policy_set(bank->pol, bank->multi ? bank->entries : bank->nodes, nullptr,
+                                 cats, nullptr, bank->err)))
       return rc;
   }
   const size_t need = (size_t)query_count * dim;
@@ -1947,11 +2279,13 @@ int grm_b200_mla_route_policy(grm_b200_mla_bank* bank, const float* queries_host
     if (bank->dtype == GRM_B200_F16)
       mla_lex_score_kernel<__half><<<grid, kLexWarps * 32, 0, st>>>(
           static_cast<const __half*>(bank->d_rows), bank->d_norms, dim, dq, bank->pol.d_hitlist,
-          bank->pol.d_counter, allow, *m, bank->pol.d_cand_s, bank->pol.d_cand_id);
+          bank->pol.d_counter, allow, *m, bank->d_entry_off, bank->pol.d_cand_s,
+          bank->pol.d_cand_id);
     else
       mla_lex_score_kernel<float><<<grid, kLexWarps * 32, 0, st>>>(
           static_cast<const float*>(bank->d_rows), bank->d_norms, dim, dq, bank->pol.d_hitlist,
-          bank->pol.d_counter, allow, *m, bank->pol.d_cand_s, bank->pol.d_cand_id);
+          bank->pol.d_counter, allow, *m, bank->d_entry_off, bank->pol.d_cand_s,
+          bank->pol.d_cand_id);
     cudaError_t le = cudaGetLastError();
     return le == cudaSuccess ? 0 : bank->err.set(cuda_status(le), "MLA lexical kernels launch failed");
   };
@@ -1978,7 +2312,13 @@ int grm_b200_mla_route_policy(grm_b200_mla_bank* bank, const float* queries_host
     cudaEventRecord(bank->ev_lex, bank->lex_stream);
   }
   bank->cur_allow = allow;
-  if (bank->dtype == GRM_B200_F16) {
+  if (bank->multi) {
+    rc = (bank->dtype == GRM_B200_F16)
+             ? launch_multi<__half>(bank, bank->d_queries, query_count, topk, bank->d_results,
+                                    bank->stream)
+             : launch_multi<float>(bank, bank->d_queries, query_count, topk, bank->d_results,
+                                   bank->stream);
+  } else if (bank->dtype == GRM_B200_F16) {
     Params<__half> p = make_params<__half>(bank, bank->d_queries, topk);  // device results
     rc = (bank->batch && !allow && query_count >= kBatchMin && topk <= kBMaxTopk)
              ? launch_batch(bank, p, query_count, bank->stream)
@@ -2205,6 +2545,9 @@ extern "C" int grm_b200_mla_route_noalloc(const void* rows_device, int64_t nodes
   p.nq = query_count;
   p.fallback_count = nullptr;
   p.allow = nullptr;
+  p.entry_of_row = nullptr;
+  p.entry_best = nullptr;
+  p.multi_unsafe = nullptr;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   scratch_init_kernel<<<(query_count + 127) / 128, 128, 0, s>>>(base + results_bytes, stride,
                                                                  query_count);

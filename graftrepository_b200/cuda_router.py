@@ -438,6 +438,34 @@ class CudaMLARouteSidecar:
         return CudaMLARouteBank(handle, ids, nodes=nodes, dim=dim, setup_wall_ms=setup,
                                 signature=signature, dtype=dtype_code)
 
+    def create_bank_multi(self, rows, entry_row_offsets, node_ids=None, *,
+                          signature=None) -> CudaMLARouteBank:
+        """A bank of multi-row entries: entry e owns rows
+        entry_row_offsets[e] .. entry_row_offsets[e+1]-1 (a digest's own
+        centroid and its child_cents) and scores the max of its rows."""
+        r32 = np.ascontiguousarray(rows, dtype=np.float32)
+        if r32.ndim != 2:
+            raise ValueError("rows must have shape (rows, dim)")
+        off = np.ascontiguousarray(entry_row_offsets, dtype=np.uint64).reshape(-1)
+        entries = off.shape[0] - 1
+        ids = np.arange(entries, dtype=np.uint64) if node_ids is None else \
+            np.ascontiguousarray(node_ids, dtype=np.uint64).reshape(-1)
+        if ids.shape[0] != entries:
+            raise ValueError("node_ids length must match the entries")
+        if _fits(r32, np.float16):
+            arr, code = r32.astype(np.float16), GRM_B200_F16
+        else:
+            arr, code = r32, GRM_B200_F32
+        handle = ctypes.c_void_p()
+        t0 = time.perf_counter_ns()
+        rc = self._lib.grm_b200_mla_bank_create_multi(arr.ctypes.data, code, arr.shape[0],
+                                                      arr.shape[1], off.ctypes.data, entries,
+                                                      self.device, ctypes.byref(handle))
+        setup = (time.perf_counter_ns() - t0) / 1.0e6
+        _lib.check(rc, _lib.thread_error)
+        return CudaMLARouteBank(handle, ids, nodes=entries, dim=arr.shape[1],
+                                setup_wall_ms=setup, signature=signature, dtype=code)
+
     def create_bank_device(self, rows_ptr: int, dtype_code: int, nodes: int, dim: int,
                            node_ids=None, *, signature=None) -> CudaMLARouteBank:
         handle = ctypes.c_void_p()

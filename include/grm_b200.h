@@ -68,6 +68,19 @@ typedef struct grm_b200_gqa_bank grm_b200_gqa_bank;
 int grm_b200_mla_bank_create(const void* rows_host, int dtype, int64_t nodes, int dim,
                              int device, grm_b200_mla_bank** out_bank);
 
+/* A bank of multi-row entries (a digest node with its child centroids,
+ * core/graft_arena.py:1670-1684): entry e owns rows entry_row_offsets[e] ..
+ * entry_row_offsets[e+1]-1 of rows_host[rows, dim] and scores the max of its
+ * finite row scores (RouterIndex::exact_mla_entry_score over
+ * entry_row_offsets, cpp/grm_runtime.cpp:3219-3260, :3518-3545); routes
+ * return entry indices.  The reference's CUDA sidecar takes single-row
+ * entries only (core/graft_arena.py:1125-1143); this replaces the CPU route
+ * those banks fall back to.  Every route entry point accepts such a bank
+ * (the batched tensor-core path is not used for it). */
+int grm_b200_mla_bank_create_multi(const void* rows_host, int dtype, int64_t rows, int dim,
+                                   const uint64_t* entry_row_offsets, int64_t entries,
+                                   int device, grm_b200_mla_bank** out_bank);
+
 /* Same, from rows already resident on the current device; the bank copies
  * them (the caller may free its buffer afterwards). */
 int grm_b200_mla_bank_create_device(const void* rows_device, int dtype, int64_t nodes,

@@ -28,7 +28,7 @@ __all__ = [
     "quant_ref", "dequant_ref", "quant_packed", "dequant_packed", "packed_group_bytes",
     "mount_scatter", "mount_rope", "swap_splice",
     "ROUTE_DEFAULTS", "split_keys", "route_allowed", "lexical_hits", "mla_route_policy",
-    "gqa_route_policy",
+    "gqa_route_policy", "mla_route_multi",
 ]
 
 _P = ctypes.c_void_p
@@ -161,6 +161,23 @@ def mla_route(rows, query, k: int, norms=None) -> tuple[np.ndarray, np.ndarray]:
     """Exact reference MLA route: (ids uint64[k] with UINT64_MAX fill, scores)."""
     ids, s, _ = topk(mla_scores(rows, query, norms), k)
     return ids, s
+
+
+def mla_route_multi(rows, entry_row_offsets, query, k: int, norms=None):
+    """route_mla_arena over multi-row entries (exact_mla_entry_score,
+    cpp/grm_runtime.cpp:3518-3545): an entry scores the max of its finite row
+    scores, NaN (dropped) if none; (score desc, entry asc)."""
+    s = mla_scores(rows, query, norms)
+    off = np.asarray(entry_row_offsets, dtype=np.int64)
+    n = off.shape[0] - 1
+    best = np.full(n, np.nan, dtype=np.float32)
+    for e in range(n):
+        seg = s[off[e]:off[e + 1]]
+        seg = seg[np.isfinite(seg)]
+        if seg.size:
+            best[e] = seg.max()
+    ids, sc, _ = topk(best, k)
+    return ids, sc
 
 
 # ------------------------------------------------------------ route policy
@@ -415,6 +432,9 @@ class RefStore:
             L.refd_mla_route_policy.restype = ctypes.c_int
             L.refd_mla_route_policy.argtypes = [_P, _P, ctypes.c_uint64] + [ctypes.c_char_p] * 5 + [
                 ctypes.c_uint64, _P, _P]
+            L.refd_mla_create_multi.restype = _P
+            L.refd_mla_create_multi.argtypes = [_P, ctypes.c_uint64, ctypes.c_uint64, _P,
+                                                ctypes.c_uint64]
             L.refd_gqa_create_policy.restype = _P
             L.refd_gqa_create_policy.argtypes = [_P, _P, ctypes.c_uint64, ctypes.c_uint64,
                                                  ctypes.c_uint64] + [_P] * 6
@@ -491,6 +511,18 @@ class RefStore:
         if rc != 0:
             raise RuntimeError(self._L.refd_last_error(self._h).decode())
         return [int(x) for x in out[: cnt.value]]
+
+    def load_mla_multi(self, rows, entry_row_offsets) -> "RefStore":
+        """MLA store whose node e carries rows off[e] .. off[e+1]-1 as its
+        route keys (grm_store_set_route_list with key_count > 1)."""
+        r = np.ascontiguousarray(rows, dtype=np.float32)
+        off = np.ascontiguousarray(entry_row_offsets, dtype=np.uint64)
+        h = self._L.refd_mla_create_multi(_ptr(r), r.shape[0], r.shape[1], _ptr(off),
+                                          off.shape[0] - 1)
+        if not h:
+            raise RuntimeError("reference MLA store load failed")
+        self._h, self.kind, self.dim = h, "mla", r.shape[1]
+        return self
 
     def load_gqa_policy(self, keys_bf16, token_offsets, kv_heads: int, head_dim: int,
                         node_lexical=None, cats=None, active=None) -> "RefStore":

@@ -76,6 +76,30 @@ int refd_mla_route_policy(grm_store_handle* h, const float* q, uint64_t dim, con
                                   mutabilities ? mutabilities : "", topk, out, topk, out_count);
 }
 
+// MLA store of multi-row entries: node e's route keys are rows off[e] ..
+// off[e+1]-1 (grm_store_set_route_list with key_count > 1).
+grm_store_handle* refd_mla_create_multi(const float* rows, uint64_t n_rows, uint64_t dim,
+                                        const uint64_t* off, uint64_t entries) {
+  grm_store_handle* h = grm_store_create_mla("RefDriverMLA", 1, 2048, 576, 0, 512, 64);
+  if (!h) return nullptr;
+  std::vector<uint64_t> offs;
+  for (uint64_t e = 0; e < entries; ++e) {
+    uint64_t id = 0;
+    int rc = grm_store_add_node(h, "", 1, nullptr, 0, &id);
+    if (rc == 0 && id != e) rc = -1;
+    const uint64_t k = off[e + 1] - off[e];
+    offs.resize(k + 1);
+    for (uint64_t j = 0; j <= k; ++j) offs[j] = j * dim;
+    if (rc == 0 && k > 0)
+      rc = grm_store_set_route_list(h, id, rows + off[e] * dim, k * dim, offs.data(), k, "");
+    if (rc != 0 || off[e + 1] > n_rows) {
+      grm_store_destroy(h);
+      return nullptr;
+    }
+  }
+  return h;
+}
+
 // grm_store_route (cpp/grm_runtime_c.h:403-410).
 int refd_mla_route(grm_store_handle* h, const float* q, uint64_t dim, uint64_t topk,
                    uint64_t* out, uint64_t* out_count) {

@@ -116,3 +116,25 @@ def test_gqa_policy_restatement_equals_reference_runtime(seed, qt):
                                             active=active, query_lexical=qlex, filters=filt)
                 got = [int(x) for x in ids if x != np.iinfo(np.uint64).max]
                 assert got == want, (t, qlex, filt, k)
+
+
+@pytest.mark.parametrize("seed,dim", [(41, 64), (42, 256)])
+def test_mla_multi_row_restatement_equals_reference_runtime(seed, dim):
+    """Entries of several rows (digest + child centroids) score the max of
+    their rows: route_mla_arena over entry_row_offsets."""
+    rng = np.random.default_rng(seed)
+    E = 400
+    counts = rng.integers(1, 6, E)
+    off = np.zeros(E + 1, np.uint64)
+    off[1:] = np.cumsum(counts)
+    rows = rng.standard_normal((int(off[-1]), dim)).astype(np.float32)
+    rows[int(off[7]):int(off[8])] = rows[int(off[3])]   # ties across entries
+    rows[int(off[11]), 0] = np.nan                        # one bad row of an entry
+    with O.RefStore().load_mla_multi(rows, off) as st:
+        for _ in range(8):
+            q = rng.standard_normal(dim).astype(np.float32)
+            for k in (1, 5, 16):
+                want = st.route(q, k)
+                ids, _ = O.mla_route_multi(rows, off, q, k)
+                got = [int(x) for x in ids if x != np.iinfo(np.uint64).max]
+                assert got == want
