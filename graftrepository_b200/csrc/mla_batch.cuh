@@ -86,6 +86,7 @@ struct BatchParams {
   CUtensorMap tmap;              // bank [nodes, D] fp16, box 64 x 128, 128-byte swizzle
   const unsigned char* qmat;     // swizzled query image, BLayout<D>::kQ bytes
   const float* rnorms;           // 2^-8 / row norm (NaN for non-finite rows)
+  const uint32_t* allow;         // route filters: routable rows (nullptr: all)
   int64_t nodes;
   int64_t tiles;
   int nq;
@@ -416,10 +417,13 @@ __global__ void __launch_bounds__(kBThreads, 1)
     // max(last entry, entry k-1 - 2*margin): rows below never enter
     float thr = active ? -INFINITY : INFINITY;
     // 2^-8 / norm of the warp's 32 rows of a tile, lane l holding row l (NaN
-    // past the bank), loaded one tile ahead.
+    // past the bank and for rows a route filter excludes: their scores never
+    // reach a threshold), loaded one tile ahead.
     auto load_rn = [&](int64_t i) -> float {
       const int64_t r = ((int64_t)blockIdx.x + i * gridDim.x) * kBM + cq * 32 + lane;
-      return (i < my_tiles && r < p.nodes) ? __ldg(p.rnorms + r) : __int_as_float(0x7FC00000);
+      return (i < my_tiles && r < p.nodes && policy::row_allowed(p.allow, r))
+                 ? __ldg(p.rnorms + r)
+                 : __int_as_float(0x7FC00000);
     };
     float rn = load_rn(0);
     // The query's header slot lb collects every CTA's k-th approximate score

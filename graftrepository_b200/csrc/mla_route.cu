@@ -71,7 +71,8 @@ struct Scratch {
   unsigned char* base;
   size_t stride;  // bytes per query
   int blocks;
-  __device__ Header* hdr(int q) const { return reinterpret_cast<Header*>(base + stride * q); }
+  // pointer arithmetic only: the host uses it to pass a query's header to kernels
+  __host__ __device__ Header* hdr(int q) const { return reinterpret_cast<Header*>(base + stride * q); }
   __device__ Entry* entries(int q) const {
     return reinterpret_cast<Entry*>(base + stride * q + sizeof(Header));
   }
@@ -766,15 +767,19 @@ __global__ void __launch_bounds__(kEntryWarps * 32) entry_top_kernel(
 }
 
 // One warp: the k-th best over the block lists -> the candidate threshold.
+// The bulk pass's ticket counter is re-armed here for the next query.
 __global__ void entry_threshold_kernel(const float* __restrict__ blk_s,
                                        const uint32_t* __restrict__ blk_id, int nblk, int topk,
-                                       float* __restrict__ thr) {
+                                       float* __restrict__ thr, Header* hdr) {
   const int lane = threadIdx.x;
   WarpList list;
   list.init();
   for (int b = 0; b < nblk; ++b) list.offer(blk_s[b * 32 + lane], blk_id[b * 32 + lane], lane);
   const float kth = __shfl_sync(kFull, list.s, topk - 1);
-  if (lane == 0) *thr = isfinite(kth) ? kth - 2.0f * kMargin : -INFINITY;
+  if (lane == 0) {
+    *thr = isfinite(kth) ? kth - 2.0f * kMargin : -INFINITY;
+    hdr->next = 0;
+  }
 }
 
 // Candidates: entries at or above the threshold (every entry with rows when
@@ -829,7 +834,7 @@ __global__ void __launch_bounds__(kEntryWarps * 32) entry_refine_kernel(
 __global__ void __launch_bounds__(kEntryWarps * 32) entry_finalize_kernel(
     const uint32_t* __restrict__ cand, const float* __restrict__ cand_s,
     unsigned* __restrict__ count, int topk, uint64_t id_offset, Result* __restrict__ r,
-    uint64_t* out_ids, float* out_scores) {
+    uint64_t* out_ids, float* out_scores, Header* hdr) {
   __shared__ float sh_s[kEntryWarps * 32];
   __shared__ uint32_t sh_id[kEntryWarps * 32];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -858,7 +863,8 @@ __global__ void __launch_bounds__(kEntryWarps * 32) entry_finalize_kernel(
     }
     if (lane == 0) {
       r->count = __popc(m);
-      r->status = kOk;
+      r->status = hdr->err ? kError : kOk;  // a bounded wait of the pass gave up
+      hdr->err = 0;
       *count = 0u;
     }
   }
@@ -894,7 +900,7 @@ constexpr int kBulkWarps = 12;
 constexpr int kHalfBytes = 8192;
 constexpr int kBulkSmem = kBulkWarps * 2 * kHalfBytes;
 
-template <int D, typename T>
+template <int D, typename T, bool MULTI = false>
 __global__ void __launch_bounds__(kBulkWarps * 32, 1)
     mla_scan_bulk_kernel(const __grid_constant__ Params<T> p) {
   constexpr int NW = kBulkWarps;
@@ -1043,10 +1049,20 @@ __global__ void __launch_bounds__(kBulkWarps * 32, 1)
       }
       if (failed) break;
       const float dot = reduce_scatter<SLOTS>(part, lane);
-      float s = -INFINITY;
-      if (my_row < p.nodes && isfinite(nrm_pre) && policy::row_allowed(p.allow, my_row))
-        s = dot * __frcp_rn(nrm_pre + e_q);
-      list.offer_margin(s, (uint32_t)my_row, lane, p.topk, 2.0f * kMargin);
+      if constexpr (MULTI) {  // fold into the row's entry (see mla_scan_kernel)
+        if (my_row < p.nodes && isfinite(nrm_pre)) {
+          const uint32_t ent = __ldg(p.entry_of_row + my_row);
+          if (policy::row_allowed(p.allow, ent)) {
+            const float s = dot * __frcp_rn(nrm_pre + e_q);
+            if (isfinite(s)) atomicMax(p.entry_best + ent, float_to_ordered(s));
+          }
+        }
+      } else {
+        float s = -INFINITY;
+        if (my_row < p.nodes && isfinite(nrm_pre) && policy::row_allowed(p.allow, my_row))
+          s = dot * __frcp_rn(nrm_pre + e_q);
+        list.offer_margin(s, (uint32_t)my_row, lane, p.topk, 2.0f * kMargin);
+      }
       g = gn;
       gn = ticket ? dyn0 + (int64_t)__shfl_sync(kFull, tk, 0) : gn + gstride;
     }
@@ -1057,6 +1073,10 @@ __global__ void __launch_bounds__(kBulkWarps * 32, 1)
           mbar_wait(&sh_bar[warp][k], (phase_bits >> k) & 1u, kWaitLimit);
       if (lane == 0) atomicOr(&p.scratch.hdr(q)->err, 1);
     }
+  }
+  if constexpr (MULTI) {  // the entry kernels reset hdr->next and read hdr->err
+    if (blockIdx.x == 0 && threadIdx.x == 0) p.multi_unsafe[q] = safe ? 0 : 1;
+    return;
   }
   asm volatile("griddepcontrol.launch_dependents;");
   scan_finish<D, T, false, NW>(p, list, safe, q, lane, warp, fsm);
@@ -1382,6 +1402,7 @@ struct grm_b200_mla_bank {
   cudaEvent_t ev_fork = nullptr, ev_lex = nullptr;
   // multi-row entries: `nodes` counts rows, `entries` the routed entries
   bool multi = false;
+  bool multi_bulk = false;             // stream the rows with the bulk-copy pass
   int64_t entries = 0;
   uint64_t* d_entry_off = nullptr;     // [entries + 1] row offsets
   uint32_t* d_entry_of_row = nullptr;  // [rows]
@@ -1443,6 +1464,23 @@ ScanFn<T> scan_multi_fn(int dim) {
     case 128: return mla_scan_kernel<128, T, false, true>;
     case 256: return mla_scan_kernel<256, T, false, true>;
     case 512: return mla_scan_kernel<512, T, false, true>;
+  }
+  return nullptr;
+}
+
+template <typename T>
+ScanFn<T> scan_bulk_multi_fn(int dim) {
+  if constexpr (sizeof(T) == 2) {
+    switch (dim) {
+      case 64: return mla_scan_bulk_kernel<64, T, true>;
+      case 128: return mla_scan_bulk_kernel<128, T, true>;
+      case 256: return mla_scan_bulk_kernel<256, T, true>;
+    }
+  } else {
+    switch (dim) {
+      case 64: return mla_scan_bulk_kernel<64, T, true>;
+      case 128: return mla_scan_bulk_kernel<128, T, true>;
+    }
   }
   return nullptr;
 }
@@ -1698,6 +1736,7 @@ int launch_batch_chunk(grm_b200_mla_bank* b, const Params<__half>& p, int nq, cu
   bp.tmap = b->tmap;
   bp.qmat = b->d_qmat;
   bp.rnorms = b->d_rnorms;
+  bp.allow = p.allow;
   bp.nodes = b->nodes;
   bp.tiles = ceil_div64(b->nodes, kBM);
   bp.nq = nq;
@@ -1750,11 +1789,14 @@ int launch_multi(grm_b200_mla_bank* b, const float* dq, int nq, int topk, Result
     const float* qp = dq + (int64_t)q * b->dim;
     Params<T> p = make_params<T>(b, qp, topk);
     if (!b->exact_only) {
-      scan_multi_fn<T>(b->dim)<<<dim3(b->grid_x, 1), kThreads, 0, s>>>(p);
+      if (b->multi_bulk)
+        scan_bulk_multi_fn<T>(b->dim)<<<dim3(b->grid_x, 1), kBulkWarps * 32, kBulkSmem, s>>>(p);
+      else
+        scan_multi_fn<T>(b->dim)<<<dim3(b->grid_x, 1), kThreads, 0, s>>>(p);
       entry_top_kernel<<<b->entry_blocks, kEntryWarps * 32, 0, s>>>(b->d_entry_best, b->entries,
                                                                      b->d_blk_s, b->d_blk_id);
       entry_threshold_kernel<<<1, 32, 0, s>>>(b->d_blk_s, b->d_blk_id, b->entry_blocks, topk,
-                                              b->d_thr);
+                                              b->d_thr, p.scratch.hdr(0));
     }
     const int cg = (int)std::max<int64_t>(1, std::min<int64_t>((int64_t)info.sms * 4,
                                                                 ceil_div64(b->entries, 256)));
@@ -1767,7 +1809,7 @@ int launch_multi(grm_b200_mla_bank* b, const float* dq, int nq, int topk, Result
     entry_finalize_kernel<<<1, kEntryWarps * 32, 0, s>>>(
         b->d_cand, b->d_cand_s, b->d_cand_count, topk, id_offset, results + q,
         out_ids ? out_ids + (int64_t)q * topk : nullptr,
-        out_scores ? out_scores + (int64_t)q * topk : nullptr);
+        out_scores ? out_scores + (int64_t)q * topk : nullptr, p.scratch.hdr(0));
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_status(e);
   }
@@ -1781,6 +1823,10 @@ int run_chunk(grm_b200_mla_bank* b, const float* dq, const float* q_host, int nq
     if (rc) return b->err.set(rc, "MLA multi-row route launch failed");
     cudaError_t e = cudaStreamSynchronize(b->stream);
     if (e != cudaSuccess) return b->err.set(cuda_status(e), "MLA multi-row route failed: %s", cudaGetErrorString(e));
+    for (int i = 0; i < nq; ++i)
+      if (((volatile Result*)b->h_results)[i].status == kError)
+        return b->err.set(GRM_B200_KERNEL_BASE + 1,
+                          "MLA scan: a bounded device wait gave up (query %d)", i);
     return 0;
   }
   Params<T> p = make_params<T>(b, dq, topk);
@@ -1788,7 +1834,7 @@ int run_chunk(grm_b200_mla_bank* b, const float* dq, const float* q_host, int nq
   if (!dq) std::memcpy(p.qinline, q_host, sizeof(float) * (size_t)b->dim);
   int rc;
   if constexpr (sizeof(T) == 2) {
-    rc = (b->batch && dq && nq >= kBatchMin && topk <= kBMaxTopk && !p.allow)
+    rc = (b->batch && dq && nq >= kBatchMin && topk <= kBMaxTopk)
              ? launch_batch(b, p, nq, b->stream)
              : launch_scan<T>(b, p, nq, b->stream);
   } else {
@@ -1975,14 +2021,26 @@ int make_multi(grm_b200_mla_bank* b, const uint64_t* off, int64_t entries) {
   if (rc) return rc;
   int occ = 1;
   cudaError_t e = cudaSuccess;
-  if (!b->exact_only) {
+  b->multi_bulk = !b->exact_only && bulk_ok(b->dtype, b->dim);
+  if (b->multi_bulk) {
+    const void* fn = b->dtype == GRM_B200_F16 ? (const void*)scan_bulk_multi_fn<__half>(b->dim)
+                                              : (const void*)scan_bulk_multi_fn<float>(b->dim);
+    e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kBulkSmem);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout,
+                               cudaSharedmemCarveoutMaxShared);
+    if (e == cudaSuccess)
+      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, kBulkWarps * 32, kBulkSmem);
+    if (e != cudaSuccess) return cuda_status(e);
+  } else if (!b->exact_only) {
     const void* fn = b->dtype == GRM_B200_F16 ? (const void*)scan_multi_fn<__half>(b->dim)
                                               : (const void*)scan_multi_fn<float>(b->dim);
     e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fn, kThreads, 0);
     if (e != cudaSuccess) return cuda_status(e);
   }
   b->grid_x = (int)std::max<int64_t>(
-      1, std::min<int64_t>((int64_t)info.sms * std::max(occ, 1), ceil_div64(ceil_div64(b->nodes, 32), kWarps)));
+      1, std::min<int64_t>((int64_t)info.sms * std::max(occ, 1),
+                           ceil_div64(ceil_div64(b->nodes, 32), b->multi_bulk ? kBulkWarps : kWarps)));
   b->entry_blocks = (int)std::max<int64_t>(
       1, std::min<int64_t>((int64_t)info.sms * 2, ceil_div64(entries, kEntryWarps * 32)));
   std::vector<uint32_t> eor((size_t)b->nodes);
@@ -2320,7 +2378,7 @@ int grm_b200_mla_route_policy(grm_b200_mla_bank* bank, const float* queries_host
                                    bank->stream);
   } else if (bank->dtype == GRM_B200_F16) {
     Params<__half> p = make_params<__half>(bank, bank->d_queries, topk);  // device results
-    rc = (bank->batch && !allow && query_count >= kBatchMin && topk <= kBMaxTopk)
+    rc = (bank->batch && query_count >= kBatchMin && topk <= kBMaxTopk)
              ? launch_batch(bank, p, query_count, bank->stream)
              : launch_scan<__half>(bank, p, query_count, bank->stream, true);
     if (!rc) rc = launch_exact<__half>(bank, p, query_count, bank->stream, true);
