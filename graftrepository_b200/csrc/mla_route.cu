@@ -743,7 +743,7 @@ constexpr int kEntryWarps = 8;
 
 // Per block: the approximate top-32 entries of a strided share.
 __global__ void __launch_bounds__(kEntryWarps * 32) entry_top_kernel(
-    const int* __restrict__ entry_best, int64_t entries, float* __restrict__ blk_s,
+    const int* __restrict__ entry_best, int64_t entries, int topk, float* __restrict__ blk_s,
     uint32_t* __restrict__ blk_id) {
   __shared__ float sh_s[kEntryWarps * 32];
   __shared__ uint32_t sh_id[kEntryWarps * 32];
@@ -754,13 +754,14 @@ __global__ void __launch_bounds__(kEntryWarps * 32) entry_top_kernel(
        e0 += (int64_t)gridDim.x * kEntryWarps * 32) {
     const int64_t e = e0 + lane;
     const float v = e < entries ? ordered_to_float(__ldcg(entry_best + e)) : -INFINITY;
-    list.offer(v, (uint32_t)e, lane);
+    list.offer_margin(v, (uint32_t)e, lane, topk, 0.0f);  // only the top k must be exact
   }
   sh_s[warp * 32 + lane] = list.s;
   sh_id[warp * 32 + lane] = list.id;
   __syncthreads();
   if (warp == 0) {
-    for (int w = 1; w < kEntryWarps; ++w) list.offer(sh_s[w * 32 + lane], sh_id[w * 32 + lane], lane);
+    for (int w = 1; w < kEntryWarps; ++w)
+      list.offer_margin(sh_s[w * 32 + lane], sh_id[w * 32 + lane], lane, topk, 0.0f);
     blk_s[blockIdx.x * 32 + lane] = list.s;
     blk_id[blockIdx.x * 32 + lane] = list.id;
   }
@@ -774,7 +775,8 @@ __global__ void entry_threshold_kernel(const float* __restrict__ blk_s,
   const int lane = threadIdx.x;
   WarpList list;
   list.init();
-  for (int b = 0; b < nblk; ++b) list.offer(blk_s[b * 32 + lane], blk_id[b * 32 + lane], lane);
+  for (int b = 0; b < nblk; ++b)
+    list.offer_margin(blk_s[b * 32 + lane], blk_id[b * 32 + lane], lane, topk, 0.0f);
   const float kth = __shfl_sync(kFull, list.s, topk - 1);
   if (lane == 0) {
     *thr = isfinite(kth) ? kth - 2.0f * kMargin : -INFINITY;
@@ -800,10 +802,70 @@ __global__ void entry_collect_kernel(int* __restrict__ entry_best, const uint64_
   }
 }
 
-// Exact entry scores of the candidates: a warp per entry, a lane per row
-// (the reference's sequential fp64 dot each), max over the finite ones.
+// Exact entry scores of the candidates: a warp per entry.  The entry's rows
+// are staged in shared memory with coalesced loads, kRows at a time, and
+// lane j runs row j's sequential fp64 dot (the reference's order) from there;
+// the entry scores the max of its finite rows.
+template <typename T>
+struct RefineShape {
+  static constexpr int kRows = sizeof(T) == 2 ? 8 : 4;   // rows staged per warp
+  static constexpr int kMaxDim = 256;
+};
+
 template <typename T>
 __global__ void __launch_bounds__(kEntryWarps * 32) entry_refine_kernel(
+    const T* __restrict__ rows, const float* __restrict__ norms, int dim,
+    const float* __restrict__ query, const uint64_t* __restrict__ off,
+    const uint32_t* __restrict__ cand, const unsigned* __restrict__ count,
+    const uint32_t* __restrict__ allow, float* __restrict__ cand_s) {
+  constexpr int NR = RefineShape<T>::kRows;
+  constexpr int MD = RefineShape<T>::kMaxDim;
+  __shared__ float qs[MD];
+  __shared__ T rbuf[kEntryWarps][NR][MD];
+  __shared__ double qn;
+  for (int d = threadIdx.x; d < dim; d += blockDim.x) qs[d] = query[d];
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double acc = 0.0;
+#pragma unroll 8
+    for (int d = 0; d < dim; ++d) acc += (double)qs[d] * (double)qs[d];
+    qn = sqrt(acc);
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const unsigned n = *count;
+  for (unsigned i = blockIdx.x * kEntryWarps + warp; i < n; i += gridDim.x * kEntryWarps) {
+    const uint32_t e = cand[i];
+    float best = -INFINITY;
+    if (policy::row_allowed(allow, e)) {
+      for (uint64_t r0 = off[e]; r0 < off[e + 1]; r0 += NR) {
+        const int nr = (int)min((uint64_t)NR, off[e + 1] - r0);
+        for (int j = 0; j < nr; ++j)
+          for (int d = lane; d < dim; d += 32) rbuf[warp][j][d] = rows[(r0 + j) * dim + d];
+        __syncwarp();
+        if (lane < nr) {
+          const float nrm = __ldg(norms + r0 + lane);
+          if (isfinite(nrm)) {
+            double dot = 0.0;
+#pragma unroll 8
+            for (int d = 0; d < dim; ++d)
+              dot = fma((double)qs[d], (double)to_f(rbuf[warp][lane][d]), dot);
+            const float sc = (float)(dot / (qn * (double)nrm + 1.0e-8));
+            if (isfinite(sc)) best = fmaxf(best, sc);
+          }
+        }
+        __syncwarp();
+      }
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) best = fmaxf(best, __shfl_xor_sync(kFull, best, o));
+    if (lane == 0) cand_s[i] = best;  // -inf: no finite row (dropped)
+  }
+}
+
+// Banks wider than the staging buffer: a lane per row reading global memory.
+template <typename T>
+__global__ void __launch_bounds__(kEntryWarps * 32) entry_refine_wide_kernel(
     const T* __restrict__ rows, const float* __restrict__ norms, int dim,
     const float* __restrict__ query, const uint64_t* __restrict__ off,
     const uint32_t* __restrict__ cand, const unsigned* __restrict__ count,
@@ -826,7 +888,7 @@ __global__ void __launch_bounds__(kEntryWarps * 32) entry_refine_kernel(
     }
 #pragma unroll
     for (int o = 16; o >= 1; o >>= 1) best = fmaxf(best, __shfl_xor_sync(kFull, best, o));
-    if (lane == 0) cand_s[i] = best;  // -inf: no finite row (dropped)
+    if (lane == 0) cand_s[i] = best;
   }
 }
 
@@ -1794,7 +1856,7 @@ int launch_multi(grm_b200_mla_bank* b, const float* dq, int nq, int topk, Result
       else
         scan_multi_fn<T>(b->dim)<<<dim3(b->grid_x, 1), kThreads, 0, s>>>(p);
       entry_top_kernel<<<b->entry_blocks, kEntryWarps * 32, 0, s>>>(b->d_entry_best, b->entries,
-                                                                     b->d_blk_s, b->d_blk_id);
+                                                                     topk, b->d_blk_s, b->d_blk_id);
       entry_threshold_kernel<<<1, 32, 0, s>>>(b->d_blk_s, b->d_blk_id, b->entry_blocks, topk,
                                               b->d_thr, p.scratch.hdr(0));
     }
@@ -1803,9 +1865,14 @@ int launch_multi(grm_b200_mla_bank* b, const float* dq, int nq, int topk, Result
     entry_collect_kernel<<<cg, 256, 0, s>>>(b->d_entry_best, b->d_entry_off, b->entries, b->d_thr,
                                             b->d_unsafe, b->exact_only ? 1 : 0, b->d_cand,
                                             b->d_cand_count);
-    entry_refine_kernel<T><<<info.sms * 2, kEntryWarps * 32, 0, s>>>(
-        static_cast<const T*>(b->d_rows), b->d_norms, b->dim, qp, b->d_entry_off, b->d_cand,
-        b->d_cand_count, b->cur_allow, b->d_cand_s);
+    if (b->dim <= RefineShape<T>::kMaxDim)
+      entry_refine_kernel<T><<<info.sms * 2, kEntryWarps * 32, 0, s>>>(
+          static_cast<const T*>(b->d_rows), b->d_norms, b->dim, qp, b->d_entry_off, b->d_cand,
+          b->d_cand_count, b->cur_allow, b->d_cand_s);
+    else
+      entry_refine_wide_kernel<T><<<info.sms * 2, kEntryWarps * 32, 0, s>>>(
+          static_cast<const T*>(b->d_rows), b->d_norms, b->dim, qp, b->d_entry_off, b->d_cand,
+          b->d_cand_count, b->cur_allow, b->d_cand_s);
     entry_finalize_kernel<<<1, kEntryWarps * 32, 0, s>>>(
         b->d_cand, b->d_cand_s, b->d_cand_count, topk, id_offset, results + q,
         out_ids ? out_ids + (int64_t)q * topk : nullptr,
