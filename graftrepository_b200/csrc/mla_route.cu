@@ -117,6 +117,7 @@ struct Params {
   const uint32_t* entry_of_row;
   int* entry_best;        // [entries] ordered float, reset to -inf by the collect step
   int* multi_unsafe;      // [Q] the query is outside the approximate pass's safe range
+  double* multi_qnorm;    // the query's reference norm, for the entry refine
   // A single query may travel inside the launch parameters (queries == nullptr):
   // the synchronous host entry then needs no host-to-device copy.
   float qinline[kInlineMax];
@@ -720,8 +721,11 @@ __global__ void __launch_bounds__(kThreads) mla_scan_kernel(const __grid_constan
       g = g_begin + __shfl_sync(kFull, nxt, 0);
     }
   }
-  if constexpr (MULTI) {
-    if (blockIdx.x == 0 && threadIdx.x == 0) p.multi_unsafe[q] = safe ? 0 : 1;
+  if constexpr (MULTI) {  // block 0 streams early groups: its tail hides the norm's chain
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+      p.multi_unsafe[q] = safe ? 0 : 1;
+      *p.multi_qnorm = query_norm_seq(query, D);
+    }
     return;
   }
   // The resolve kernel may be scheduled as blocks leave the streaming loop;
@@ -750,11 +754,20 @@ __global__ void __launch_bounds__(kEntryWarps * 32) entry_top_kernel(
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   WarpList list;
   list.init();
+  // chunks of 32 entries, kPre loaded at once so their latencies overlap
+  constexpr int kPre = 8;
+  const int64_t step = (int64_t)gridDim.x * kEntryWarps * 32;
   for (int64_t e0 = ((int64_t)blockIdx.x * kEntryWarps + warp) * 32; e0 < entries;
-       e0 += (int64_t)gridDim.x * kEntryWarps * 32) {
-    const int64_t e = e0 + lane;
-    const float v = e < entries ? ordered_to_float(__ldcg(entry_best + e)) : -INFINITY;
-    list.offer_margin(v, (uint32_t)e, lane, topk, 0.0f);  // only the top k must be exact
+       e0 += kPre * step) {
+    float v[kPre];
+#pragma unroll
+    for (int j = 0; j < kPre; ++j) {
+      const int64_t e = e0 + j * step + lane;
+      v[j] = e < entries ? ordered_to_float(__ldcg(entry_best + e)) : -INFINITY;
+    }
+#pragma unroll
+    for (int j = 0; j < kPre; ++j)  // only the top k must be exact
+      list.offer_margin(v[j], (uint32_t)(e0 + j * step + lane), lane, topk, 0.0f);
   }
   sh_s[warp * 32 + lane] = list.s;
   sh_id[warp * 32 + lane] = list.id;
@@ -768,19 +781,33 @@ __global__ void __launch_bounds__(kEntryWarps * 32) entry_top_kernel(
 }
 
 // One warp: the k-th best over the block lists -> the candidate threshold.
-// The bulk pass's ticket counter is re-armed here for the next query.
-__global__ void entry_threshold_kernel(const float* __restrict__ blk_s,
-                                       const uint32_t* __restrict__ blk_id, int nblk, int topk,
-                                       float* __restrict__ thr, Header* hdr) {
-  const int lane = threadIdx.x;
+// The k-th best over the block lists -> the candidate threshold.  One block
+// of 32 warps: warp w merges lists w, w+32, ... (their loads overlap across
+// warps), then warp 0 merges the 32 warp lists from shared memory.  The bulk
+// pass's ticket counter is re-armed here for the next query.
+constexpr int kThrWarps = 32;
+
+__global__ void __launch_bounds__(kThrWarps * 32) entry_threshold_kernel(
+    const float* __restrict__ blk_s, const uint32_t* __restrict__ blk_id, int nblk, int topk,
+    float* __restrict__ thr, Header* hdr) {
+  __shared__ float sh_s[kThrWarps * 32];
+  __shared__ uint32_t sh_id[kThrWarps * 32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   WarpList list;
   list.init();
-  for (int b = 0; b < nblk; ++b)
+  for (int b = warp; b < nblk; b += kThrWarps)
     list.offer_margin(blk_s[b * 32 + lane], blk_id[b * 32 + lane], lane, topk, 0.0f);
-  const float kth = __shfl_sync(kFull, list.s, topk - 1);
-  if (lane == 0) {
-    *thr = isfinite(kth) ? kth - 2.0f * kMargin : -INFINITY;
-    hdr->next = 0;
+  sh_s[warp * 32 + lane] = list.s;
+  sh_id[warp * 32 + lane] = list.id;
+  __syncthreads();
+  if (warp == 0) {
+    for (int w = 1; w < kThrWarps; ++w)
+      list.offer_margin(sh_s[w * 32 + lane], sh_id[w * 32 + lane], lane, topk, 0.0f);
+    const float kth = __shfl_sync(kFull, list.s, topk - 1);
+    if (lane == 0) {
+      *thr = isfinite(kth) ? kth - 2.0f * kMargin : -INFINITY;
+      hdr->next = 0;
+    }
   }
 }
 
@@ -812,27 +839,37 @@ struct RefineShape {
   static constexpr int kMaxDim = 256;
 };
 
+// qnorm_in: the query's reference norm computed by an earlier kernel, or
+// nullptr (computed here).  Rows go to shared memory with 16-byte loads when
+// a row is a whole number of 16-byte chunks.
 template <typename T>
 __global__ void __launch_bounds__(kEntryWarps * 32) entry_refine_kernel(
     const T* __restrict__ rows, const float* __restrict__ norms, int dim,
     const float* __restrict__ query, const uint64_t* __restrict__ off,
     const uint32_t* __restrict__ cand, const unsigned* __restrict__ count,
-    const uint32_t* __restrict__ allow, float* __restrict__ cand_s) {
+    const uint32_t* __restrict__ allow, float* __restrict__ cand_s,
+    const double* __restrict__ qnorm_in) {
   constexpr int NR = RefineShape<T>::kRows;
   constexpr int MD = RefineShape<T>::kMaxDim;
+  constexpr int EV = 16 / (int)sizeof(T);  // elements per 16-byte chunk
   __shared__ float qs[MD];
-  __shared__ T rbuf[kEntryWarps][NR][MD];
+  __shared__ __align__(16) T rbuf[kEntryWarps][NR][MD];
   __shared__ double qn;
   for (int d = threadIdx.x; d < dim; d += blockDim.x) qs[d] = query[d];
   __syncthreads();
   if (threadIdx.x == 0) {
-    double acc = 0.0;
+    if (qnorm_in) {
+      qn = *qnorm_in;
+    } else {
+      double acc = 0.0;
 #pragma unroll 8
-    for (int d = 0; d < dim; ++d) acc += (double)qs[d] * (double)qs[d];
-    qn = sqrt(acc);
+      for (int d = 0; d < dim; ++d) acc += (double)qs[d] * (double)qs[d];
+      qn = sqrt(acc);
+    }
   }
   __syncthreads();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const bool vec = dim % EV == 0;
   const unsigned n = *count;
   for (unsigned i = blockIdx.x * kEntryWarps + warp; i < n; i += gridDim.x * kEntryWarps) {
     const uint32_t e = cand[i];
@@ -840,8 +877,19 @@ __global__ void __launch_bounds__(kEntryWarps * 32) entry_refine_kernel(
     if (policy::row_allowed(allow, e)) {
       for (uint64_t r0 = off[e]; r0 < off[e + 1]; r0 += NR) {
         const int nr = (int)min((uint64_t)NR, off[e + 1] - r0);
-        for (int j = 0; j < nr; ++j)
-          for (int d = lane; d < dim; d += 32) rbuf[warp][j][d] = rows[(r0 + j) * dim + d];
+        const T* src = rows + r0 * dim;  // nr consecutive rows
+        if (vec) {  // rbuf rows are MD elements apart, source rows dim apart
+          const int cpr = dim / EV;
+#pragma unroll 4
+          for (int x = lane; x < nr * cpr; x += 32) {
+            const int j = x / cpr, c = x - j * cpr;
+            *reinterpret_cast<uint4*>(&rbuf[warp][j][c * EV]) =
+                __ldg(reinterpret_cast<const uint4*>(src + (int64_t)j * dim) + c);
+          }
+        } else {
+#pragma unroll 8
+          for (int x = lane; x < nr * dim; x += 32) rbuf[warp][x / dim][x % dim] = src[x];
+        }
         __syncwarp();
         if (lane < nr) {
           const float nrm = __ldg(norms + r0 + lane);
@@ -1137,7 +1185,10 @@ __global__ void __launch_bounds__(kBulkWarps * 32, 1)
     }
   }
   if constexpr (MULTI) {  // the entry kernels reset hdr->next and read hdr->err
-    if (blockIdx.x == 0 && threadIdx.x == 0) p.multi_unsafe[q] = safe ? 0 : 1;
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+      p.multi_unsafe[q] = safe ? 0 : 1;
+      *p.multi_qnorm = query_norm_seq(query, D);
+    }
     return;
   }
   asm volatile("griddepcontrol.launch_dependents;");
@@ -1472,6 +1523,7 @@ struct grm_b200_mla_bank {
   float* d_blk_s = nullptr;            // [entry_blocks * 32]
   uint32_t* d_blk_id = nullptr;
   float* d_thr = nullptr;
+  double* d_qn = nullptr;              // the query's reference norm (entry refine)
   int* d_unsafe = nullptr;
   uint32_t* d_cand = nullptr;          // [entries]
   float* d_cand_s = nullptr;
@@ -1645,6 +1697,7 @@ Params<T> make_params(grm_b200_mla_bank* b, const float* dq, int topk) {
   p.entry_of_row = b->d_entry_of_row;
   p.entry_best = b->d_entry_best;
   p.multi_unsafe = b->d_unsafe;
+  p.multi_qnorm = b->d_qn;
   return p;
 }
 
@@ -1857,8 +1910,9 @@ int launch_multi(grm_b200_mla_bank* b, const float* dq, int nq, int topk, Result
         scan_multi_fn<T>(b->dim)<<<dim3(b->grid_x, 1), kThreads, 0, s>>>(p);
       entry_top_kernel<<<b->entry_blocks, kEntryWarps * 32, 0, s>>>(b->d_entry_best, b->entries,
                                                                      topk, b->d_blk_s, b->d_blk_id);
-      entry_threshold_kernel<<<1, 32, 0, s>>>(b->d_blk_s, b->d_blk_id, b->entry_blocks, topk,
-                                              b->d_thr, p.scratch.hdr(0));
+      entry_threshold_kernel<<<1, kThrWarps * 32, 0, s>>>(b->d_blk_s, b->d_blk_id,
+                                                          b->entry_blocks, topk, b->d_thr,
+                                                          p.scratch.hdr(0));
     }
     const int cg = (int)std::max<int64_t>(1, std::min<int64_t>((int64_t)info.sms * 4,
                                                                 ceil_div64(b->entries, 256)));
@@ -1868,7 +1922,7 @@ int launch_multi(grm_b200_mla_bank* b, const float* dq, int nq, int topk, Result
     if (b->dim <= RefineShape<T>::kMaxDim)
       entry_refine_kernel<T><<<info.sms * 2, kEntryWarps * 32, 0, s>>>(
           static_cast<const T*>(b->d_rows), b->d_norms, b->dim, qp, b->d_entry_off, b->d_cand,
-          b->d_cand_count, b->cur_allow, b->d_cand_s);
+          b->d_cand_count, b->cur_allow, b->d_cand_s, b->exact_only ? nullptr : b->d_qn);
     else
       entry_refine_wide_kernel<T><<<info.sms * 2, kEntryWarps * 32, 0, s>>>(
           static_cast<const T*>(b->d_rows), b->d_norms, b->dim, qp, b->d_entry_off, b->d_cand,
@@ -2020,7 +2074,7 @@ void bank_free(grm_b200_mla_bank* b) {
   grm_b200::policy::policy_free(b->pol);
   if (b->lex_stream) cudaStreamSynchronize(b->lex_stream);
   void* mptrs[] = {b->d_entry_off, b->d_entry_of_row, b->d_entry_best, b->d_blk_s, b->d_blk_id,
-                   b->d_thr, b->d_unsafe, b->d_cand, b->d_cand_s, b->d_cand_count};
+                   b->d_thr, b->d_qn, b->d_unsafe, b->d_cand, b->d_cand_s, b->d_cand_count};
   for (void* m : mptrs)
     if (m) cudaFree(m);
   if (b->ev_fork) cudaEventDestroy(b->ev_fork);
@@ -2122,6 +2176,7 @@ int make_multi(grm_b200_mla_bank* b, const uint64_t* off, int64_t entries) {
   alloc((void**)&b->d_blk_s, sizeof(float) * 32 * (size_t)b->entry_blocks);
   alloc((void**)&b->d_blk_id, sizeof(uint32_t) * 32 * (size_t)b->entry_blocks);
   alloc((void**)&b->d_thr, sizeof(float));
+  alloc((void**)&b->d_qn, sizeof(double));
   alloc((void**)&b->d_unsafe, sizeof(int) * 64);
   alloc((void**)&b->d_cand, sizeof(uint32_t) * (size_t)entries);
   alloc((void**)&b->d_cand_s, sizeof(float) * (size_t)entries);
@@ -2673,6 +2728,7 @@ extern "C" int grm_b200_mla_route_noalloc(const void* rows_device, int64_t nodes
   p.entry_of_row = nullptr;
   p.entry_best = nullptr;
   p.multi_unsafe = nullptr;
+  p.multi_qnorm = nullptr;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   scratch_init_kernel<<<(query_count + 127) / 128, 128, 0, s>>>(base + results_bytes, stride,
                                                                  query_count);
