@@ -13,7 +13,7 @@
 //
 // Operands.  The bank tile is loaded by TMA (2D tensor map, 128-byte swizzle,
 // box 64 elements x 128 rows, one box per 128-byte K atom) into a ring of
-// kBStages shared-memory stages.  The query matrix is built once per batch by
+// shared-memory stages (as many as fit).  The query matrix is built once per batch by
 // batch_prep_kernel: q' = q / |q| (fp64 norm), scaled by 2^8 (no fp16
 // subnormals) and rounded to fp16, written in the same K-major swizzled layout
 // and copied into shared memory with one bulk copy.
@@ -53,7 +53,7 @@ namespace mla {
 constexpr int kBQ = 64;                    // queries per launch
 constexpr int kBMq = 128;                  // MMA M: the kBQ queries, twice
 constexpr int kBM = 128;                   // bank rows per tile (MMA N)
-constexpr int kBStages = 4;                // shared-memory stages
+constexpr int kBSmemMax = 232448;          // dynamic shared memory a CTA may use (227 KB)
 constexpr int kBEpi = 8;                   // epilogue warps 0..7
 constexpr int kBThreads = 10 * 32;
 constexpr int kBProducerWarp = 8;
@@ -77,9 +77,14 @@ struct BLayout {
   static constexpr int kStage = SA * kAtomT;
   static constexpr int kQ = KA * kAtomQ;
   static constexpr int kMerge = kBQ * 4 * 32 * 8;      // end-of-scan list exchange
-  static constexpr int kSmem = 1024 + kQ + kBStages * kStage;  // + alignment slack
+  // As many stages as fit beside the query image (1 KB alignment slack, 1 KB
+  // for the static shared variables).  D = 256: 5 stages (2.5 tiles), 128: 6
+  // (6 tiles), 64: 13.
+  static constexpr int kStages = (kBSmemMax - 2048 - kQ) / kStage;
+  static constexpr int kSmem = 1024 + kQ + kStages * kStage;  // + alignment slack
   static_assert(D % 64 == 0 && D <= 256, "batched dims: 64, 128, 256");
-  static_assert(kMerge <= kBStages * kStage, "the list exchange reuses the stages");
+  static_assert(kStages >= 2 * SPT && kStages <= 16, "stage ring: two tiles at least");
+  static_assert(kMerge <= kStages * kStage, "the list exchange reuses the stages");
 };
 
 struct BatchParams {
@@ -281,7 +286,9 @@ __global__ void batch_rnorm_kernel(const float* norms, int64_t n, float* rnorms)
   }
 }
 
-template <int D>
+// C: per-thread list capacity (>= top-k; 8 serves top-k <= 4 with a quarter
+// of the insert cost of 16).
+template <int D, int C>
 __global__ void __launch_bounds__(kBThreads, 1)
     mla_batch_kernel(const __grid_constant__ BatchParams p) {
   using LY = BLayout<D>;
@@ -289,7 +296,7 @@ __global__ void __launch_bounds__(kBThreads, 1)
   unsigned char* const sm = bsm_raw + ((1024u - (smem_u32(bsm_raw) & 1023u)) & 1023u);
   unsigned char* const smQ = sm;
   unsigned char* const smT = sm + LY::kQ;
-  __shared__ __align__(8) uint64_t full[kBStages], empty[kBStages], tfull[2], tempty[2], bq_bar,
+  __shared__ __align__(8) uint64_t full[LY::kStages], empty[LY::kStages], tfull[2], tempty[2], bq_bar,
       mma_done;
   __shared__ uint32_t sh_tmem;
   __shared__ int sh_fail;
@@ -301,7 +308,7 @@ __global__ void __launch_bounds__(kBThreads, 1)
   // epilogue warps 0..7: tensor-memory lane quarter lq holds queries
   // 32*(lq & 1) + lane (quarters 2, 3: the second copy); the warp takes the
   // tile's bank rows 32*cq .. 32*cq + 31
-  constexpr int C = kBList;
+  static_assert(C == 8 || C == kBList, "list capacity");
   const bool epi = warp < kBEpi;
   const int lq = warp & 3;
   const int cq = (warp >> 2) * 2 + (lq >> 1);
@@ -310,7 +317,7 @@ __global__ void __launch_bounds__(kBThreads, 1)
   // The query image comes from batch_prep_kernel (programmatic dependent launch).
   asm volatile("griddepcontrol.wait;" ::: "memory");
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kBStages; ++s) {
+    for (int s = 0; s < LY::kStages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
@@ -355,7 +362,7 @@ __global__ void __launch_bounds__(kBThreads, 1)
             tma_load_2d(smT + st * LY::kStage + a * LY::kAtomT, &p.tmap, (sp * LY::SA + a) * 64,
                         y, &full[st], pol);
           ++issued;
-          if (++st == kBStages) {
+          if (++st == LY::kStages) {
             st = 0;
             ph ^= 1u;
           }
@@ -394,7 +401,7 @@ __global__ void __launch_bounds__(kBThreads, 1)
               umma_f16(d, qd, td, kBIdesc, (sp | a | kk) != 0 ? 1u : 0u);
             }
           umma_commit(&empty[st]);  // the stage is free once these MMAs completed
-          if (++st == kBStages) {
+          if (++st == LY::kStages) {
             st = 0;
             ph ^= 1u;
           }
@@ -451,12 +458,25 @@ __global__ void __launch_bounds__(kBThreads, 1)
       // hot path: scores and a bit per row that reaches the threshold (the
       // shuffles run in every lane; lanes past the batch have thr = +inf)
       float sc[32];
+#pragma unroll
+      for (int c = 0; c < 32; ++c) sc[c] = __uint_as_float(v[c]) * __shfl_sync(kFull, rn, c);
+      if (i == 0 && active) {
+        // The first tile finds an empty list: start the threshold at the k-th
+        // largest distinct score of this tile (k rows score at least that, so
+        // the k-th best is no lower), minus the margin, instead of letting
+        // every row through the insert path.
+        float vk = INFINITY;
+        for (int j = 0; j < p.topk; ++j) {
+          float mx = -INFINITY;
+#pragma unroll
+          for (int c = 0; c < 32; ++c) mx = sc[c] < vk ? fmaxf(mx, sc[c]) : mx;
+          vk = mx;
+        }
+        if (vk > -INFINITY) thr = fmaxf(thr, vk - m2);
+      }
       uint32_t mask = 0;
 #pragma unroll
-      for (int c = 0; c < 32; ++c) {
-        sc[c] = __uint_as_float(v[c]) * __shfl_sync(kFull, rn, c);
-        mask |= (sc[c] >= thr ? 1u : 0u) << c;
-      }
+      for (int c = 0; c < 32; ++c) mask |= (sc[c] >= thr ? 1u : 0u) << c;
       // rare path, rolled so the insert is inlined once
 #pragma unroll 1
       while (mask) {
@@ -491,7 +511,7 @@ __global__ void __launch_bounds__(kBThreads, 1)
   // Teardown: every bulk load issued has landed, every MMA has completed.
   if (warp == kBProducerWarp && lane == 0 && sh_fail) {
     for (unsigned k = sh_consumed; k < sh_issued; ++k)
-      mbar_wait(&full[k % kBStages], (k / kBStages) & 1u, kWaitLimit);
+      mbar_wait(&full[k % LY::kStages], (k / LY::kStages) & 1u, kWaitLimit);
   }
   __syncthreads();
   if (warp == kBMmaWarp) {

@@ -1784,9 +1784,13 @@ EncodeTiledFn encode_tiled() {
 
 template <int D>
 int batch_smem_attr() {
-  return cuda_status(cudaFuncSetAttribute(mla_batch_kernel<D>,
-                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          BLayout<D>::kSmem));
+  cudaError_t e = cudaFuncSetAttribute(mla_batch_kernel<D, 8>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       BLayout<D>::kSmem);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(mla_batch_kernel<D, kBList>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, BLayout<D>::kSmem);
+  return cuda_status(e);
 }
 
 // Enables the batched route for fp16 banks of dim 64/128/256 whose rows all
@@ -1860,7 +1864,8 @@ int launch_batch_chunk(grm_b200_mla_bank* b, const Params<__half>& p, int nq, cu
   const int grid = (int)std::min<int64_t>(b->grid_x, bp.tiles);
   cudaLaunchAttribute attr[1];
   cudaLaunchConfig_t cfg = pdl_config(dim3(grid), dim3(kBThreads), BLayout<D>::kSmem, s, attr);
-  e = cudaLaunchKernelEx(&cfg, mla_batch_kernel<D>, bp);
+  e = p.topk <= 4 ? cudaLaunchKernelEx(&cfg, mla_batch_kernel<D, 8>, bp)
+                  : cudaLaunchKernelEx(&cfg, mla_batch_kernel<D, kBList>, bp);
   if (e != cudaSuccess) return cuda_status(e);
   cfg = pdl_config(dim3(nq), dim3(kBMergeWarps * 32), 0, s, attr);
   e = cudaLaunchKernelEx(&cfg, mla_batch_merge_kernel<D>, p);
