@@ -719,13 +719,14 @@ __global__ void __launch_bounds__(1024) select_kernel(RouteParams p) {
       v = p.lo[n];
       if (!isfinite(v)) v = -INFINITY;
     }
-    list.offer(v, (uint32_t)n, lane);
+    list.offer_margin(v, (uint32_t)n, lane, p.topk, 0.0f);  // only the k-th is needed
   }
   sh_s[warp * 32 + lane] = list.s;
   sh_id[warp * 32 + lane] = list.id;
   __syncthreads();
   if (warp == 0) {
-    for (int w = 1; w < 32; ++w) list.offer(sh_s[w * 32 + lane], sh_id[w * 32 + lane], lane);
+    for (int w = 1; w < 32; ++w)
+      list.offer_margin(sh_s[w * 32 + lane], sh_id[w * 32 + lane], lane, p.topk, 0.0f);
     const float L = __shfl_sync(kFull, list.s, p.topk - 1);
     if (lane == 0) sh_L = L;
   }
@@ -1068,12 +1069,16 @@ __global__ void query_info_kernel(RouteParams p) {
 }
 
 constexpr int kRefineSmemMax = 96 * 1024;
+constexpr int kRefineSmemCopy = 16 * 1024;  // largest query staged in shared memory
 
 template <typename KT>
 void launch_refine(grm_b200_gqa_bank* b, const RouteParams& p) {
   dim3 grid(std::max(1, b->sms), kRefineY);
   const size_t qbytes = sizeof(float) * (size_t)p.heads * p.qt * p.dim;
-  if (qbytes <= (size_t)kRefineSmemMax) {
+  // A block takes about one 32-token chunk per kv head of a candidate, so
+  // copying a large query into shared memory costs more than it saves: large
+  // queries are read through L1 instead.
+  if (qbytes <= (size_t)kRefineSmemCopy) {
     static bool attr_set[64] = {};
     if (!attr_set[b->device]) {
       cudaFuncSetAttribute(refine_kernel<KT, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
