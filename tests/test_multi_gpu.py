@@ -75,7 +75,7 @@ def test_sharded_routes_equal_single_gpu_oracle():
     import torch.multiprocessing as mp
 
     world = min(_ngpu(), 4)
-    mgr = mp.Manager()
+    mgr = mp.get_context("spawn").Manager()
     out = mgr.dict()
     mp.spawn(_worker, args=(world, _port(), out), nprocs=world, join=True)
     rows = synth.mla_bank(51, 300_001)

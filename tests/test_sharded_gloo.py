@@ -72,7 +72,7 @@ def _mla_worker(rank, world, port, out):
 
 def test_sharded_mla_merge_equals_global_route():
     world = 2
-    mgr = mp.Manager()
+    mgr = mp.get_context("spawn").Manager()
     out = mgr.dict()
     mp.spawn(_mla_worker, args=(world, _port(), out), nprocs=world, join=True)
     rows = synth.mla_bank(21, 3001).astype(np.float32)
@@ -109,7 +109,7 @@ def _gqa_worker(rank, world, port, out):
 
 def test_sharded_gqa_token_balanced_merge():
     world = 2
-    mgr = mp.Manager()
+    mgr = mp.get_context("spawn").Manager()
     out = mgr.dict()
     mp.spawn(_gqa_worker, args=(world, _port(), out), nprocs=world, join=True)
     lengths = synth.gqa_lengths(5, 60, "lognormal") // 8 + 1
@@ -150,7 +150,7 @@ def _dead_rank_worker(rank, world, port, out):
 
 def test_dead_rank_surfaces_as_error_not_hang():
     world = 2
-    mgr = mp.Manager()
+    mgr = mp.get_context("spawn").Manager()
     out = mgr.dict()
     ctx = mp.spawn(_dead_rank_worker, args=(world, _port(), out), nprocs=world, join=False)
     for p in ctx.processes:
