@@ -572,14 +572,24 @@ template <int D>
 __global__ void __launch_bounds__(kBMergeWarps * 32)
     mla_batch_merge_kernel(const __grid_constant__ Params<__half> p) {
   __shared__ FinishSmem<kBMergeWarps, D> fsm;
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-  asm volatile("griddepcontrol.launch_dependents;");
   const int q = blockIdx.x;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  // The query side before the wait on the scan: the queries were written
+  // before batch_prep_kernel ran, and this grid starts only after every
+  // block of the scan passed its own wait on that kernel.  The last warp's
+  // reference query norm (a serial fp64 chain) overlaps the scan's tail.
   const float* query = p.queries + (int64_t)q * D;
-  for (int d = threadIdx.x; d < D; d += blockDim.x) fsm.qraw[d] = query[d];
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    const float v = query[d];
+    fsm.qraw[d] = v;
+    fsm.qd[d] = (double)v;
+  }
+  __syncthreads();
+  if (warp == kBMergeWarps - 1 && lane == 0) fsm.qn = query_norm_seq_t<D>(fsm.qraw);
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;");
   const bool safe = __ldcg(&p.scratch.hdr(q)->qsafe) != 0;
-  final_merge<D, __half, false, kBMergeWarps>(p, q, kBMargin, safe, lane, warp, fsm);
+  final_merge<D, __half, false, kBMergeWarps, true>(p, q, kBMargin, safe, lane, warp, fsm);
 }
 
 }  // namespace mla

@@ -359,8 +359,9 @@ constexpr int kSelR = 4;  // candidates per lane in the final selection (128 per
 // T_k by k rounds of warp arg-max, and recomputes every entry >= T_k -
 // 2*margin with the reference arithmetic.  When 32 or more entries, or a
 // block's dropped rows (hdr->floor), reach that threshold, the exact
-// fallback kernel is flagged instead.
-template <int D, typename T, bool INL, int NW>
+// fallback kernel is flagged instead.  QREADY: the caller already filled
+// sm.qd and sm.qn (warp NW-1 then only waits at the barriers).
+template <int D, typename T, bool INL, int NW, bool QREADY = false>
 __device__ __forceinline__ void final_merge(const Params<T>& p, int q, float margin, bool safe,
                                             int lane, int warp, FinishSmem<NW, D>& sm) {
   static_assert(NW >= 2, "final_merge needs two warps");
@@ -374,8 +375,10 @@ __device__ __forceinline__ void final_merge(const Params<T>& p, int q, float mar
   const bool failed = __ldcg(&hdr->err) != 0;
   const uint2* ents = reinterpret_cast<const uint2*>(p.scratch.entries(q));
   if (warp == NW - 1) {
-    for (int d = lane; d < D; d += 32) sm.qd[d] = (double)sm.qraw[d];
-    if (lane == 0) sm.qn = query_norm_seq_t<D>(sm.qraw);
+    if constexpr (!QREADY) {
+      for (int d = lane; d < D; d += 32) sm.qd[d] = (double)sm.qraw[d];
+      if (lane == 0) sm.qn = query_norm_seq_t<D>(sm.qraw);
+    }
   } else {
 #pragma unroll 2
     for (int i = threadIdx.x; i < nent; i += (NW - 1) * 32) {
