@@ -1223,6 +1223,8 @@ int route_device_queries(grm_b200_gqa_bank* b, const float* dq, int qc, int head
     int rc = route_one(b, dq + i * qsize, heads, qt, topk);
     if (rc) return rc;
     e = cudaMemcpyAsync(b->h_result, b->d_result, sizeof(Result), cudaMemcpyDeviceToHost, b->stream);
+    // the end event goes in before the last wait, so timing costs no extra round trip
+    if (e == cudaSuccess && i == qc - 1) e = cudaEventRecord(b->ev1, b->stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(b->stream);
     if (e != cudaSuccess) return b->err.set(cuda_status(e), "GQA route failed: %s", cudaGetErrorString(e));
     if (b->h_result->count < 0)
@@ -1232,7 +1234,6 @@ int route_device_queries(grm_b200_gqa_bank* b, const float* dq, int qc, int head
       if (out_scores) out_scores[(int64_t)i * topk + j] = b->h_result->scores[j];
     }
   }
-  cudaEventRecord(b->ev1, b->stream);
   e = cudaEventSynchronize(b->ev1);
   float ms = 0.0f;
   if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, b->ev0, b->ev1);
@@ -1559,6 +1560,7 @@ int grm_b200_gqa_route_policy(grm_b200_gqa_bank* bank, const float* queries_host
       return rc;  // leaves hits zero for the next query
     e = cudaMemcpyAsync(bank->h_result, bank->d_result, sizeof(Result), cudaMemcpyDeviceToHost,
                         bank->stream);
+    if (e == cudaSuccess && q == query_count - 1) e = cudaEventRecord(bank->ev1, bank->stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(bank->stream);
     if (e != cudaSuccess) return bank->err.set(cuda_status(e), "GQA policy route failed: %s", cudaGetErrorString(e));
     if (bank->h_result->count < 0)
@@ -1568,7 +1570,6 @@ int grm_b200_gqa_route_policy(grm_b200_gqa_bank* bank, const float* queries_host
       if (out_scores_host) out_scores_host[(int64_t)q * topk + j] = bank->h_result->scores[j];
     }
   }
-  cudaEventRecord(bank->ev1, bank->stream);
   e = cudaEventSynchronize(bank->ev1);
   float ms = 0.0f;
   if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, bank->ev0, bank->ev1);

@@ -1896,8 +1896,11 @@ int launch_batch(grm_b200_mla_bank* b, const Params<__half>& p0, int nq, cudaStr
 // device memory (dq), or one host query carried inline in the launch
 // parameters (dq == nullptr, q_host != nullptr).  Results are written by the
 // kernels straight into mapped pinned host memory (no copy-back call).
+// `done` (optional) is recorded after the chunk's last launch, before the
+// host waits, so the caller's elapsed time needs no second round trip.
 template <typename T>
-int run_chunk(grm_b200_mla_bank* b, const float* dq, const float* q_host, int nq, int topk);
+int run_chunk(grm_b200_mla_bank* b, const float* dq, const float* q_host, int nq, int topk,
+              cudaEvent_t done);
 
 // Multi-row bank, stream-ordered: per query the folding scan, the entry
 // threshold and candidates, their exact scores and the top-k into
@@ -1946,10 +1949,12 @@ int launch_multi(grm_b200_mla_bank* b, const float* dq, int nq, int topk, Result
 }
 
 template <typename T>
-int run_chunk(grm_b200_mla_bank* b, const float* dq, const float* q_host, int nq, int topk) {
+int run_chunk(grm_b200_mla_bank* b, const float* dq, const float* q_host, int nq, int topk,
+              cudaEvent_t done) {
   if (b->multi) {
     int rc = launch_multi<T>(b, dq, nq, topk, b->d_results_mapped, b->stream);
     if (rc) return b->err.set(rc, "MLA multi-row route launch failed");
+    if (done) cudaEventRecord(done, b->stream);
     cudaError_t e = cudaStreamSynchronize(b->stream);
     if (e != cudaSuccess) return b->err.set(cuda_status(e), "MLA multi-row route failed: %s", cudaGetErrorString(e));
     for (int i = 0; i < nq; ++i)
@@ -1972,6 +1977,7 @@ int run_chunk(grm_b200_mla_bank* b, const float* dq, const float* q_host, int nq
   if (rc) return b->err.set(rc, "MLA scan launch failed: %s", cudaGetErrorString(cudaGetLastError()));
   bool need_exact = b->exact_only;
   if (!b->exact_only) {
+    if (done) cudaEventRecord(done, b->stream);
     cudaError_t e = cudaStreamSynchronize(b->stream);
     if (e != cudaSuccess) return b->err.set(cuda_status(e), "MLA route failed: %s", cudaGetErrorString(e));
     for (int i = 0; i < nq; ++i) {
@@ -1985,6 +1991,7 @@ int run_chunk(grm_b200_mla_bank* b, const float* dq, const float* q_host, int nq
   if (need_exact) {
     rc = launch_exact<T>(b, p, nq, b->stream);
     if (rc) return b->err.set(rc, "MLA exact pass launch failed");
+    if (done) cudaEventRecord(done, b->stream);
     cudaError_t e = cudaStreamSynchronize(b->stream);
     if (e != cudaSuccess) return b->err.set(cuda_status(e), "MLA exact pass failed: %s", cudaGetErrorString(e));
   }
@@ -2002,10 +2009,10 @@ int route_device_queries(grm_b200_mla_bank* b, const float* dq, int query_count,
   if (e != cudaSuccess) return b->err.set(cuda_status(e), "cudaSetDevice failed");
   int rc = reserve(b, query_count);
   if (rc) return rc;
-  auto chunk = [&](int q0, int nq) -> int {
+  auto chunk = [&](int q0, int nq, cudaEvent_t done) -> int {
     const float* qd = dq ? dq + (int64_t)q0 * b->dim : nullptr;
-    rc = (b->dtype == GRM_B200_F16) ? run_chunk<__half>(b, qd, q_host, nq, topk)
-                                    : run_chunk<float>(b, qd, q_host, nq, topk);
+    rc = (b->dtype == GRM_B200_F16) ? run_chunk<__half>(b, qd, q_host, nq, topk, done)
+                                    : run_chunk<float>(b, qd, q_host, nq, topk, done);
     if (rc) return rc;
     for (int i = 0; i < nq; ++i) {
       const Result& r = b->h_results[i];
@@ -2016,11 +2023,10 @@ int route_device_queries(grm_b200_mla_bank* b, const float* dq, int query_count,
     }
     return 0;
   };
-  if (warmup > 0 && (rc = chunk(0, warmup))) return rc;
+  if (warmup > 0 && (rc = chunk(0, warmup, nullptr))) return rc;
   cudaEventRecord(b->ev0, b->stream);
-  if ((rc = chunk(warmup, query_count - warmup))) return rc;
-  cudaEventRecord(b->ev1, b->stream);
-  e = cudaEventSynchronize(b->ev1);
+  if ((rc = chunk(warmup, query_count - warmup, b->ev1))) return rc;
+  e = cudaEventSynchronize(b->ev1);  // recorded before the chunk's last wait: already done
   float ms = 0.0f;
   if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, b->ev0, b->ev1);
   if (e != cudaSuccess) return b->err.set(cuda_status(e), "MLA route timing failed");

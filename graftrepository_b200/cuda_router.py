@@ -63,7 +63,7 @@ def _receipt(route_walls, device_times, measured, repeats) -> CudaRouteReceipt:
         device_route_ms_per_query=device_times[-1] / measured,
         route_wall_ms=route_walls[-1],
         route_wall_ms_first=route_walls[0],
-        route_wall_ms_min=float(np.min(route_walls)),
+        route_wall_ms_min=float(min(route_walls)),
         route_wall_ms_runs=tuple(route_walls),
         device_route_ms_runs=tuple(device_times),
         measured_queries=measured,
@@ -266,7 +266,7 @@ class CudaMLARouteBank:
         return out, scores, float(elapsed.value), wall
 
     def _finish(self, rows, scores, walls, devs, count, warmup, repeats):
-        if np.any(rows >= self.node_ids.shape[0]):
+        if rows.size and int(rows.max()) >= self.node_ids.shape[0]:
             raise RuntimeError("CUDA MLA route returned an out-of-range row ID")
         self.last_scores = scores
         mapped = self.node_ids[rows]
@@ -569,7 +569,7 @@ class CudaGQARouteBank:
         return out, scores, float(elapsed.value), wall
 
     def _finish(self, rows, scores, walls, devs, count, warmup, repeats):
-        if np.any(rows >= self.node_ids.shape[0]):
+        if rows.size and int(rows.max()) >= self.node_ids.shape[0]:
             raise RuntimeError("CUDA GQA route returned an out-of-range row ID")
         self.last_scores = scores
         return self.node_ids[rows], _receipt(walls, devs, max(1, int(count) - int(warmup)),
