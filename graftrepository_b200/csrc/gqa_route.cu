@@ -220,6 +220,8 @@ __host__ __device__ constexpr int chunk_dim(int c, int w) { return (w / 2) * 64 
 // <-> dim chunk_dim(c, s / 2) + 4 * (s % 2) + j.
 template <typename KT, int D, int NT>
 __global__ void __launch_bounds__(128) query_prep_kernel(RouteParams p) {
+  // the scan is launched chained to this kernel and waits for all of it
+  asm volatile("griddepcontrol.launch_dependents;");
   constexpr int KSTEPS = D / 16;
   constexpr int NVP = NT * 4;  // padded vector count: hi cols [0, NVP), lo cols [NVP, 2 NVP)
   const int kh = blockIdx.x;
@@ -303,6 +305,9 @@ __global__ void __launch_bounds__(kThreads) gqa_scan_kernel(RouteParams p) {
   constexpr int W = D / 32;         // 16-byte loads per key row per thread (D/4 dims)
   constexpr int NVP = NT * 4;
   const int lane = threadIdx.x & 31;
+  // Chained launch after query_prep_kernel, whose outputs are read below.  No
+  // early trigger: node_bounds_kernel is scheduled as the scan's CTAs exit.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   if (!p.qinfo->fast_ok) return;
   const int g = lane >> 2, c = lane & 3;
   const int64_t wid = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -466,6 +471,9 @@ __global__ void __launch_bounds__(kTmaWarps * 32, 1)
   unsigned char* const gsm = gsm_raw + ((1024u - (smem_u32(gsm_raw) & 1023u)) & 1023u);
   __shared__ __align__(8) uint64_t bar[kTmaWarps][2];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  // Chained launch after query_prep_kernel, whose outputs are read below.  No
+  // early trigger: node_bounds_kernel is scheduled as the scan's CTAs exit.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   if (!p.qinfo->fast_ok) return;
   const int g = lane >> 2, c = lane & 3;
   if (lane == 0) {
@@ -652,6 +660,11 @@ __global__ void __launch_bounds__(kTmaWarps * 32, 1)
 
 // Per node: approximate score interval [lo, hi]; resets headmax.  One warp per node.
 __global__ void node_bounds_kernel(RouteParams p, float eps_abs) {
+  // Programmatic dependent launch: wait for the previous kernel's grid (a
+  // no-op for a plain launch) before touching memory, then let the next one
+  // be scheduled.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;");
   const int lane = threadIdx.x & 31;
   const int64_t wid = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
@@ -709,6 +722,8 @@ __global__ void __launch_bounds__(1024) select_kernel(RouteParams p) {
   __shared__ float sh_s[32 * 32];
   __shared__ uint32_t sh_id[32 * 32];
   __shared__ float sh_L;
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // chained launch, as node_bounds_kernel
+  asm volatile("griddepcontrol.launch_dependents;");
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   WarpList list;
   list.init();
@@ -759,6 +774,8 @@ __global__ void __launch_bounds__(1024) select_kernel(RouteParams p) {
 template <typename KT, bool SMEM>
 __global__ void __launch_bounds__(256) refine_kernel(RouteParams p) {
   extern __shared__ float sh_query[];
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // chained launch, as node_bounds_kernel
+  asm volatile("griddepcontrol.launch_dependents;");
   const int count = *p.cand_count;
   if ((int)blockIdx.y >= count) return;
   const int qvals = p.heads * p.qt * p.dim;
@@ -840,6 +857,8 @@ __global__ void __launch_bounds__(256) refine_kernel(RouteParams p) {
 // pass and the maximum over the candidates (which contain the top raw) sets
 // the norm.
 __global__ void finalize_kernel(RouteParams p) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // chained launch, as node_bounds_kernel
+  asm volatile("griddepcontrol.launch_dependents;");
   const int lane = threadIdx.x;
   const int count = *p.cand_count;
   WarpList list;
@@ -965,15 +984,33 @@ bool fast_bank(const grm_b200_gqa_bank* b) {
 
 int nt_for(int nv) { return nv <= 4 ? 1 : (nv <= 8 ? 2 : (nv <= 16 ? 4 : 0)); }
 
+// Launch chained to the previous kernel of the stream (programmatic stream
+// serialization); the kernel waits on that grid with griddepcontrol.wait.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_chained(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                           cudaStream_t s, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 template <typename KT, int D, int NT>
 void launch_fast(grm_b200_gqa_bank* b, const RouteParams& p) {
   query_prep_kernel<KT, D, NT><<<b->kh_n, 128, 0, b->stream>>>(p);
   if (b->n_items <= 0) return;
   if (b->tma)
-    gqa_scan_tma_kernel<KT, D, NT>
-        <<<b->grid_tma, kTmaWarps * 32, TmaLayout<D>::kSmem, b->stream>>>(b->tmap, p);
+    launch_chained(gqa_scan_tma_kernel<KT, D, NT>, dim3(b->grid_tma), dim3(kTmaWarps * 32),
+                   (size_t)TmaLayout<D>::kSmem, b->stream, b->tmap, p);
   else
-    gqa_scan_kernel<KT, D, NT><<<b->grid_scan, kThreads, 0, b->stream>>>(p);
+    launch_chained(gqa_scan_kernel<KT, D, NT>, dim3(b->grid_scan), dim3(kThreads), 0, b->stream, p);
 }
 
 template <typename KT, int D>
@@ -1072,7 +1109,7 @@ constexpr int kRefineSmemMax = 96 * 1024;
 constexpr int kRefineSmemCopy = 16 * 1024;  // largest query staged in shared memory
 
 template <typename KT>
-void launch_refine(grm_b200_gqa_bank* b, const RouteParams& p) {
+cudaError_t launch_refine(grm_b200_gqa_bank* b, const RouteParams& p) {
   dim3 grid(std::max(1, b->sms), kRefineY);
   const size_t qbytes = sizeof(float) * (size_t)p.heads * p.qt * p.dim;
   // A block takes about one 32-token chunk per kv head of a candidate, so
@@ -1085,10 +1122,9 @@ void launch_refine(grm_b200_gqa_bank* b, const RouteParams& p) {
                            kRefineSmemMax);
       attr_set[b->device] = true;
     }
-    refine_kernel<KT, true><<<grid, 256, qbytes, b->stream>>>(p);
-  } else {
-    refine_kernel<KT, false><<<grid, 256, 0, b->stream>>>(p);
+    return launch_chained(refine_kernel<KT, true>, grid, dim3(256), qbytes, b->stream, p);
   }
+  return launch_chained(refine_kernel<KT, false>, grid, dim3(256), 0, b->stream, p);
 }
 
 int ensure_heads(grm_b200_gqa_bank* b, int heads, int nt) {
@@ -1194,16 +1230,20 @@ int route_one(grm_b200_gqa_bank* b, const float* dq, int heads, int qt, int topk
   // eps_abs: absolute query-representation error of an f16 split (subnormal lo parts)
   const float eps_abs = (b->dtype == GRM_B200_F16) ? 2.0e-7f * std::sqrt((float)b->dim) : 1.0e-30f;
   const int nb_grid = (int)std::min<int64_t>(ceil_div64(b->nodes, kWarps), (int64_t)b->sms * 8);
-  node_bounds_kernel<<<nb_grid, kThreads, 0, b->stream>>>(p, eps_abs);
-  select_kernel<<<1, 1024, 0, b->stream>>>(p);
-  switch (b->dtype) {
-    case GRM_B200_BF16: launch_refine<__nv_bfloat16>(b, p); break;
-    case GRM_B200_F16: launch_refine<__half>(b, p); break;
-    default: launch_refine<float>(b, p); break;
+  cudaError_t le =
+      launch_chained(node_bounds_kernel, dim3(nb_grid), dim3(kThreads), 0, b->stream, p, eps_abs);
+  if (le == cudaSuccess) le = launch_chained(select_kernel, dim3(1), dim3(1024), 0, b->stream, p);
+  if (le == cudaSuccess) {
+    switch (b->dtype) {
+      case GRM_B200_BF16: le = launch_refine<__nv_bfloat16>(b, p); break;
+      case GRM_B200_F16: le = launch_refine<__half>(b, p); break;
+      default: le = launch_refine<float>(b, p); break;
+    }
   }
-  finalize_kernel<<<1, 32, 0, b->stream>>>(p);
-  rc = cuda_status(cudaGetLastError());
-  if (rc) return b->err.set(rc, "GQA route launch failed: %s", cudaGetErrorString(cudaGetLastError()));
+  if (le == cudaSuccess) le = launch_chained(finalize_kernel, dim3(1), dim3(32), 0, b->stream, p);
+  if (le == cudaSuccess) le = cudaGetLastError();
+  rc = cuda_status(le);
+  if (rc) return b->err.set(rc, "GQA route launch failed: %s", cudaGetErrorString(le));
   return 0;
 }
 
