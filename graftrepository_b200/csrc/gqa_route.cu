@@ -46,7 +46,7 @@ constexpr int kWarps = kThreads / 32;
 constexpr int kChunk = 128;      // key tokens per work item
 constexpr float kEps = 2.44140625e-4f;  // 2^-12 relative to |q||k|: >= 5x the proven bound
 constexpr float kHuge = 1.0e30f;
-constexpr int kRefineY = 32;     // candidates refined concurrently
+constexpr int kRefineChunk = 256;  // candidates per unit scan (the refine's block size)
 
 struct Result {
   int count;
@@ -761,9 +761,11 @@ __global__ void __launch_bounds__(1024) select_kernel(RouteParams p) {
   }
 }
 
-// Exact refine: grid.y strides candidates; grid.x x threads stride warp-aligned
-// units (kv head, key token): a warp always works on 32 tokens of one kv head
-// (tokens padded to a multiple of 32 per head).  Each thread reads its key row
+// Exact refine: one wave of blocks shares the warp units of all candidates,
+// a unit being 32 tokens of one kv head of one candidate (tokens padded to a
+// multiple of 32 per head).  Candidates go in chunks of 256: the block scans
+// their unit counts in shared memory and each warp strides the flattened
+// units, finding its candidate by binary search.  Each thread reads its key row
 // once with 16-byte loads and computes the dots of every query vector of that
 // kv head (the reference's sequential fp32 arithmetic, products and sums
 // rounded separately), four vectors at a time; the query sits in shared memory
@@ -776,8 +778,9 @@ __global__ void __launch_bounds__(256) refine_kernel(RouteParams p) {
   extern __shared__ float sh_query[];
   asm volatile("griddepcontrol.wait;" ::: "memory");  // chained launch, as node_bounds_kernel
   asm volatile("griddepcontrol.launch_dependents;");
+  __shared__ int64_t s_pref[kRefineChunk + 1];  // units before candidate i of the chunk
   const int count = *p.cand_count;
-  if ((int)blockIdx.y >= count) return;
+  if (count == 0) return;
   const int qvals = p.heads * p.qt * p.dim;
   if constexpr (SMEM) {
     for (int i = threadIdx.x; i < qvals; i += blockDim.x) sh_query[i] = p.query[i];
@@ -789,19 +792,47 @@ __global__ void __launch_bounds__(256) refine_kernel(RouteParams p) {
   const int lane = threadIdx.x & 31;
   const int nvec = p.group * p.qt;               // query vectors per kv head
   const int dim = p.dim;
-  for (int ci = blockIdx.y; ci < count; ci += gridDim.y) {
-    const int64_t node = p.cand[ci];
-    const int64_t T = (int64_t)(p.off[node + 1] - p.off[node]);
-    if (T == 0 || p.key_bad[node] || !p.qinfo->finite) continue;
-    const int64_t Tp = (T + 31) & ~(int64_t)31;
-    const KT* base = keys + (int64_t)p.off[node] * p.kh_n * dim;
-    unsigned* best_out = p.headmax + (int64_t)ci * p.heads;
-    const int64_t units = (int64_t)p.kh_n * Tp;
-    for (int64_t u0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) & ~(int64_t)31; u0 < units;
-         u0 += (int64_t)gridDim.x * blockDim.x) {
-      const int kh = (int)(u0 / Tp);
-      const int64_t t = u0 - (int64_t)kh * Tp + lane;
+  // 16-byte query loads when every query vector starts on a 16-byte boundary
+  const bool qvec = dim % 4 == 0 && (reinterpret_cast<uintptr_t>(qbase) & 15) == 0;
+  const bool qfinite = p.qinfo->finite != 0;
+  const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int c0 = 0; c0 < count; c0 += kRefineChunk) {
+    const int cn = min(kRefineChunk, count - c0);
+    int64_t my_units = 0;
+    if ((int)threadIdx.x < cn) {
+      const int64_t node = p.cand[c0 + threadIdx.x];
+      const int64_t T = (int64_t)(p.off[node + 1] - p.off[node]);
+      if (T > 0 && !p.key_bad[node] && qfinite) my_units = (int64_t)p.kh_n * ((T + 31) >> 5);
+    }
+    if (threadIdx.x == 0) s_pref[0] = 0;
+    s_pref[threadIdx.x + 1] = my_units;
+    __syncthreads();
+#pragma unroll 1
+    for (int o = 1; o < kRefineChunk; o <<= 1) {  // inclusive scan of s_pref[1..256]
+      const int64_t v = (int)threadIdx.x >= o ? s_pref[threadIdx.x + 1 - o] : 0;
+      __syncthreads();
+      s_pref[threadIdx.x + 1] += v;
+      __syncthreads();
+    }
+    const int64_t total = s_pref[cn];
+    for (int64_t w = gw; w < total; w += nw) {
+      int lo = 0, hi = cn - 1;  // the last candidate whose units start at or before w
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (s_pref[mid] <= w) lo = mid;
+        else hi = mid - 1;
+      }
+      const int ci = c0 + lo;
+      const int64_t node = p.cand[ci];
+      const int64_t T = (int64_t)(p.off[node + 1] - p.off[node]);
+      const int64_t tiles = (T + 31) >> 5;  // 32-token units per kv head
+      const int64_t local = w - s_pref[lo];
+      const int kh = (int)(local / tiles);
+      const int64_t t = (local - (int64_t)kh * tiles) * 32 + lane;
       const bool live = t < T;
+      const KT* base = keys + (int64_t)p.off[node] * p.kh_n * dim;
+      unsigned* best_out = p.headmax + (int64_t)ci * p.heads;
       const KT* k = base + ((int64_t)kh * T + (live ? t : 0)) * dim;
       for (int v0 = 0; v0 < nvec; v0 += 4) {
         float dot[4] = {0.0f, 0.0f, 0.0f, 0.0f};
@@ -812,17 +843,43 @@ __global__ void __launch_bounds__(256) refine_kernel(RouteParams p) {
           const int h = kh * p.group + vi / p.qt, qi = vi % p.qt;
           qv[j] = qbase + ((int64_t)h * p.qt + qi) * dim;
         }
-        for (int d0 = 0; d0 < dim; d0 += E) {
-          const uint4 raw = *reinterpret_cast<const uint4*>(k + d0);
+        // dims d..d+E-1 of the four dots, in the reference's order
+        auto dots_of = [&](const uint4& raw, int d) {
           const KT* kk = reinterpret_cast<const KT*>(&raw);
+          if (qvec) {
 #pragma unroll
-          for (int e = 0; e < E; ++e) {
-            const float kvf = key_to_f(kk[e]);
+            for (int e4 = 0; e4 < E; e4 += 4) {
+              float4 q4[4];
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
-              dot[j] = __fadd_rn(dot[j], __fmul_rn(qv[j][d0 + e], kvf));
+              for (int j = 0; j < 4; ++j) q4[j] = *reinterpret_cast<const float4*>(qv[j] + d + e4);
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float kvf = key_to_f(kk[e4 + e]);
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                  dot[j] = __fadd_rn(dot[j], __fmul_rn((&q4[j].x)[e], kvf));
+              }
+            }
+          } else {
+#pragma unroll
+            for (int e = 0; e < E; ++e) {
+              const float kvf = key_to_f(kk[e]);
+#pragma unroll
+              for (int j = 0; j < 4; ++j)
+                dot[j] = __fadd_rn(dot[j], __fmul_rn(qv[j][d + e], kvf));
+            }
           }
+        };
+        // four 16-byte row loads in flight per thread
+        int d0 = 0;
+        for (; d0 + 4 * E <= dim; d0 += 4 * E) {
+          uint4 r[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) r[u] = *reinterpret_cast<const uint4*>(k + d0 + u * E);
+#pragma unroll
+          for (int u = 0; u < 4; ++u) dots_of(r[u], d0 + u * E);
         }
+        for (; d0 < dim; d0 += E) dots_of(*reinterpret_cast<const uint4*>(k + d0), d0);
         if (p.qt4) {
           // vectors v0..v0+3 are the four query tokens of one head
           const float rb = std_max(std_max(fabsf(dot[0]), fabsf(dot[1])),
@@ -847,6 +904,7 @@ __global__ void __launch_bounds__(256) refine_kernel(RouteParams p) {
         }
       }
     }
+    __syncthreads();  // s_pref is rewritten for the next chunk
   }
 }
 
@@ -1110,7 +1168,18 @@ constexpr int kRefineSmemCopy = 16 * 1024;  // largest query staged in shared me
 
 template <typename KT>
 cudaError_t launch_refine(grm_b200_gqa_bank* b, const RouteParams& p) {
-  dim3 grid(std::max(1, b->sms), kRefineY);
+  // one wave: as many blocks as are resident together (measured once)
+  static int per_sm[2][64] = {};
+  const bool smem_q = sizeof(float) * (size_t)p.heads * p.qt * p.dim <= (size_t)kRefineSmemCopy;
+  int& occ = per_sm[smem_q ? 1 : 0][b->device & 63];
+  if (occ == 0) {
+    const size_t qb = smem_q ? sizeof(float) * (size_t)p.heads * p.qt * p.dim : 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+            &occ, smem_q ? refine_kernel<KT, true> : refine_kernel<KT, false>, kRefineChunk,
+            qb) != cudaSuccess || occ < 1)
+      occ = 1;
+  }
+  dim3 grid(std::max(1, b->sms) * occ);
   const size_t qbytes = sizeof(float) * (size_t)p.heads * p.qt * p.dim;
   // A block takes about one 32-token chunk per kv head of a candidate, so
   // copying a large query into shared memory costs more than it saves: large
@@ -1122,9 +1191,9 @@ cudaError_t launch_refine(grm_b200_gqa_bank* b, const RouteParams& p) {
                            kRefineSmemMax);
       attr_set[b->device] = true;
     }
-    return launch_chained(refine_kernel<KT, true>, grid, dim3(256), qbytes, b->stream, p);
+    return launch_chained(refine_kernel<KT, true>, grid, dim3(kRefineChunk), qbytes, b->stream, p);
   }
-  return launch_chained(refine_kernel<KT, false>, grid, dim3(256), 0, b->stream, p);
+  return launch_chained(refine_kernel<KT, false>, grid, dim3(kRefineChunk), 0, b->stream, p);
 }
 
 int ensure_heads(grm_b200_gqa_bank* b, int heads, int nt) {
