@@ -917,6 +917,10 @@ __global__ void __launch_bounds__(256) refine_kernel(RouteParams p) {
 __global__ void finalize_kernel(RouteParams p) {
   asm volatile("griddepcontrol.wait;" ::: "memory");  // chained launch, as node_bounds_kernel
   asm volatile("griddepcontrol.launch_dependents;");
+  // head maxima of 32 candidates x 64 heads, staged by coalesced loads (and
+  // reset for the next route in the same pass); lane c then sums candidate
+  // c's heads in order from shared memory
+  __shared__ float sh_best[32][65];
   const int lane = threadIdx.x;
   const int count = *p.cand_count;
   WarpList list;
@@ -924,22 +928,38 @@ __global__ void finalize_kernel(RouteParams p) {
   float max_abs = 0.0f;
   for (int base = 0; base < count; base += 32) {
     const int ci = base + lane;
+    const int nc = min(32, count - base);
+    float total = 0.0f;
+    for (int h0 = 0; h0 < p.heads; h0 += 64) {
+      const int hn = min(64, p.heads - h0);
+      __syncwarp();
+      for (int c = 0; c < nc; ++c) {
+        unsigned* bc = p.headmax + (int64_t)(base + c) * p.heads + h0;
+        if (lane < hn) {
+          sh_best[c][lane] = __uint_as_float(bc[lane]);
+          bc[lane] = 0u;
+        }
+        if (lane + 32 < hn) {
+          sh_best[c][lane + 32] = __uint_as_float(bc[lane + 32]);
+          bc[lane + 32] = 0u;
+        }
+      }
+      __syncwarp();
+      if (ci < count)
+        for (int h = 0; h < hn; ++h) total = __fadd_rn(total, sh_best[lane][h]);
+    }
     float score = -INFINITY;
     uint32_t node = kNoRow;
     if (ci < count) {
       node = p.cand[ci];
       const int64_t T = (int64_t)(p.off[node + 1] - p.off[node]);
-      unsigned* best = p.headmax + (int64_t)ci * p.heads;
       if (T == 0) {
         score = 0.0f;
       } else if (p.key_bad[node] || !p.qinfo->finite) {
         score = __int_as_float(0x7FC00000);
       } else {
-        float total = 0.0f;
-        for (int h = 0; h < p.heads; ++h) total = __fadd_rn(total, __uint_as_float(best[h]));
         score = __fdiv_rn(total, (float)p.heads);
       }
-      for (int h = 0; h < p.heads; ++h) best[h] = 0u;
       if (p.lex_m) {
         p.lo[node] = score;
         if (isfinite(score)) max_abs = fmaxf(max_abs, fabsf(score));
