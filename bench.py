@@ -22,7 +22,13 @@ Printed (rank 0, one JSON line):
              from source, OpenMP, all host cores) on the same bank;
   clocks     SM clock and throttle reasons sampled (NVML) during the run.
 --impl reference times that reference CPU route alone (rank 0; other ranks
-exit), each step one probe over a 1/32 slice of the bank, scaled to 1M nodes.
+exit): each step routes one probe over the same full 1,048,576-node bank.
+
+Both arms use config 2's recipe from one generator (synth.mla_config: rows
+N(0,1), L2-normalised in fp32, stored fp16, then the queries as the next
+draws of default_rng(1)), so they route identical inputs.  After the timed
+region the outputs of timed steps are checked against the reference runtime
+(ids) and the C restatement (scores); the line reports how many were checked.
 """
 
 from __future__ import annotations
@@ -165,9 +171,11 @@ class ClockSampler:
                 "samples": len(self.samples)}
 
 
-def cpu_reference_full(rows_f32: np.ndarray, queries: np.ndarray, budget_s: float = 8.0):
+def cpu_reference_full(rows_f32: np.ndarray, queries: np.ndarray, budget_s: float = 8.0,
+                       check=None):
     """The reference's CPU route on the full bank (oracle/_ref OpenMP build),
-    falling back to the C restatement when the reference was not built."""
+    falling back to the C restatement when the reference was not built.
+    check(store) runs the parity checker with the loaded store before timing."""
     import oracle as O
 
     cores = len(os.sched_getaffinity(0))
@@ -176,7 +184,11 @@ def cpu_reference_full(rows_f32: np.ndarray, queries: np.ndarray, budget_s: floa
         st.route(queries[0], TOPK)                  # first call: arena rebuild + snapshot
         kind = "reference"
         route = lambda q: st.route(q, TOPK)  # noqa: E731
+        if check is not None:
+            check(st)
     else:
+        if check is not None:
+            check(None)
         norms = O.mla_row_norms(rows_f32)
         kind = "port"
         route = lambda q: O.mla_route(rows_f32, q, TOPK, norms=norms)  # noqa: E731
@@ -195,56 +207,79 @@ def cpu_reference_full(rows_f32: np.ndarray, queries: np.ndarray, budget_s: floa
                       f"{statistics.median(times) * 1e3:.1f} ms (OpenMP, {cores} threads)"}
 
 
+def mla_inputs(n_queries: int):
+    """Config 2's bank and queries (one generator, identical in both arms)."""
+    from graftrepository_b200 import synth
+
+    return synth.mla_config(1, NODES, queries=n_queries)
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     import oracle as O
-    from graftrepository_b200 import synth
 
     cores = len(os.sched_getaffinity(0))
-    slices = 32   # 32,768-node slices: at the reference's OpenMP threshold (cpp/grm_runtime.cpp:4320)
-    per = NODES // slices
-    rows = synth.mla_bank(1, NODES).astype(np.float32)
-    qs = synth.mla_queries(1, max(8, min(args.warmup + args.steps, 4096)))
-    omp = O.ref_available(omp=True)
-    stores = []
-    if omp:
-        for s in range(slices):
-            st = O.RefStore(omp=True).load_mla(rows[s * per:(s + 1) * per])
-            st.route(qs[0], TOPK)
-            stores.append(st)
-        route = lambda s, q: stores[s].route(q, TOPK)  # noqa: E731
+    n_q = max(8, min(args.warmup + args.steps, 4096))
+    rows16, qs = mla_inputs(n_q)
+    rows = rows16.astype(np.float32)
+    del rows16
+    if O.ref_available(omp=True):
+        st = O.RefStore(omp=True).load_mla(rows)
+        st.route(qs[0], TOPK)          # first call: the reference's arena rebuild + snapshot
+        route = lambda q: st.route(q, TOPK)  # noqa: E731
         kind = "reference"
     else:
+        st = None
         norms = O.mla_row_norms(rows)
-        route = lambda s, q: O.mla_route(rows[s * per:(s + 1) * per], q, TOPK,  # noqa: E731
-                                         norms=norms[s * per:(s + 1) * per])
+        route = lambda q: O.mla_route(rows, q, TOPK, norms=norms)  # noqa: E731
         kind = "port"
     for i in range(args.warmup):
-        route(i % slices, qs[i % len(qs)])
-    t0 = time.perf_counter()
+        route(qs[i % n_q])
+    times = []
     for i in range(args.steps):
-        route(i % slices, qs[(args.warmup + i) % len(qs)])
-    dt = time.perf_counter() - t0
-    per_probe = dt / args.steps * slices
-    value = 1.0 / per_probe
-    for st in stores:
+        t0 = time.perf_counter()
+        route(qs[(args.warmup + i) % n_q])
+        times.append(time.perf_counter() - t0)
+    dt = sum(times)
+    if st is not None:
         st.close()
-    sample = (f"each step routes one probe over one {per}-node slice (1/{slices}) of the 1M bank; "
-              f"probe time = {slices} x mean step time ({dt / args.steps * 1e3:.2f} ms)")
+    value = args.steps / dt
+    sample = (f"each step routes one probe over the full {NODES}-node bank "
+              f"(grm_store_route, OpenMP, {cores} threads); median step "
+              f"{statistics.median(times) * 1e3:.1f} ms")
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": per_probe * 1e3, "higher_is_better": True, "scaling": "strong",
-        "vs_baseline": None, "dtype": "f32/f64", "data": "synthetic",
+        "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32 bank (fp16 values), f64 dot", "data": "synthetic",
         "config": {"workload": args.workload, "nodes": NODES, "dim": DIM, "topk": TOPK,
-                   "batch": batch_of(args.workload),
-                   "bank_dtype": "fp16 values (reference stores fp32)"},
+                   "batch": 1, "bank_dtype": "fp16 values (reference stores fp32)",
+                   "recipe": "synth.mla_config(1): default_rng(1), rows then queries"},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": kind,
                          "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
+
+
+def mla_parity(rows_f32, queries, got_ids, got_scores, ref_store=None):
+    """Checker (outside every timed region): each routed query's ids against
+    the reference runtime's route when a store is given, else against the C
+    restatement, and its scores against the restatement's exact scores.
+    Returns the number of queries checked; raises on a mismatch."""
+    import oracle as O
+
+    norms = O.mla_row_norms(rows_f32)
+    for q, ids, sc in zip(queries, got_ids, got_scores):
+        want, want_s = O.mla_route(rows_f32, q, TOPK, norms=norms)
+        if ref_store is not None:
+            ref_ids = ref_store.route(q, TOPK)
+            if [int(x) for x in want] != ref_ids:
+                raise RuntimeError(f"restatement {want} != reference {ref_ids}")
+        if [int(x) for x in ids] != [int(x) for x in want] or not np.array_equal(sc, want_s):
+            raise RuntimeError(f"timed route result {ids} {sc} != reference {want} {want_s}")
+    return len(queries)
 
 
 def run_ours(args):
@@ -265,9 +300,11 @@ def run_ours(args):
     lib = _lib.load()
 
     B = batch_of(args.workload)   # queries per step
-    rows = synth.mla_bank_device(1, NODES)
+    # distinct queries every step (a pool of batches, cycled for long runs)
+    n_q = min(args.warmup + args.steps, 4096 // B)
+    rows16, qs_np = mla_inputs(n_q * B)
     a, b = mla_shard_range(NODES, world, rank)
-    shard = rows[a:b].contiguous()
+    shard = torch.from_numpy(rows16[a:b]).cuda()
     route = ShardedMLARoute(group, shard, a, DIM, max_queries=64, device=local) if world > 1 \
         else None
     if world == 1:
@@ -276,12 +313,9 @@ def run_ours(args):
         bank.reserve(64)
     else:
         bank = route.bank
-    rows_host = rows.float().cpu().numpy() if (rank == 0 and world == 1 and
-                                               not args.no_cpu_baseline) else None
-    del rows
-    # distinct queries every step (a pool of batches, cycled for long runs)
-    n_q = min(args.warmup + args.steps, 4096 // B)
-    qs_host = torch.from_numpy(synth.mla_queries(1, n_q * B)).pin_memory()
+    rows_host = rows16.astype(np.float32) if rank == 0 else None
+    del rows16
+    qs_host = torch.from_numpy(qs_np).pin_memory()
     qs_dev = qs_host.cuda()
     # route results go straight into one packed block per rank (ids, scores,
     # padding: 16 B per entry), so the exchange is a single all-gather
@@ -308,19 +342,24 @@ def run_ours(args):
 
     def step(i, ev):
         """One route of B queries: scan + resolve (programmatic dependent launch)
-        [+ gather + merge]."""
+        [+ gather + merge].  ev: [start, end] or, at N > 1, [start, routed,
+        gathered, end] for the per-phase split."""
         q = batch(i)
         if ev:
             ev[0].record(stream)
         rc = lib.grm_b200_mla_route_async(bank._h, q.data_ptr(), B, TOPK, a, out_i.data_ptr(),
                                           out_s.data_ptr(), sptr)
         if world > 1:
+            if ev and len(ev) == 4:
+                ev[1].record(stream)
             dist.all_gather_into_tensor(gblk, blk)
+            if ev and len(ev) == 4:
+                ev[2].record(stream)
             rc |= lib.grm_b200_merge_topk_strided(gs.data_ptr(), gs.stride(0), gi.data_ptr(),
                                                   gi.stride(0), B, world, TOPK, TOPK,
                                                   ms_s.data_ptr(), ms_i.data_ptr(), sptr)
         if ev:
-            ev[1].record(stream)
+            ev[-1].record(stream)
         if rc:
             raise RuntimeError("route launch failed")
 
@@ -346,7 +385,8 @@ def run_ours(args):
     # a flush each step is bracketed by its own events so the flush is not
     # timed.  A second pass with per-step events gives the step distribution.
     n_dist = min(args.steps, 1000)
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    n_ev = 4 if world > 1 else 2
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(n_ev)]
            for _ in range(args.steps if flush is not None else n_dist)]
     ev_all = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
     n_scan = min(args.steps, 1000)
@@ -368,6 +408,10 @@ def run_ours(args):
                 step(args.warmup + i, evs[i])
         torch.cuda.synchronize()
         wall = time.perf_counter() - wall0
+        # the last timed step's result, kept for the parity check
+        last_q = qs_host[((args.warmup + args.steps - 1) % n_q) * B:][:B].numpy().copy()
+        last_i = (ms_i if world > 1 else out_i).cpu().numpy().view(np.uint64).copy()
+        last_s = (ms_s if world > 1 else out_s).cpu().numpy().copy()
         fallbacks = bank.stats()[1] - fb0
         if world > 1:
             dist.barrier()
@@ -382,7 +426,18 @@ def run_ours(args):
                 l2_flush(flush)
             scan_only(args.warmup + i, sevs[i])
         torch.cuda.synchronize()
-    step_ms = [e[0].elapsed_time(e[1]) for e in evs]
+    step_ms = [e[0].elapsed_time(e[-1]) for e in evs]
+    phases = None
+    if world > 1:   # per-phase medians, max over ranks
+        ph = torch.tensor([statistics.median(e[0].elapsed_time(e[1]) for e in evs),
+                           statistics.median(e[1].elapsed_time(e[2]) for e in evs),
+                           statistics.median(e[2].elapsed_time(e[3]) for e in evs)],
+                          dtype=torch.float64, device="cuda")
+        dist.all_reduce(ph, op=dist.ReduceOp.MAX)
+        phases = {"route_us": ph[0].item() * 1e3, "allgather_us": ph[1].item() * 1e3,
+                  "merge_us": ph[2].item() * 1e3,
+                  "note": "medians of per-step event pairs (second pass), max over ranks; "
+                          "route = this rank's scan + resolve"}
     scan_ms = [e[0].elapsed_time(e[1]) for e in sevs]
     timed_ms = ev_all[0].elapsed_time(ev_all[1]) if flush is None else sum(step_ms)
     tot = torch.tensor([timed_ms], dtype=torch.float64, device="cuda")
@@ -391,8 +446,6 @@ def run_ours(args):
     total_ms = float(tot.item())
     value = args.steps * B / (total_ms / 1e3)
 
-    # correctness of the timed steps: the last route equals a fresh exact route
-    # (the full parity suite lives in tests/)
     # e2e: the public API with host buffers every step
     e2e_steps = min(args.steps, 500)
     if world == 1:
@@ -430,9 +483,27 @@ def run_ours(args):
     bytes_per_launch = shard_bytes + B * DIM * 4
     achieved = bytes_per_launch / (scan_mean / 1e3) / 1e9
     flops_per_launch = 2 * (b - a) * DIM * B
+    # parity of timed outputs: the last timed step's result, plus the results
+    # of the last e2e (public API) calls, all on queries of the timed pool
+    checked = {"n": 0}
+    if world == 1:
+        e2e_q = qn[(args.warmup + e2e_steps - 1) % n_q]
+        e2e_ids = bank.route_topk(e2e_q, topk=TOPK)[0]
+        e2e_s = bank.last_scores.copy()
+        chk_q = np.concatenate([last_q[:2], e2e_q[:1]])
+        chk_i = np.concatenate([last_i[:2], e2e_ids[:1]])
+        chk_s = np.concatenate([last_s[:2], e2e_s[:1]])
+    else:
+        chk_q, chk_i, chk_s = last_q[:3], last_i[:3], last_s[:3]
+
+    def check(store):
+        checked["n"] = mla_parity(rows_host, chk_q, chk_i, chk_s, store)
+
     cpu = None
-    if rank == 0 and world == 1 and rows_host is not None:
-        cpu = cpu_reference_full(rows_host, synth.mla_queries(1, 64))
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_reference_full(rows_host, qs_np[:64], check=check)
+    elif rank == 0:
+        check(None)
     if world > 1:
         dist.destroy_process_group()
     if rank != 0:
@@ -461,6 +532,11 @@ def run_ours(args):
                      "step_us_median": statistics.median(step_ms) * 1e3,
                      "step_us_p99": sorted(step_ms)[int(0.99 * (len(step_ms) - 1))] * 1e3},
         "exact_fallbacks_in_timed_steps": fallbacks,
+        "parity_checked": checked["n"],
+        "parity": ("timed-step results: ids == reference runtime route (full bank), scores == "
+                   "exact restatement" if world == 1 and not args.no_cpu_baseline else
+                   "timed-step results: ids and scores == exact restatement (full bank)"),
+        "phases": phases,
         "cpu_baseline": cpu,
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "steps": e2e_steps,
@@ -568,6 +644,10 @@ def run_gqa(args):
             evs[i][1].record(stream)
         torch.cuda.synchronize()
     step_ms = [e[0].elapsed_time(e[1]) for e in evs]
+    # this rank's result of the last timed step (its shard's top-k), for the check
+    last_q = qs_host[(args.warmup + args.steps - 1) % n_q].numpy().copy()
+    last_i = out_i.cpu().numpy().view(np.uint64)[0].copy()
+    last_s = out_s.cpu().numpy()[0].copy()
     tot = torch.tensor([sum(step_ms)], dtype=torch.float64, device="cuda")
     if world > 1:
         dist.all_reduce(tot, op=dist.ReduceOp.MAX)
@@ -604,6 +684,12 @@ def run_gqa(args):
     peak, peak_kind = peaks()
     step_mean = statistics.mean(step_ms)
     achieved = bytes_per_probe / (step_mean / 1e3) / 1e9
+    # every rank checks its own timed top-k (the merge is exact given them)
+    checked = gqa_parity(keys, off, a, last_q, last_i, last_s, KH, D)
+    if world > 1:
+        c = torch.tensor([checked], dtype=torch.int64, device="cuda")
+        dist.all_reduce(c)
+        checked = int(c.item())
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_gqa_baseline(keys, off, qn[0], KH, D)
@@ -629,12 +715,56 @@ def run_gqa(args):
                      "algorithmic_bytes_per_launch": bytes_per_probe, "traffic": None,
                      "step_us_mean": step_mean * 1e3},
         "refined_nodes_per_route": refined / max(routes, 1),
+        "parity_checked": checked,
+        "parity": ("each rank's last timed top-k: scores == exact restatement of those nodes, "
+                   "and no node of a <=300k-token shard prefix outranks them (restatement)"),
         "cpu_baseline": cpu,
         "e2e": {"value": e2e_steps / e2e_s, "unit": "probes/s", "h2d_bytes_per_step": qsz * 4,
                 "d2h_bytes_per_step": 400 if world == 1 else k * 12, "steps": e2e_steps},
         "gpu_launches": args.steps * (6 + (1 if world > 1 else 0)),
         "clocks": clk.summary(),
     }), flush=True)
+
+
+def gqa_parity(keys_dev, off, id_offset, q, ids, scores, KH, D, max_tokens=300_000):
+    """Checker (outside every timed region) of one timed GQA result over a
+    shard: the returned nodes' scores equal the C restatement's exact scores
+    of those nodes, and no node of the shard's first <= max_tokens tokens that
+    is not returned outranks the k-th returned one (score desc, id asc).
+    Returns the number of checks passed; raises on a mismatch."""
+    import torch
+
+    import oracle as O
+
+    row = KH * D
+    flat = keys_dev.view(torch.int16)
+
+    def host_keys(t0, t1):
+        return flat[t0 * row: t1 * row].cpu().numpy().view(np.uint16)
+
+    fin = ids != np.iinfo(np.uint64).max
+    loc = (ids[fin] - np.uint64(id_offset)).astype(np.int64)
+    parts, lens = [], []
+    for n in loc:
+        t0, t1 = int(off[n]), int(off[n + 1])
+        parts.append(host_keys(t0, t1))
+        lens.append(t1 - t0)
+    mini_off = np.zeros(len(lens) + 1, dtype=np.uint64)
+    mini_off[1:] = np.cumsum(lens)
+    exact = O.gqa_scores(np.concatenate(parts) if parts else np.zeros(0, np.uint16), mini_off,
+                         KH, D, q)
+    if not np.array_equal(exact, scores[fin]):
+        raise RuntimeError(f"timed GQA scores {scores[fin]} != exact {exact}")
+    n_pre = max(1, int(np.searchsorted(off, max_tokens, side="right")) - 1)
+    s_pre = O.gqa_scores(host_keys(0, int(off[n_pre])), off[: n_pre + 1], KH, D, q)
+    if fin.sum() == len(ids):
+        ks, kid = float(scores[-1]), int(loc[-1])
+        chosen = set(int(x) for x in loc)
+        for i in np.nonzero(np.isfinite(s_pre) & (s_pre >= ks))[0]:
+            i = int(i)
+            if i not in chosen and (s_pre[i] > ks or i < kid):
+                raise RuntimeError(f"node {i} (score {s_pre[i]}) outranks the timed top-k")
+    return 2
 
 
 def cpu_gqa_baseline(keys_dev, off, q, KH, D, max_tokens=40_000, budget_s=8.0):

@@ -1,6 +1,7 @@
 // abi_common.cu -- handle-less entry points of libgrm_b200.so: thread-local
 // error text, device-property cache, upload/free helpers and the top-k merge
 // used after the all-gather of per-shard route results.
+#include <cstdlib>
 #include <cstring>
 
 #include "common.cuh"
@@ -20,6 +21,17 @@ void set_thread_error(const char* fmt, ...) {
   vsnprintf(buf, sizeof(buf), fmt, ap);
   va_end(ap);
   g_thread_error = buf;
+}
+
+unsigned scan_wait_limit() {
+  static const unsigned limit = [] {
+    const char* v = std::getenv("GRM_B200_WAIT_LIMIT");
+    if (!v || !*v) return kWaitLimit;
+    char* end = nullptr;
+    const unsigned long n = std::strtoul(v, &end, 10);
+    return (end && *end == '\0' && n <= kWaitLimit) ? (unsigned)n : kWaitLimit;
+  }();
+  return limit;
 }
 
 int device_info(int device, DeviceInfo* out) {

@@ -213,6 +213,13 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
 
 constexpr unsigned kWaitLimit = 1u << 24;
 
+// Probe limit of the streaming scans' bounded waits: kWaitLimit, unless the
+// environment variable GRM_B200_WAIT_LIMIT (read once per process) gives
+// another value.  Tests set it to 0 so that every wait gives up at once and
+// the error path (drain the copies in flight, report status 3001) runs
+// without any wait actually hanging.  The drain itself always uses kWaitLimit.
+unsigned scan_wait_limit();
+
 __host__ __device__ inline int64_t ceil_div64(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
 // Device properties cached per device.

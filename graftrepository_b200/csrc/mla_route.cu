@@ -118,6 +118,7 @@ struct Params {
   int* entry_best;        // [entries] ordered float, reset to -inf by the collect step
   int* multi_unsafe;      // [Q] the query is outside the approximate pass's safe range
   double* multi_qnorm;    // the query's reference norm, for the entry refine
+  unsigned wait_limit;    // probes per bounded wait of the bulk scan (scan_wait_limit())
   // A single query may travel inside the launch parameters (queries == nullptr):
   // the synchronous host entry then needs no host-to-device copy.
   float qinline[kInlineMax];
@@ -1126,7 +1127,7 @@ __global__ void __launch_bounds__(kBulkWarps * 32, 1)
       float part[SLOTS];
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
-        if (!mbar_wait(&sh_bar[warp][h], (phase_bits >> h) & 1u, kWaitLimit)) {
+        if (!mbar_wait(&sh_bar[warp][h], (phase_bits >> h) & 1u, p.wait_limit)) {
           failed = true;
           break;
         }
@@ -1701,6 +1702,7 @@ Params<T> make_params(grm_b200_mla_bank* b, const float* dq, int topk) {
   p.entry_best = b->d_entry_best;
   p.multi_unsafe = b->d_unsafe;
   p.multi_qnorm = b->d_qn;
+  p.wait_limit = scan_wait_limit();
   return p;
 }
 
@@ -2693,6 +2695,18 @@ extern "C" int grm_b200_mla_route_noalloc(const void* rows_device, int64_t nodes
                      kNoAllocMaxQueries, query_count);
     return GRM_B200_EINVAL;
   }
+  // The scans read rows with 16-byte vector loads, queries as floats, and
+  // store whole uint64 / float result words: a misaligned view (an offset into
+  // a caller's pool) is rejected here instead of faulting on the device.
+  const uintptr_t rows_a = reinterpret_cast<uintptr_t>(rows_device);
+  const uintptr_t q_a = reinterpret_cast<uintptr_t>(queries_device);
+  if ((rows_a & 15) || (q_a & 3) || (reinterpret_cast<uintptr_t>(out_ids_device) & 7) ||
+      (reinterpret_cast<uintptr_t>(out_scores_device) & 3)) {
+    set_thread_error("allocation-free MLA route needs rows 16-byte, queries 4-byte, ids 8-byte "
+                     "and scores 4-byte aligned device pointers (rows %% 16 = %d)",
+                     (int)(rows_a & 15));
+    return GRM_B200_EINVAL;
+  }
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) {
@@ -2713,9 +2727,15 @@ extern "C" int grm_b200_mla_route_noalloc(const void* rows_device, int64_t nodes
   }
   if (rc) return rc;
   const int64_t groups = ceil_div64(nodes, 32);
-  const int grid_x = (int)std::max<int64_t>(
+  int grid_x = (int)std::max<int64_t>(
       1, std::min<int64_t>((int64_t)info.sms * occ, ceil_div64(groups, kWarps)));
   const size_t results_bytes = (sizeof(Result) * (size_t)query_count + 255) & ~(size_t)255;
+  // The per-query scratch grows with the grid; shrink the grid until every
+  // query's slice fits (the scan's block ranges and the exact pass accept any
+  // grid width), so a full batch of queries always routes.
+  while (grid_x > 1 &&
+         results_bytes + scratch_stride(grid_x) * (size_t)query_count > kNoAllocScratchBytes)
+    --grid_x;
   const size_t stride = scratch_stride(grid_x);
   const size_t need = results_bytes + stride * (size_t)query_count;
   if (need > kNoAllocScratchBytes) {
@@ -2743,6 +2763,7 @@ extern "C" int grm_b200_mla_route_noalloc(const void* rows_device, int64_t nodes
   p.entry_best = nullptr;
   p.multi_unsafe = nullptr;
   p.multi_qnorm = nullptr;
+  p.wait_limit = scan_wait_limit();
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   scratch_init_kernel<<<(query_count + 127) / 128, 128, 0, s>>>(base + results_bytes, stride,
                                                                  query_count);

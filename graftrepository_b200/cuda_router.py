@@ -11,6 +11,8 @@ calls use the sm_100a library unchanged:
 * ``validate_/..._route_bank_signature`` :35-75, :293-332
 * ``CudaGQARouteSidecar`` / ``Bank``  :87-282 (the bank is CSR-ragged here)
 * ``CudaMLARouteSidecar`` / ``Bank``  :344-539
+* ``PaddedGQARouteSidecar``           the arena's dense padded GQA bank plus its
+  ``row_token_counts`` receipt (core/graft_arena.py:2980-3042) -> CSR
 
 Every route goes through ``libgrm_b200.so``; there is no host fallback inside
 this module.  Exactly as in the reference, a UINT64_MAX sentinel (fewer finite
@@ -37,7 +39,7 @@ __all__ = [
     "validate_mla_route_bank", "mla_route_bank_signature",
     "validate_gqa_route_bank", "gqa_route_bank_signature", "dense_to_csr",
     "CudaMLARouteSidecar", "CudaMLARouteBank", "CudaGQARouteSidecar", "CudaGQARouteBank",
-    "DeviceQueries", "upload_queries",
+    "PaddedGQARouteSidecar", "DeviceQueries", "upload_queries",
 ]
 
 UINT64_MAX = np.iinfo(np.uint64).max
@@ -746,6 +748,12 @@ class CudaGQARouteSidecar:
         return CudaGQARouteBank(handle, ids, kv_heads=kv_heads, head_dim=head_dim,
                                 setup_wall_ms=setup, signature=signature)
 
+    def create_bank_padded(self, keys, node_ids, row_token_counts, *, signature=None):
+        """The arena's dense zero-padded bank plus its padding receipt
+        (``row_token_counts``, core/graft_arena.py:3026-3041): stored as CSR."""
+        return self.create_bank(keys, node_ids, signature=signature,
+                                token_counts=row_token_counts)
+
     def create_bank_device(self, keys_ptr: int, dtype_code: int, token_offsets, kv_heads: int,
                            head_dim: int, node_ids=None, *, signature=None, keepalive=None):
         """Borrow keys already on the current device (no copy)."""
@@ -763,3 +771,31 @@ class CudaGQARouteSidecar:
 
     def close(self) -> None:
         pass
+
+
+class PaddedGQARouteSidecar:
+    """Sidecar for ``NativeGraftStore.configure_cuda_gqa_route_bank(...,
+    sidecar=...)`` (core/grm_native.py:1498-1531) while the arena still passes
+    its dense zero-padded bank (core/graft_arena.py:2980-3042): the store
+    calls ``create_bank(route_bank, node_ids, signature=...)`` and this adapter
+    hands the arena's ``row_token_counts`` padding receipt along, so the
+    device bank is CSR (no padded bytes are stored or streamed).  Routing
+    results equal the padded law's (a zero key scores |q.0| = 0, which never
+    raises a node's maximum)."""
+
+    def __init__(self, sidecar: CudaGQARouteSidecar, row_token_counts):
+        self.sidecar = sidecar
+        self.row_token_counts = np.ascontiguousarray(row_token_counts, dtype=np.int64).reshape(-1)
+
+    @classmethod
+    def build(cls, row_token_counts, build_dir: Path | None = None, *, nvcc: str = "nvcc",
+              device: int = 0) -> "PaddedGQARouteSidecar":
+        return cls(CudaGQARouteSidecar.build(build_dir, nvcc=nvcc, device=device),
+                   row_token_counts)
+
+    def create_bank(self, keys, node_ids=None, *, signature=None):
+        return self.sidecar.create_bank_padded(keys, node_ids, self.row_token_counts,
+                                               signature=signature)
+
+    def close(self) -> None:
+        self.sidecar.close()

@@ -42,6 +42,19 @@ def mla_queries(seed: int, count: int, dim: int = MLA_DIM) -> np.ndarray:
     return rng.standard_normal((count, dim), dtype=np.float32)
 
 
+def mla_config(seed: int, nodes: int, queries: int = 1,
+               dim: int = MLA_DIM) -> tuple[np.ndarray, np.ndarray]:
+    """The configs' exact recipe from ONE generator: rng = default_rng(seed);
+    rows N(0,1) fp32 [nodes, dim], L2-normalised per row in fp32, stored fp16;
+    then the queries N(0,1) fp32 [queries, dim] as the generator's next draws
+    (config 1: seed 0, 10,000 nodes, one query)."""
+    rng = np.random.default_rng(seed)
+    rows = rng.standard_normal((nodes, dim), dtype=np.float32)
+    rows /= np.linalg.norm(rows, axis=1, keepdims=True)
+    qs = rng.standard_normal((queries, dim), dtype=np.float32)
+    return rows.astype(np.float16), qs
+
+
 def mla_bank_device(seed: int, nodes: int, dim: int = MLA_DIM, device: str = "cuda"):
     """The same recipe drawn on the device (torch CUDA generator), fp16 tensor."""
     import torch
@@ -68,6 +81,24 @@ def gqa_lengths(seed: int, nodes: int, kind: str = "uniform") -> np.ndarray:
     raise ValueError(kind)
 
 
+def longest_plus_prefix(lengths: np.ndarray, longest: int, max_tokens: int) -> np.ndarray:
+    """Node indices (ascending) of a checkable subset of a large ragged bank:
+    the `longest` longest nodes (ties to the lower index) plus the longest
+    contiguous prefix that keeps the subset within `max_tokens` tokens.  The
+    tail of the length distribution (config 4's 4,096-token nodes) is then
+    always part of the check."""
+    t = np.asarray(lengths, dtype=np.int64)
+    top = np.argsort(-t, kind="stable")[:longest]
+    budget = max_tokens - int(t[top].sum())
+    in_top = np.zeros(len(t), dtype=bool)
+    in_top[top] = True
+    extra = np.cumsum(np.where(in_top, 0, t))
+    prefix = int(np.searchsorted(extra, budget, side="right"))
+    keep = in_top.copy()
+    keep[:prefix] = True
+    return np.nonzero(keep)[0]
+
+
 def offsets(lengths: np.ndarray) -> np.ndarray:
     off = np.zeros(len(lengths) + 1, dtype=np.uint64)
     off[1:] = np.cumsum(lengths)
@@ -80,7 +111,11 @@ def gqa_bank(seed: int, lengths: np.ndarray, kv_heads: int = GQA_LAYERS * GQA_KV
     rng = np.random.default_rng(seed + 7)
     off = offsets(lengths)
     n = int(off[-1]) * kv_heads * dim
-    keys = bf16_bits(rng.standard_normal(n, dtype=np.float32))
+    keys = np.empty(n, dtype=np.uint16)
+    step = 1 << 26      # chunked draws: the same stream, a bounded temporary
+    for a in range(0, n, step):
+        b = min(n, a + step)
+        keys[a:b] = bf16_bits(rng.standard_normal(b - a, dtype=np.float32))
     return keys, off
 
 

@@ -192,7 +192,12 @@ int grm_b200_mla_paths(grm_b200_mla_bank* bank, int* flags);
  * queries[query_count, dim] (query_count <= 16) in device memory and receives
  * ids/scores[query_count, topk] in its own device buffers on `stream`; row
  * norms are computed inline, results are bit-exact with the bank entry
- * points.  Scratch is a fixed 2 MiB __device__ array inside the library (held
+ * points.  rows_device must be 16-byte aligned (rows are read with 16-byte
+ * vector loads), queries_device and out_scores_device 4-byte and
+ * out_ids_device 8-byte aligned; a misaligned pointer (e.g. an odd offset into
+ * a pool) returns -1 before anything is launched.  Large banks with many
+ * queries route on a narrower grid so that every query's scratch fits.
+ * Scratch is a fixed 2 MiB __device__ array inside the library (held
  * by every GPU that loads it until exit), shared by all calls: calls that
  * overlap on the GPU race and must be serialised by the caller.  The first
  * call on each device looks up the array's device address; make it before any

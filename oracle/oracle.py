@@ -16,12 +16,24 @@ from pathlib import Path
 import numpy as np
 
 HERE = Path(__file__).resolve().parent
+
+
+def reference_root() -> Path:
+    """The GraftRepository checkout: $GRM_REFERENCE_ROOT, else the single
+    default written in oracle/reference_root (also read by oracle/Makefile
+    and the build hook)."""
+    env = os.environ.get("GRM_REFERENCE_ROOT")
+    if env:
+        return Path(env)
+    return Path((HERE / "reference_root").read_text().strip())
+
+
 LIB_PATH = HERE / "liboracle.so"
 REF_LIB_PATH = HERE / "_ref" / "libgrm_ref.so"
 REF_OMP_LIB_PATH = HERE / "_ref" / "libgrm_ref_omp.so"
 
 __all__ = [
-    "ensure_built", "lib", "ref_available", "RefStore",
+    "ensure_built", "lib", "ref_available", "RefStore", "reference_root",
     "f32_to_f16_bits", "f16_bits_to_f32", "f32_to_bf16_bits", "bf16_bits_to_f32",
     "mla_row_norms", "mla_scores", "mla_route", "topk",
     "gqa_scores", "gqa_route",
@@ -40,7 +52,7 @@ def ensure_built(ref_root: str | os.PathLike | None = None, with_ref: bool = Fal
     reference runtime) with oracle/Makefile."""
     targets = ["oracle"]
     if with_ref:
-        root = Path(ref_root or os.environ.get("GRM_REFERENCE_ROOT", "/root/reference"))
+        root = Path(ref_root) if ref_root else reference_root()
         if (root / "cpp" / "grm_runtime.cpp").is_file():
             targets.append("ref")
     src = HERE / "grm_oracle.c"
@@ -50,8 +62,8 @@ def ensure_built(ref_root: str | os.PathLike | None = None, with_ref: bool = Fal
     if not need:
         return
     cmd = ["make", "-s", "-C", str(HERE), *targets]
-    if ref_root is not None:
-        cmd.append(f"REF_ROOT={ref_root}")
+    if with_ref:
+        cmd.append(f"REF_ROOT={root}")
     subprocess.run(cmd, check=True)
 
 

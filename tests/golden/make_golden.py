@@ -1,7 +1,7 @@
 """Generate the committed golden vectors from the REFERENCE implementation.
 
-Run in a container that has the GraftRepository checkout (default
-/root/reference, or GRM_REFERENCE_ROOT) and a C++ compiler:
+Run in a container that has the GraftRepository checkout (the path in
+oracle/reference_root, or GRM_REFERENCE_ROOT) and a C++ compiler:
 
     python tests/golden/make_golden.py [fixture ...]
 
@@ -42,11 +42,12 @@ import numpy as np
 
 HERE = Path(__file__).resolve().parent
 REPO = HERE.parents[1]
-REF = Path(os.environ.get("GRM_REFERENCE_ROOT", "/root/reference"))
 sys.path.insert(0, str(REPO))
-sys.path.insert(0, str(REF))
 
 import oracle as O  # noqa: E402
+
+REF = O.reference_root()
+sys.path.insert(0, str(REF))
 
 
 def mla_case(seed: int, n: int, dim: int, topk: int):

@@ -203,3 +203,26 @@ def test_async_route_device_outputs_and_offset(sidecar):
     assert np.array_equal(got, want_ids + 1000)
     assert np.array_equal(sc.cpu().numpy(), want_s)
     bank.close()
+
+
+def test_config4_lognormal_subset(sidecar):
+    """Config 4's length distribution (lognormal(ln 192, 0.8) clipped 8..4096,
+    100,000 nodes, default_rng(3)) on a subset the oracle finishes in seconds:
+    the 20 longest nodes (eight at 4,096 tokens) plus the longest node prefix
+    that keeps the subset under 400k tokens.  Long nodes exercise the per-item
+    chunk count, the work-item list and the key-norm bounds."""
+    lengths = synth.gqa_lengths(3, 100_000, "lognormal")
+    idx = synth.longest_plus_prefix(lengths, 20, 400_000)
+    sub = lengths[idx]
+    assert int((sub == 4096).sum()) == 8 and int(sub.sum()) <= 400_000
+    keys, off = synth.gqa_bank(3, sub)
+    qs = synth.gqa_query(3, count=2)
+    bank = sidecar.create_bank_csr(keys, off, 32, 128, dtype="bf16")
+    assert bank.paths() == {"fast": True, "tma": True}
+    for k in (3, 16):
+        ids, scores = raw_route(bank, qs, k)
+        for i in range(2):
+            want, want_s = O.gqa_route(keys, off, 32, 128, qs[i], k)
+            assert np.array_equal(ids[i], want), (k, i, ids[i], want)
+            assert np.array_equal(scores[i], want_s), (k, i)
+    bank.close()

@@ -215,3 +215,21 @@ def test_async_route_resolves_ties_after_scan(sidecar):
         assert ids[i].cpu().numpy().view(np.uint64).tolist() == want.tolist()
         assert np.array_equal(sc[i].cpu().numpy(), want_s)
     bank.close()
+
+
+def test_config1_exact_recipe(sidecar):
+    """BASELINE config 1 as written (default_rng(0), 10,000 x 256 fp16
+    unit rows, the query the generator's next draw, top-3): ids and scores
+    against the oracle and ids against the reference runtime itself."""
+    rows16, qs = synth.mla_config(0, 10_000)
+    rows = rows16.astype(np.float32)
+    bank = sidecar.create_bank(rows)
+    assert bank.dtype == 1
+    ids, scores = raw_route(bank, qs, 3)
+    want, want_s = O.mla_route(rows, qs[0], 3)
+    assert np.array_equal(ids[0], want)
+    assert np.array_equal(scores[0], want_s)
+    if O.ref_available():
+        with O.RefStore().load_mla(rows) as st:
+            assert [int(x) for x in ids[0]] == st.route(qs[0], 3)
+    bank.close()

@@ -138,3 +138,35 @@ def test_mla_multi_row_restatement_equals_reference_runtime(seed, dim):
                 ids, _ = O.mla_route_multi(rows, off, q, k)
                 got = [int(x) for x in ids if x != np.iinfo(np.uint64).max]
                 assert got == want
+
+
+def test_config1_exact_recipe_equals_reference_runtime():
+    """BASELINE config 1 as written: default_rng(0), 10,000 x 256 N(0,1) rows
+    L2-normalised in fp32 and stored fp16, the query the generator's next draw,
+    top-3."""
+    from graftrepository_b200 import synth
+
+    rows16, qs = synth.mla_config(0, 10_000)
+    rows = rows16.astype(np.float32)
+    ids, _ = O.mla_route(rows, qs[0], 3)
+    with O.RefStore().load_mla(rows) as st:
+        assert [int(x) for x in ids] == st.route(qs[0], 3)
+
+
+def test_config4_longest_nodes_equal_reference_runtime():
+    """The tail of config 4's length distribution (lognormal(ln 192, 0.8)
+    clipped 8..4096, 100,000 nodes): its 20 longest nodes, eight of them at
+    4,096 tokens, routed by the reference runtime (4 layers x 8 kv heads on the
+    head axis, 128 query heads) and by the restatement."""
+    from graftrepository_b200 import synth
+
+    lengths = synth.gqa_lengths(3, 100_000, "lognormal")
+    top = np.sort(np.argsort(-lengths, kind="stable")[:20])
+    sub = lengths[top]
+    assert int((sub == 4096).sum()) == 8
+    keys, off = synth.gqa_bank(3, sub)
+    q = synth.gqa_query(3)[0]
+    ids, _ = O.gqa_route(keys, off, 32, 128, q, 5)
+    with O.RefStore().load_gqa(keys, off, 32, 128) as st:
+        want = st.route(q, 5)
+    assert [int(x) for x in ids] == want
