@@ -64,6 +64,17 @@ def l2_flush(buf) -> None:
     buf.sum(dtype=torch.int64)
 
 
+def launch_gate(steps: int, per_step_us: float = 25.0) -> None:
+    """Keep the stream busy with a fixed-length sleep kernel (torch.cuda._sleep:
+    a clock-count spin that ends by itself) while the host queues the timed
+    steps behind it, so the device-timed region holds back-to-back steps and
+    no host launch gaps (the host path is what e2e measures)."""
+    import torch
+
+    us = min(200_000.0, max(1_000.0, steps * per_step_us))
+    torch.cuda._sleep(int(us * 2_000))     # ~2,000 cycles per us at the B200's 1,965 MHz
+
+
 def batch_of(workload: str) -> int:
     """Queries per step of an MLA workload (config 2: batch 1 and batch 64)."""
     return 64 if workload == "mla_1m_b64" else 1
@@ -151,6 +162,9 @@ class ClockSampler:
         if self.nv is not None:
             self._t = threading.Thread(target=self._run, daemon=True)
             self._t.start()
+            t_end = time.perf_counter() + 1.0   # first sample before the timed region
+            while not self.samples and time.perf_counter() < t_end:
+                time.sleep(0.002)
         return self
 
     def __exit__(self, *exc):
@@ -398,6 +412,7 @@ def run_ours(args):
         torch.cuda.synchronize()
         wall0 = time.perf_counter()
         if flush is None:
+            launch_gate(args.steps)
             ev_all[0].record(stream)
             for i in range(args.steps):
                 step(args.warmup + i, None)
@@ -542,7 +557,8 @@ def run_ours(args):
                 "d2h_bytes_per_step": d2h, "steps": e2e_steps,
                 "api": "CudaMLARouteBank.route_topk" if world == 1 else "ShardedMLARoute.route"},
         "gpu_launches": args.steps * ((2 if B == 1 else 4) + (0 if world == 1 else 1)),
-        "timing": ("one event pair around the K back-to-back steps" if flush is None else
+        "timing": ("one event pair around the K back-to-back steps, queued behind a sleep "
+                   "kernel so no host launch gap is timed" if flush is None else
                    "per-step event pairs, L2 flush between steps outside them"),
         "roofline_launches": n_scan,
         "clocks": clocks,

@@ -79,6 +79,12 @@ struct Scratch {
   __device__ int* counts(int q) const {
     return reinterpret_cast<int*>(base + stride * q + sizeof(Header) + sizeof(Entry) * 32 * blocks);
   }
+  // exact (reference-arithmetic) score of each appended entry, written by the
+  // single-probe scans before they publish
+  __device__ float* exact(int q) const {
+    return reinterpret_cast<float*>(base + stride * q + sizeof(Header) +
+                                    sizeof(Entry) * 32 * blocks + 8 * (size_t)blocks);
+  }
 };
 
 // Back to the state a launch starts from (err is cleared by whoever reports it).
@@ -91,7 +97,8 @@ __device__ __forceinline__ void reset_header(Header* h) {
 }
 
 inline size_t scratch_stride(int blocks) {
-  size_t b = sizeof(Header) + sizeof(Entry) * 32 * (size_t)blocks + 8 * (size_t)blocks;
+  size_t b = sizeof(Header) + sizeof(Entry) * 32 * (size_t)blocks + 8 * (size_t)blocks +
+             sizeof(float) * 32 * (size_t)blocks;
   return (b + 255) & ~(size_t)255;
 }
 
@@ -263,6 +270,7 @@ template <int NW, int D>
 struct FinishSmem {
   float s[NW * 32];
   uint32_t id[NW * 32];
+  float ex[NW * 32];  // exact scores of the list (pre-refined entries)
   float kth[NW];
   float floor[NW];
   float qraw[D];
@@ -361,8 +369,10 @@ constexpr int kSelR = 4;  // candidates per lane in the final selection (128 per
 // 2*margin with the reference arithmetic.  When 32 or more entries, or a
 // block's dropped rows (hdr->floor), reach that threshold, the exact
 // fallback kernel is flagged instead.  QREADY: the caller already filled
-// sm.qd and sm.qn (warp NW-1 then only waits at the barriers).
-template <int D, typename T, bool INL, int NW, bool QREADY = false>
+// sm.qd and sm.qn (warp NW-1 then only waits at the barriers).  PRE: every
+// appended entry already carries its exact score (p.scratch.exact), computed
+// by the block that published it, so no row is read here.
+template <int D, typename T, bool INL, int NW, bool QREADY = false, bool PRE = false>
 __device__ __forceinline__ void final_merge(const Params<T>& p, int q, float margin, bool safe,
                                             int lane, int warp, FinishSmem<NW, D>& sm) {
   static_assert(NW >= 2, "final_merge needs two warps");
@@ -375,14 +385,16 @@ __device__ __forceinline__ void final_merge(const Params<T>& p, int q, float mar
   const int fl = __ldcg(&hdr->floor);
   const bool failed = __ldcg(&hdr->err) != 0;
   const uint2* ents = reinterpret_cast<const uint2*>(p.scratch.entries(q));
-  if (warp == NW - 1) {
-    if constexpr (!QREADY) {
+  const float* exs = p.scratch.exact(q);
+  if (warp == NW - 1 && !PRE) {
+    if constexpr (!QREADY && !PRE) {
       for (int d = lane; d < D; d += 32) sm.qd[d] = (double)sm.qraw[d];
       if (lane == 0) sm.qn = query_norm_seq_t<D>(sm.qraw);
     }
   } else {
+    constexpr int FW = PRE ? NW : NW - 1;  // filtering warps
 #pragma unroll 2
-    for (int i = threadIdx.x; i < nent; i += (NW - 1) * 32) {
+    for (int i = threadIdx.x; i < nent; i += FW * 32) {
       const uint2 e = __ldcg(ents + i);
       const float es = __uint_as_float(e.x);
       if (es >= fthr) {
@@ -390,11 +402,14 @@ __device__ __forceinline__ void final_merge(const Params<T>& p, int q, float mar
         if (slot < NW * 32) {
           sm.s[slot] = es;
           sm.id[slot] = e.y;
+          if constexpr (PRE) sm.ex[slot] = __ldcg(exs + i);
         }
-        const char* rb = reinterpret_cast<const char*>(p.rows + (int64_t)e.y * D);
+        if constexpr (!PRE) {
+          const char* rb = reinterpret_cast<const char*>(p.rows + (int64_t)e.y * D);
 #pragma unroll 1
-        for (int o = 0; o < D * (int)sizeof(T); o += 128)
-          asm volatile("prefetch.global.L1 [%0];" ::"l"(rb + o));
+          for (int o = 0; o < D * (int)sizeof(T); o += 128)
+            asm volatile("prefetch.global.L1 [%0];" ::"l"(rb + o));
+        }
       }
     }
   }
@@ -402,12 +417,13 @@ __device__ __forceinline__ void final_merge(const Params<T>& p, int q, float mar
   const int ncand = sm.ncand;
   const int n = min(ncand, NW * 32);
   if (n > 32 * kSelR) {  // rare: rank sort so the best 32*kSelR come first
-    float cs = -INFINITY;
+    float cs = -INFINITY, cx = -INFINITY;
     uint32_t ci = kNoRow;
     int rank = 0;
     if ((int)threadIdx.x < n) {
       cs = sm.s[threadIdx.x];
       ci = sm.id[threadIdx.x];
+      if constexpr (PRE) cx = sm.ex[threadIdx.x];
 #pragma unroll 1
       for (int j = 0; j < n; ++j) rank += better(sm.s[j], sm.id[j], cs, ci) ? 1 : 0;
     }
@@ -415,18 +431,20 @@ __device__ __forceinline__ void final_merge(const Params<T>& p, int q, float mar
     if ((int)threadIdx.x < n) {
       sm.s[rank] = cs;  // the ranks are a permutation of [0, n)
       sm.id[rank] = ci;
+      if constexpr (PRE) sm.ex[rank] = cx;
     }
     __syncthreads();
   }
   if (warp != 0) return;
   const int m = min(n, 32 * kSelR);
-  float v[kSelR], w[kSelR];
+  float v[kSelR], w[kSelR], xr[kSelR];
   uint32_t vid[kSelR];
 #pragma unroll
   for (int r = 0; r < kSelR; ++r) {
     const int i = r * 32 + lane;
     v[r] = i < m ? sm.s[i] : -INFINITY;
     vid[r] = i < m ? sm.id[i] : kNoRow;
+    xr[r] = (PRE && i < m) ? sm.ex[i] : -INFINITY;
     w[r] = v[r];
   }
   // T_k: remove the best entry k-1 times, then take the best.
@@ -482,6 +500,7 @@ __device__ __forceinline__ void final_merge(const Params<T>& p, int q, float mar
       const int pos = base + __popc(bal & ((1u << lane) - 1u));
       sm.s[pos] = v[r];
       sm.id[pos] = vid[r];
+      if constexpr (PRE) sm.ex[pos] = xr[r];
     }
     base += __popc(bal);
   }
@@ -490,8 +509,12 @@ __device__ __forceinline__ void final_merge(const Params<T>& p, int q, float mar
   const uint32_t ci = lane < base ? sm.id[lane] : kNoRow;
   float es = -INFINITY;
   if (isfinite(cs)) {
-    es = exact_score_tail<D, T, INL>(p.rows + (int64_t)ci * D, sm.qd, sm.qn,
-                                     INL ? 0.0f : __ldg(p.norms + ci));
+    if constexpr (PRE) {
+      es = sm.ex[lane];
+    } else {
+      es = exact_score_tail<D, T, INL>(p.rows + (int64_t)ci * D, sm.qd, sm.qn,
+                                       INL ? 0.0f : __ldg(p.norms + ci));
+    }
   }
   WarpList ex;
   ex.init();
@@ -504,6 +527,7 @@ __device__ __forceinline__ void final_merge(const Params<T>& p, int q, float mar
 }  // namespace grm_b200
 
 #include "mla_batch.cuh"
+#include "mla_int4.cuh"
 
 namespace grm_b200 {
 namespace mla {
@@ -512,10 +536,16 @@ namespace mla {
 // warp list whose k-th score is the largest (a copy: lists are sorted) and
 // the other warps' entries are merged with offer_margin, so the block's k-th
 // approximate score is exact while entries that cannot reach a candidate are
-// skipped.  The block appends its entries within 2*kMargin of its k-th score
-// to the query's published list, raises hdr->lb to that k-th score and
-// hdr->floor to the largest score a row it dropped for lack of room can have.
-// The last block to finish runs final_merge.
+// skipped.  The block raises hdr->lb to its k-th score (atomicMax returns the
+// best k-th published before it), raises hdr->floor to the largest score a
+// row it dropped for lack of room can have, and appends only its entries
+// within 2*kMargin of the larger of the two: hdr->lb only grows and stays a
+// lower bound of the final approximate k-th T_k, so no entry below it can be
+// a final candidate, and blocks that finish late usually append nothing.
+// Before appending, the block recomputes its entries with the reference
+// arithmetic (one entry per lane of warp 0; the reference query norm was
+// computed by warp 1 while the block streamed), so the last block to finish
+// only selects (final_merge<..., PRE>) and reads no row.
 template <int D, typename T, bool INL, int NW>
 __device__ __forceinline__ void scan_finish(const Params<T>& p, WarpList& list, bool safe, int q,
                                             int lane, int warp, FinishSmem<NW, D>& sm) {
@@ -549,17 +579,32 @@ __device__ __forceinline__ void scan_finish(const Params<T>& p, WarpList& list, 
       if (w != wbest)
         m.offer_margin(sm.s[w * 32 + lane], sm.id[w * 32 + lane], lane, p.topk, 2.0f * kMargin);
     const float kth = __shfl_sync(kFull, m.s, p.topk - 1);
-    const float wthr = isfinite(kth) ? kth - 2.0f * kMargin : -INFINITY;
     floor = fmaxf(floor, __shfl_sync(kFull, m.s, 31));
-    const int cnt = __popc(__ballot_sync(kFull, isfinite(m.s) && m.s >= wthr));
-    unsigned at = 0;
-    if (lane == 0) {  // the two maxima need no reply; only the append offset does
-      if (isfinite(kth)) atomicMax(&hdr->lb, float_to_ordered(kth));
+    int lbv = kOrderedNegInf;
+    if (lane == 0) {
+      lbv = isfinite(kth) ? max(atomicMax(&hdr->lb, float_to_ordered(kth)), float_to_ordered(kth))
+                          : __ldcg(&hdr->lb);
       if (isfinite(floor)) atomicMax(&hdr->floor, float_to_ordered(floor));
-      if (cnt) at = atomicAdd(&hdr->nent, (unsigned)cnt);
     }
-    at = __shfl_sync(kFull, at, 0);
-    if (lane < cnt) p.scratch.entries(q)[at + lane] = Entry{m.s, m.id};
+    lbv = __shfl_sync(kFull, lbv, 0);
+    const float pthr = lbv == kOrderedNegInf ? -INFINITY : ordered_to_float(lbv) - 2.0f * kMargin;
+    const bool pub = isfinite(m.s) && m.s >= pthr;
+    const int cnt = __popc(__ballot_sync(kFull, pub));
+    if (cnt) {
+      // lanes 0..cnt-1 hold the published entries (the list is sorted)
+      float es = -INFINITY;
+      if (pub) {
+        es = exact_score_tail<D, T, INL>(p.rows + (int64_t)m.id * D, sm.qd, sm.qn,
+                                         INL ? 0.0f : __ldg(p.norms + m.id));
+      }
+      unsigned at = 0;
+      if (lane == 0) at = atomicAdd(&hdr->nent, (unsigned)cnt);
+      at = __shfl_sync(kFull, at, 0);
+      if (pub) {
+        p.scratch.entries(q)[at + lane] = Entry{m.s, m.id};
+        p.scratch.exact(q)[at + lane] = es;
+      }
+    }
     __syncwarp();
     if (lane == 0) {
       // acq_rel: releases this warp's entries (ordered before by __syncwarp)
@@ -575,7 +620,15 @@ __device__ __forceinline__ void scan_finish(const Params<T>& p, WarpList& list, 
   }
   __syncthreads();
   if (!sm.last) return;
-  final_merge<D, T, INL, NW>(p, q, kMargin, safe, lane, warp, sm);
+  final_merge<D, T, INL, NW, false, true>(p, q, kMargin, safe, lane, warp, sm);
+}
+
+// The reference query (as doubles) and its reference norm for the blocks'
+// exact refine, by one warp while the others stream.
+template <int D, int NW>
+__device__ __forceinline__ void prep_exact_query(FinishSmem<NW, D>& sm, int lane) {
+  for (int d = lane; d < D; d += 32) sm.qd[d] = (double)sm.qraw[d];
+  if (lane == 0) sm.qn = query_norm_seq_t<D>(sm.qraw);
 }
 
 // Approximate streaming pass (one launch per batch of queries: grid.y = query).
@@ -630,6 +683,9 @@ __global__ void __launch_bounds__(kThreads) mla_scan_kernel(const __grid_constan
   __syncthreads();
   const bool safe = sh_safe != 0;
   const float e_q = sh_eq;
+  if constexpr (!MULTI) {
+    if (warp == 1 && safe) prep_exact_query<D, kWarps>(fsm, lane);
+  }
 
   float qr[CPL * E];
 #pragma unroll
@@ -1033,11 +1089,40 @@ __global__ void __launch_bounds__(kBulkWarps * 32, 1)
   __shared__ float sh_eq;
   __shared__ int sh_safe;
 
-  // May be launched as a programmatic dependent of the previous route's
-  // resolve kernel: wait for it (and for the query's producer) first.
-  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int q = blockIdx.y;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  unsigned char* const buf0 = dsmem + (warp * 2) * kHalfBytes;
+  const int64_t groups = ceil_div64(p.nodes, 32);
+  const uint64_t l2_stream = l2_evict_first_policy();
+  // half h of group g -> buffer h (lane 0 only)
+  auto issue = [&](int64_t g, int h) {
+    const int64_t r0 = g * 32 + 16 * h;
+    const int64_t rows = max((int64_t)0, min((int64_t)16, p.nodes - r0));
+    const unsigned bytes = (unsigned)(rows * D * (int64_t)sizeof(T));
+    if (bytes == 0) {
+      mbar_arrive_expect_tx(&sh_bar[warp][h], 0);  // completes the phase at once
+      return;
+    }
+    mbar_arrive_expect_tx(&sh_bar[warp][h], bytes);
+    bulk_g2s_hint(buf0 + h * kHalfBytes, p.rows + r0 * D, bytes, &sh_bar[warp][h], l2_stream);
+  };
+  // The bank is written only when it is created, so each warp starts its
+  // first group's two copies before waiting for the kernel this launch may
+  // depend on (the previous route's resolve kernel, or the query's
+  // producer): the first bytes land while that kernel ends and the query is
+  // normalised.  Scratch and queries are touched only after the wait.
+  const int64_t g_first = (int64_t)blockIdx.x * NW + warp;
+  if (lane == 0) {
+    mbar_init(&sh_bar[warp][0], 1);
+    mbar_init(&sh_bar[warp][1], 1);
+    mbar_fence_init();
+    if (g_first < groups) {
+      issue(g_first, 0);
+      issue(g_first, 1);
+    }
+  }
+  unsigned pending_bits = g_first < groups ? 3u : 0u;  // bit h: a copy into buffer h is in flight
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const float* query = query_ptr(p, q, D);
 
   if (warp == 0) {
@@ -1061,21 +1146,17 @@ __global__ void __launch_bounds__(kBulkWarps * 32, 1)
       sh_eq = safe ? (float)(1.0e-8 / qn) : 0.0f;
     }
   }
-  if (lane == 0) {
-    mbar_init(&sh_bar[warp][0], 1);
-    mbar_init(&sh_bar[warp][1], 1);
-    mbar_fence_init();
-  }
   __syncthreads();
   const bool safe = sh_safe != 0;
   const float e_q = sh_eq;
+  if constexpr (!MULTI) {
+    if (warp == 1 && safe) prep_exact_query<D, NW>(fsm, lane);
+  }
   const int c = lane % L;
   float2 q2[E / 2];
 #pragma unroll
   for (int e = 0; e < E / 2; ++e) q2[e] = make_float2(sh_q[c * E + 2 * e], sh_q[c * E + 2 * e + 1]);
 
-  unsigned char* const buf0 = dsmem + (warp * 2) * kHalfBytes;
-  const int64_t groups = ceil_div64(p.nodes, 32);
   // Static interleaved assignment: warp w of block b takes groups
   // b*NW + w, then every gridDim.x*NW-th group after it, so the warps of the
   // whole grid sweep the bank front to back together.  The last two rounds
@@ -1085,35 +1166,19 @@ __global__ void __launch_bounds__(kBulkWarps * 32, 1)
   const int64_t gstride = (int64_t)gridDim.x * NW;
   const int64_t dyn0 = groups >= 4 * gstride ? (groups / gstride - 2) * gstride : groups;
   unsigned* const next = &p.scratch.hdr(q)->next;
-  const uint64_t l2_stream = l2_evict_first_policy();
-  // half h of group g -> buffer h (lane 0 only)
-  auto issue = [&](int64_t g, int h) {
-    const int64_t r0 = g * 32 + 16 * h;
-    const int64_t rows = max((int64_t)0, min((int64_t)16, p.nodes - r0));
-    const unsigned bytes = (unsigned)(rows * D * (int64_t)sizeof(T));
-    if (bytes == 0) {
-      mbar_arrive_expect_tx(&sh_bar[warp][h], 0);  // completes the phase at once
-      return;
-    }
-    mbar_arrive_expect_tx(&sh_bar[warp][h], bytes);
-    bulk_g2s_hint(buf0 + h * kHalfBytes, p.rows + r0 * D, bytes, &sh_bar[warp][h], l2_stream);
-  };
 
   WarpList list;
   list.init();
   bool failed = false;
   unsigned phase_bits = 0u;    // bit h: parity of the next phase to wait for on buffer h
-  unsigned pending_bits = 0u;  // bit h: a copy into buffer h is in flight
+  if (!safe && pending_bits) {
+    // nothing is streamed for this query: drain the copies started above
+    for (int k = 0; k < 2; ++k) mbar_wait(&sh_bar[warp][k], 0u, kWaitLimit);
+    pending_bits = 0u;
+  }
   if (safe) {
-    int64_t g = (int64_t)blockIdx.x * NW + warp;
+    int64_t g = g_first;
     int64_t gn = g + gstride;
-    if (g < groups) {
-      if (lane == 0) {
-        issue(g, 0);
-        issue(g, 1);
-      }
-      pending_bits = 3u;
-    }
     while (g < groups) {
       // the group after gn: static, or a ticket whose atomic completes while
       // this group is processed
@@ -1533,6 +1598,16 @@ struct grm_b200_mla_bank {
   float* d_cand_s = nullptr;
   unsigned* d_cand_count = nullptr;
   int entry_blocks = 1;
+  // INT4 bulk/refine mode (route_mla_int4), built by the bank's first INT4 route
+  bool q4_ready = false;
+  uint32_t* d_q4 = nullptr;      // biased nibbles, 64-row tiles [tiles][dim / 8][64]
+  float* d_q4ns = nullptr;       // [nodes] norm scales
+  uint32_t* d_q4key = nullptr;   // [nodes] ordered bulk keys of the route in progress
+  uint32_t* d_q4cand = nullptr;  // [nodes] candidate rows
+  uint2* d_q4bnd = nullptr;      // [nodes] boundary (key, row) pairs
+  float* d_q4ex = nullptr;       // [nodes] exact scores of the candidates
+  uint32_t* d_q4tie = nullptr;   // [nodes / 32] tie bitmap (kept zero between routes)
+  grm_b200::mla::Q4Hdr* d_q4hdr = nullptr;
 };
 
 namespace {
@@ -2037,6 +2112,124 @@ int route_device_queries(grm_b200_mla_bank* b, const float* dq, int query_count,
   return 0;
 }
 
+// ---- INT4 bulk/refine mode ---------------------------------------------------
+
+// The INT4 arena and the route buffers, built once per bank on its stream.
+int int4_prepare(grm_b200_mla_bank* b) {
+  if (b->q4_ready) return 0;
+  if (b->multi)
+    return b->err.set(GRM_B200_EINVAL, "the INT4 route mode takes banks of single-row entries");
+  if (b->dim % 8 != 0)
+    return b->err.set(GRM_B200_EINVAL, "the INT4 route mode needs dim %% 8 == 0 (dim %d)", b->dim);
+  const int64_t n = b->nodes;
+  const size_t words = (size_t)ceil_div64(n, kQ4Tile) * kQ4Tile * (size_t)(b->dim / 8);
+  const size_t tie_words = (size_t)ceil_div64(n, 32);
+  cudaError_t e = cudaMalloc(&b->d_q4, words * sizeof(uint32_t));
+  if (e == cudaSuccess) e = cudaMalloc(&b->d_q4ns, (size_t)n * sizeof(float));
+  if (e == cudaSuccess) e = cudaMalloc(&b->d_q4key, (size_t)n * sizeof(uint32_t));
+  if (e == cudaSuccess) e = cudaMalloc(&b->d_q4cand, (size_t)n * sizeof(uint32_t));
+  if (e == cudaSuccess) e = cudaMalloc(&b->d_q4bnd, (size_t)n * sizeof(uint2));
+  if (e == cudaSuccess) e = cudaMalloc(&b->d_q4ex, (size_t)n * sizeof(float));
+  if (e == cudaSuccess) e = cudaMalloc(&b->d_q4tie, tie_words * sizeof(uint32_t));
+  if (e == cudaSuccess) e = cudaMalloc(&b->d_q4hdr, sizeof(Q4Hdr));
+  if (e == cudaSuccess) e = cudaMemsetAsync(b->d_q4tie, 0, tie_words * sizeof(uint32_t), b->stream);
+  if (e == cudaSuccess) e = cudaMemsetAsync(b->d_q4hdr, 0, sizeof(Q4Hdr), b->stream);
+  if (e != cudaSuccess)
+    return b->err.set(cuda_status(e), "INT4 arena allocation failed: %s", cudaGetErrorString(e));
+  DeviceInfo info;
+  int rc = device_info(b->device, &info);
+  if (rc) return b->err.set(rc, "device query failed");
+  const int grid = info.sms * 8;
+  // the bulk kernel holds the query as float2 [dim] beside its 16 KB histogram
+  e = cudaFuncSetAttribute(int4_bulk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)(sizeof(float2) * 4096));
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(int4_refine_kernel<__half>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)(sizeof(double) * 4096));
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(int4_refine_kernel<float>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)(sizeof(double) * 4096));
+  if (e != cudaSuccess)
+    return b->err.set(cuda_status(e), "INT4 kernel set-up failed: %s", cudaGetErrorString(e));
+  if (b->dtype == GRM_B200_F16)
+    int4_arena_kernel<__half><<<grid, 256, 0, b->stream>>>(
+        static_cast<const __half*>(b->d_rows), b->d_norms, n, b->dim, b->d_q4, b->d_q4ns);
+  else
+    int4_arena_kernel<float><<<grid, 256, 0, b->stream>>>(
+        static_cast<const float*>(b->d_rows), b->d_norms, n, b->dim, b->d_q4, b->d_q4ns);
+  e = cudaGetLastError();
+  if (e == cudaSuccess) e = cudaStreamSynchronize(b->stream);
+  if (e != cudaSuccess)
+    return b->err.set(cuda_status(e), "INT4 arena build failed: %s", cudaGetErrorString(e));
+  b->q4_ready = true;
+  return 0;
+}
+
+// Route queries dq[nq, dim] (device) in the INT4 mode on `s`: four kernels
+// per query, each after the first a programmatic dependent of the one before
+// (the first waits for whatever precedes it, including the previous query's
+// refine, which resets the shared header).
+template <typename T>
+int int4_launch(grm_b200_mla_bank* b, const float* dq, int nq, int topk, int64_t refine_m,
+                uint64_t id_offset, Result* results, uint64_t* out_ids, float* out_scores,
+                cudaStream_t s) {
+  DeviceInfo info;
+  int rc = device_info(b->device, &info);
+  if (rc) return rc;
+  const int64_t n = b->nodes;
+  const unsigned M = (unsigned)std::min<int64_t>(std::max<int64_t>(topk, refine_m), n);
+  const int64_t tiles = ceil_div64(n, kQ4Tile);
+  const int bulk_grid = (int)std::max<int64_t>(
+      1, std::min<int64_t>((int64_t)info.sms * 4, ceil_div64(tiles, kQ4BulkThreads / 32)));
+  const int coll_grid = (int)std::max<int64_t>(1, std::min<int64_t>((int64_t)info.sms * 4,
+                                                                    ceil_div64(n, 256)));
+  const int ref_grid = (int)std::max<int64_t>(
+      1, std::min<int64_t>((int64_t)info.sms * 2, ceil_div64(M, kQ4RefThreads)));
+  cudaLaunchAttribute attr[1];
+  for (int q = 0; q < nq; ++q) {
+    const float* qp = dq + (int64_t)q * b->dim;
+    cudaLaunchConfig_t cfg = pdl_config(dim3(bulk_grid), dim3(kQ4BulkThreads),
+                                        sizeof(float2) * (size_t)b->dim, s, attr);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, int4_bulk_kernel, (const uint32_t*)b->d_q4,
+                                       (const float*)b->d_q4ns, n, b->dim, qp, b->d_q4key,
+                                       b->d_q4hdr);
+    if (e == cudaSuccess) {
+      cfg = pdl_config(dim3(coll_grid), dim3(256), 0, s, attr);
+      e = cudaLaunchKernelEx(&cfg, int4_collect_kernel, (const uint32_t*)b->d_q4key, n, M,
+                             b->d_q4hdr, b->d_q4cand, b->d_q4bnd);
+    }
+    if (e == cudaSuccess) {
+      cfg = pdl_config(dim3(1), dim3(kQ4SelThreads), 0, s, attr);
+      e = cudaLaunchKernelEx(&cfg, int4_select_kernel, (const uint2*)b->d_q4bnd, n, M,
+                             b->d_q4hdr, b->d_q4cand, b->d_q4tie);
+    }
+    if (e == cudaSuccess) {
+      cfg = pdl_config(dim3(ref_grid), dim3(kQ4RefThreads), sizeof(double) * (size_t)b->dim, s,
+                       attr);
+      e = cudaLaunchKernelEx(&cfg, int4_refine_kernel<T>, static_cast<const T*>(b->d_rows),
+                             (const float*)b->d_norms, b->dim, qp, (const uint32_t*)b->d_q4cand,
+                             b->d_q4hdr, b->d_q4ex, topk, id_offset,
+                             results ? results + q : nullptr,
+                             out_ids ? out_ids + (int64_t)q * topk : nullptr,
+                             out_scores ? out_scores + (int64_t)q * topk : nullptr);
+    }
+    if (e != cudaSuccess) return cuda_status(e);
+  }
+  return 0;
+}
+
+int int4_launch_any(grm_b200_mla_bank* b, const float* dq, int nq, int topk, int64_t refine_m,
+                    uint64_t id_offset, Result* results, uint64_t* out_ids, float* out_scores,
+                    cudaStream_t s) {
+  return b->dtype == GRM_B200_F16
+             ? int4_launch<__half>(b, dq, nq, topk, refine_m, id_offset, results, out_ids,
+                                   out_scores, s)
+             : int4_launch<float>(b, dq, nq, topk, refine_m, id_offset, results, out_ids,
+                                  out_scores, s);
+}
+
 int bank_finish_create(grm_b200_mla_bank* b) {
   cudaError_t e = cudaStreamCreateWithFlags(&b->stream, cudaStreamNonBlocking);
   if (e == cudaSuccess) e = cudaEventCreate(&b->ev0);
@@ -2090,7 +2283,9 @@ void bank_free(grm_b200_mla_bank* b) {
   grm_b200::policy::policy_free(b->pol);
   if (b->lex_stream) cudaStreamSynchronize(b->lex_stream);
   void* mptrs[] = {b->d_entry_off, b->d_entry_of_row, b->d_entry_best, b->d_blk_s, b->d_blk_id,
-                   b->d_thr, b->d_qn, b->d_unsafe, b->d_cand, b->d_cand_s, b->d_cand_count};
+                   b->d_thr, b->d_qn, b->d_unsafe, b->d_cand, b->d_cand_s, b->d_cand_count,
+                   b->d_q4, b->d_q4ns, b->d_q4key, b->d_q4cand, b->d_q4bnd, b->d_q4ex,
+                   b->d_q4tie, b->d_q4hdr};
   for (void* m : mptrs)
     if (m) cudaFree(m);
   if (b->ev_fork) cudaEventDestroy(b->ev_fork);
@@ -2295,6 +2490,76 @@ int grm_b200_mla_route_device(grm_b200_mla_bank* bank, const float* queries_devi
     return bank->err.set(GRM_B200_EINVAL, "query dim %d does not match bank dim %d", dim, bank->dim);
   return route_device_queries(bank, queries_device, query_count, warmup, topk, out_ids_host,
                               out_scores_host, elapsed_ms);
+}
+
+int grm_b200_mla_route_int4(grm_b200_mla_bank* bank, const float* queries_host, int query_count,
+                            int dim, int topk, int64_t refine_m, uint64_t* out_ids_host,
+                            float* out_scores_host, float* elapsed_ms) {
+  if (!bank) return GRM_B200_EINVAL;
+  std::lock_guard<std::mutex> lock(bank->mu);
+  if (!queries_host || query_count <= 0 || dim != bank->dim || !out_ids_host || topk <= 0 ||
+      topk > GRM_B200_MAX_TOPK || refine_m < 0)
+    return bank->err.set(GRM_B200_EINVAL,
+                         "invalid MLA INT4 route arguments (queries=%d dim=%d topk=%d refine_m=%lld)",
+                         query_count, dim, topk, (long long)refine_m);
+  cudaError_t e = cudaSetDevice(bank->device);
+  if (e != cudaSuccess) return bank->err.set(cuda_status(e), "cudaSetDevice failed");
+  int rc = int4_prepare(bank);
+  if (rc) return rc;
+  if ((rc = reserve(bank, query_count))) return rc;
+  const size_t need = (size_t)query_count * dim;
+  if (need > bank->dq_cap) {
+    if (bank->d_queries) cudaFree(bank->d_queries);
+    bank->d_queries = nullptr;
+    bank->dq_cap = 0;
+    e = cudaMalloc(&bank->d_queries, need * sizeof(float));
+    if (e == cudaSuccess) bank->dq_cap = need;
+  }
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(bank->d_queries, queries_host, need * sizeof(float), cudaMemcpyHostToDevice,
+                        bank->stream);
+  if (e != cudaSuccess)
+    return bank->err.set(cuda_status(e), "MLA query upload failed: %s", cudaGetErrorString(e));
+  cudaEventRecord(bank->ev0, bank->stream);
+  rc = int4_launch_any(bank, bank->d_queries, query_count, topk, refine_m, 0,
+                       bank->d_results_mapped, nullptr, nullptr, bank->stream);
+  if (rc) return bank->err.set(rc, "MLA INT4 route launch failed");
+  cudaEventRecord(bank->ev1, bank->stream);
+  e = cudaStreamSynchronize(bank->stream);
+  if (e != cudaSuccess)
+    return bank->err.set(cuda_status(e), "MLA INT4 route failed: %s", cudaGetErrorString(e));
+  for (int i = 0; i < query_count; ++i) {
+    const Result& r = bank->h_results[i];
+    for (int j = 0; j < topk; ++j) {
+      out_ids_host[(int64_t)i * topk + j] = r.ids[j];
+      if (out_scores_host) out_scores_host[(int64_t)i * topk + j] = r.scores[j];
+    }
+  }
+  float ms = 0.0f;
+  e = cudaEventElapsedTime(&ms, bank->ev0, bank->ev1);
+  if (e != cudaSuccess) return bank->err.set(cuda_status(e), "MLA INT4 route timing failed");
+  if (elapsed_ms) *elapsed_ms = ms;
+  bank->routes += (uint64_t)query_count;
+  return 0;
+}
+
+int grm_b200_mla_route_int4_async(grm_b200_mla_bank* bank, const float* queries_device,
+                                  int query_count, int topk, int64_t refine_m, uint64_t id_offset,
+                                  uint64_t* out_ids_device, float* out_scores_device,
+                                  void* stream) {
+  if (!bank) return GRM_B200_EINVAL;
+  std::lock_guard<std::mutex> lock(bank->mu);
+  if (!queries_device || query_count <= 0 || topk <= 0 || topk > GRM_B200_MAX_TOPK ||
+      refine_m < 0 || (!out_ids_device && !out_scores_device))
+    return bank->err.set(GRM_B200_EINVAL, "invalid MLA INT4 async route arguments");
+  cudaError_t e = cudaSetDevice(bank->device);
+  if (e != cudaSuccess) return bank->err.set(cuda_status(e), "cudaSetDevice failed");
+  int rc = int4_prepare(bank);
+  if (rc) return rc;
+  rc = int4_launch_any(bank, queries_device, query_count, topk, refine_m, id_offset, nullptr,
+                       out_ids_device, out_scores_device, static_cast<cudaStream_t>(stream));
+  if (rc) return bank->err.set(rc, "MLA INT4 async route launch failed");
+  return 0;
 }
 
 }  // extern "C"
