@@ -67,6 +67,8 @@ _SIGS = {
                                        ctypes.c_char_p, ctypes.c_char_p, ctypes.c_char_p,
                                        _P, _P, _P]),
     "grm_b200_mla_route_noalloc": (_I, [_P, _I64, _I, _P, _I, _I, _P, _P, _P]),
+    "grm_b200_mla_route_int4": (_I, [_P, _P, _I, _I, _I, _I64, _P, _P, _P]),
+    "grm_b200_mla_route_int4_async": (_I, [_P, _P, _I, _I, _I64, _U64, _P, _P, _P]),
     "grm_b200_gqa_bank_create": (_I, [_P, _I, _P, _I64, _I, _I, _I, _P]),
     "grm_b200_gqa_bank_create_device": (_I, [_P, _I, _P, _I64, _I, _I, _P]),
     "grm_b200_gqa_route": (_I, [_P, _P, _I, _I, _I, _I, _I, _P, _P, _P]),

@@ -323,6 +323,49 @@ class CudaMLARouteBank:
             devs.append(dev)
         return self._finish(rows, scores, walls, devs, count, warmup, repeats)
 
+    def route_topk_int4(self, queries, *, topk: int, refine_m: int = 4096,
+                        route_repeats: int = 1):
+        """The reference's INT4 bulk/refine mode (route_mla_int4,
+        cpp/grm_runtime.cpp:4363-4482; GRM_ROUTER_INT4=1 with
+        GRM_ROUTER_INT4_REFINE_M=refine_m): exact top-k among the refine_m
+        best INT4 bulk scores.  Returns (node ids [Q, topk], receipt) with the
+        same sentinel law as route_topk; exact scores in ``last_scores``."""
+        if self._h is None:
+            raise RuntimeError("CUDA MLA route bank is closed")
+        q = np.ascontiguousarray(queries, dtype=np.float32)
+        if q.ndim == 1:
+            q = q[None, ...]
+        if q.ndim != 2 or q.shape[1] != self.dim:
+            raise ValueError("query dim does not match rows")
+        if int(topk) <= 0 or int(topk) > MAX_TOPK:
+            raise ValueError(f"topk must be in 1..{MAX_TOPK}")
+        if int(refine_m) < 0:
+            raise ValueError("refine_m must be >= 0")
+        fn = _lib.load().grm_b200_mla_route_int4
+        repeats = max(1, int(route_repeats))
+        walls, devs = [], []
+        rows = scores = None
+        for _ in range(repeats):
+            rows = np.empty((q.shape[0], int(topk)), dtype=np.uint64)
+            scores = np.empty((q.shape[0], int(topk)), dtype=np.float32)
+            elapsed = ctypes.c_float(0.0)
+            t0 = time.perf_counter_ns()
+            rc = fn(self._h, q.ctypes.data, q.shape[0], self.dim, int(topk), int(refine_m),
+                    rows.ctypes.data, scores.ctypes.data, ctypes.byref(elapsed))
+            walls.append((time.perf_counter_ns() - t0) / 1.0e6)
+            _lib.check(rc, self._err)
+            devs.append(float(elapsed.value))
+        return self._finish(rows, scores, walls, devs, q.shape[0], 0, repeats)
+
+    def route_int4_async(self, queries_ptr: int, count: int, topk: int, out_ids_ptr: int,
+                         out_scores_ptr: int, stream: int = 0, id_offset: int = 0,
+                         refine_m: int = 4096) -> None:
+        """Stream-ordered INT4-mode route with device outputs (no host sync)."""
+        rc = _lib.load().grm_b200_mla_route_int4_async(self._h, queries_ptr, count, topk,
+                                                       int(refine_m), id_offset, out_ids_ptr,
+                                                       out_scores_ptr, stream)
+        _lib.check(rc, self._err)
+
     def route_async(self, queries_ptr: int, count: int, topk: int, out_ids_ptr: int,
                     out_scores_ptr: int, stream: int = 0, id_offset: int = 0) -> None:
         """Stream-ordered route with device outputs (no host sync)."""

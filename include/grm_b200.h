@@ -177,6 +177,34 @@ int grm_b200_mla_route_policy(grm_b200_mla_bank* bank, const float* queries_host
                               const char* mutability_filters, uint64_t* out_ids_host,
                               float* out_scores_host, float* elapsed_ms);
 
+/* The reference's INT4 bulk/refine route mode: RouterIndex::route_mla_int4
+ * (cpp/grm_runtime.cpp:4363-4482), which RouterIndex::route selects when
+ * GRM_ROUTER_INT4 is set (:4486-4494); replaces grm_store_route in that mode
+ * for a store of single-row entries routed without lexical keys or filters.
+ * Each row is quantised to INT4 as rebuild_mla_arena does (:3241-3266:
+ * per-row max-abs scale / 7, values in [-7, 7], norm scale = scale / norm),
+ * every row gets the bulk score of int4_mla_row_score (:3568-3585, the default
+ * build's sequential fp32 dot), the refine_m best bulk scores (score desc, row
+ * asc; GRM_ROUTER_INT4_REFINE_M, default 4096; values below topk act as
+ * topk) are rescored with the exact MLA law, and their top-k is returned
+ * (exact scores), bit-exact with the reference's mode.  The INT4 arena (4
+ * bits per value plus ~24 bytes per row of route buffers: ~152 MB at
+ * 1M x 256) is built on the device by the bank's first INT4 call and kept
+ * with the bank.  dim must be a multiple of 8; multi-row banks are refused.
+ * Outputs as grm_b200_mla_route. */
+int grm_b200_mla_route_int4(grm_b200_mla_bank* bank, const float* queries_host, int query_count,
+                            int dim, int topk, int64_t refine_m, uint64_t* out_ids_host,
+                            float* out_scores_host, float* elapsed_ms);
+
+/* The same, stream-ordered with device queries and device outputs (as
+ * grm_b200_mla_route_async; no scratch reservation is needed).  Calls on one
+ * bank must not overlap on the GPU.  No reference counterpart beyond the
+ * mode itself. */
+int grm_b200_mla_route_int4_async(grm_b200_mla_bank* bank, const float* queries_device,
+                                  int query_count, int topk, int64_t refine_m,
+                                  uint64_t id_offset, uint64_t* out_ids_device,
+                                  float* out_scores_device, void* stream);
+
 /* Which kernels serve this bank (no reference counterpart; for tests and
  * diagnostics): GRM_B200_PATH_* bits. */
 #define GRM_B200_PATH_BULK 1   /* single queries: bulk-copy streaming scan */

@@ -16,6 +16,10 @@
  *               sequential dot, score = float(dot / (qnorm*norm + 1e-8))),
  *               :4299-4361 (route_mla_arena: drop non-finite, sort),
  *               :75-82 (score_node_better: score desc, node id asc).
+ *   MLA INT4    cpp/grm_runtime.cpp:3241-3266 (INT4 arena: per-row max-abs
+ *               scale, values clamped to [-7, 7]), :3568-3585
+ *               (int4_mla_row_score, default non-OpenMP build: sequential fp32),
+ *               :4363-4482 (route_mla_int4: top-M bulk, exact refine).
  *   GQA route   cpp/grm_runtime.cpp:3588-3671 (gqa_arena_key_score, general
  *               path: fp32 sequential dot, best = std::max(best, |dot|*inv),
  *               total += best over heads, total / H), :3673-3739 (the
@@ -174,6 +178,107 @@ ORC_API int64_t orc_mla_route(const float* rows, const float* norms, int64_t n, 
   orc_mla_scores(rows, norms, n, dim, q, scores);
   const int64_t got = orc_topk(scores, NULL, n, topk, out_ids, out_scores);
   free(scores);
+  return got;
+}
+
+/* ------------------------------------------------------------ MLA, INT4 mode */
+
+static inline float std_min_f(float a, float b) { return (b < a) ? b : a; }  /* std::min */
+static inline float std_max_f(float a, float b) { return (a < b) ? b : a; }  /* std::max */
+
+/* The INT4 part of rebuild_mla_arena (cpp/grm_runtime.cpp:3241-3266), per
+ * row: max |v| over the row (std::max, so NaN values are skipped), scale =
+ * max_abs > 0 ? max_abs / 7 : 1, value_d = int8(clamp(round(v_d / scale),
+ * -7, 7)) with std::round (half away from zero) and std::min / std::max
+ * (a NaN quotient becomes 7), norm_scale = scale * (norm > 0 ? 1 / norm : 0)
+ * with the row's fp32 norm. */
+ORC_API void orc_mla_int4_arena(const float* rows, const float* norms, int64_t n, int64_t dim,
+                                int8_t* values, float* norm_scales) {
+#pragma omp parallel for schedule(static)
+  for (int64_t i = 0; i < n; ++i) {
+    const float* r = rows + i * dim;
+    float max_abs = 0.0f;
+    for (int64_t d = 0; d < dim; ++d) max_abs = std_max_f(max_abs, fabsf(r[d]));
+    const float norm = norms[i];
+    const float inv_norm = norm > 0.0f ? 1.0f / norm : 0.0f;
+    const float scale = max_abs > 0.0f ? max_abs / 7.0f : 1.0f;
+    norm_scales[i] = scale * inv_norm;
+    for (int64_t d = 0; d < dim; ++d)
+      values[i * dim + d] = (int8_t)std_max_f(-7.0f, std_min_f(7.0f, roundf(r[d] / scale)));
+  }
+}
+
+/* int4_mla_row_score (cpp/grm_runtime.cpp:3568-3585) as the default build
+ * (no OpenMP) computes it: dot_i4 += q_d * float(value_d) in fp32, element
+ * order; score = dot_i4 * norm_scale * float(1 / (qnorm + 1e-8)); then the
+ * route's `score += lexical_bonus` (0 without lexical keys, :4401-4402). */
+ORC_API void orc_mla_int4_scores(const int8_t* values, const float* norm_scales, int64_t n,
+                                 int64_t dim, const float* q, float* out) {
+  const double qnorm = orc_mla_query_norm(q, dim);
+  const float qinv = (float)(1.0 / (qnorm + 1.0e-8));
+#pragma omp parallel for schedule(static)
+  for (int64_t i = 0; i < n; ++i) {
+    const int8_t* v = values + i * dim;
+    float dot = 0.0f;
+    for (int64_t d = 0; d < dim; ++d) dot += q[d] * (float)v[d];
+    float s = dot * norm_scales[i] * qinv;
+    s += 0.0f;
+    out[i] = s;
+  }
+}
+
+static int pair_better(const void* a, const void* b) {
+  const orc_pair* x = (const orc_pair*)a;
+  const orc_pair* y = (const orc_pair*)b;
+  if (better(x->s, x->id, y->s, y->id)) return -1;
+  if (better(y->s, y->id, x->s, x->id)) return 1;
+  return 0;
+}
+
+/* route_mla_int4 (cpp/grm_runtime.cpp:4363-4482) for single-row entries
+ * without lexical keys or filters: the M = max(topk, refine_m) best finite
+ * bulk scores by (score desc, node id asc) -- every finite one when M >= n --
+ * are rescored with exact_mla_entry_score; the top-k of those finite exact
+ * scores, ordered by score_node_better.  Returns the number placed. */
+ORC_API int64_t orc_mla_int4_route(const float* rows, const float* norms, int64_t n, int64_t dim,
+                                   const float* q, int64_t topk, int64_t refine_m,
+                                   uint64_t* out_ids, float* out_scores) {
+  int8_t* values = (int8_t*)malloc((size_t)(n > 0 ? n : 1) * (size_t)dim);
+  float* ns = (float*)malloc(sizeof(float) * (size_t)(n > 0 ? n : 1));
+  float* bulk = (float*)malloc(sizeof(float) * (size_t)(n > 0 ? n : 1));
+  orc_pair* cand = (orc_pair*)malloc(sizeof(orc_pair) * (size_t)(n > 0 ? n : 1));
+  orc_mla_int4_arena(rows, norms, n, dim, values, ns);
+  orc_mla_int4_scores(values, ns, n, dim, q, bulk);
+  int64_t nc = 0;
+  for (int64_t i = 0; i < n; ++i)
+    if (isfinite(bulk[i])) {
+      cand[nc].s = bulk[i];
+      cand[nc].id = (uint64_t)i;
+      ++nc;
+    }
+  const int64_t m = refine_m > topk ? refine_m : topk;
+  if (m < nc) {
+    qsort(cand, (size_t)nc, sizeof(orc_pair), pair_better);
+    nc = m;
+  }
+  const double qnorm = orc_mla_query_norm(q, dim);
+  float* ex = (float*)malloc(sizeof(float) * (size_t)(nc > 0 ? nc : 1));
+  uint64_t* ids = (uint64_t*)malloc(sizeof(uint64_t) * (size_t)(nc > 0 ? nc : 1));
+  for (int64_t c = 0; c < nc; ++c) {
+    const int64_t i = (int64_t)cand[c].id;
+    const float* r = rows + i * dim;
+    double dot = 0.0;
+    for (int64_t d = 0; d < dim; ++d) dot += (double)q[d] * (double)r[d];
+    ex[c] = (float)(dot / ((qnorm * (double)norms[i]) + 1.0e-8));
+    ids[c] = (uint64_t)i;
+  }
+  const int64_t got = topk_select(ex, ids, nc, topk, out_ids, out_scores);
+  free(values);
+  free(ns);
+  free(bulk);
+  free(cand);
+  free(ex);
+  free(ids);
   return got;
 }
 

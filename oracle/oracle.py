@@ -40,7 +40,7 @@ __all__ = [
     "quant_ref", "dequant_ref", "quant_packed", "dequant_packed", "packed_group_bytes",
     "mount_scatter", "mount_rope", "swap_splice",
     "ROUTE_DEFAULTS", "split_keys", "route_allowed", "lexical_hits", "mla_route_policy",
-    "gqa_route_policy", "mla_route_multi",
+    "gqa_route_policy", "mla_route_multi", "mla_int4_arena", "mla_int4_scores", "mla_int4_route",
 ]
 
 _P = ctypes.c_void_p
@@ -85,6 +85,12 @@ def lib() -> ctypes.CDLL:
         L.orc_mla_query_norm.restype = ctypes.c_double
         L.orc_mla_scores.argtypes = [_P, _P, _I64, _I64, _P, _P]
         L.orc_mla_scores.restype = None
+        L.orc_mla_int4_arena.argtypes = [_P, _P, _I64, _I64, _P, _P]
+        L.orc_mla_int4_arena.restype = None
+        L.orc_mla_int4_scores.argtypes = [_P, _P, _I64, _I64, _P, _P]
+        L.orc_mla_int4_scores.restype = None
+        L.orc_mla_int4_route.argtypes = [_P, _P, _I64, _I64, _P, _I64, _I64, _P, _P]
+        L.orc_mla_int4_route.restype = _I64
         L.orc_topk.argtypes = [_P, _P, _I64, _I64, _P, _P]
         L.orc_topk.restype = _I64
         L.orc_gqa_scores.argtypes = [_P, _P, _I64, _I64, _I64, _P, _I64, _I64, _P]
@@ -173,6 +179,40 @@ def mla_route(rows, query, k: int, norms=None) -> tuple[np.ndarray, np.ndarray]:
     """Exact reference MLA route: (ids uint64[k] with UINT64_MAX fill, scores)."""
     ids, s, _ = topk(mla_scores(rows, query, norms), k)
     return ids, s
+
+
+def mla_int4_arena(rows, norms=None) -> tuple[np.ndarray, np.ndarray]:
+    """The reference's INT4 route arena (cpp/grm_runtime.cpp:3241-3266):
+    (int8 values [n, dim] in [-7, 7], fp32 norm scales [n])."""
+    r = np.ascontiguousarray(rows, dtype=np.float32)
+    nrm = mla_row_norms(r) if norms is None else np.ascontiguousarray(norms, dtype=np.float32)
+    vals = np.empty(r.shape, dtype=np.int8)
+    ns = np.empty(r.shape[0], dtype=np.float32)
+    lib().orc_mla_int4_arena(_ptr(r), _ptr(nrm), r.shape[0], r.shape[1], _ptr(vals), _ptr(ns))
+    return vals, ns
+
+
+def mla_int4_scores(rows, query, norms=None) -> np.ndarray:
+    """Bulk INT4 scores of every row (int4_mla_row_score, default build)."""
+    vals, ns = mla_int4_arena(rows, norms)
+    q = np.ascontiguousarray(query, dtype=np.float32).reshape(-1)
+    out = np.empty(vals.shape[0], dtype=np.float32)
+    lib().orc_mla_int4_scores(_ptr(vals), _ptr(ns), vals.shape[0], vals.shape[1], _ptr(q),
+                              _ptr(out))
+    return out
+
+
+def mla_int4_route(rows, query, k: int, refine_m: int = 4096, norms=None):
+    """route_mla_int4 (cpp/grm_runtime.cpp:4363-4482): exact top-k among the
+    refine_m best INT4 bulk scores.  (ids uint64[k], exact scores)."""
+    r = np.ascontiguousarray(rows, dtype=np.float32)
+    nrm = mla_row_norms(r) if norms is None else np.ascontiguousarray(norms, dtype=np.float32)
+    q = np.ascontiguousarray(query, dtype=np.float32).reshape(-1)
+    ids = np.empty(k, dtype=np.uint64)
+    sc = np.empty(k, dtype=np.float32)
+    lib().orc_mla_int4_route(_ptr(r), _ptr(nrm), r.shape[0], r.shape[1], _ptr(q), k,
+                             int(refine_m), _ptr(ids), _ptr(sc))
+    return ids, sc
 
 
 def mla_route_multi(rows, entry_row_offsets, query, k: int, norms=None):

@@ -170,3 +170,50 @@ def test_config4_longest_nodes_equal_reference_runtime():
     with O.RefStore().load_gqa(keys, off, 32, 128) as st:
         want = st.route(q, 5)
     assert [int(x) for x in ids] == want
+
+
+@pytest.mark.parametrize("seed,n,dim,m", [(51, 3000, 256, 200), (52, 1500, 64, 64),
+                                          (53, 800, 128, 5000), (54, 5000, 256, 4096)])
+def test_mla_int4_restatement_equals_reference_runtime(seed, n, dim, m, monkeypatch):
+    """The INT4 bulk/refine route (GRM_ROUTER_INT4=1, route_mla_int4,
+    cpp/grm_runtime.cpp:4363-4482) of the reference runtime's default build
+    against the restatement: fp16-valued rows (duplicate rows, a NaN row, an
+    Inf row, a zero row), refine sets smaller than, equal to and larger than
+    the bank."""
+    rng = np.random.default_rng(seed)
+    rows = rng.standard_normal((n, dim)).astype(np.float32)
+    rows /= np.linalg.norm(rows, axis=1, keepdims=True)
+    rows = rows.astype(np.float16).astype(np.float32)
+    rows[::97] = rows[3]
+    rows[5, 1] = np.nan
+    rows[6, 2] = np.inf
+    rows[7] = 0.0
+    qs = rng.standard_normal((5, dim)).astype(np.float32)
+    qs[1] = rows[3]
+    qs[2] *= 1e-6
+    monkeypatch.setenv("GRM_ROUTER_INT4", "1")
+    monkeypatch.setenv("GRM_ROUTER_INT4_REFINE_M", str(m))
+    with O.RefStore().load_mla(rows) as st:
+        for q in qs:
+            for k in (1, 3, 16):
+                ids, _ = O.mla_int4_route(rows, q, k, refine_m=m)
+                want = st.route(q, k)
+                got = [int(x) for x in ids if x != np.iinfo(np.uint64).max]
+                assert got == want, (k, got, want)
+
+
+def test_mla_int4_mode_differs_from_the_exact_route():
+    """With a small refine set the INT4 mode's answer can differ from the exact
+    route (the bulk pass decides which rows are refined): the restatement must
+    reproduce that, not the exact answer."""
+    rng = np.random.default_rng(55)
+    n, dim = 20_000, 64
+    rows = rng.standard_normal((n, dim)).astype(np.float32)
+    norms = O.mla_row_norms(rows)
+    diffs = 0
+    for _ in range(20):
+        q = rng.standard_normal(dim).astype(np.float32)
+        a, _ = O.mla_int4_route(rows, q, 16, refine_m=16, norms=norms)
+        b, _ = O.mla_route(rows, q, 16, norms=norms)
+        diffs += int(not np.array_equal(a, b))
+    assert diffs > 0
