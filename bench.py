@@ -93,7 +93,7 @@ def parse():
     p.add_argument("--workload", default="mla_1m_b1",
                    choices=["mla_1m_b1", "mla_1m_b64", "gqa_512", "gqa_100k", "mount_int4",
                             "mount_int6", "mount_int8", "mount_ref8", "mount_int4_rope",
-                            "mount_ref8_rope", "mla_1m_policy", "mla_1m_multi"],
+                            "mount_ref8_rope", "mla_1m_policy", "mla_1m_multi", "mla_1m_int4"],
                    help="mla_1m_b1 is the headline (BASELINE config 2); the others measure "
                         "the GQA route (configs 3/4) and the quantised mount (config 5)")
     return p.parse_args()
@@ -1037,6 +1037,117 @@ def run_policy(args):
     }), flush=True)
 
 
+def run_int4(args):
+    """The reference's INT4 bulk/refine mode (route_mla_int4) on config 2's
+    bank: a step is one probe through grm_b200_mla_route_int4_async (device
+    query in, device ids out) with the reference's default refine set (4,096
+    rows).  The INT4 arena (~134 MB) barely exceeds L2, so L2 is flushed
+    before every step, outside the step's events.  The bank and arena are
+    built during warm-up (the arena by the first INT4 route)."""
+    import torch
+
+    import oracle as O
+    from graftrepository_b200.cuda_router import CudaMLARouteSidecar
+
+    world, rank, local = _dist_setup()
+    M = 4096
+    n_q = max(8, min(args.warmup + args.steps, 4096))
+    rows16, qs = mla_inputs(n_q)
+    shard = torch.from_numpy(rows16).cuda()
+    bank = CudaMLARouteSidecar(device=local).create_bank_device(shard.data_ptr(), 1, NODES, DIM)
+    del shard
+    qs_host = torch.from_numpy(qs).pin_memory()
+    qd = qs_host.cuda()
+    oi = torch.empty((1, TOPK), dtype=torch.int64, device="cuda")
+    osc = torch.empty((1, TOPK), dtype=torch.float32, device="cuda")
+    stream = torch.cuda.current_stream()
+    flush = torch.empty(2 * L2_BYTES, dtype=torch.uint8, device="cuda")
+
+    def step(i):
+        bank.route_int4_async(qd[i % n_q].data_ptr(), 1, TOPK, oi.data_ptr(), osc.data_ptr(),
+                              stream.cuda_stream, 0, M)
+
+    for i in range(args.warmup):
+        l2_flush(flush)
+        step(i)
+    torch.cuda.synchronize()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(args.steps)]
+    with ClockSampler(local) as clk:
+        for i in range(args.steps):
+            l2_flush(flush)
+            evs[i][0].record(stream)
+            step(args.warmup + i)
+            evs[i][1].record(stream)
+        torch.cuda.synchronize()
+    step_ms = [e[0].elapsed_time(e[1]) for e in evs]
+    last_i = oi.cpu().numpy().view(np.uint64)[0].copy()
+    last_s = osc.cpu().numpy()[0].copy()
+    last_q = qs[(args.warmup + args.steps - 1) % n_q]
+    walls = []
+    e2e_steps = min(args.steps, 200)
+    for i in range(e2e_steps):
+        t0 = time.perf_counter()
+        bank.route_topk_int4(qs[(args.warmup + i) % n_q], topk=TOPK, refine_m=M)
+        walls.append(time.perf_counter() - t0)
+    rows = rows16.astype(np.float32)
+    norms = O.mla_row_norms(rows)
+    want, want_s = O.mla_int4_route(rows, last_q, TOPK, refine_m=M, norms=norms)
+    if not (np.array_equal(last_i, want) and np.array_equal(last_s, want_s)):
+        raise RuntimeError(f"timed INT4 route {last_i} {last_s} != restatement {want} {want_s}")
+    cpu = None
+    if rank == 0 and not args.no_cpu_baseline and O.ref_available(omp=True):
+        os.environ["GRM_ROUTER_INT4"] = "1"
+        os.environ["GRM_ROUTER_INT4_REFINE_M"] = str(M)
+        with O.RefStore(omp=True).load_mla(rows) as st:
+            st.route(qs[0], TOPK)
+            ts = []
+            t_end = time.perf_counter() + 8.0
+            i = 1
+            while (time.perf_counter() < t_end or len(ts) < 3) and len(ts) < 64:
+                t0 = time.perf_counter()
+                st.route(qs[i % n_q], TOPK)
+                ts.append(time.perf_counter() - t0)
+                i += 1
+        del os.environ["GRM_ROUTER_INT4"]
+        cpu = {"value": 1.0 / statistics.median(ts), "unit": UNIT,
+               "cores": len(os.sched_getaffinity(0)), "kind": "reference",
+               "sample": f"grm_store_route with GRM_ROUTER_INT4=1 (route_mla_int4, OpenMP) over "
+                         f"the full bank, median of {len(ts)} probes "
+                         f"({statistics.median(ts) * 1e3:.1f} ms)"}
+    bank.close()
+    peak, peak_kind = peaks()
+    mean_ms = statistics.mean(step_ms)
+    algo = NODES * DIM // 2 + 3 * 4 * NODES + M * DIM * 2
+    achieved = algo / (mean_ms / 1e3) / 1e9
+    if rank != 0:
+        return
+    print(json.dumps({
+        "metric": "1M-node MLA route, INT4 bulk/refine mode (route_mla_int4, refine set 4,096)",
+        "value": 1.0 / (mean_ms / 1e3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": mean_ms, "higher_is_better": True,
+        "scaling": "replicas", "vs_baseline": None,
+        "dtype": "INT4 values, f32 sequential bulk dot, f64 exact refine", "data": "synthetic",
+        "config": {"workload": "mla_1m_int4", "nodes": NODES, "dim": DIM, "topk": TOPK,
+                   "refine_m": M, "recipe": "synth.mla_config(1)",
+                   "l2": "256 MB L2 flush (written, then read back) before every step, outside "
+                         "the step's events"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "peak_kind": peak_kind,
+                     "algorithmic_bytes_per_launch": algo, "traffic": None,
+                     "note": "packed INT4 arena + norm scales + bulk keys written and read + "
+                             "the refine set's fp16 rows, over the whole route's device time "
+                             "(4 kernels)"},
+        "parity_checked": 1,
+        "parity": "last timed step: ids and scores == the INT4-mode restatement",
+        "cpu_baseline": cpu,
+        "e2e": {"value": len(walls) / sum(walls), "unit": UNIT,
+                "h2d_bytes_per_step": DIM * 4, "d2h_bytes_per_step": TOPK * 12,
+                "api": "CudaMLARouteBank.route_topk_int4"},
+        "step_us_p50": statistics.median(step_ms) * 1e3, "gpu_launches": 4 * args.steps,
+        "clocks": clk.summary(),
+    }), flush=True)
+
+
 def run_multi(args):
     """Multi-row entries: the 1,048,576 x 256 fp16 rows of config 2 grouped
     into entries of 1..4 rows (a digest's centroid and child centroids), an
@@ -1130,6 +1241,8 @@ def main():
         run_policy(args)
     elif args.workload == "mla_1m_multi":
         run_multi(args)
+    elif args.workload == "mla_1m_int4":
+        run_int4(args)
     else:
         run_ours(args)
 

@@ -76,8 +76,20 @@ def test_edge_rows_and_queries(sidecar):
     qs[3] *= 1e-12
     qs[4, 9] = np.nan
     bank = sidecar.create_bank(rows)
-    assert bank.dtype == 0     # the Inf/NaN rows keep the bank fp32
     for k, m in ((3, 4096), (16, 50), (8, 8)):
+        _check(bank, rows, qs, k, m)
+    bank.close()
+
+
+def test_fp32_bank(sidecar):
+    """Values that fp16 cannot hold keep the bank fp32 (both the INT4 arena
+    build and the exact refine read fp32 rows)."""
+    rng = np.random.default_rng(65)
+    rows = rng.standard_normal((7_000, 128)).astype(np.float32)
+    qs = rng.standard_normal((3, 128)).astype(np.float32)
+    bank = sidecar.create_bank(rows)
+    assert bank.dtype == 0
+    for k, m in ((3, 4096), (16, 100)):
         _check(bank, rows, qs, k, m)
     bank.close()
 
