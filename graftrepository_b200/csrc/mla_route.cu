@@ -1605,8 +1605,10 @@ struct grm_b200_mla_bank {
   uint32_t* d_q4key = nullptr;   // [nodes] ordered bulk keys of the route in progress
   uint32_t* d_q4cand = nullptr;  // [nodes] candidate rows
   uint2* d_q4bnd = nullptr;      // [nodes] boundary (key, row) pairs
-  float* d_q4ex = nullptr;       // [nodes] exact scores of the candidates
   uint32_t* d_q4tie = nullptr;   // [nodes / 32] tie bitmap (kept zero between routes)
+  float* d_q4slot_s = nullptr;   // [refine blocks * 32] per-block top entries
+  uint32_t* d_q4slot_id = nullptr;
+  int q4_slots = 0;              // refine blocks the slots hold
   grm_b200::mla::Q4Hdr* d_q4hdr = nullptr;
 };
 
@@ -2122,14 +2124,19 @@ int int4_prepare(grm_b200_mla_bank* b) {
   if (b->dim % 8 != 0)
     return b->err.set(GRM_B200_EINVAL, "the INT4 route mode needs dim %% 8 == 0 (dim %d)", b->dim);
   const int64_t n = b->nodes;
-  const size_t words = (size_t)ceil_div64(n, kQ4Tile) * kQ4Tile * (size_t)(b->dim / 8);
+  const size_t words = (size_t)ceil_div64(n, kQ4Tile) * kQ4Tile * 4 * (size_t)q4_quads(b->dim);
   const size_t tie_words = (size_t)ceil_div64(n, 32);
+  DeviceInfo dinfo;
+  if (int drc = device_info(b->device, &dinfo)) return b->err.set(drc, "device query failed");
+  b->q4_slots = dinfo.sms * 2;
   cudaError_t e = cudaMalloc(&b->d_q4, words * sizeof(uint32_t));
+  if (e == cudaSuccess) e = cudaMalloc(&b->d_q4slot_s, sizeof(float) * 32 * (size_t)b->q4_slots);
+  if (e == cudaSuccess)
+    e = cudaMalloc(&b->d_q4slot_id, sizeof(uint32_t) * 32 * (size_t)b->q4_slots);
   if (e == cudaSuccess) e = cudaMalloc(&b->d_q4ns, (size_t)n * sizeof(float));
   if (e == cudaSuccess) e = cudaMalloc(&b->d_q4key, (size_t)n * sizeof(uint32_t));
   if (e == cudaSuccess) e = cudaMalloc(&b->d_q4cand, (size_t)n * sizeof(uint32_t));
   if (e == cudaSuccess) e = cudaMalloc(&b->d_q4bnd, (size_t)n * sizeof(uint2));
-  if (e == cudaSuccess) e = cudaMalloc(&b->d_q4ex, (size_t)n * sizeof(float));
   if (e == cudaSuccess) e = cudaMalloc(&b->d_q4tie, tie_words * sizeof(uint32_t));
   if (e == cudaSuccess) e = cudaMalloc(&b->d_q4hdr, sizeof(Q4Hdr));
   if (e == cudaSuccess) e = cudaMemsetAsync(b->d_q4tie, 0, tie_words * sizeof(uint32_t), b->stream);
@@ -2142,15 +2149,15 @@ int int4_prepare(grm_b200_mla_bank* b) {
   const int grid = info.sms * 8;
   // the bulk kernel holds the query as float2 [dim] beside its 16 KB histogram
   e = cudaFuncSetAttribute(int4_bulk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           (int)(sizeof(float2) * 4096));
+                           (int)(sizeof(float4) * 16 * q4_quads(4096)));
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(int4_refine_kernel<__half>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)(sizeof(double) * 4096));
+                             (int)(sizeof(double) * 4096) + kQ4StageMax);
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(int4_refine_kernel<float>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)(sizeof(double) * 4096));
+                             (int)(sizeof(double) * 4096) + kQ4StageMax);
   if (e != cudaSuccess)
     return b->err.set(cuda_status(e), "INT4 kernel set-up failed: %s", cudaGetErrorString(e));
   if (b->dtype == GRM_B200_F16)
@@ -2182,22 +2189,28 @@ int int4_launch(grm_b200_mla_bank* b, const float* dq, int nq, int topk, int64_t
   const unsigned M = (unsigned)std::min<int64_t>(std::max<int64_t>(topk, refine_m), n);
   const int64_t tiles = ceil_div64(n, kQ4Tile);
   const int bulk_grid = (int)std::max<int64_t>(
-      1, std::min<int64_t>((int64_t)info.sms * 4, ceil_div64(tiles, kQ4BulkThreads / 32)));
-  const int coll_grid = (int)std::max<int64_t>(1, std::min<int64_t>((int64_t)info.sms * 4,
-                                                                    ceil_div64(n, 256)));
+      1, std::min<int64_t>((int64_t)info.sms * 6, ceil_div64(tiles, kQ4BulkThreads / 32)));
+  const int coll_grid = (int)std::max<int64_t>(
+      1, std::min<int64_t>((int64_t)info.sms * 2, ceil_div64(n, kQ4Chunk)));
   const int ref_grid = (int)std::max<int64_t>(
-      1, std::min<int64_t>((int64_t)info.sms * 2, ceil_div64(M, kQ4RefThreads)));
+      1, std::min<int64_t>((int64_t)b->q4_slots, ceil_div64(M, kQ4RefThreads)));
+  // candidate rows staged in shared memory when 32 padded rows per warp fit
+  const size_t row_vecs = (size_t)b->dim * (b->dtype == GRM_B200_F16 ? 2 : 4) / 16 + 1;
+  const size_t stage_bytes = (size_t)(kQ4RefThreads / 32) * 32 * row_vecs * 16;
+  const int stage = stage_bytes <= (size_t)kQ4StageMax ? 1 : 0;
+  const size_t ref_smem = (((size_t)8 * b->dim + 15) & ~(size_t)15) + (stage ? stage_bytes : 0);
   cudaLaunchAttribute attr[1];
   for (int q = 0; q < nq; ++q) {
     const float* qp = dq + (int64_t)q * b->dim;
     cudaLaunchConfig_t cfg = pdl_config(dim3(bulk_grid), dim3(kQ4BulkThreads),
-                                        sizeof(float2) * (size_t)b->dim, s, attr);
-    cudaError_t e = cudaLaunchKernelEx(&cfg, int4_bulk_kernel, (const uint32_t*)b->d_q4,
+                                        sizeof(float4) * 16 * (size_t)q4_quads(b->dim), s, attr);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, int4_bulk_kernel,
+                                       reinterpret_cast<const uint4*>(b->d_q4),
                                        (const float*)b->d_q4ns, n, b->dim, qp, b->d_q4key,
-                                       b->d_q4hdr);
+                                       b->d_q4hdr, M);
     if (e == cudaSuccess) {
-      cfg = pdl_config(dim3(coll_grid), dim3(256), 0, s, attr);
-      e = cudaLaunchKernelEx(&cfg, int4_collect_kernel, (const uint32_t*)b->d_q4key, n, M,
+      cfg = pdl_config(dim3(coll_grid), dim3(kQ4CollThreads), 0, s, attr);
+      e = cudaLaunchKernelEx(&cfg, int4_collect_kernel, (const uint32_t*)b->d_q4key, n,
                              b->d_q4hdr, b->d_q4cand, b->d_q4bnd);
     }
     if (e == cudaSuccess) {
@@ -2206,14 +2219,13 @@ int int4_launch(grm_b200_mla_bank* b, const float* dq, int nq, int topk, int64_t
                              b->d_q4hdr, b->d_q4cand, b->d_q4tie);
     }
     if (e == cudaSuccess) {
-      cfg = pdl_config(dim3(ref_grid), dim3(kQ4RefThreads), sizeof(double) * (size_t)b->dim, s,
-                       attr);
+      cfg = pdl_config(dim3(ref_grid), dim3(kQ4RefThreads), ref_smem, s, attr);
       e = cudaLaunchKernelEx(&cfg, int4_refine_kernel<T>, static_cast<const T*>(b->d_rows),
                              (const float*)b->d_norms, b->dim, qp, (const uint32_t*)b->d_q4cand,
-                             b->d_q4hdr, b->d_q4ex, topk, id_offset,
+                             b->d_q4hdr, b->d_q4slot_s, b->d_q4slot_id, topk, id_offset,
                              results ? results + q : nullptr,
                              out_ids ? out_ids + (int64_t)q * topk : nullptr,
-                             out_scores ? out_scores + (int64_t)q * topk : nullptr);
+                             out_scores ? out_scores + (int64_t)q * topk : nullptr, stage);
     }
     if (e != cudaSuccess) return cuda_status(e);
   }
@@ -2284,8 +2296,8 @@ void bank_free(grm_b200_mla_bank* b) {
   if (b->lex_stream) cudaStreamSynchronize(b->lex_stream);
   void* mptrs[] = {b->d_entry_off, b->d_entry_of_row, b->d_entry_best, b->d_blk_s, b->d_blk_id,
                    b->d_thr, b->d_qn, b->d_unsafe, b->d_cand, b->d_cand_s, b->d_cand_count,
-                   b->d_q4, b->d_q4ns, b->d_q4key, b->d_q4cand, b->d_q4bnd, b->d_q4ex,
-                   b->d_q4tie, b->d_q4hdr};
+                   b->d_q4, b->d_q4ns, b->d_q4key, b->d_q4cand, b->d_q4bnd,
+                   b->d_q4tie, b->d_q4slot_s, b->d_q4slot_id, b->d_q4hdr};
   for (void* m : mptrs)
     if (m) cudaFree(m);
   if (b->ev_fork) cudaEventDestroy(b->ev_fork);
