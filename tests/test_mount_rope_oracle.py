@@ -5,7 +5,10 @@ reference's rotation of the positional key part at the mount seats
 x' = pair_swap(x), out = bf16(x' * cos[pos] + rotate_half(x') * sin[pos]).
 `apply_rotary` lives in the reference's compiled tensor library, which is not
 part of the reference tree, so the restatement follows the standard
-rotate-half form the Python fallback calls."""
+rotate-half form the Python fallback calls.  The same law as the reference
+writes it in Python (rope / rope_tables of tests/gemma4_int4_sim.py:60-76 and
+_deepseek_rope_prep of core/deepseek_v2_lite_tc.py:99-103), executed by
+tests/golden/make_rope_golden.py, pins the oracle to a stated tolerance."""
 
 import numpy as np
 import pytest
@@ -115,3 +118,51 @@ def test_oracle_rope_rejects_seats_past_the_tables():
     cos, sin = graft_mount.rope_tables(50, 32)
     with pytest.raises(ValueError):
         O.mount_rope(arena, 1, 1, 8, [45], cos, sin, 256, 32)
+
+
+GOLDEN = __import__("pathlib").Path(__file__).resolve().parent / "golden" / "rope_law.npz"
+
+
+@pytest.mark.parametrize("name", ["mla_kpe", "gqa_k", "p_rope"])
+def test_oracle_rope_matches_the_reference_rotary_functions(name):
+    """orc_mount_rope against the reference's own rotation law, executed by
+    tests/golden/make_rope_golden.py: rope() and rope_tables() of
+    tests/gemma4_int4_sim.py:60-76 (full rotary and p-RoPE tables, fp64) and
+    the pair permutation _deepseek_rope_prep of core/deepseek_v2_lite_tc.py:99-103.
+    The reference computes in fp64; the mount computes x*cos + rot(x)*sin in
+    fp32 with the tables rounded to fp32, then rounds to bf16.  Tolerance:
+    every value within one bf16 ulp of the reference's fp64 value (2^-8
+    relative, plus 1e-5 absolute for results that cancel to near zero), and
+    at least 99.9% of them equal to its round-to-nearest-even bf16 (all of them
+    are, on this fixture)."""
+    g = np.load(GOLDEN)
+    W, off, dim, heads, swap, T, L = (int(v) for v in g[f"{name}_meta"])
+    windows, seats = g[f"{name}_windows"], g[f"{name}_seats"]
+    cos, sin = g[f"{name}_cos"], g[f"{name}_sin"]
+    S = cos.shape[0]
+    arena = np.zeros((L, S, W), np.uint16)
+    for w, s in zip(windows, seats):
+        arena[:, s:s + T] = w
+    got = O.mount_rope(arena, len(seats), L, T, seats, cos.astype(np.float32),
+                       sin.astype(np.float32), off, dim, bool(swap))
+    want = g[f"{name}_want"]
+    for gi, s in enumerate(seats):
+        mine = _to_f32(got[:, s:s + T, off:off + heads * dim]).astype(np.float64)
+        ref = want[gi]
+        assert np.all(np.abs(mine - ref) <= np.abs(ref) * 2.0 ** -8 + 1e-5), (name, s)
+        exact = np.mean(mine == _to_f32(_bf16_bits(ref.astype(np.float32))))
+        assert exact >= 0.999, (name, s, exact)
+        # the position-free columns keep their bytes
+        assert np.array_equal(got[:, s:s + T, :off], arena[:, s:s + T, :off])
+
+
+def test_rope_tables_match_the_reference_table_builder():
+    """graft_mount.rope_tables (fp32, the construction of core/minicpm3_tc.py:345-355)
+    against the reference's fp64 rope_tables (tests/gemma4_int4_sim.py:60-65) for
+    full rotary at dim 32, theta 1e4: equal to fp32 angle rounding (pos * 2^-24)."""
+    g = np.load(GOLDEN)
+    want_c, want_s = g["tables32_cos"], g["tables32_sin"]
+    cos, sin = graft_mount.rope_tables(want_c.shape[0], 32, theta=1e4)
+    tol = np.arange(want_c.shape[0])[:, None] * 2.0 ** -22 + 1e-7
+    assert np.all(np.abs(cos - want_c) <= tol)
+    assert np.all(np.abs(sin - want_s) <= tol)
