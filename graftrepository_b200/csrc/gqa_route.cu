@@ -88,6 +88,7 @@ __device__ __forceinline__ bool key_nonfinite_bits(KT v) { return !isfinite(key_
 
 __device__ __forceinline__ float std_max(float a, float b) { return (a < b) ? b : a; }
 
+
 // fp32 -> (hi, lo) pair of the key type, packed two per 32-bit word.
 template <typename KT>
 __device__ __forceinline__ uint32_t pack2(float a, float b);
@@ -203,7 +204,22 @@ struct RouteParams {
   const uint32_t* allow;       // bitmap of routable nodes (nullptr: all)
   const uint32_t* hits;        // [N] lexical hits of this query (lexical routes)
   int lex_m;                   // query lexical keys; > 0 selects the normalised lexical law
+  // query vectors transposed for the staged refine: [KH][ceil(nv/4)][D][4],
+  // vector 4*v4 + j of kv head kh at dim d (zero past nv); nullptr: not used
+  float* qT;
 };
+
+// Writes kv head kh's slice of p.qT (one block, any size).
+__device__ __forceinline__ void write_qT(const RouteParams& p, int kh) {
+  const int D = p.dim, nv4 = (p.nv + 3) >> 2;
+  const int n = nv4 * D * 4;
+  float* dst = p.qT + (int64_t)kh * n;
+  const float* src = p.query + (int64_t)kh * p.nv * D;   // this kv head's nv vectors
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const int j = i & 3, d = (i >> 2) % D, vi = ((i >> 2) / D) * 4 + j;
+    dst[i] = vi < p.nv ? src[(int64_t)vi * D + d] : 0.0f;
+  }
+}
 
 // K permutation shared by the query fragments and the scan kernels: thread
 // c (lane & 3) holds, for each key row, the 16-byte chunks w = 0 .. D/32-1 at
@@ -282,6 +298,7 @@ __global__ void __launch_bounds__(128) query_prep_kernel(RouteParams p) {
       dst[2 * s + 1] = pack2<KT>(v[2], v[3]);
     }
   }
+  if (p.qT) write_qT(p, kh);
   if (threadIdx.x == 0) {
     p.qparts[kh] = (bad ? 1 : 0) | (big ? 2 : 0);
     __threadfence();
@@ -908,6 +925,213 @@ __global__ void __launch_bounds__(256) refine_kernel(RouteParams p) {
   }
 }
 
+// Exact refine with staged keys, for banks the TMA scan serves (16-bit keys,
+// dim 64 or 128).  The work units are those of refine_kernel (32 tokens of one
+// kv head of one candidate); a unit's 32 key rows are contiguous, so one pair
+// of TMA boxes (the scan's tensor map: 32 rows x 64 dims, 128-byte swizzle)
+// stages it in shared memory.  Each warp owns a contiguous range of the
+// flattened units (consecutive tokens, then kv heads, then candidates), so
+// the next unit follows from the current one without global reads, and keeps
+// kRefStages units in flight in its own ring while it computes.  Lane l takes
+// row l of the unit (token t0 + l) and reads its 16-byte chunks through the
+// swizzle (eight lanes cover all 32 banks).  The dots are the reference's
+// sequential fp32 sums of separately rounded products, four query vectors at
+// a time: the query, transposed to [kh][v4][d][4] by the query kernel (p.qT),
+// gives the four vectors' values at dim d in one 16-byte load.  The head
+// maxima and atomics are those of refine_kernel.  Every wait is bounded: a
+// wait that gives up drains the warp's loads and sets qinfo->err, which makes
+// the route report an error.
+constexpr int kRefWarps = 8;
+constexpr int kRefStages = 3;
+
+template <int D>
+struct RefLayout {
+  static constexpr int kBuf = TmaLayout<D>::kBuf;                     // one staged unit
+  static constexpr int kSmem = 1024 + kRefWarps * kRefStages * kBuf;  // + alignment slack
+};
+
+template <typename KT, int D>
+__global__ void __launch_bounds__(kRefWarps * 32, 1)
+    refine_tma_kernel(const __grid_constant__ CUtensorMap tmap, RouteParams p) {
+  using LY = TmaLayout<D>;
+  static_assert(kRefWarps * 32 == kRefineChunk, "one candidate of a chunk per thread");
+  extern __shared__ unsigned char rsm_raw[];
+  unsigned char* const rsm = rsm_raw + ((1024u - (smem_u32(rsm_raw) & 1023u)) & 1023u);
+  __shared__ __align__(8) uint64_t bar[kRefWarps][kRefStages];
+  __shared__ int64_t s_pref[kRefineChunk + 1];  // units before candidate i of the chunk
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // chained launch, as node_bounds_kernel
+  asm volatile("griddepcontrol.launch_dependents;");
+  const int count = *p.cand_count;
+  if (count == 0) return;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane == 0) {
+    for (int st = 0; st < kRefStages; ++st) mbar_init(&bar[warp][st], 1);
+    mbar_fence_init();
+  }
+  __syncwarp();
+  unsigned char* const buf0 = rsm + warp * kRefStages * LY::kBuf;
+  const uint64_t pol = l2_evict_first_policy();
+  const bool qfinite = p.qinfo->finite != 0;
+  const int nv4 = (p.nv + 3) >> 2;
+  const int64_t gw = (int64_t)blockIdx.x * kRefWarps + warp;
+  const int64_t nw = (int64_t)gridDim.x * kRefWarps;
+  unsigned phase_bits = 0u, pending_bits = 0u;
+  bool failed = false;
+
+  // A position in the chunk's flattened units.
+  struct Unit {
+    int lo;        // candidate index within the chunk
+    int kh;
+    int64_t T;     // tokens of the candidate
+    int64_t t0;    // first token of the unit
+    uint64_t o0;   // the candidate's first token
+  };
+  for (int c0 = 0; c0 < count; c0 += kRefineChunk) {
+    const int cn = min(kRefineChunk, count - c0);
+    int64_t my_units = 0;
+    if ((int)threadIdx.x < cn) {
+      const int64_t node = p.cand[c0 + threadIdx.x];
+      const int64_t T = (int64_t)(p.off[node + 1] - p.off[node]);
+      if (T > 0 && !p.key_bad[node] && qfinite) my_units = (int64_t)p.kh_n * ((T + 31) >> 5);
+    }
+    if (threadIdx.x == 0) s_pref[0] = 0;
+    s_pref[threadIdx.x + 1] = my_units;
+    __syncthreads();
+#pragma unroll 1
+    for (int o = 1; o < kRefineChunk; o <<= 1) {  // inclusive scan of s_pref[1..256]
+      const int64_t v = (int)threadIdx.x >= o ? s_pref[threadIdx.x + 1 - o] : 0;
+      __syncthreads();
+      s_pref[threadIdx.x + 1] += v;
+      __syncthreads();
+    }
+    const int64_t total = failed ? 0 : s_pref[cn];
+    // this warp's units [u_begin, u_end)
+    const int64_t u_begin = total * gw / nw, u_end = total * (gw + 1) / nw;
+    auto load_cand = [&](Unit& u) {
+      const int64_t node = p.cand[c0 + u.lo];
+      u.o0 = p.off[node];
+      u.T = (int64_t)(p.off[node + 1] - u.o0);
+    };
+    auto decode = [&](int64_t w, Unit& u) {
+      int lo = 0, hi = cn - 1;  // the last candidate whose units start at or before w
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (s_pref[mid] <= w) lo = mid;
+        else hi = mid - 1;
+      }
+      u.lo = lo;
+      load_cand(u);
+      const int64_t tiles = (u.T + 31) >> 5;
+      const int64_t local = w - s_pref[lo];
+      u.kh = (int)(local / tiles);
+      u.t0 = (local - (int64_t)u.kh * tiles) * 32;
+    };
+    auto advance = [&](Unit& u) {  // the next unit (valid while units remain)
+      u.t0 += 32;
+      if (u.t0 < u.T) return;
+      u.t0 = 0;
+      if (++u.kh < p.kh_n) return;
+      u.kh = 0;
+      do {
+        ++u.lo;
+      } while (u.lo < cn - 1 && s_pref[u.lo + 1] == s_pref[u.lo]);  // candidates without units
+      if (u.lo < cn) load_cand(u);
+    };
+    auto issue = [&](const Unit& u, int st) {
+      if (lane == 0) {
+        const int row = (int)(u.o0 * (uint64_t)p.kh_n + (uint64_t)u.kh * u.T + u.t0);
+        unsigned char* dst = buf0 + st * LY::kBuf;
+        mbar_arrive_expect_tx(&bar[warp][st], LY::kBuf);
+#pragma unroll
+        for (int x = 0; x < LY::kBoxes; ++x)
+          tma_load_2d_g(dst + x * LY::kBox, &tmap, 64 * x, row, &bar[warp][st], pol);
+      }
+      pending_bits |= 1u << st;
+    };
+    Unit cur, fetch;
+    if (u_begin < u_end) {
+      decode(u_begin, cur);
+      fetch = cur;
+    }
+    int64_t w_fetch = u_begin;
+    for (int st = 0; st < kRefStages && w_fetch < u_end; ++st, ++w_fetch) {
+      issue(fetch, st);
+      if (w_fetch + 1 < u_end) advance(fetch);
+    }
+    int st = 0;
+    for (int64_t w = u_begin; w < u_end; ++w) {
+      if (!mbar_wait(&bar[warp][st], (phase_bits >> st) & 1u, kWaitLimit)) {
+        failed = true;
+        break;
+      }
+      phase_bits ^= 1u << st;
+      pending_bits &= ~(1u << st);
+      const unsigned char* sb = buf0 + st * LY::kBuf;
+      const bool live = cur.t0 + lane < cur.T;  // rows past the candidate's tokens are masked
+      unsigned* best_out = p.headmax + (int64_t)(c0 + cur.lo) * p.heads;
+      const float4* qk = reinterpret_cast<const float4*>(p.qT) + (int64_t)cur.kh * nv4 * D;
+      for (int v4 = 0; v4 < nv4; ++v4) {
+        const float4* q = qk + (int64_t)v4 * D;
+        float dot[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+        for (int c = 0; c < D / 8; ++c) {  // 16-byte chunk c: dims 8c .. 8c+7, in order
+          const uint4 raw = *reinterpret_cast<const uint4*>(
+              sb + (c / 8) * LY::kBox + lane * 128 + (((c % 8) ^ (lane & 7)) * 16));
+          const KT* kk = reinterpret_cast<const KT*>(&raw);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const float kf = key_to_f(kk[e]);
+            const float4 qv = __ldg(q + c * 8 + e);
+            dot[0] = __fadd_rn(dot[0], __fmul_rn(qv.x, kf));
+            dot[1] = __fadd_rn(dot[1], __fmul_rn(qv.y, kf));
+            dot[2] = __fadd_rn(dot[2], __fmul_rn(qv.z, kf));
+            dot[3] = __fadd_rn(dot[3], __fmul_rn(qv.w, kf));
+          }
+        }
+        const int v0 = v4 * 4;
+        if (p.qt4) {
+          // vectors v0..v0+3 are the four query tokens of one head
+          const float rb = std_max(std_max(fabsf(dot[0]), fabsf(dot[1])),
+                                   std_max(fabsf(dot[2]), fabsf(dot[3])));
+          float v = live ? __fmul_rn(rb, p.inv_denom) : 0.0f;
+          if (!(v == v)) v = 0.0f;   // a NaN row never raises best
+#pragma unroll
+          for (int o = 16; o >= 1; o >>= 1) v = fmaxf(v, __shfl_xor_sync(kFull, v, o));
+          if (lane == 0 && v > 0.0f)
+            atomicMax(best_out + cur.kh * p.group + v0 / 4, __float_as_uint(v));
+        } else {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            if (v0 + j >= p.nv) break;
+            float v = live ? __fmul_rn(fabsf(dot[j]), p.inv_denom) : 0.0f;
+            if (!(v == v)) v = 0.0f;
+#pragma unroll
+            for (int o = 16; o >= 1; o >>= 1) v = fmaxf(v, __shfl_xor_sync(kFull, v, o));
+            if (lane == 0 && v > 0.0f)
+              atomicMax(best_out + cur.kh * p.group + (v0 + j) / p.qt, __float_as_uint(v));
+          }
+        }
+      }
+      // stage st is read: the unit kRefStages ahead goes into it
+      __syncwarp();
+      fence_proxy_async_smem();
+      if (w_fetch < u_end) {
+        issue(fetch, st);
+        if (w_fetch + 1 < u_end) advance(fetch);
+        ++w_fetch;
+      }
+      if (w + 1 < u_end) advance(cur);
+      st = (st + 1 == kRefStages) ? 0 : st + 1;
+    }
+    __syncthreads();  // s_pref is rewritten for the next chunk
+  }
+  if (failed) {
+    for (int k = 0; k < kRefStages; ++k)
+      if ((pending_bits >> k) & 1u) mbar_wait(&bar[warp][k], (phase_bits >> k) & 1u, kWaitLimit);
+    if (lane == 0) atomicOr(&p.qinfo->err, 1);
+  }
+}
+
 // Final scores of the candidates (sequential fp32 head sum, as the reference)
 // and the exact top-k.  One warp.  Lexical routes (lex_m > 0) rank by the
 // reference's S = raw / (max raw + 1e-8) + hits / m instead
@@ -1035,6 +1259,8 @@ struct grm_b200_gqa_bank {
   int qnorm_cap = 0;
   QueryInfo* d_qinfo = nullptr;
   int* d_qparts = nullptr;
+  float* d_qT = nullptr;     // transposed query for refine_tma_kernel
+  size_t qT_cap = 0;         // floats
   unsigned* d_qcount = nullptr;
   Result* d_result = nullptr;
   Result* h_result = nullptr;
@@ -1099,6 +1325,9 @@ cudaError_t tma_smem_attr() {
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                TmaLayout<D>::kSmem);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(refine_tma_kernel<KT, D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             RefLayout<D>::kSmem);
   return e;
 }
 
@@ -1176,6 +1405,8 @@ __global__ void query_info_kernel(RouteParams p) {
   for (int i = threadIdx.x; i < nq; i += blockDim.x)
     if (!isfinite(p.query[i])) s_bad = 1;
   for (int h = threadIdx.x; h < p.heads; h += blockDim.x) p.qnorm_h[h] = 0.0f;
+  if (p.qT)
+    for (int kh = 0; kh < p.kh_n; ++kh) write_qT(p, kh);
   __syncthreads();
   if (threadIdx.x == 0) {
     p.qinfo->finite = !s_bad;
@@ -1188,6 +1419,16 @@ constexpr int kRefineSmemCopy = 16 * 1024;  // largest query staged in shared me
 
 template <typename KT>
 cudaError_t launch_refine(grm_b200_gqa_bank* b, const RouteParams& p) {
+  if constexpr (sizeof(KT) == 2) {
+    if (p.qT) {  // staged keys (the TMA scan's tensor map): one CTA per SM
+      const dim3 grid(std::max(1, b->sms)), block(kRefWarps * 32);
+      if (b->dim == 128)
+        return launch_chained(refine_tma_kernel<KT, 128>, grid, block,
+                              (size_t)RefLayout<128>::kSmem, b->stream, b->tmap, p);
+      return launch_chained(refine_tma_kernel<KT, 64>, grid, block,
+                            (size_t)RefLayout<64>::kSmem, b->stream, b->tmap, p);
+    }
+  }
   // one wave: as many blocks as are resident together (measured once)
   static int per_sm[2][64] = {};
   const bool smem_q = sizeof(float) * (size_t)p.heads * p.qt * p.dim <= (size_t)kRefineSmemCopy;
@@ -1249,6 +1490,20 @@ int ensure_heads(grm_b200_gqa_bank* b, int heads, int nt) {
   return 0;
 }
 
+// The transposed query of refine_tma_kernel: KH x ceil(nv / 4) x D x 4 floats.
+int ensure_qT(grm_b200_gqa_bank* b, int nv) {
+  const size_t n = (size_t)b->kh_n * (size_t)((nv + 3) / 4) * (size_t)b->dim * 4;
+  if (n > b->qT_cap) {
+    if (b->d_qT) cudaFree(b->d_qT);
+    b->d_qT = nullptr;
+    b->qT_cap = 0;
+    cudaError_t e = cudaMalloc(&b->d_qT, n * sizeof(float));
+    if (e != cudaSuccess) return b->err.set(cuda_status(e), "GQA scratch allocation failed");
+    b->qT_cap = n;
+  }
+  return 0;
+}
+
 // `use_bank_stream`: launch on the bank's private stream (synchronous entry
 // points); otherwise on `stream`, where 0 is the legacy default stream.
 // `allow`, `hits`, `lex_m`: route policy inputs (see RouteParams).
@@ -1263,6 +1518,7 @@ int route_one(grm_b200_gqa_bank* b, const float* dq, int heads, int qt, int topk
   const int nt = nt_for(nv);
   const bool fast = fast_bank(b) && nt > 0;
   int rc = ensure_heads(b, heads, nt);
+  if (rc == 0 && b->tma) rc = ensure_qT(b, nv);
   if (rc) return rc;
   RouteParams p;
   p.keys = b->d_keys;
@@ -1301,6 +1557,7 @@ int route_one(grm_b200_gqa_bank* b, const float* dq, int heads, int qt, int topk
   p.allow = allow;
   p.hits = hits;
   p.lex_m = lex_m;
+  p.qT = b->tma ? b->d_qT : nullptr;
   cudaStream_t saved = b->stream;
   b->stream = stream;  // every launch below goes to the caller's stream
   struct Restore {
@@ -1379,7 +1636,7 @@ void bank_free(grm_b200_gqa_bank* b) {
   if (b->owns_keys && b->d_keys) cudaFree(b->d_keys);
   void* ptrs[] = {b->d_off, b->d_items, b->d_kmax, b->d_key_bad, b->d_headmax, b->d_lo, b->d_hi,
                   b->d_cand, b->d_cand_count, b->d_frag, b->d_qnorm, b->d_qinfo, b->d_result,
-                  b->d_queries, b->d_qparts, b->d_qcount, b->d_refined};
+                  b->d_queries, b->d_qparts, b->d_qcount, b->d_refined, b->d_qT};
   for (void* q : ptrs)
     if (q) cudaFree(q);
   if (b->h_result) cudaFreeHost(b->h_result);

@@ -47,7 +47,6 @@ namespace mla {
 
 constexpr int kQ4Bins = 4096;  // 12-bit histogram levels
 constexpr int kQ4Tile = 64;    // rows per interleaved tile
-constexpr int kQ4BulkThreads = 256;
 constexpr int kQ4CollThreads = 256;
 constexpr int kQ4RefThreads = 64;
 constexpr int kQ4StageMax = 96 * 1024;  // shared bytes for staged candidate rows per block
@@ -62,6 +61,7 @@ struct Q4Hdr {
   int b1;              // level-1 boundary bin, -1: every finite row is a candidate
   unsigned above1;     // rows in bins above b1
   float qinv;          // float(1 / (qnorm + 1e-8))
+  int err;             // a bounded wait of the refine gave up (reported as kError)
   double qnorm;        // the query's reference norm
 };
 
@@ -213,21 +213,66 @@ __device__ __forceinline__ void q4_append(bool take, uint32_t row, unsigned* cou
 
 // ---- bulk pass -----------------------------------------------------------------
 
-// Two rows per lane (rows l and 32 + l of a 64-row tile), as the two halves of
-// packed f32x2 operations: per element one exact nibble -> float conversion
-// (2^23 + u, minus 2^23 + 8), one multiply and one add, each rounded
-// separately, in element order.
-__global__ void __launch_bounds__(kQ4BulkThreads) int4_bulk_kernel(
+// Two rows per lane (rows l and 32 + l of a 64-row tile): per element one
+// exact nibble -> float conversion (2^23 + u, minus 2^23 + 8; a packed f32x2
+// subtract for both rows), then one multiply and one add, each rounded
+// separately, in element order.  The multiply and add are scalar
+// __fmul_rn / __fadd_rn: a packed __fmul2_rn whose product feeds a packed
+// __fadd2_rn was measured on sm_100a to be contracted into a fused
+// multiply-add (results differing from the separately rounded pair), and
+// the reference rounds both.
+//
+// STAGED: each warp streams its tiles through a two-tile shared-memory ring,
+// one bulk copy (cp.async.bulk) per tile (a tile's quads are contiguous), so
+// two whole tiles per warp are in flight while it computes; NW warps per
+// block, sized by the host to the stage bytes a dim needs.  Otherwise (dims
+// whose tiles do not fit) lanes load their quads directly, one quad ahead.
+// A bounded wait that gives up drains the warp's copies and sets hdr->err
+// (the route then reports kError).
+template <int NW, bool STAGED>
+__global__ void __launch_bounds__(NW * 32) int4_bulk_kernel(
     const uint4* __restrict__ q4, const float* __restrict__ nscale, int64_t nodes, int dim,
     const float* __restrict__ query, uint32_t* __restrict__ keys, Q4Hdr* hdr, unsigned M) {
-  extern __shared__ float4 qq[];  // [quads * 16] (q_2j, q_2j, q_2j+1, q_2j+1)
+  // [quads * 16] float4 (q_2j, q_2j, q_2j+1, q_2j+1), then (STAGED) the
+  // warps' rings: NW x 2 x quads KB
+  extern __shared__ __align__(128) unsigned char b4_smem[];
+  float4* const qq = reinterpret_cast<float4*>(b4_smem);
   __shared__ unsigned hist[kQ4Bins];
   __shared__ float sh_qinv;
-  __shared__ unsigned sh_scan[kQ4BulkThreads / 32 + 1];
+  __shared__ unsigned sh_scan[NW + 1];
   __shared__ unsigned sh_above;
   __shared__ int sh_flag;
-  asm volatile("griddepcontrol.wait;" ::: "memory");
+  __shared__ __align__(8) uint64_t bar[NW][2];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int quads = q4_quads(dim);
+  const int64_t tiles = ceil_div64(nodes, kQ4Tile);
+  const int64_t stride = (int64_t)gridDim.x * NW;
+  const unsigned tile_bytes = (unsigned)quads * kQ4Tile * 16;
+  unsigned char* const ring = b4_smem + quads * 16 * sizeof(float4) +
+                              (size_t)warp * 2 * tile_bytes;
+  unsigned phase_bits = 0u, pending_bits = 0u;
+  // the arena is read-only after its build, so the first tiles' copies start
+  // before the wait on the previous kernel of the stream
+  auto issue = [&](int64_t t, int b) {
+    if (lane == 0) {
+      mbar_arrive_expect_tx(&bar[warp][b], tile_bytes);
+      bulk_g2s(ring + b * tile_bytes, q4 + t * (int64_t)quads * kQ4Tile, tile_bytes,
+               &bar[warp][b]);
+    }
+    pending_bits |= 1u << b;
+  };
+  const int64_t t_first = (int64_t)blockIdx.x * NW + warp;
+  if constexpr (STAGED) {
+    if (lane == 0) {
+      mbar_init(&bar[warp][0], 1);
+      mbar_init(&bar[warp][1], 1);
+      mbar_fence_init();
+    }
+    __syncwarp();
+    if (t_first < tiles) issue(t_first, 0);
+    if (t_first + stride < tiles) issue(t_first + stride, 1);
+  }
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   for (int j = threadIdx.x; j < quads * 16; j += blockDim.x) {
     const float a = 2 * j < dim ? query[2 * j] : 0.0f;
     const float b = 2 * j + 1 < dim ? query[2 * j + 1] : 0.0f;
@@ -245,40 +290,35 @@ __global__ void __launch_bounds__(kQ4BulkThreads) int4_bulk_kernel(
   }
   __syncthreads();
   const float qinv = sh_qinv;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  constexpr int NW = kQ4BulkThreads / 32;
-  const int64_t tiles = ceil_div64(nodes, kQ4Tile);
   const float2 magic = make_float2(-8388616.0f, -8388616.0f);  // -(2^23 + 8)
-  for (int64_t t = (int64_t)blockIdx.x * NW + warp; t < tiles; t += (int64_t)gridDim.x * NW) {
-    const uint4* base = q4 + t * (int64_t)quads * kQ4Tile + lane;
-    float2 acc = make_float2(0.0f, 0.0f);
-    uint4 na = __ldg(base), nb = __ldg(base + 32);  // quad 0, loaded one quad ahead
-    for (int kq = 0; kq < quads; ++kq) {
-      const uint4 ua = na, ub = nb;
-      if (kq + 1 < quads) {
-        na = __ldg(base + (int64_t)(kq + 1) * kQ4Tile);
-        nb = __ldg(base + (int64_t)(kq + 1) * kQ4Tile + 32);
-      }
-      const uint32_t wa4[4] = {ua.x, ua.y, ua.z, ua.w};
-      const uint32_t wb4[4] = {ub.x, ub.y, ub.z, ub.w};
+  // elements 32 kq .. 32 kq + 31 of both rows, in order
+  auto quad = [&](float2& acc, const uint4& ua, const uint4& ub, int kq) {
+    const uint32_t wa4[4] = {ua.x, ua.y, ua.z, ua.w};
+    const uint32_t wb4[4] = {ub.x, ub.y, ub.z, ub.w};
 #pragma unroll
-      for (int w = 0; w < 4; ++w) {
-        const uint32_t la = wa4[w] & 0x0F0F0F0Fu, ha = (wa4[w] >> 4) & 0x0F0F0F0Fu;
-        const uint32_t lb = wb4[w] & 0x0F0F0F0Fu, hb = (wb4[w] >> 4) & 0x0F0F0F0Fu;
-        const float4* qk = qq + (kq * 4 + w) * 4;  // elements (kq*4 + w)*8 .. +7
+    for (int w = 0; w < 4; ++w) {
+      const uint32_t la = wa4[w] & 0x0F0F0F0Fu, ha = (wa4[w] >> 4) & 0x0F0F0F0Fu;
+      const uint32_t lb = wb4[w] & 0x0F0F0F0Fu, hb = (wb4[w] >> 4) & 0x0F0F0F0Fu;
+      const float4* qk = qq + (kq * 4 + w) * 4;  // elements (kq*4 + w)*8 .. +7
 #pragma unroll
-        for (int m = 0; m < 4; ++m) {
-          const float4 qp = qk[m];
-          const unsigned sel = 0x7440u + (unsigned)m;  // [byte m, 0, 0, 0x4B]
-          float2 v = make_float2(__uint_as_float(__byte_perm(la, 0x4B000000u, sel)),
-                                 __uint_as_float(__byte_perm(lb, 0x4B000000u, sel)));
-          acc = __fadd2_rn(acc, __fmul2_rn(make_float2(qp.x, qp.y), __fadd2_rn(v, magic)));
-          v = make_float2(__uint_as_float(__byte_perm(ha, 0x4B000000u, sel)),
-                          __uint_as_float(__byte_perm(hb, 0x4B000000u, sel)));
-          acc = __fadd2_rn(acc, __fmul2_rn(make_float2(qp.z, qp.w), __fadd2_rn(v, magic)));
-        }
+      for (int m = 0; m < 4; ++m) {
+        const float4 qp = qk[m];
+        const unsigned sel = 0x7440u + (unsigned)m;  // [byte m, 0, 0, 0x4B]
+        // the values, exact small integers (a packed subtract: nothing to fuse)
+        float2 v = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(la, 0x4B000000u, sel)),
+                                          __uint_as_float(__byte_perm(lb, 0x4B000000u, sel))),
+                              magic);
+        acc.x = __fadd_rn(acc.x, __fmul_rn(qp.x, v.x));
+        acc.y = __fadd_rn(acc.y, __fmul_rn(qp.y, v.y));
+        v = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(ha, 0x4B000000u, sel)),
+                                   __uint_as_float(__byte_perm(hb, 0x4B000000u, sel))),
+                       magic);
+        acc.x = __fadd_rn(acc.x, __fmul_rn(qp.z, v.x));
+        acc.y = __fadd_rn(acc.y, __fmul_rn(qp.w, v.y));
       }
     }
+  };
+  auto finish_tile = [&](int64_t t, const float2& acc) {
     const int64_t ra = t * kQ4Tile + lane, rb = ra + 32;
     if (ra < nodes) {
       const float s = __fadd_rn(__fmul_rn(__fmul_rn(acc.x, __ldg(nscale + ra)), qinv), 0.0f);
@@ -291,6 +331,47 @@ __global__ void __launch_bounds__(kQ4BulkThreads) int4_bulk_kernel(
       const uint32_t key = isfinite(s) ? q4_key(s) : 0u;
       keys[rb] = key;
       if (key) atomicAdd(&hist[key >> 20], 1u);
+    }
+  };
+  if constexpr (STAGED) {
+    int b = 0;
+    bool failed = false;
+    for (int64_t t = t_first; t < tiles; t += stride) {
+      if (!mbar_wait(&bar[warp][b], (phase_bits >> b) & 1u, kWaitLimit)) {
+        failed = true;
+        break;
+      }
+      phase_bits ^= 1u << b;
+      pending_bits &= ~(1u << b);
+      const uint4* tb = reinterpret_cast<const uint4*>(ring + b * tile_bytes) + lane;
+      float2 acc = make_float2(0.0f, 0.0f);
+      for (int kq = 0; kq < quads; ++kq) quad(acc, tb[kq * kQ4Tile], tb[kq * kQ4Tile + 32], kq);
+      // buffer b is read: the tile after the next one goes into it
+      __syncwarp();
+      fence_proxy_async_smem();
+      if (t + 2 * stride < tiles) issue(t + 2 * stride, b);
+      finish_tile(t, acc);
+      b ^= 1;
+    }
+    if (failed) {
+      for (int k = 0; k < 2; ++k)
+        if ((pending_bits >> k) & 1u) mbar_wait(&bar[warp][k], (phase_bits >> k) & 1u, kWaitLimit);
+      if (lane == 0) atomicOr(&hdr->err, 1);
+    }
+  } else {
+    for (int64_t t = t_first; t < tiles; t += stride) {
+      const uint4* base = q4 + t * (int64_t)quads * kQ4Tile + lane;
+      float2 acc = make_float2(0.0f, 0.0f);
+      uint4 na = __ldg(base), nb = __ldg(base + 32);  // quad 0, loaded one quad ahead
+      for (int kq = 0; kq < quads; ++kq) {
+        const uint4 ua = na, ub = nb;
+        if (kq + 1 < quads) {
+          na = __ldg(base + (int64_t)(kq + 1) * kQ4Tile);
+          nb = __ldg(base + (int64_t)(kq + 1) * kQ4Tile + 32);
+        }
+        quad(acc, ua, ub, kq);
+      }
+      finish_tile(t, acc);
     }
   }
   __syncthreads();
@@ -558,11 +639,13 @@ __device__ __forceinline__ float exact_score_smem(const uint4* rs, int dim, cons
 }
 
 // One candidate per lane, the exact route's arithmetic.  With `stage` set
-// each warp first copies its 32 candidate rows into shared memory with
-// coalesced 16-byte loads (rows padded by 16 bytes, so the lanes' reads of
-// their own rows hit distinct banks), then every lane runs its row's
-// sequential fp64 chain from there; otherwise lanes read their rows from
-// global memory.  Each block keeps its top entries (score desc, row asc,
+// each lane copies its candidate row into the warp's shared-memory stage with
+// one bulk copy (the 32 copies of a warp are in flight together and complete
+// on one mbarrier; rows padded by 16 bytes, so the lanes' reads of their own
+// rows hit distinct banks), then every lane runs its row's sequential fp64
+// chain from there; otherwise lanes read their rows from global memory.  A
+// bounded wait that gives up waits once more for the warp's copies, leaves
+// the warp's candidates out and makes the route report kError.  Each block keeps its top entries (score desc, row asc,
 // non-finite dropped) in slot_s / slot_id [block * topk ..]; the last block to
 // finish merges the slots, writes the result and resets the header for the
 // next route.
@@ -577,7 +660,12 @@ __global__ void __launch_bounds__(kQ4RefThreads) int4_refine_kernel(
   __shared__ float sh_s[NW * 32];
   __shared__ uint32_t sh_id[NW * 32];
   __shared__ int sh_flag;
+  __shared__ __align__(8) uint64_t rbar[NW];
   double* const qd = reinterpret_cast<double*>(ref_smem);  // [dim]
+  if (stage && (threadIdx.x & 31) == 0) {
+    mbar_init(&rbar[threadIdx.x >> 5], 1);
+    mbar_fence_init();
+  }
   asm volatile("griddepcontrol.wait;" ::: "memory");
   for (int i = threadIdx.x; i < dim; i += blockDim.x) qd[i] = (double)query[i];
   __syncthreads();
@@ -590,33 +678,30 @@ __global__ void __launch_bounds__(kQ4RefThreads) int4_refine_kernel(
                          (size_t)warp * 32 * rs_vec;
   WarpList list;
   list.init();
-  for (unsigned c0 = (blockIdx.x * NW + warp) * 32u; c0 < n; c0 += gridDim.x * NW * 32u) {
+  unsigned rphase = 0;
+  bool failed = false;
+  const unsigned row_bytes = (unsigned)(nv * 16);
+  for (unsigned c0 = (blockIdx.x * NW + warp) * 32u; c0 < n && !failed;
+       c0 += gridDim.x * NW * 32u) {
     const unsigned c = c0 + lane;
     const uint32_t id = c < n ? __ldcg(cand + c) : kNoRow;
     float es = -INFINITY;
     if (stage) {
-      // vector v of candidate row i goes to lane v % 32: eight rows' loads are
-      // issued together before any is stored
-      for (int v0 = 0; v0 < nv; v0 += 32) {
-        const int v = v0 + lane;
-#pragma unroll 1
-        for (int i0 = 0; i0 < 32; i0 += 8) {
-          uint4 buf[8];
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const uint32_t ri = __shfl_sync(kFull, id, i0 + i);
-            buf[i] = (ri != kNoRow && v < nv)
-                         ? ld_nc16(reinterpret_cast<const uint4*>(rows + (int64_t)ri * dim) + v)
-                         : make_uint4(0, 0, 0, 0);
-          }
-#pragma unroll
-          for (int i = 0; i < 8; ++i)
-            if (v < nv) stage_w[(i0 + i) * rs_vec + v] = buf[i];
-        }
-      }
+      const unsigned rows_in = __popc(__ballot_sync(kFull, id != kNoRow));
+      if (lane == 0) mbar_arrive_expect_tx(&rbar[warp], rows_in * row_bytes);
       __syncwarp();
+      if (id != kNoRow)
+        bulk_g2s(stage_w + lane * rs_vec, rows + (int64_t)id * dim, row_bytes, &rbar[warp]);
+      if (!mbar_wait(&rbar[warp], rphase, kWaitLimit)) {
+        mbar_wait(&rbar[warp], rphase, kWaitLimit);  // the copies still in flight
+        failed = true;
+        if (lane == 0) atomicOr(&hdr->err, 1);
+        break;
+      }
+      rphase ^= 1u;
       if (c < n) es = exact_score_smem<T>(stage_w + lane * rs_vec, dim, qd, qn, __ldg(norms + id));
       __syncwarp();
+      fence_proxy_async_smem();  // the next copies overwrite what this round read
     } else if (c < n) {
       es = exact_score_vec<T>(rows + (int64_t)id * dim, dim, qd, qn, __ldg(norms + id));
     }
@@ -653,7 +738,7 @@ __global__ void __launch_bounds__(kQ4RefThreads) int4_refine_kernel(
     }
     if (lane == 0 && result) {
       result->count = __popc(m);
-      result->status = kOk;
+      result->status = __ldcg(&hdr->err) ? kError : kOk;
     }
   }
   // back to the state the next route starts from
@@ -665,6 +750,7 @@ __global__ void __launch_bounds__(kQ4RefThreads) int4_refine_kernel(
     hdr->ncand = 0;
     hdr->nbnd = 0;
     hdr->done_ref = 0;
+    hdr->err = 0;
   }
 }
 

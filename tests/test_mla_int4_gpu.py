@@ -167,3 +167,30 @@ def test_full_size_config2(sidecar):
         assert np.array_equal(ids[i], want), i
         assert np.array_equal(sc[i], want_s), i
     bank.close()
+
+
+def _permutation_bank(seed, n, dim):
+    """Rows that are permutations of one integer vector (values -7..7, so the
+    INT4 arena holds them exactly and every row has the same norm and norm
+    scale): with a query whose values are all equal, every row's bulk dot is
+    the same multiset of rounded products summed in a different order, so the
+    bulk ranking -- and with it the refine set -- is decided by fp32 rounding
+    alone.  A bulk pass that fused a multiply into an add, or summed in another
+    order, picks a different set.  The exact scores all tie (the fp64 sums are
+    exact), so the answer lists the refine set's lowest row ids."""
+    rng = np.random.default_rng(seed)
+    base = rng.integers(-7, 8, dim).astype(np.float32)
+    base[0], base[1] = 7.0, -7.0
+    rows = np.stack([base[rng.permutation(dim)] for _ in range(n)])
+    return rows.astype(np.float16).astype(np.float32)
+
+
+def test_bulk_rounding_order_decides_the_refine_set(sidecar):
+    rows = _permutation_bank(66, 20_000, 256)
+    q_const = np.full(256, 0.7317093, np.float32)
+    q_alt = np.where(np.arange(256) % 3 == 0, -1.3371, 0.4142).astype(np.float32)
+    qs = np.stack([q_const, q_alt])
+    bank = sidecar.create_bank(rows)
+    for k, m in ((1, 1), (3, 3), (16, 16), (5, 4096), (8, 19_000)):
+        _check(bank, rows, qs, k, m)
+    bank.close()

@@ -202,6 +202,29 @@ def test_mla_int4_restatement_equals_reference_runtime(seed, n, dim, m, monkeypa
                 assert got == want, (k, got, want)
 
 
+def test_mla_int4_restatement_rounding_order_equals_reference_runtime(monkeypatch):
+    """Rows that are permutations of one integer vector, queried with equal
+    values in every dim: the INT4 bulk ranking is decided by the rounding of
+    the sequential fp32 sum alone (the refine scores all tie), so this pins the
+    restatement's bulk arithmetic -- separately rounded products and sums in
+    element order -- to the reference runtime's default build."""
+    rng = np.random.default_rng(66)
+    base = rng.integers(-7, 8, 256).astype(np.float32)
+    base[0], base[1] = 7.0, -7.0
+    rows = np.stack([base[rng.permutation(256)] for _ in range(3000)]).astype(np.float32)
+    qs = [np.full(256, 0.7317093, np.float32),
+          np.where(np.arange(256) % 3 == 0, -1.3371, 0.4142).astype(np.float32)]
+    monkeypatch.setenv("GRM_ROUTER_INT4", "1")
+    for m in (1, 16, 700):
+        monkeypatch.setenv("GRM_ROUTER_INT4_REFINE_M", str(m))
+        with O.RefStore().load_mla(rows) as st:
+            for q in qs:
+                for k in (1, 5):
+                    ids, _ = O.mla_int4_route(rows, q, k, refine_m=m)
+                    got = [int(x) for x in ids if x != np.iinfo(np.uint64).max]
+                    assert got == st.route(q, k), (m, k)
+
+
 def test_mla_int4_mode_differs_from_the_exact_route():
     """With a small refine set the INT4 mode's answer can differ from the exact
     route (the bulk pass decides which rows are refined): the restatement must
