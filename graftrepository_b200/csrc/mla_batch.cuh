@@ -256,6 +256,9 @@ __device__ __forceinline__ float pick32(const float (&v)[32], int c) {
 template <int D>
 __global__ void __launch_bounds__(32) batch_prep_kernel(const float* queries, int nq,
                                                         unsigned char* qmat, Scratch scratch) {
+  // The batch kernel may start now: it streams the read-only bank into its
+  // stage ring and waits for this grid before it reads the query image.
+  asm volatile("griddepcontrol.launch_dependents;");
   const int j = blockIdx.x, lane = threadIdx.x;
   bool safe = false;
   float inv = 0.0f;
@@ -314,8 +317,10 @@ __global__ void __launch_bounds__(kBThreads, 1)
   const int cq = (warp >> 2) * 2 + (lq >> 1);
   const int qi = (lq & 1) * 32 + lane;  // this thread's query
 
-  // The query image comes from batch_prep_kernel (programmatic dependent launch).
-  asm volatile("griddepcontrol.wait;" ::: "memory");
+  // The query image and the scratch headers come from batch_prep_kernel
+  // (programmatic dependent launch): every thread waits for it after the
+  // set-up below, except the producer lane, which first fills the stage ring
+  // from the read-only bank.
   if (threadIdx.x == 0) {
     for (int s = 0; s < LY::kStages; ++s) {
       mbar_init(&full[s], 1);
@@ -340,12 +345,19 @@ __global__ void __launch_bounds__(kBThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sh_tmem;
+  const bool producer = warp == kBProducerWarp && lane == 0;
+  if (!producer) asm volatile("griddepcontrol.wait;" ::: "memory");
 
   if (warp == kBProducerWarp) {
     if (lane == 0) {  // TMA producer
       const uint64_t pol = l2_evict_first_policy();
-      mbar_arrive_expect_tx(&bq_bar, LY::kQ);
-      bulk_g2s(smQ, p.qmat, LY::kQ, &bq_bar);
+      bool qcopied = false;
+      auto copy_query = [&]() {  // after batch_prep_kernel has completed
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        mbar_arrive_expect_tx(&bq_bar, LY::kQ);
+        bulk_g2s(smQ, p.qmat, LY::kQ, &bq_bar);
+        qcopied = true;
+      };
       int st = 0;
       unsigned ph = 0, issued = 0;
       bool ok = true;
@@ -366,8 +378,10 @@ __global__ void __launch_bounds__(kBThreads, 1)
             st = 0;
             ph ^= 1u;
           }
+          if (!qcopied && issued == LY::kStages) copy_query();  // the ring is full
         }
       }
+      if (!qcopied) copy_query();
       sh_issued = issued;
       if (!ok) atomicOr(&sh_fail, 1);
     }
@@ -525,6 +539,7 @@ __global__ void __launch_bounds__(kBThreads, 1)
   // its entries as scan_finish does.
   Entry* const mrg = reinterpret_cast<Entry*>(smT);
   const bool failed = sh_fail != 0;
+  __shared__ int sh_cnt[kBQ];  // per query: published count | first slot << 8
   for (int q = warp; q < p.nq; q += kBThreads / 32) {
     Header* hdr = p.scratch.hdr(q);
     if (failed) {
@@ -543,6 +558,7 @@ __global__ void __launch_bounds__(kBThreads, 1)
       }
       floor = fmaxf(floor, e[w * 32 + C - 1].s);
     }
+    const int lb_seen = __ldcg(&hdr->lb);  // the best CTA k-th published so far
     WarpList m;
     m.s = e[best * 32 + lane].s;
     m.id = e[best * 32 + lane].id;
@@ -551,17 +567,32 @@ __global__ void __launch_bounds__(kBThreads, 1)
       if (w != best)
         m.offer_margin(e[w * 32 + lane].s, e[w * 32 + lane].id, lane, p.topk, 2.0f * kBMargin);
     const float kth = __shfl_sync(kFull, m.s, p.topk - 1);
-    const float wthr = isfinite(kth) ? kth - 2.0f * kBMargin : -INFINITY;
+    // Entries below (any CTA's k-th) - 2 margins cannot reach the final top-k:
+    // k rows score at least that k-th, so the final k-th approximate score is
+    // no lower.
+    const float kmax = lb_seen == kOrderedNegInf ? kth : fmaxf(kth, ordered_to_float(lb_seen));
+    const float wthr = isfinite(kmax) ? kmax - 2.0f * kBMargin : -INFINITY;
     floor = fmaxf(floor, __shfl_sync(kFull, m.s, 31));
     const int cnt = __popc(__ballot_sync(kFull, isfinite(m.s) && m.s >= wthr));
-    unsigned at = 0;
-    if (lane == 0) {
+    if (lane == 0) {  // fire-and-forget reductions
       if (isfinite(kth)) atomicMax(&hdr->lb, float_to_ordered(kth));
       if (isfinite(floor)) atomicMax(&hdr->floor, float_to_ordered(floor));
-      if (cnt) at = atomicAdd(&hdr->nent, (unsigned)cnt);
+      sh_cnt[q] = cnt;
     }
-    at = __shfl_sync(kFull, at, 0);
-    if (lane < cnt) p.scratch.entries(q)[at + lane] = Entry{m.s, m.id};
+    Entry* const out = reinterpret_cast<Entry*>(smT) + q * 4 * 32;  // this warp's own rows
+    out[lane] = Entry{m.s, m.id};  // sorted: the first cnt are the published ones
+  }
+  // One returning atomic per query, all of them in flight together (a warp
+  // taking its queries' slots one after another would wait out a round trip
+  // to L2 per query), then the appends.
+  __syncthreads();
+  if (!failed && (int)threadIdx.x < p.nq && sh_cnt[threadIdx.x] > 0)
+    sh_cnt[threadIdx.x] |= (int)(atomicAdd(&p.scratch.hdr(threadIdx.x)->nent,
+                                           (unsigned)sh_cnt[threadIdx.x]) << 8);
+  __syncthreads();
+  for (int q = warp; q < p.nq && !failed; q += kBThreads / 32) {
+    const int c = sh_cnt[q] & 0xFF, at = sh_cnt[q] >> 8;
+    if (lane < c) p.scratch.entries(q)[at + lane] = mrg[q * 4 * 32 + lane];
   }
 }
 

@@ -222,56 +222,30 @@ __device__ __forceinline__ void q4_append(bool take, uint32_t row, unsigned* cou
 // multiply-add (results differing from the separately rounded pair), and
 // the reference rounds both.
 //
-// STAGED: each warp streams its tiles through a two-tile shared-memory ring,
-// one bulk copy (cp.async.bulk) per tile (a tile's quads are contiguous), so
-// two whole tiles per warp are in flight while it computes; NW warps per
-// block, sized by the host to the stage bytes a dim needs.  Otherwise (dims
-// whose tiles do not fit) lanes load their quads directly, one quad ahead.
-// A bounded wait that gives up drains the warp's copies and sets hdr->err
-// (the route then reports kError).
-template <int NW, bool STAGED>
-__global__ void __launch_bounds__(NW * 32) int4_bulk_kernel(
+// Lanes load their quads directly, one quad ahead.  The pass is bound by
+// issue (conversion, multiply and add per element, each its own
+// instruction), not by HBM: it keeps many warps per SM resident rather than
+// staging tiles in shared memory, which measured slower (126 vs 114 us per
+// 1M route) with the one block per SM the stages allow.
+constexpr int kQ4BulkWarps = 8;
+
+__global__ void __launch_bounds__(kQ4BulkWarps * 32) int4_bulk_kernel(
     const uint4* __restrict__ q4, const float* __restrict__ nscale, int64_t nodes, int dim,
     const float* __restrict__ query, uint32_t* __restrict__ keys, Q4Hdr* hdr, unsigned M) {
-  // [quads * 16] float4 (q_2j, q_2j, q_2j+1, q_2j+1), then (STAGED) the
-  // warps' rings: NW x 2 x quads KB
-  extern __shared__ __align__(128) unsigned char b4_smem[];
+  constexpr int NW = kQ4BulkWarps;
+  // [quads * 16] float4 (q_2j, q_2j, q_2j+1, q_2j+1)
+  extern __shared__ __align__(16) unsigned char b4_smem[];
   float4* const qq = reinterpret_cast<float4*>(b4_smem);
   __shared__ unsigned hist[kQ4Bins];
   __shared__ float sh_qinv;
   __shared__ unsigned sh_scan[NW + 1];
   __shared__ unsigned sh_above;
   __shared__ int sh_flag;
-  __shared__ __align__(8) uint64_t bar[NW][2];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int quads = q4_quads(dim);
   const int64_t tiles = ceil_div64(nodes, kQ4Tile);
   const int64_t stride = (int64_t)gridDim.x * NW;
-  const unsigned tile_bytes = (unsigned)quads * kQ4Tile * 16;
-  unsigned char* const ring = b4_smem + quads * 16 * sizeof(float4) +
-                              (size_t)warp * 2 * tile_bytes;
-  unsigned phase_bits = 0u, pending_bits = 0u;
-  // the arena is read-only after its build, so the first tiles' copies start
-  // before the wait on the previous kernel of the stream
-  auto issue = [&](int64_t t, int b) {
-    if (lane == 0) {
-      mbar_arrive_expect_tx(&bar[warp][b], tile_bytes);
-      bulk_g2s(ring + b * tile_bytes, q4 + t * (int64_t)quads * kQ4Tile, tile_bytes,
-               &bar[warp][b]);
-    }
-    pending_bits |= 1u << b;
-  };
   const int64_t t_first = (int64_t)blockIdx.x * NW + warp;
-  if constexpr (STAGED) {
-    if (lane == 0) {
-      mbar_init(&bar[warp][0], 1);
-      mbar_init(&bar[warp][1], 1);
-      mbar_fence_init();
-    }
-    __syncwarp();
-    if (t_first < tiles) issue(t_first, 0);
-    if (t_first + stride < tiles) issue(t_first + stride, 1);
-  }
   asm volatile("griddepcontrol.wait;" ::: "memory");
   for (int j = threadIdx.x; j < quads * 16; j += blockDim.x) {
     const float a = 2 * j < dim ? query[2 * j] : 0.0f;
@@ -333,46 +307,19 @@ __global__ void __launch_bounds__(NW * 32) int4_bulk_kernel(
       if (key) atomicAdd(&hist[key >> 20], 1u);
     }
   };
-  if constexpr (STAGED) {
-    int b = 0;
-    bool failed = false;
-    for (int64_t t = t_first; t < tiles; t += stride) {
-      if (!mbar_wait(&bar[warp][b], (phase_bits >> b) & 1u, kWaitLimit)) {
-        failed = true;
-        break;
+  for (int64_t t = t_first; t < tiles; t += stride) {
+    const uint4* base = q4 + t * (int64_t)quads * kQ4Tile + lane;
+    float2 acc = make_float2(0.0f, 0.0f);
+    uint4 na = __ldg(base), nb = __ldg(base + 32);  // quad 0, loaded one quad ahead
+    for (int kq = 0; kq < quads; ++kq) {
+      const uint4 ua = na, ub = nb;
+      if (kq + 1 < quads) {
+        na = __ldg(base + (int64_t)(kq + 1) * kQ4Tile);
+        nb = __ldg(base + (int64_t)(kq + 1) * kQ4Tile + 32);
       }
-      phase_bits ^= 1u << b;
-      pending_bits &= ~(1u << b);
-      const uint4* tb = reinterpret_cast<const uint4*>(ring + b * tile_bytes) + lane;
-      float2 acc = make_float2(0.0f, 0.0f);
-      for (int kq = 0; kq < quads; ++kq) quad(acc, tb[kq * kQ4Tile], tb[kq * kQ4Tile + 32], kq);
-      // buffer b is read: the tile after the next one goes into it
-      __syncwarp();
-      fence_proxy_async_smem();
-      if (t + 2 * stride < tiles) issue(t + 2 * stride, b);
-      finish_tile(t, acc);
-      b ^= 1;
+      quad(acc, ua, ub, kq);
     }
-    if (failed) {
-      for (int k = 0; k < 2; ++k)
-        if ((pending_bits >> k) & 1u) mbar_wait(&bar[warp][k], (phase_bits >> k) & 1u, kWaitLimit);
-      if (lane == 0) atomicOr(&hdr->err, 1);
-    }
-  } else {
-    for (int64_t t = t_first; t < tiles; t += stride) {
-      const uint4* base = q4 + t * (int64_t)quads * kQ4Tile + lane;
-      float2 acc = make_float2(0.0f, 0.0f);
-      uint4 na = __ldg(base), nb = __ldg(base + 32);  // quad 0, loaded one quad ahead
-      for (int kq = 0; kq < quads; ++kq) {
-        const uint4 ua = na, ub = nb;
-        if (kq + 1 < quads) {
-          na = __ldg(base + (int64_t)(kq + 1) * kQ4Tile);
-          nb = __ldg(base + (int64_t)(kq + 1) * kQ4Tile + 32);
-        }
-        quad(acc, ua, ub, kq);
-      }
-      finish_tile(t, acc);
-    }
+    finish_tile(t, acc);
   }
   __syncthreads();
   for (int i = threadIdx.x; i < kQ4Bins; i += blockDim.x)

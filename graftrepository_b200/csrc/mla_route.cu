@@ -1430,11 +1430,13 @@ __device__ __forceinline__ void exact_one(const Params<T>& p, int q, int lane, i
 template <int D, typename T, bool INL = false>
 __global__ void __launch_bounds__(kThreads) mla_exact_kernel(const __grid_constant__ Params<T> p) {
   __shared__ ExactSmem<D> sm;
-  // Launched with programmatic dependent launch after the scan: wait until the
-  // scan grid has completed and its writes are visible (no-op otherwise).
-  // The next route's scan may then be scheduled; it waits for this grid in turn.
-  asm volatile("griddepcontrol.wait;" ::: "memory");
+  // Launched with programmatic dependent launch after the scan.  Every block
+  // of this grid is resident once it reaches the trigger, so the next route's
+  // scan may be scheduled at once: until its own wait on this grid it only
+  // starts copies of the read-only bank, overlapping the scan's last block.
+  // Then wait until the scan grid has completed and its writes are visible.
   asm volatile("griddepcontrol.launch_dependents;");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int q0 = (int)blockIdx.y * kExactQ;
   const int nq = min(kExactQ, p.nq - q0);
@@ -1609,9 +1611,6 @@ struct grm_b200_mla_bank {
   float* d_q4slot_s = nullptr;   // [refine blocks * 32] per-block top entries
   uint32_t* d_q4slot_id = nullptr;
   int q4_slots = 0;              // refine blocks the slots hold
-  int q4_nw = 0;                 // bulk pass: warps per block of the staged kernel (0: direct loads)
-  size_t q4_bulk_smem = 0;       // its dynamic shared memory
-  int q4_bulk_bps = 1;           // its resident blocks per SM
   grm_b200::mla::Q4Hdr* d_q4hdr = nullptr;
 };
 
@@ -2150,37 +2149,9 @@ int int4_prepare(grm_b200_mla_bank* b) {
   int rc = device_info(b->device, &info);
   if (rc) return b->err.set(rc, "device query failed");
   const int grid = info.sms * 8;
-  // The bulk kernel holds the query (quads x 256 B) beside its 16 KB
-  // histogram and, staged, each warp's two-tile ring (quads KB per tile): the
-  // most warps per block (8, 4, 2, 1) whose rings fit.
-  const size_t qq_bytes = sizeof(float4) * 16 * (size_t)q4_quads(b->dim);
-  const size_t tile_kb = (size_t)q4_quads(b->dim) * 1024;
-  constexpr size_t kBulkSmemMax = 200 * 1024;  // dynamic part; the static part is ~17 KB
-  b->q4_nw = 0;
-  for (int nw = 8; nw >= 1 && !b->q4_nw; nw >>= 1)
-    if (qq_bytes + (size_t)nw * 2 * tile_kb <= kBulkSmemMax) b->q4_nw = nw;
-  b->q4_bulk_smem = qq_bytes + (size_t)b->q4_nw * 2 * tile_kb;
-  b->q4_bulk_bps = 1;
-  {
-    auto set_bulk = [&](auto kern) -> cudaError_t {
-      cudaError_t r = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           (int)b->q4_bulk_smem);
-      int bps = 0;
-      if (r == cudaSuccess)
-        r = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&bps, kern,
-                                                          (b->q4_nw ? b->q4_nw : 8) * 32,
-                                                          b->q4_bulk_smem);
-      b->q4_bulk_bps = std::max(1, bps);
-      return r;
-    };
-    switch (b->q4_nw) {
-      case 8: e = set_bulk(int4_bulk_kernel<8, true>); break;
-      case 4: e = set_bulk(int4_bulk_kernel<4, true>); break;
-      case 2: e = set_bulk(int4_bulk_kernel<2, true>); break;
-      case 1: e = set_bulk(int4_bulk_kernel<1, true>); break;
-      default: e = set_bulk(int4_bulk_kernel<8, false>); break;
-    }
-  }
+  // the bulk kernel holds the query (quads x 256 B) beside its 16 KB histogram
+  e = cudaFuncSetAttribute(int4_bulk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)(sizeof(float4) * 16 * q4_quads(4096)));
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(int4_refine_kernel<__half>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -2219,10 +2190,8 @@ int int4_launch(grm_b200_mla_bank* b, const float* dq, int nq, int topk, int64_t
   const int64_t n = b->nodes;
   const unsigned M = (unsigned)std::min<int64_t>(std::max<int64_t>(topk, refine_m), n);
   const int64_t tiles = ceil_div64(n, kQ4Tile);
-  const int bulk_nw = b->q4_nw ? b->q4_nw : 8;
   const int bulk_grid = (int)std::max<int64_t>(
-      1, std::min<int64_t>((int64_t)info.sms * (b->q4_nw ? b->q4_bulk_bps : 6),
-                           ceil_div64(tiles, bulk_nw)));
+      1, std::min<int64_t>((int64_t)info.sms * 6, ceil_div64(tiles, kQ4BulkWarps)));
   const int coll_grid = (int)std::max<int64_t>(
       1, std::min<int64_t>((int64_t)info.sms * 2, ceil_div64(n, kQ4Chunk)));
   const int ref_grid = (int)std::max<int64_t>(
@@ -2238,23 +2207,12 @@ int int4_launch(grm_b200_mla_bank* b, const float* dq, int nq, int topk, int64_t
   cudaLaunchAttribute attr[1];
   for (int q = 0; q < nq; ++q) {
     const float* qp = dq + (int64_t)q * b->dim;
-    cudaLaunchConfig_t cfg = pdl_config(dim3(bulk_grid), dim3(bulk_nw * 32), b->q4_bulk_smem,
-                                        s, attr);
-    const uint4* q4 = reinterpret_cast<const uint4*>(b->d_q4);
-    const float* ns = b->d_q4ns;
-    cudaError_t e;
-    switch (b->q4_nw) {
-      case 8: e = cudaLaunchKernelEx(&cfg, int4_bulk_kernel<8, true>, q4, ns, n, b->dim, qp,
-                                     b->d_q4key, b->d_q4hdr, M); break;
-      case 4: e = cudaLaunchKernelEx(&cfg, int4_bulk_kernel<4, true>, q4, ns, n, b->dim, qp,
-                                     b->d_q4key, b->d_q4hdr, M); break;
-      case 2: e = cudaLaunchKernelEx(&cfg, int4_bulk_kernel<2, true>, q4, ns, n, b->dim, qp,
-                                     b->d_q4key, b->d_q4hdr, M); break;
-      case 1: e = cudaLaunchKernelEx(&cfg, int4_bulk_kernel<1, true>, q4, ns, n, b->dim, qp,
-                                     b->d_q4key, b->d_q4hdr, M); break;
-      default: e = cudaLaunchKernelEx(&cfg, int4_bulk_kernel<8, false>, q4, ns, n, b->dim, qp,
-                                      b->d_q4key, b->d_q4hdr, M); break;
-    }
+    cudaLaunchConfig_t cfg = pdl_config(dim3(bulk_grid), dim3(kQ4BulkWarps * 32),
+                                        sizeof(float4) * 16 * (size_t)q4_quads(b->dim), s, attr);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, int4_bulk_kernel,
+                                       reinterpret_cast<const uint4*>(b->d_q4),
+                                       (const float*)b->d_q4ns, n, b->dim, qp, b->d_q4key,
+                                       b->d_q4hdr, M);
     if (e == cudaSuccess) {
       cfg = pdl_config(dim3(coll_grid), dim3(kQ4CollThreads), 0, s, attr);
       e = cudaLaunchKernelEx(&cfg, int4_collect_kernel, (const uint32_t*)b->d_q4key, n,
