@@ -228,6 +228,51 @@ def mla_inputs(n_queries: int):
     return synth.mla_config(1, NODES, queries=n_queries)
 
 
+def reference_cuda_probe(rows_f32: np.ndarray, queries: np.ndarray, want_ids=None):
+    """The reference's own GPU route (scripts/grm_mla_cuda_probe.py: cuBLAS
+    Sgemv dots over the fp32 arena, fp64 query norm, cosine scores, a
+    one-block top-k kernel), compiled from its CUDA_SOURCE for sm_100a by
+    oracle/Makefile (ref_cuda) and timed here with the probe's own CUDA-event
+    timing of its device query loop, on the same bank and queries.  Returns
+    None when the probe library was not built."""
+    import ctypes
+
+    lib_path = ROOT / "oracle" / "_ref" / "libgrm_mla_cuda_probe.so"
+    if not lib_path.exists():
+        return None
+    lib = ctypes.CDLL(str(lib_path))
+    fp = ctypes.POINTER(ctypes.c_float)
+    lib.grm_mla_cuda_arena_create.argtypes = [fp, ctypes.c_int, ctypes.c_int,
+                                              ctypes.POINTER(ctypes.c_void_p)]
+    lib.grm_mla_cuda_arena_route.argtypes = [ctypes.c_void_p, fp, ctypes.c_int, ctypes.c_int,
+                                             ctypes.c_int, ctypes.c_int,
+                                             ctypes.POINTER(ctypes.c_uint64), fp]
+    lib.grm_mla_cuda_arena_destroy.argtypes = [ctypes.c_void_p]
+    rows = np.ascontiguousarray(rows_f32, dtype=np.float32)
+    q = np.ascontiguousarray(queries, dtype=np.float32)
+    h = ctypes.c_void_p()
+    rc = lib.grm_mla_cuda_arena_create(rows.ctypes.data_as(fp), rows.shape[0], rows.shape[1],
+                                       ctypes.byref(h))
+    if rc != 0:
+        return {"unavailable": f"probe arena create returned {rc}"}
+    out = np.empty((q.shape[0], TOPK), dtype=np.uint64)
+    ms = ctypes.c_float()
+    rc = lib.grm_mla_cuda_arena_route(h, q.ctypes.data_as(fp), q.shape[0], q.shape[1], 3, TOPK,
+                                      out.ctypes.data_as(ctypes.POINTER(ctypes.c_uint64)),
+                                      ctypes.byref(ms))
+    lib.grm_mla_cuda_arena_destroy(h)
+    if rc != 0:
+        return {"unavailable": f"probe route returned {rc}"}
+    per_q = ms.value / q.shape[0]
+    res = {"value": 1e3 / per_q, "unit": UNIT, "ms_per_probe": per_q,
+           "kernels": "cublasSgemv + query_norm + cosine_score + 1-block topk, fp32 arena",
+           "sample": f"{q.shape[0]} probes after 3 warm-up probes, the probe's own event timing"}
+    if want_ids is not None:
+        want = [w[0] if isinstance(w, tuple) else w for w in want_ids]  # (ids, scores) or ids
+        res["ids_equal_exact_route"] = f"{sum([int(x) for x in a] == [int(x) for x in b] for a, b in zip(out, want))}/{len(want)}"
+    return res
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -257,9 +302,17 @@ def run_reference(args):
         route(qs[(args.warmup + i) % n_q])
         times.append(time.perf_counter() - t0)
     dt = sum(times)
+    # the reference's own GPU route kernels on the same bank (same box), with
+    # their top-3 compared to the exact route's (outside the timed steps)
+    n_gpu_q = 8
+    want = [route(qv) for qv in qs[:n_gpu_q]]
     if st is not None:
         st.close()
     value = args.steps / dt
+    try:
+        probe = reference_cuda_probe(rows, qs[:n_gpu_q], want)
+    except Exception as exc:  # no GPU on this host, or the probe failed
+        probe = {"unavailable": f"{type(exc).__name__}: {exc}"}
     sample = (f"each step routes one probe over the full {NODES}-node bank "
               f"(grm_store_route, OpenMP, {cores} threads); median step "
               f"{statistics.median(times) * 1e3:.1f} ms")
@@ -274,6 +327,7 @@ def run_reference(args):
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": kind,
                          "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "reference_cuda_probe": probe,
     }), flush=True)
 
 
