@@ -51,6 +51,7 @@ sys.path.insert(0, str(ROOT))
 METRIC = "1M-node MLA route throughput (1,048,576 x 256 fp16 centroids, top-3, bit-exact)"
 UNIT = "probes/s"
 NODES, DIM, TOPK = 1 << 20, 256, 3
+CFG_SEED = 1   # synth.mla_config seed: config 2 (config 1 is seed 0, 10,000 nodes)
 L2_BYTES = 126 * 1024 * 1024
 
 
@@ -91,11 +92,12 @@ def parse():
                    help="gqa_100k on one GPU: size of the resident node prefix (the whole "
                         "216.5 GB bank does not fit one B200)")
     p.add_argument("--workload", default="mla_1m_b1",
-                   choices=["mla_1m_b1", "mla_1m_b64", "gqa_512", "gqa_100k", "mount_int4",
+                   choices=["mla_1m_b1", "mla_1m_b64", "mla_10k", "gqa_512", "gqa_100k", "mount_int4",
                             "mount_int6", "mount_int8", "mount_ref8", "mount_int4_rope",
                             "mount_ref8_rope", "mla_1m_policy", "mla_1m_multi", "mla_1m_int4"],
-                   help="mla_1m_b1 is the headline (BASELINE config 2); the others measure "
-                        "the GQA route (configs 3/4) and the quantised mount (config 5)")
+                   help="mla_1m_b1 is the headline (BASELINE config 2); mla_10k is config 1; "
+                        "the others measure the GQA route (configs 3/4) and the quantised "
+                        "mount (config 5)")
     return p.parse_args()
 
 
@@ -108,7 +110,10 @@ def peaks():
 
 
 def profile_traffic(batch: int = 1):
-    """dram bytes per scan launch from the committed ncu summary, if any."""
+    """dram bytes per scan launch from the committed ncu summary, if any (the
+    summaries describe the 1M bank)."""
+    if NODES != 1 << 20:
+        return None
     f = ROOT / "profiles" / ("mla_scan_1m.md" if batch == 1 else "mla_batch_1m_b64.md")
     if not f.exists():
         return None
@@ -225,7 +230,7 @@ def mla_inputs(n_queries: int):
     """Config 2's bank and queries (one generator, identical in both arms)."""
     from graftrepository_b200 import synth
 
-    return synth.mla_config(1, NODES, queries=n_queries)
+    return synth.mla_config(CFG_SEED, NODES, queries=n_queries)
 
 
 def reference_cuda_probe(rows_f32: np.ndarray, queries: np.ndarray, want_ids=None):
@@ -313,6 +318,21 @@ def run_reference(args):
         probe = reference_cuda_probe(rows, qs[:n_gpu_q], want)
     except Exception as exc:  # no GPU on this host, or the probe failed
         probe = {"unavailable": f"{type(exc).__name__}: {exc}"}
+    one = None
+    if O.ref_available(omp=False):   # the default single-threaded build CMake ships
+        st1 = O.RefStore(omp=False).load_mla(rows)
+        st1.route(qs[0], TOPK)
+        ts = []
+        t_end = time.perf_counter() + 10.0
+        while (time.perf_counter() < t_end and len(ts) < 20) or len(ts) < 2:
+            t0 = time.perf_counter()
+            st1.route(qs[(len(ts) + 1) % n_q], TOPK)
+            ts.append(time.perf_counter() - t0)
+        st1.close()
+        one = {"value": 1.0 / statistics.median(ts), "unit": UNIT, "cores": 1,
+               "kind": "reference",
+               "sample": f"{len(ts)} probes over the full bank, median "
+                         f"{statistics.median(ts) * 1e3:.2f} ms (default build, no OpenMP)"}
     sample = (f"each step routes one probe over the full {NODES}-node bank "
               f"(grm_store_route, OpenMP, {cores} threads); median step "
               f"{statistics.median(times) * 1e3:.1f} ms")
@@ -326,6 +346,112 @@ def run_reference(args):
                    "recipe": "synth.mla_config(1): default_rng(1), rows then queries"},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": kind,
                          "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "reference_cuda_probe": probe,
+        "cpu_1thread": one,
+    }), flush=True)
+
+
+def run_reference_gqa(args):
+    """Reference arm of the GQA workload gqa_512 (config 3): the reference's CPU
+    route (grm_store_route_gqa, OpenMP and single-threaded builds) on a node
+    prefix scaled per token, and its own GPU route (scripts/grm_gqa_cuda_probe.py:
+    a zero-padded dense fp32 bank, per-kv-head cublasSgemm, an abs-max reduce
+    kernel, a one-block top-k) on the whole bank, same box.  The bank is drawn
+    by the same device generator as the other arm (synth.gqa_bank_device)."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import ctypes
+
+    import torch
+
+    import oracle as O
+    from graftrepository_b200 import synth
+
+    KH, D, H = 32, 128, 128
+    lengths = synth.gqa_lengths(2, 512, "uniform")
+    keys_dev, off = synth.gqa_bank_device(2 * 1000, lengths)
+    n_q = max(4, min(args.warmup + args.steps, 64))
+    qs = synth.gqa_query(2, count=n_q)
+    tokens = int(off[-1])
+    cpu = cpu_gqa_baseline(keys_dev, off, qs[0], KH, D)
+    keys16 = keys_dev.view(torch.int16).cpu().numpy().view(np.uint16)
+    del keys_dev
+    torch.cuda.empty_cache()
+    one = None
+    n_pre = int(np.searchsorted(off, 40_000, side="right")) - 1
+    t_pre = int(off[n_pre])
+    if O.ref_available(omp=False):
+        with O.RefStore(omp=False).load_gqa(keys16[: t_pre * KH * D], off[: n_pre + 1], KH,
+                                             D) as st1:
+            st1.route(qs[0], TOPK)
+            ts = []
+            for i in range(3):
+                t0 = time.perf_counter()
+                st1.route(qs[i % n_q], TOPK)
+                ts.append(time.perf_counter() - t0)
+        per_tok = statistics.median(ts) / t_pre
+        one = {"value": 1.0 / (per_tok * tokens), "unit": UNIT, "cores": 1, "kind": "reference",
+               "sample": f"{n_pre}-node prefix ({t_pre} tokens), median "
+                         f"{statistics.median(ts) * 1e3:.1f} ms, scaled per token to {tokens}"}
+    probe = None
+    lib_path = ROOT / "oracle" / "_ref" / "libgrm_gqa_cuda_probe.so"
+    if lib_path.exists():
+        tmax = int(lengths.max())
+        dense = np.zeros((len(lengths), KH, tmax, D), np.float32)
+        bits = keys16.astype(np.uint32) << 16
+        f32 = bits.view(np.float32)
+        for i in range(len(lengths)):
+            t = int(lengths[i])
+            dense[i, :, :t] = f32[int(off[i]) * KH * D: int(off[i + 1]) * KH * D].reshape(KH, t, D)
+        del bits, f32
+        lib = ctypes.CDLL(str(lib_path))
+        fp = ctypes.POINTER(ctypes.c_float)
+        lib.grm_gqa_cuda_arena_create.argtypes = [fp, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                                  ctypes.c_int, ctypes.POINTER(ctypes.c_void_p)]
+        lib.grm_gqa_cuda_arena_route.argtypes = [ctypes.c_void_p, fp, ctypes.c_int, ctypes.c_int,
+                                                 ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                                 ctypes.POINTER(ctypes.c_uint64), fp]
+        lib.grm_gqa_cuda_arena_destroy.argtypes = [ctypes.c_void_p]
+        h = ctypes.c_void_p()
+        rc = lib.grm_gqa_cuda_arena_create(dense.ctypes.data_as(fp), len(lengths), KH, tmax, D,
+                                           ctypes.byref(h))
+        del dense
+        if rc != 0:
+            probe = {"unavailable": f"probe arena create returned {rc}"}
+        else:
+            nq = min(8, n_q)
+            qv = np.ascontiguousarray(qs[:nq], dtype=np.float32)
+            out = np.empty((nq, TOPK), dtype=np.uint64)
+            ms = ctypes.c_float()
+            rc = lib.grm_gqa_cuda_arena_route(h, qv.ctypes.data_as(fp), nq, H, 1, 3, TOPK,
+                                              out.ctypes.data_as(ctypes.POINTER(ctypes.c_uint64)),
+                                              ctypes.byref(ms))
+            lib.grm_gqa_cuda_arena_destroy(h)
+            if rc != 0:
+                probe = {"unavailable": f"probe route returned {rc}"}
+            else:
+                want = [O.gqa_route(keys16, off, KH, D, q, TOPK)[0] for q in qv[:2]]
+                same = sum([int(x) for x in a] == [int(x) for x in b] for a, b in zip(out, want))
+                probe = {"value": 1e3 / (ms.value / nq), "unit": UNIT,
+                         "ms_per_probe": ms.value / nq,
+                         "kernels": "per-kv-head cublasSgemm over a zero-padded fp32 bank + "
+                                    "abs-max reduce + 1-block topk",
+                         "padded_bank_bytes": len(lengths) * KH * tmax * D * 4,
+                         "sample": f"{nq} probes after 3 warm-up probes, the probe's own event "
+                                   f"timing",
+                         "ids_equal_exact_route": f"{same}/{len(want)}"}
+    value = cpu["value"]
+    print(json.dumps({
+        "impl": "reference", "metric": f"ragged GQA route throughput ({args.workload})",
+        "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": 1e3 / value, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32 keys (bf16 values), f32 dots",
+        "data": "synthetic",
+        "config": {"workload": args.workload, "nodes": int(len(lengths)), "tokens_total": tokens,
+                   "kv_heads": KH, "q_heads": H, "head_dim": D, "topk": TOPK},
+        "cpu_baseline": cpu, "cpu_1thread": one,
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "reference_cuda_probe": probe,
     }), flush=True)
@@ -1284,9 +1410,16 @@ def run_multi(args):
 
 
 def main():
+    global NODES, METRIC, CFG_SEED
     args = parse()
+    if args.workload == "mla_10k":   # seed 0, 10,000 x 256, top-3
+        NODES, CFG_SEED = 10_000, 0
+        METRIC = "10k-node MLA route throughput (config 1: 10,000 x 256 fp16, top-3, bit-exact)"
     if args.impl == "reference":
-        run_reference(args)
+        if args.workload.startswith("gqa"):
+            run_reference_gqa(args)
+        else:
+            run_reference(args)
     elif args.workload.startswith("gqa"):
         run_gqa(args)
     elif args.workload.startswith("mount"):
