@@ -13,10 +13,10 @@
 //
 // Operands.  The bank tile is loaded by TMA (2D tensor map, 128-byte swizzle,
 // box 64 elements x 128 rows, one box per 128-byte K atom) into a ring of
-// shared-memory stages (as many as fit).  The query matrix is built once per batch by
-// batch_prep_kernel: q' = q / |q| (fp64 norm), scaled by 2^8 (no fp16
-// subnormals) and rounded to fp16, written in the same K-major swizzled layout
-// and copied into shared memory with one bulk copy.
+// shared-memory stages (as many as fit).  The query matrix is built by every
+// CTA in its own shared memory (build_query_image): q' = q / |q| (fp64 norm),
+// scaled by 2^8 (no fp16 subnormals) and rounded to fp16, in the same K-major
+// swizzled layout; no separate prep kernel stands between two batches.
 //
 // Roles (one CTA per SM, persistent over 128-row tiles b, b + grid, ...):
 //   warps 0..7         epilogue: warp w reads tensor-memory lanes 32*(w % 4)..
@@ -54,6 +54,7 @@ constexpr int kBQ = 64;                    // queries per launch
 constexpr int kBMq = 128;                  // MMA M: the kBQ queries, twice
 constexpr int kBM = 128;                   // bank rows per tile (MMA N)
 constexpr int kBSmemMax = 232448;          // dynamic shared memory a CTA may use (227 KB)
+constexpr int kBCoResident = 32 * 1024;    // left free for other kernels' blocks
 constexpr int kBEpi = 8;                   // epilogue warps 0..7
 constexpr int kBThreads = 10 * 32;
 constexpr int kBProducerWarp = 8;
@@ -78,9 +79,11 @@ struct BLayout {
   static constexpr int kQ = KA * kAtomQ;
   static constexpr int kMerge = kBQ * 4 * 32 * 8;      // end-of-scan list exchange
   // As many stages as fit beside the query image (1 KB alignment slack, 1 KB
-  // for the static shared variables).  D = 256: 5 stages (2.5 tiles), 128: 6
-  // (6 tiles), 64: 13.
-  static constexpr int kStages = (kBSmemMax - 2048 - kQ) / kStage;
+  // for the static shared variables), leaving kBCoResident bytes so that the
+  // previous batch's merge and resolve blocks fit on the SM beside this CTA
+  // (the next batch starts while they run).  D = 256: 4 stages (2 tiles),
+  // 128: 5 (5 tiles), 64: 11.
+  static constexpr int kStages = (kBSmemMax - 2048 - kBCoResident - kQ) / kStage;
   static constexpr int kSmem = 1024 + kQ + kStages * kStage;  // + alignment slack
   static_assert(D % 64 == 0 && D <= 256, "batched dims: 64, 128, 256");
   static_assert(kStages >= 2 * SPT && kStages <= 16, "stage ring: two tiles at least");
@@ -89,7 +92,8 @@ struct BLayout {
 
 struct BatchParams {
   CUtensorMap tmap;              // bank [nodes, D] fp16, box 64 x 128, 128-byte swizzle
-  const unsigned char* qmat;     // swizzled query image, BLayout<D>::kQ bytes
+  const float* queries;          // [nq, D] fp32 probes of this batch
+  int overlap;                   // 1: the scratch rows are this launch's own (see the kernel)
   const float* rnorms;           // 2^-8 / row norm (NaN for non-finite rows)
   const uint32_t* allow;         // route filters: routable rows (nullptr: all)
   int64_t nodes;
@@ -249,35 +253,36 @@ __device__ __forceinline__ float pick32(const float (&v)[32], int c) {
 
 // ---- kernels -----------------------------------------------------------------
 
-// One warp per query 0..kBQ-1: unit-normalise (fp64 norm), scale by 2^8,
-// round to fp16, write the swizzled image at rows j and kBQ + j; queries past
-// the batch are zero.  Records whether the query is inside the batched path's
-// safe range.
+// The batch's query image in this CTA's shared memory, in the swizzled
+// K-major layout of the MMA's A operand, the queries at rows j and kBQ + j:
+// q' = q / |q| (fp64 sum of squares, lane-strided then a butterfly, so every
+// CTA builds the same bits), scaled by 2^8 (no fp16 subnormals) and rounded to
+// fp16.  Rows of queries outside the safe range, and rows past the batch, are
+// zero.  Builder warp w of nw takes queries w, w + nw, ...; qsafe[j] records
+// whether query j is inside the batched path's safe range.
 template <int D>
-__global__ void __launch_bounds__(32) batch_prep_kernel(const float* queries, int nq,
-                                                        unsigned char* qmat, Scratch scratch) {
-  // The batch kernel may start now: it streams the read-only bank into its
-  // stage ring and waits for this grid before it reads the query image.
-  asm volatile("griddepcontrol.launch_dependents;");
-  const int j = blockIdx.x, lane = threadIdx.x;
-  bool safe = false;
-  float inv = 0.0f;
-  if (j < nq) {
-    const float* q = queries + (int64_t)j * D;
-    double acc = 0.0;
-    for (int d = lane; d < D; d += 32) acc = fma((double)q[d], (double)q[d], acc);
+__device__ __forceinline__ void build_query_image(const float* queries, int nq, unsigned char* img,
+                                                  int* qsafe, int w, int nw, int lane) {
+  for (int j = w; j < kBQ; j += nw) {
+    bool safe = false;
+    float inv = 0.0f;
+    if (j < nq) {
+      const float* q = queries + (int64_t)j * D;
+      double acc = 0.0;
+      for (int d = lane; d < D; d += 32) acc = fma((double)q[d], (double)q[d], acc);
 #pragma unroll
-    for (int o = 16; o >= 1; o >>= 1) acc += __shfl_xor_sync(kFull, acc, o);
-    const double qn = sqrt(acc);
-    safe = isfinite(qn) && qn >= kBSafeLo && qn < kSafeHi;
-    inv = safe ? (float)(1.0 / qn) : 0.0f;
+      for (int o = 16; o >= 1; o >>= 1) acc += __shfl_xor_sync(kFull, acc, o);
+      const double qn = sqrt(acc);
+      safe = isfinite(qn) && qn >= kBSafeLo && qn < kSafeHi;
+      inv = safe ? (float)(1.0 / qn) : 0.0f;
+    }
+    for (int d = lane; d < D; d += 32) {
+      const __half h = __float2half_rn(safe ? queries[(int64_t)j * D + d] * inv * kBQScale : 0.0f);
+      *reinterpret_cast<__half*>(img + qmat_offset(j, d)) = h;
+      *reinterpret_cast<__half*>(img + qmat_offset(kBQ + j, d)) = h;  // second copy
+    }
+    if (lane == 0) qsafe[j] = safe ? 1 : 0;
   }
-  for (int d = lane; d < D; d += 32) {
-    const __half h = __float2half_rn(safe ? queries[(int64_t)j * D + d] * inv * kBQScale : 0.0f);
-    *reinterpret_cast<__half*>(qmat + qmat_offset(j, d)) = h;
-    *reinterpret_cast<__half*>(qmat + qmat_offset(kBQ + j, d)) = h;  // second copy
-  }
-  if (j < nq && lane == 0) scratch.hdr(j)->qsafe = safe ? 1 : 0;
 }
 
 // 2^-8 / row norm for the batch epilogue (NaN for non-finite rows).
@@ -304,6 +309,7 @@ __global__ void __launch_bounds__(kBThreads, 1)
   __shared__ uint32_t sh_tmem;
   __shared__ int sh_fail;
   __shared__ unsigned sh_issued, sh_consumed;
+  __shared__ int sh_qsafe[kBQ];
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t my_tiles =
@@ -317,10 +323,17 @@ __global__ void __launch_bounds__(kBThreads, 1)
   const int cq = (warp >> 2) * 2 + (lq >> 1);
   const int qi = (lq & 1) * 32 + lane;  // this thread's query
 
-  // The query image and the scratch headers come from batch_prep_kernel
-  // (programmatic dependent launch): every thread waits for it after the
-  // set-up below, except the producer lane, which first fills the stage ring
-  // from the read-only bank.
+  // Programmatic dependent launch: nothing before this grid's wait reads
+  // memory the preceding kernel writes.  The bank and its norms are written
+  // only at attach; the queries are the caller's input (none of this
+  // library's kernels that let their dependents start early writes them), so
+  // the producer streams the bank and the other warps build the query image
+  // at once.  The scratch rows are read before the wait only when this
+  // launch owns them (p.overlap: consecutive batches alternate between two
+  // scratch sets, and the set was released by a merge that completed before
+  // the previous batch passed its own wait); otherwise the epilogue waits
+  // first.  Every thread waits before the publish, so this grid completes
+  // after its predecessor.
   if (threadIdx.x == 0) {
     for (int s = 0; s < LY::kStages; ++s) {
       mbar_init(&full[s], 1);
@@ -330,7 +343,7 @@ __global__ void __launch_bounds__(kBThreads, 1)
     mbar_init(&tfull[1], 1);
     mbar_init(&tempty[0], kBEpi);
     mbar_init(&tempty[1], kBEpi);
-    mbar_init(&bq_bar, 1);
+    mbar_init(&bq_bar, kBEpi + 1);  // the image builders: warps 0..7 and the MMA warp
     mbar_init(&mma_done, 1);
     sh_fail = 0;
     sh_issued = 0;
@@ -345,19 +358,18 @@ __global__ void __launch_bounds__(kBThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sh_tmem;
-  const bool producer = warp == kBProducerWarp && lane == 0;
-  if (!producer) asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (warp != kBProducerWarp) {
+    build_query_image<D>(p.queries, p.nq, smQ, sh_qsafe, warp < kBEpi ? warp : kBEpi, kBEpi + 1,
+                         lane);
+    fence_proxy_async_smem();  // generic-proxy writes, read by the tensor cores
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&bq_bar);
+    if (epi && !p.overlap) asm volatile("griddepcontrol.wait;" ::: "memory");
+  }
 
   if (warp == kBProducerWarp) {
     if (lane == 0) {  // TMA producer
       const uint64_t pol = l2_evict_first_policy();
-      bool qcopied = false;
-      auto copy_query = [&]() {  // after batch_prep_kernel has completed
-        asm volatile("griddepcontrol.wait;" ::: "memory");
-        mbar_arrive_expect_tx(&bq_bar, LY::kQ);
-        bulk_g2s(smQ, p.qmat, LY::kQ, &bq_bar);
-        qcopied = true;
-      };
       int st = 0;
       unsigned ph = 0, issued = 0;
       bool ok = true;
@@ -378,10 +390,8 @@ __global__ void __launch_bounds__(kBThreads, 1)
             st = 0;
             ph ^= 1u;
           }
-          if (!qcopied && issued == LY::kStages) copy_query();  // the ring is full
         }
       }
-      if (!qcopied) copy_query();
       sh_issued = issued;
       if (!ok) atomicOr(&sh_fail, 1);
     }
@@ -519,8 +529,11 @@ __global__ void __launch_bounds__(kBThreads, 1)
       for (int j = 0; j < 32; ++j) e[j] = j < C ? Entry{L.s[j], L.id[j]} : Entry{-INFINITY, kNoRow};
     }
   }
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // every thread, before the publish
   __syncwarp();
   __syncthreads();
+  if (blockIdx.x == 0)  // the merge kernel reads the safe flags
+    for (int j = threadIdx.x; j < p.nq; j += blockDim.x) p.scratch.hdr(j)->qsafe = sh_qsafe[j];
 
   // Teardown: every bulk load issued has landed, every MMA has completed.
   if (warp == kBProducerWarp && lane == 0 && sh_fail) {
@@ -605,10 +618,15 @@ __global__ void __launch_bounds__(kBMergeWarps * 32)
   __shared__ FinishSmem<kBMergeWarps, D> fsm;
   const int q = blockIdx.x;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  // The query side before the wait on the scan: the queries were written
-  // before batch_prep_kernel ran, and this grid starts only after every
-  // block of the scan passed its own wait on that kernel.  The last warp's
-  // reference query norm (a serial fp64 chain) overlaps the scan's tail.
+  // The resolve kernel, and after it the next batch, may be scheduled at once:
+  // the resolve waits for this grid; the next batch, until its own wait, reads
+  // only the bank, its queries and the scratch set this batch did not use.
+  asm volatile("griddepcontrol.launch_dependents;");
+  // The query side before the wait on the scan: the queries are the caller's
+  // input (read by the scan before its own wait, see mla_batch_kernel), and
+  // this grid starts only after every block of the scan passed its wait.  The
+  // last warp's reference query norm (a serial fp64 chain) overlaps the
+  // scan's tail.
   const float* query = p.queries + (int64_t)q * D;
   for (int d = threadIdx.x; d < D; d += blockDim.x) {
     const float v = query[d];
@@ -618,7 +636,6 @@ __global__ void __launch_bounds__(kBMergeWarps * 32)
   __syncthreads();
   if (warp == kBMergeWarps - 1 && lane == 0) fsm.qn = query_norm_seq_t<D>(fsm.qraw);
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  asm volatile("griddepcontrol.launch_dependents;");
   const bool safe = __ldcg(&p.scratch.hdr(q)->qsafe) != 0;
   final_merge<D, __half, false, kBMergeWarps, true>(p, q, kBMargin, safe, lane, warp, fsm);
 }

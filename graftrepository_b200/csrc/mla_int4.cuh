@@ -222,36 +222,35 @@ __device__ __forceinline__ void q4_append(bool take, uint32_t row, unsigned* cou
 // multiply-add (results differing from the separately rounded pair), and
 // the reference rounds both.
 //
-// Lanes load their quads directly, one quad ahead.  The pass is bound by
-// issue (conversion, multiply and add per element, each its own
-// instruction), not by HBM: it keeps many warps per SM resident rather than
-// staging tiles in shared memory, which measured slower (126 vs 114 us per
-// 1M route) with the one block per SM the stages allow.
+// Lanes load their quads directly.  The pass is bound by issue (conversion,
+// multiply and add per element, each its own instruction), not by HBM: it
+// keeps many warps per SM resident rather than staging tiles in shared
+// memory, which measured slower (126 vs 114 us per 1M route) with the one
+// block per SM the stages allow.  QC > 0: the dim's quad count at compile
+// time (dims 64/128/256), the tile loop fully unrolled with each quad loaded
+// two quads ahead; QC == 0: any dim, one quad ahead.
 constexpr int kQ4BulkWarps = 8;
 
+template <int QC>
 __global__ void __launch_bounds__(kQ4BulkWarps * 32) int4_bulk_kernel(
     const uint4* __restrict__ q4, const float* __restrict__ nscale, int64_t nodes, int dim,
     const float* __restrict__ query, uint32_t* __restrict__ keys, Q4Hdr* hdr, unsigned M) {
   constexpr int NW = kQ4BulkWarps;
-  // [quads * 16] float4 (q_2j, q_2j, q_2j+1, q_2j+1)
+  // the query, zero-padded to quads * 32 values
   extern __shared__ __align__(16) unsigned char b4_smem[];
-  float4* const qq = reinterpret_cast<float4*>(b4_smem);
+  float* const qf = reinterpret_cast<float*>(b4_smem);
   __shared__ unsigned hist[kQ4Bins];
   __shared__ float sh_qinv;
   __shared__ unsigned sh_scan[NW + 1];
   __shared__ unsigned sh_above;
   __shared__ int sh_flag;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int quads = q4_quads(dim);
+  const int quads = QC > 0 ? QC : q4_quads(dim);
   const int64_t tiles = ceil_div64(nodes, kQ4Tile);
   const int64_t stride = (int64_t)gridDim.x * NW;
   const int64_t t_first = (int64_t)blockIdx.x * NW + warp;
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  for (int j = threadIdx.x; j < quads * 16; j += blockDim.x) {
-    const float a = 2 * j < dim ? query[2 * j] : 0.0f;
-    const float b = 2 * j + 1 < dim ? query[2 * j + 1] : 0.0f;
-    qq[j] = make_float4(a, a, b, b);
-  }
+  for (int j = threadIdx.x; j < quads * 32; j += blockDim.x) qf[j] = j < dim ? query[j] : 0.0f;
   for (int i = threadIdx.x; i < kQ4Bins; i += blockDim.x) hist[i] = 0;
   if (threadIdx.x == 0) {
     const double qn = query_norm_seq(query, dim);
@@ -273,22 +272,25 @@ __global__ void __launch_bounds__(kQ4BulkWarps * 32) int4_bulk_kernel(
     for (int w = 0; w < 4; ++w) {
       const uint32_t la = wa4[w] & 0x0F0F0F0Fu, ha = (wa4[w] >> 4) & 0x0F0F0F0Fu;
       const uint32_t lb = wb4[w] & 0x0F0F0F0Fu, hb = (wb4[w] >> 4) & 0x0F0F0F0Fu;
-      const float4* qk = qq + (kq * 4 + w) * 4;  // elements (kq*4 + w)*8 .. +7
+      // the query at elements (kq*4 + w)*8 .. +7
+      const float4 q0 = *reinterpret_cast<const float4*>(qf + (kq * 4 + w) * 8);
+      const float4 q1 = *reinterpret_cast<const float4*>(qf + (kq * 4 + w) * 8 + 4);
+      const float qe[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
 #pragma unroll
       for (int m = 0; m < 4; ++m) {
-        const float4 qp = qk[m];
+        const float qlo = qe[2 * m], qhi = qe[2 * m + 1];  // elements 2m, 2m + 1
         const unsigned sel = 0x7440u + (unsigned)m;  // [byte m, 0, 0, 0x4B]
         // the values, exact small integers (a packed subtract: nothing to fuse)
         float2 v = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(la, 0x4B000000u, sel)),
                                           __uint_as_float(__byte_perm(lb, 0x4B000000u, sel))),
                               magic);
-        acc.x = __fadd_rn(acc.x, __fmul_rn(qp.x, v.x));
-        acc.y = __fadd_rn(acc.y, __fmul_rn(qp.y, v.y));
+        acc.x = __fadd_rn(acc.x, __fmul_rn(qlo, v.x));
+        acc.y = __fadd_rn(acc.y, __fmul_rn(qlo, v.y));
         v = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(ha, 0x4B000000u, sel)),
                                    __uint_as_float(__byte_perm(hb, 0x4B000000u, sel))),
                        magic);
-        acc.x = __fadd_rn(acc.x, __fmul_rn(qp.z, v.x));
-        acc.y = __fadd_rn(acc.y, __fmul_rn(qp.w, v.y));
+        acc.x = __fadd_rn(acc.x, __fmul_rn(qhi, v.x));
+        acc.y = __fadd_rn(acc.y, __fmul_rn(qhi, v.y));
       }
     }
   };
@@ -307,19 +309,42 @@ __global__ void __launch_bounds__(kQ4BulkWarps * 32) int4_bulk_kernel(
       if (key) atomicAdd(&hist[key >> 20], 1u);
     }
   };
-  for (int64_t t = t_first; t < tiles; t += stride) {
-    const uint4* base = q4 + t * (int64_t)quads * kQ4Tile + lane;
-    float2 acc = make_float2(0.0f, 0.0f);
-    uint4 na = __ldg(base), nb = __ldg(base + 32);  // quad 0, loaded one quad ahead
-    for (int kq = 0; kq < quads; ++kq) {
-      const uint4 ua = na, ub = nb;
-      if (kq + 1 < quads) {
-        na = __ldg(base + (int64_t)(kq + 1) * kQ4Tile);
-        nb = __ldg(base + (int64_t)(kq + 1) * kQ4Tile + 32);
+  if constexpr (QC > 0) {
+    for (int64_t t = t_first; t < tiles; t += stride) {
+      const uint4* base = q4 + t * (int64_t)QC * kQ4Tile + lane;
+      float2 acc = make_float2(0.0f, 0.0f);
+      uint4 ra[QC], rb[QC];  // static indices only: the loop below is unrolled
+      ra[0] = __ldg(base);
+      rb[0] = __ldg(base + 32);
+      if (QC > 1) {
+        ra[1] = __ldg(base + kQ4Tile);
+        rb[1] = __ldg(base + kQ4Tile + 32);
       }
-      quad(acc, ua, ub, kq);
+#pragma unroll
+      for (int kq = 0; kq < QC; ++kq) {
+        if (kq + 2 < QC) {
+          ra[kq + 2] = __ldg(base + (kq + 2) * kQ4Tile);
+          rb[kq + 2] = __ldg(base + (kq + 2) * kQ4Tile + 32);
+        }
+        quad(acc, ra[kq], rb[kq], kq);
+      }
+      finish_tile(t, acc);
     }
-    finish_tile(t, acc);
+  } else {
+    for (int64_t t = t_first; t < tiles; t += stride) {
+      const uint4* base = q4 + t * (int64_t)quads * kQ4Tile + lane;
+      float2 acc = make_float2(0.0f, 0.0f);
+      uint4 na = __ldg(base), nb = __ldg(base + 32);  // quad 0, loaded one quad ahead
+      for (int kq = 0; kq < quads; ++kq) {
+        const uint4 ua = na, ub = nb;
+        if (kq + 1 < quads) {
+          na = __ldg(base + (int64_t)(kq + 1) * kQ4Tile);
+          nb = __ldg(base + (int64_t)(kq + 1) * kQ4Tile + 32);
+        }
+        quad(acc, ua, ub, kq);
+      }
+      finish_tile(t, acc);
+    }
   }
   __syncthreads();
   for (int i = threadIdx.x; i < kQ4Bins; i += blockDim.x)

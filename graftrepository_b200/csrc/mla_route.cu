@@ -1562,11 +1562,11 @@ struct grm_b200_mla_bank {
   bool exact_only = false;
   bool bulk = false;         // scan with the bulk-copy kernel
   bool batch = false;        // batches of queries go to the tensor-core route
-  unsigned char* d_qmat = nullptr;  // its swizzled query image
   float* d_rnorms = nullptr;        // its 2^-8 / row norm table
   CUtensorMap tmap;                 // its bank tensor map
   int grid_x = 1;
   int scratch_queries = 0;
+  int scratch_set = 0;  // the scratch set of the last route launched (see scratch_base)
   size_t stride = 0;
   unsigned char* d_scratch = nullptr;
   Result* d_results = nullptr;         // async entries
@@ -1743,7 +1743,8 @@ int reserve(grm_b200_mla_bank* b, int queries) {
   b->d_results_mapped = nullptr;
   b->scratch_queries = 0;
   b->stride = scratch_stride(b->grid_x);
-  cudaError_t e = cudaMalloc(&b->d_scratch, b->stride * n);
+  // two scratch sets (see scratch_base)
+  cudaError_t e = cudaMalloc(&b->d_scratch, b->stride * n * 2);
   if (e == cudaSuccess) e = cudaMalloc(&b->d_results, sizeof(Result) * n);
   if (e == cudaSuccess)
     e = cudaHostAlloc(reinterpret_cast<void**>(&b->h_results), sizeof(Result) * n,
@@ -1751,12 +1752,22 @@ int reserve(grm_b200_mla_bank* b, int queries) {
   if (e == cudaSuccess)
     e = cudaHostGetDevicePointer(reinterpret_cast<void**>(&b->d_results_mapped), b->h_results, 0);
   if (e != cudaSuccess) return b->err.set(cuda_status(e), "scratch allocation failed: %s", cudaGetErrorString(e));
-  scratch_init_kernel<<<(n + 127) / 128, 128, 0, b->stream>>>(b->d_scratch, b->stride, n);
+  scratch_init_kernel<<<(2 * n + 127) / 128, 128, 0, b->stream>>>(b->d_scratch, b->stride, 2 * n);
   e = cudaGetLastError();
   if (e == cudaSuccess) e = cudaStreamSynchronize(b->stream);
   if (e != cudaSuccess) return b->err.set(cuda_status(e), "scratch init failed: %s", cudaGetErrorString(e));
   b->scratch_queries = n;
   return 0;
+}
+
+// Two scratch sets of scratch_queries rows each.  A batched route takes the
+// set the previous route did not use and touches its rows before its
+// programmatic-launch wait (mla_batch_kernel, p.overlap); every other launch
+// uses the current set and touches scratch only after its wait.  A set a
+// batch takes was last used two routes back, whose merge completed before
+// the previous route passed its own wait.
+unsigned char* scratch_base(const grm_b200_mla_bank* b) {
+  return b->d_scratch + (size_t)b->scratch_set * b->stride * (size_t)b->scratch_queries;
 }
 
 template <typename T>
@@ -1768,7 +1779,7 @@ Params<T> make_params(grm_b200_mla_bank* b, const float* dq, int topk) {
   p.dim = b->dim;
   p.queries = dq;
   p.topk = topk;
-  p.scratch = Scratch{b->d_scratch, b->stride, b->grid_x};
+  p.scratch = Scratch{scratch_base(b), b->stride, b->grid_x};
   p.results = b->d_results;
   p.out_ids = nullptr;
   p.out_scores = nullptr;
@@ -1898,10 +1909,7 @@ int setup_batch(grm_b200_mla_bank* b) {
   int rc = b->dim == 64 ? batch_smem_attr<64>() : b->dim == 128 ? batch_smem_attr<128>()
                                                                  : batch_smem_attr<256>();
   if (rc) return b->err.set(rc, "batched route setup failed");
-  const size_t qbytes = (size_t)(b->dim / 64) * kBMq * 128;
-  cudaError_t e = cudaMalloc(&b->d_qmat, qbytes);
-  if (e == cudaSuccess) e = cudaMemsetAsync(b->d_qmat, 0, qbytes, b->stream);  // zero query rows
-  if (e == cudaSuccess) e = cudaMalloc(&b->d_rnorms, sizeof(float) * (size_t)b->nodes);
+  cudaError_t e = cudaMalloc(&b->d_rnorms, sizeof(float) * (size_t)b->nodes);
   if (e == cudaSuccess) {
     const int grid = (int)std::min<int64_t>(ceil_div64(b->nodes, 256), 148 * 8);
     batch_rnorm_kernel<<<grid, 256, 0, b->stream>>>(b->d_norms, b->nodes, b->d_rnorms);
@@ -1932,12 +1940,10 @@ cudaLaunchConfig_t pdl_config(dim3 grid, dim3 block, size_t smem, cudaStream_t s
 // are resolved by the exact kernel launched after it.
 template <int D>
 int launch_batch_chunk(grm_b200_mla_bank* b, const Params<__half>& p, int nq, cudaStream_t s) {
-  batch_prep_kernel<D><<<kBQ, 32, 0, s>>>(p.queries, nq, b->d_qmat, p.scratch);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_status(e);
   BatchParams bp;
   bp.tmap = b->tmap;
-  bp.qmat = b->d_qmat;
+  bp.queries = p.queries;
+  bp.overlap = 1;
   bp.rnorms = b->d_rnorms;
   bp.allow = p.allow;
   bp.nodes = b->nodes;
@@ -1948,7 +1954,7 @@ int launch_batch_chunk(grm_b200_mla_bank* b, const Params<__half>& p, int nq, cu
   const int grid = (int)std::min<int64_t>(b->grid_x, bp.tiles);
   cudaLaunchAttribute attr[1];
   cudaLaunchConfig_t cfg = pdl_config(dim3(grid), dim3(kBThreads), BLayout<D>::kSmem, s, attr);
-  e = p.topk <= 4 ? cudaLaunchKernelEx(&cfg, mla_batch_kernel<D, 8>, bp)
+  cudaError_t e = p.topk <= 4 ? cudaLaunchKernelEx(&cfg, mla_batch_kernel<D, 8>, bp)
                   : cudaLaunchKernelEx(&cfg, mla_batch_kernel<D, kBList>, bp);
   if (e != cudaSuccess) return cuda_status(e);
   cfg = pdl_config(dim3(nq), dim3(kBMergeWarps * 32), 0, s, attr);
@@ -1956,7 +1962,11 @@ int launch_batch_chunk(grm_b200_mla_bank* b, const Params<__half>& p, int nq, cu
   return cuda_status(e);
 }
 
-int launch_batch(grm_b200_mla_bank* b, const Params<__half>& p0, int nq, cudaStream_t s) {
+// Switches the bank to the other scratch set and points p0 (the caller's
+// params, which its resolve launch reuses) at it.
+int launch_batch(grm_b200_mla_bank* b, Params<__half>& p0, int nq, cudaStream_t s) {
+  b->scratch_set ^= 1;
+  p0.scratch.base = scratch_base(b);
   for (int c0 = 0; c0 < nq; c0 += kBQ) {
     const int n = std::min(kBQ, nq - c0);
     Params<__half> p = p0;
@@ -2149,9 +2159,9 @@ int int4_prepare(grm_b200_mla_bank* b) {
   int rc = device_info(b->device, &info);
   if (rc) return b->err.set(rc, "device query failed");
   const int grid = info.sms * 8;
-  // the bulk kernel holds the query (quads x 256 B) beside its 16 KB histogram
-  e = cudaFuncSetAttribute(int4_bulk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           (int)(sizeof(float4) * 16 * q4_quads(4096)));
+  // the bulk kernel holds the query (quads x 128 B) beside its 16 KB histogram
+  e = cudaFuncSetAttribute(int4_bulk_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)(sizeof(float) * 32 * q4_quads(4096)));
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(int4_refine_kernel<__half>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -2208,11 +2218,19 @@ int int4_launch(grm_b200_mla_bank* b, const float* dq, int nq, int topk, int64_t
   for (int q = 0; q < nq; ++q) {
     const float* qp = dq + (int64_t)q * b->dim;
     cudaLaunchConfig_t cfg = pdl_config(dim3(bulk_grid), dim3(kQ4BulkWarps * 32),
-                                        sizeof(float4) * 16 * (size_t)q4_quads(b->dim), s, attr);
-    cudaError_t e = cudaLaunchKernelEx(&cfg, int4_bulk_kernel,
-                                       reinterpret_cast<const uint4*>(b->d_q4),
-                                       (const float*)b->d_q4ns, n, b->dim, qp, b->d_q4key,
-                                       b->d_q4hdr, M);
+                                        sizeof(float) * 32 * (size_t)q4_quads(b->dim), s, attr);
+    const uint4* q4 = reinterpret_cast<const uint4*>(b->d_q4);
+    const float* ns = b->d_q4ns;
+    const int qc = q4_quads(b->dim);
+    cudaError_t e =
+        qc == 8   ? cudaLaunchKernelEx(&cfg, int4_bulk_kernel<8>, q4, ns, n, b->dim, qp,
+                                       b->d_q4key, b->d_q4hdr, M)
+        : qc == 4 ? cudaLaunchKernelEx(&cfg, int4_bulk_kernel<4>, q4, ns, n, b->dim, qp,
+                                       b->d_q4key, b->d_q4hdr, M)
+        : qc == 2 ? cudaLaunchKernelEx(&cfg, int4_bulk_kernel<2>, q4, ns, n, b->dim, qp,
+                                       b->d_q4key, b->d_q4hdr, M)
+                  : cudaLaunchKernelEx(&cfg, int4_bulk_kernel<0>, q4, ns, n, b->dim, qp,
+                                       b->d_q4key, b->d_q4hdr, M);
     if (e == cudaSuccess) {
       cfg = pdl_config(dim3(coll_grid), dim3(kQ4CollThreads), 0, s, attr);
       e = cudaLaunchKernelEx(&cfg, int4_collect_kernel, (const uint32_t*)b->d_q4key, n,
@@ -2291,7 +2309,6 @@ void bank_free(grm_b200_mla_bank* b) {
   if (b->d_rows) cudaFree(b->d_rows);
   if (b->d_norms) cudaFree(b->d_norms);
   if (b->d_fallbacks) cudaFree(b->d_fallbacks);
-  if (b->d_qmat) cudaFree(b->d_qmat);
   if (b->d_rnorms) cudaFree(b->d_rnorms);
   if (b->d_scratch) cudaFree(b->d_scratch);
   if (b->d_results) cudaFree(b->d_results);

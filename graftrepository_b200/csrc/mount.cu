@@ -45,7 +45,16 @@ struct Rope {
   int dim;
   int pair_swap;
   int aligned;  // dim a power of two <= 256, offset % dim == 0, 16-byte aligned tables
+  // aligned mode: ceil(2^32 / d) for d = rope pieces per row and d = width, so
+  // n / d = umulhi(n, m) for the n the kernel divides (0: divide instead)
+  uint32_t m_nrp, m_w;
 };
+
+// n / d by the precomputed multiplier m = ceil(2^32 / d), exact while
+// n * d < 2^32 (the host sets m = 0 otherwise, and d's integer division runs).
+__device__ __forceinline__ int div_pre(int n, uint32_t m, int d) {
+  return m ? (int)__umulhi((uint32_t)n, m) : n / d;
+}
 
 __device__ __forceinline__ float bf16_round(float f) {
   return __bfloat162float(__float2bfloat16_rn(f));
@@ -137,17 +146,14 @@ __device__ __forceinline__ void unpack8(uint4 o, float (&f)[8]) {
 // at 2*(j0 mod dim/2)) from obuf, rotates and stores it.  A head never
 // straddles a tile: tiles start at multiples of 2048 values, heads at
 // multiples of dim.  Rope pieces are numbered over the slice, nrp per row.
-__device__ __forceinline__ int rope_pieces_before(int u, int width, int offset, int nrp) {
-  const int t = u / width, c = u - t * width;
-  return t * nrp + min(max((c - offset) >> 3, 0), nrp);
-}
-
-// The tile's rope pieces [p0, p1), numbered over the slice.
+// The tile's rope pieces [p0, p1), numbered over the slice.  The tile ends
+// in row t0 + (col0 + nv) / width (a small quotient: col0 + nv < width + 2048).
 __device__ __forceinline__ void rope_range(int v0, int t0, int col0, int nv, int width,
                                            const Rope& rope, int& p0, int& p1) {
   const int nrp = (width - rope.offset) >> 3;
   p0 = t0 * nrp + min(max((col0 - rope.offset) >> 3, 0), nrp);
-  p1 = rope_pieces_before(v0 + nv, width, rope.offset, nrp);
+  const int e = col0 + nv, dt = div_pre(e, rope.m_w, width);
+  p1 = (t0 + dt) * nrp + min(max((e - dt * width - rope.offset) >> 3, 0), nrp);
 }
 
 __device__ __forceinline__ void rope_pass(const uint4* obuf, uint16_t* dst, int v0, int p0,
@@ -156,18 +162,17 @@ __device__ __forceinline__ void rope_pass(const uint4* obuf, uint16_t* dst, int 
   const int nrp = (width - rope.offset) >> 3;
   const int half = rope.dim >> 1;
   for (int pc = p0 + lane; pc < p1; pc += 32) {
-    const int r = pc / nrp, q = pc - r * nrp;
+    const int r = div_pre(pc, rope.m_nrp, nrp), q = pc - r * nrp;
     const int v = r * width + rope.offset + 8 * q - v0;  // in the tile
     const int j0 = (8 * q) & (rope.dim - 1);
     const int head = v - j0;
-    const bool lo = j0 < half;
-    uint32_t xw[8], rw[8];  // x' and rotate_half(x') as fp32 bit patterns
+    const bool lo = j0 < half;  // first half: r = -x'_{partner}, by a sign-flip multiply below
+    uint32_t xw[8], rw[8];  // x' and the partner values as fp32 bit patterns
     if (!rope.pair_swap) {
       const uint4 a = obuf[v >> 3];
-      uint4 b = obuf[(head + (lo ? j0 + half : j0 - half)) >> 3];
-      const uint32_t neg = lo ? 0x80008000u : 0u;  // first half: r = -x'_{j+half}
+      const uint4 b = obuf[(head + (lo ? j0 + half : j0 - half)) >> 3];
       const uint32_t aw[4] = {a.x, a.y, a.z, a.w};
-      const uint32_t bw[4] = {b.x ^ neg, b.y ^ neg, b.z ^ neg, b.w ^ neg};
+      const uint32_t bw[4] = {b.x, b.y, b.z, b.w};
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
         xw[2 * k] = aw[k] << 16;
@@ -179,13 +184,17 @@ __device__ __forceinline__ void rope_pass(const uint4* obuf, uint16_t* dst, int 
       const int base = head + (lo ? 2 * j0 : 2 * (j0 - half));
       const uint4 a = obuf[base >> 3], b = obuf[(base >> 3) + 1];
       const uint32_t sw8[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+      // one byte permute per value: the even (low) or odd (high) half of S[k]
+      // under a zero low half; x' takes the even values in the first half of
+      // the head, the partner the odd ones, and the other way round after
+      const unsigned sel_x = lo ? 0x1044u : 0x3244u, sel_r = lo ? 0x3244u : 0x1044u;
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
-        const uint32_t ev = sw8[k] << 16, od = sw8[k] & 0xFFFF0000u;
-        xw[k] = lo ? ev : od;
-        rw[k] = lo ? od ^ 0x80000000u : ev;
+        xw[k] = __byte_perm(sw8[k], 0u, sel_x);
+        rw[k] = __byte_perm(sw8[k], 0u, sel_r);
       }
     }
+    const float sgn = lo ? -1.0f : 1.0f;  // -(r * s) == (-r) * s, exactly
     const int at = (int)(seat + r) * rope.dim + j0;
     const float4* cs = reinterpret_cast<const float4*>(rope.cos + at);
     const float4* sn = reinterpret_cast<const float4*>(rope.sin + at);
@@ -196,7 +205,7 @@ __device__ __forceinline__ void rope_pass(const uint4* obuf, uint16_t* dst, int 
 #pragma unroll
     for (int k = 0; k < 8; ++k)
       f[k] = __fadd_rn(__fmul_rn(__uint_as_float(xw[k]), cv[k]),
-                       __fmul_rn(__uint_as_float(rw[k]), sv[k]));
+                       __fmul_rn(__fmul_rn(__uint_as_float(rw[k]), sv[k]), sgn));
     uint4 o;
     o.x = bf16x2_bits(f[0], f[1]);
     o.y = bf16x2_bits(f[2], f[3]);
@@ -532,7 +541,7 @@ int mount_grid(int64_t slices, int64_t vals) {
 // tables' rows.
 bool rope_ok(const grm_b200_rope_spec* spec, int64_t width, const Seats& seats, int64_t n_grafts,
              int64_t tokens, Rope* out) {
-  *out = Rope{nullptr, nullptr, 0, 0, 0, 0};
+  *out = Rope{nullptr, nullptr, 0, 0, 0, 0, 0, 0};
   if (!spec) return true;
   if (!spec->cos_device || !spec->sin_device || spec->dim <= 0 || spec->dim % 16 != 0 ||
       spec->offset < 0 || spec->offset % 8 != 0 || spec->offset >= width ||
@@ -546,8 +555,17 @@ bool rope_ok(const grm_b200_rope_spec* spec, int64_t width, const Seats& seats, 
                        spec->rows * d < ((int64_t)1 << 31) &&  // 32-bit table index
                        reinterpret_cast<uintptr_t>(spec->cos_device) % 16 == 0 &&
                        reinterpret_cast<uintptr_t>(spec->sin_device) % 16 == 0;
+  // division multipliers of the aligned rope pass: pieces numbered up to
+  // tokens * nrp are divided by nrp, in-tile column sums below width + 2048
+  // by width; each is exact while numerator x divisor < 2^32
+  auto magic = [](int64_t n_max, int64_t d) -> uint32_t {
+    if (d <= 1 || n_max * d >= ((int64_t)1 << 32)) return 0u;
+    return (uint32_t)((((uint64_t)1 << 32) + (uint64_t)d - 1) / (uint64_t)d);
+  };
+  const int64_t nrp = (width - spec->offset) / 8;
   *out = Rope{spec->cos_device, spec->sin_device, (int)spec->offset, (int)d,
-              spec->pair_swap ? 1 : 0, aligned ? 1 : 0};
+              spec->pair_swap ? 1 : 0, aligned ? 1 : 0, magic(tokens * nrp + 32, nrp),
+              magic(width + 2048, width)};
   return true;
 }
 
