@@ -753,12 +753,21 @@ __global__ void __launch_bounds__(1024) select_kernel(RouteParams p) {
     }
     list.offer_margin(v, (uint32_t)n, lane, p.topk, 0.0f);  // only the k-th is needed
   }
-  sh_s[warp * 32 + lane] = list.s;
-  sh_id[warp * 32 + lane] = list.id;
-  __syncthreads();
+  // the 32 warp lists merged pairwise in five rounds (offer_margin keeps the
+  // k best by (score, node), so the merge order does not change the result)
+#pragma unroll 1
+  for (int stride = 16; stride >= 1; stride >>= 1) {
+    if (warp >= stride && warp < 2 * stride) {
+      sh_s[warp * 32 + lane] = list.s;
+      sh_id[warp * 32 + lane] = list.id;
+    }
+    __syncthreads();
+    if (warp < stride)
+      list.offer_margin(sh_s[(warp + stride) * 32 + lane], sh_id[(warp + stride) * 32 + lane],
+                        lane, p.topk, 0.0f);
+    __syncthreads();
+  }
   if (warp == 0) {
-    for (int w = 1; w < 32; ++w)
-      list.offer_margin(sh_s[w * 32 + lane], sh_id[w * 32 + lane], lane, p.topk, 0.0f);
     const float L = __shfl_sync(kFull, list.s, p.topk - 1);
     if (lane == 0) sh_L = L;
   }
@@ -941,20 +950,21 @@ __global__ void __launch_bounds__(256) refine_kernel(RouteParams p) {
 // maxima and atomics are those of refine_kernel.  Every wait is bounded: a
 // wait that gives up drains the warp's loads and sets qinfo->err, which makes
 // the route report an error.
-constexpr int kRefWarps = 8;
-constexpr int kRefStages = 3;
+constexpr int kRefWarps = 12;
+constexpr int kRefStages = 2;
 
 template <int D>
 struct RefLayout {
-  static constexpr int kBuf = TmaLayout<D>::kBuf;                     // one staged unit
-  static constexpr int kSmem = 1024 + kRefWarps * kRefStages * kBuf;  // + alignment slack
+  static constexpr int kBuf = TmaLayout<D>::kBuf;  // one staged unit
+  static constexpr int kQSlice = D * 16;           // one kv head's four query vectors
+  static constexpr int kSmem = 1024 + kRefWarps * (kRefStages * kBuf + kQSlice);
 };
 
 template <typename KT, int D>
 __global__ void __launch_bounds__(kRefWarps * 32, 1)
     refine_tma_kernel(const __grid_constant__ CUtensorMap tmap, RouteParams p) {
   using LY = TmaLayout<D>;
-  static_assert(kRefWarps * 32 == kRefineChunk, "one candidate of a chunk per thread");
+  static_assert(kRefWarps * 32 >= kRefineChunk, "one candidate of a chunk per thread");
   extern __shared__ unsigned char rsm_raw[];
   unsigned char* const rsm = rsm_raw + ((1024u - (smem_u32(rsm_raw) & 1023u)) & 1023u);
   __shared__ __align__(8) uint64_t bar[kRefWarps][kRefStages];
@@ -970,6 +980,12 @@ __global__ void __launch_bounds__(kRefWarps * 32, 1)
   }
   __syncwarp();
   unsigned char* const buf0 = rsm + warp * kRefStages * LY::kBuf;
+  // this warp's copy of the current kv head's transposed query (when a kv head
+  // has at most four query vectors: the whole query does not fit beside the
+  // rings, and read through L1 it misses, L1 being what the rings leave)
+  float4* const qs_w = reinterpret_cast<float4*>(rsm + kRefWarps * kRefStages * LY::kBuf) +
+                       warp * D;
+  int cached_kh = -1;
   const uint64_t pol = l2_evict_first_policy();
   const bool qfinite = p.qinfo->finite != 0;
   const int nv4 = (p.nv + 3) >> 2;
@@ -994,14 +1010,15 @@ __global__ void __launch_bounds__(kRefWarps * 32, 1)
       const int64_t T = (int64_t)(p.off[node + 1] - p.off[node]);
       if (T > 0 && !p.key_bad[node] && qfinite) my_units = (int64_t)p.kh_n * ((T + 31) >> 5);
     }
+    const bool scanner = threadIdx.x < kRefineChunk;
     if (threadIdx.x == 0) s_pref[0] = 0;
-    s_pref[threadIdx.x + 1] = my_units;
+    if (scanner) s_pref[threadIdx.x + 1] = my_units;
     __syncthreads();
 #pragma unroll 1
     for (int o = 1; o < kRefineChunk; o <<= 1) {  // inclusive scan of s_pref[1..256]
-      const int64_t v = (int)threadIdx.x >= o ? s_pref[threadIdx.x + 1 - o] : 0;
+      const int64_t v = (scanner && (int)threadIdx.x >= o) ? s_pref[threadIdx.x + 1 - o] : 0;
       __syncthreads();
-      s_pref[threadIdx.x + 1] += v;
+      if (scanner) s_pref[threadIdx.x + 1] += v;
       __syncthreads();
     }
     const int64_t total = failed ? 0 : s_pref[cn];
@@ -1070,8 +1087,16 @@ __global__ void __launch_bounds__(kRefWarps * 32, 1)
       const bool live = cur.t0 + lane < cur.T;  // rows past the candidate's tokens are masked
       unsigned* best_out = p.headmax + (int64_t)(c0 + cur.lo) * p.heads;
       const float4* qk = reinterpret_cast<const float4*>(p.qT) + (int64_t)cur.kh * nv4 * D;
+      if (nv4 == 1 && cur.kh != cached_kh) {
+        __syncwarp();
+        for (int i = lane; i < D; i += 32) qs_w[i] = __ldg(qk + i);
+        __syncwarp();
+        cached_kh = cur.kh;
+      }
       for (int v4 = 0; v4 < nv4; ++v4) {
         const float4* q = qk + (int64_t)v4 * D;
+        // the four vectors' values at dim d: shared memory or global
+        auto qat = [&](int d) -> float4 { return nv4 == 1 ? qs_w[d] : __ldg(q + d); };
         float dot[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
         for (int c = 0; c < D / 8; ++c) {  // 16-byte chunk c: dims 8c .. 8c+7, in order
@@ -1081,7 +1106,7 @@ __global__ void __launch_bounds__(kRefWarps * 32, 1)
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
             const float kf = key_to_f(kk[e]);
-            const float4 qv = __ldg(q + c * 8 + e);
+            const float4 qv = qat(c * 8 + e);
             dot[0] = __fadd_rn(dot[0], __fmul_rn(qv.x, kf));
             dot[1] = __fadd_rn(dot[1], __fmul_rn(qv.y, kf));
             dot[2] = __fadd_rn(dot[2], __fmul_rn(qv.z, kf));
