@@ -204,6 +204,10 @@ struct RouteParams {
   const uint32_t* allow;       // bitmap of routable nodes (nullptr: all)
   const uint32_t* hits;        // [N] lexical hits of this query (lexical routes)
   int lex_m;                   // query lexical keys; > 0 selects the normalised lexical law
+  // per (node, head) approximate maxima of the scan, kept by node_bounds for
+  // the filtered refine (nullptr: not kept); eps_abs as node_bounds uses it
+  float* amax;
+  float eps_abs;
   // query vectors transposed for the staged refine: [KH][ceil(nv/4)][D][4],
   // vector 4*v4 + j of kv head kh at dim d (zero past nv); nullptr: not used
   float* qT;
@@ -695,6 +699,7 @@ __global__ void node_bounds_kernel(RouteParams p, float eps_abs) {
       unsigned* slot = p.headmax + node * p.heads + h;
       const float b = __uint_as_float(*slot);
       *slot = 0u;
+      if (p.amax) p.amax[node * p.heads + h] = b;
       const float km = p.kmax[node * p.kh_n + h / p.group];
       const float qn = p.qnorm_h[h];
       const float mag = qn * km;
@@ -950,6 +955,17 @@ __global__ void __launch_bounds__(256) refine_kernel(RouteParams p) {
 // maxima and atomics are those of refine_kernel.  Every wait is bounded: a
 // wait that gives up drains the warp's loads and sets qinfo->err, which makes
 // the route report an error.
+//
+// Filtered mode (NT > 0, p.amax set, the query on the fast path): a head's
+// exact maximum is the exact dot of some (token, query vector) pair, and only
+// pairs whose approximate dot comes within twice the approximation bound of
+// the scan's approximate maximum can hold it.  Each unit first recomputes the
+// scan's approximate dots on the tensor cores (the scan's query fragments and
+// MMA over the staged rows), queues the pairs that pass that test, and the
+// lanes then take the queued pairs one each for the exact sequential dot.
+// The maximum over the queued pairs equals the maximum over all pairs, so the
+// result is bit-identical to the unfiltered refine.  Heads whose |q||k| bound
+// overflows the approximation's range queue every pair.
 constexpr int kRefWarps = 12;
 constexpr int kRefStages = 2;
 
@@ -960,10 +976,12 @@ struct RefLayout {
   static constexpr int kSmem = 1024 + kRefWarps * (kRefStages * kBuf + kQSlice);
 };
 
-template <typename KT, int D>
+template <typename KT, int D, int NT>
 __global__ void __launch_bounds__(kRefWarps * 32, 1)
     refine_tma_kernel(const __grid_constant__ CUtensorMap tmap, RouteParams p) {
   using LY = TmaLayout<D>;
+  constexpr int KSTEPS = D / 16;
+  constexpr int W = D / 32;
   static_assert(kRefWarps * 32 >= kRefineChunk, "one candidate of a chunk per thread");
   extern __shared__ unsigned char rsm_raw[];
   unsigned char* const rsm = rsm_raw + ((1024u - (smem_u32(rsm_raw) & 1023u)) & 1023u);
@@ -993,6 +1011,22 @@ __global__ void __launch_bounds__(kRefWarps * 32, 1)
   const int64_t nw = (int64_t)gridDim.x * kRefWarps;
   unsigned phase_bits = 0u, pending_bits = 0u;
   bool failed = false;
+  // filtered mode: the scan's query fragments of the current kv head, the
+  // thresholds of this lane's (head, vector) columns for the current
+  // (node, kv head), and the warp's queue of pairs for the exact pass (it
+  // takes the place of qs_w, which filtered mode does not use)
+  const bool filt = NT > 0 && p.amax != nullptr && p.qinfo->fast_ok != 0;
+  constexpr int NTR = NT > 0 ? NT : 1;
+  constexpr int kTiles = NT <= 1 ? 1 : NT / 2;  // 8-vector column tiles after the hi/lo sum
+  const int g = lane >> 2, c4 = lane & 3;
+  const int cmax = NT <= 1 ? 2 : 4;  // lanes c4 < cmax hold distinct columns
+  uint32_t bq[NTR][2 * KSTEPS];
+  float thr[kTiles][2];
+  int frag_kh = -1;
+  int64_t thr_key = -1;
+  uint16_t* const queue = reinterpret_cast<uint16_t*>(qs_w);
+  static_assert(32 * 16 * sizeof(uint16_t) <= D * 16, "queue fits the query slice");
+  const float* const qTf = reinterpret_cast<const float*>(p.qT);
 
   // A position in the chunk's flattened units.
   struct Unit {
@@ -1001,6 +1035,7 @@ __global__ void __launch_bounds__(kRefWarps * 32, 1)
     int64_t T;     // tokens of the candidate
     int64_t t0;    // first token of the unit
     uint64_t o0;   // the candidate's first token
+    int64_t node;
   };
   for (int c0 = 0; c0 < count; c0 += kRefineChunk) {
     const int cn = min(kRefineChunk, count - c0);
@@ -1026,6 +1061,7 @@ __global__ void __launch_bounds__(kRefWarps * 32, 1)
     const int64_t u_begin = total * gw / nw, u_end = total * (gw + 1) / nw;
     auto load_cand = [&](Unit& u) {
       const int64_t node = p.cand[c0 + u.lo];
+      u.node = node;
       u.o0 = p.off[node];
       u.T = (int64_t)(p.off[node + 1] - u.o0);
     };
@@ -1087,13 +1123,123 @@ __global__ void __launch_bounds__(kRefWarps * 32, 1)
       const bool live = cur.t0 + lane < cur.T;  // rows past the candidate's tokens are masked
       unsigned* best_out = p.headmax + (int64_t)(c0 + cur.lo) * p.heads;
       const float4* qk = reinterpret_cast<const float4*>(p.qT) + (int64_t)cur.kh * nv4 * D;
-      if (nv4 == 1 && cur.kh != cached_kh) {
+      if constexpr (NT > 0) {
+        if (filt) {
+          if (cur.kh != frag_kh) {
+            const uint32_t* fsrc = p.frag + ((int64_t)cur.kh * NT * 32 + lane) * (2 * KSTEPS);
+#pragma unroll
+            for (int t = 0; t < NT; ++t)
+#pragma unroll
+              for (int w2 = 0; w2 < 2 * KSTEPS; ++w2)
+                bq[t][w2] = __ldg(fsrc + (int64_t)t * 32 * 2 * KSTEPS + w2);
+            frag_kh = cur.kh;
+          }
+          const int64_t key = cur.node * p.kh_n + cur.kh;
+          if (key != thr_key) {
+            // column (t, e) of this lane is query vector t*8 + 2*c4 + e; a
+            // NaN threshold never queues (lanes without a column, vectors
+            // past nv), -inf queues every live row (forced heads)
+            const float km = p.kmax[key];
+#pragma unroll
+            for (int t = 0; t < kTiles; ++t)
+#pragma unroll
+              for (int e = 0; e < 2; ++e) {
+                const int vi = t * 8 + 2 * c4 + e;
+                float th = __int_as_float(0x7FC00000);
+                if (c4 < cmax && vi < p.nv) {
+                  const int h = cur.kh * p.group + vi / p.qt;
+                  const float qn = p.qnorm_h[h];
+                  const float mag = qn * km;
+                  if (!(mag < kHuge)) {
+                    th = -INFINITY;
+                  } else {
+                    const float err = kEps * p.inv_denom * mag + p.eps_abs * p.inv_denom * km;
+                    th = p.amax[cur.node * p.heads + h] - 2.0f * err;
+                  }
+                }
+                thr[t][e] = th;
+              }
+            thr_key = key;
+          }
+          const int valid = (int)(cur.T - cur.t0 < 32 ? cur.T - cur.t0 : 32);
+          const unsigned below = (1u << lane) - 1u;
+          int qn_w = 0;  // pairs queued by the warp (uniform)
+#pragma unroll
+          for (int tl = 0; tl < 2; ++tl) {
+            uint32_t ra[2 * KSTEPS], rb[2 * KSTEPS];
+            const int r0 = tl * 16 + g, r1 = r0 + 8;
+#pragma unroll
+            for (int w2 = 0; w2 < W; ++w2) {
+              const int box = w2 / 2, chunk = 2 * c4 + (w2 % 2);
+              const uint4 va = *reinterpret_cast<const uint4*>(
+                  sb + box * LY::kBox + r0 * 128 + ((chunk ^ (r0 & 7)) * 16));
+              const uint4 vb = *reinterpret_cast<const uint4*>(
+                  sb + box * LY::kBox + r1 * 128 + ((chunk ^ (r1 & 7)) * 16));
+              ra[4 * w2] = va.x; ra[4 * w2 + 1] = va.y; ra[4 * w2 + 2] = va.z; ra[4 * w2 + 3] = va.w;
+              rb[4 * w2] = vb.x; rb[4 * w2 + 1] = vb.y; rb[4 * w2 + 2] = vb.z; rb[4 * w2 + 3] = vb.w;
+            }
+            float acc[NTR][4];
+#pragma unroll
+            for (int t = 0; t < NT; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.0f;
+#pragma unroll
+            for (int s2 = 0; s2 < KSTEPS; ++s2) {
+              const uint32_t a[4] = {ra[2 * s2], rb[2 * s2], ra[2 * s2 + 1], rb[2 * s2 + 1]};
+#pragma unroll
+              for (int t = 0; t < NT; ++t) mma16816<KT>(acc[t], a, bq[t][2 * s2], bq[t][2 * s2 + 1]);
+            }
+            // o[t][j]: j = 0/1 row r0 columns e = 0/1, j = 2/3 row r1
+            float o[kTiles][4];
+            if constexpr (NT == 1) {
+#pragma unroll
+              for (int j = 0; j < 4; ++j) o[0][j] = acc[0][j] + __shfl_xor_sync(kFull, acc[0][j], 2);
+            } else {
+#pragma unroll
+              for (int t = 0; t < kTiles; ++t)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) o[t][j] = acc[t][j] + acc[t + kTiles][j];
+            }
+#pragma unroll
+            for (int t = 0; t < kTiles; ++t)
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const int e = j & 1;
+                const int r = (j < 2) ? r0 : r1;
+                const float th = thr[t][e];
+                const bool m = r < valid && (th == -INFINITY || fabsf(o[t][j]) * p.inv_denom >= th);
+                const unsigned bal = __ballot_sync(kFull, m);
+                if (m) queue[qn_w + __popc(bal & below)] = (uint16_t)((r << 8) | (t * 8 + 2 * c4 + e));
+                qn_w += __popc(bal);
+              }
+          }
+          __syncwarp();
+          // exact pass: lane i takes queued pairs i, i + 32, ...
+          for (int i = lane; i < qn_w; i += 32) {
+            const int ent = queue[i];
+            const int r = ent >> 8, vi = ent & 255;
+            const float* qv = qTf + (((int64_t)cur.kh * nv4 + (vi >> 2)) * D) * 4 + (vi & 3);
+            float dot = 0.0f;
+#pragma unroll 4
+            for (int c = 0; c < D / 8; ++c) {
+              const uint4 raw = *reinterpret_cast<const uint4*>(
+                  sb + (c / 8) * LY::kBox + r * 128 + (((c % 8) ^ (r & 7)) * 16));
+              const KT* kk = reinterpret_cast<const KT*>(&raw);
+#pragma unroll
+              for (int e = 0; e < 8; ++e)
+                dot = __fadd_rn(dot, __fmul_rn(__ldg(qv + (c * 8 + e) * 4), key_to_f(kk[e])));
+            }
+            float v = __fmul_rn(fabsf(dot), p.inv_denom);
+            if (!(v == v)) v = 0.0f;  // a NaN row never raises best
+            if (v > 0.0f) atomicMax(best_out + cur.kh * p.group + vi / p.qt, __float_as_uint(v));
+          }
+        }
+      }
+      if (!filt && nv4 == 1 && cur.kh != cached_kh) {
         __syncwarp();
         for (int i = lane; i < D; i += 32) qs_w[i] = __ldg(qk + i);
         __syncwarp();
         cached_kh = cur.kh;
       }
-      for (int v4 = 0; v4 < nv4; ++v4) {
+      for (int v4 = 0; v4 < (filt ? 0 : nv4); ++v4) {
         const float4* q = qk + (int64_t)v4 * D;
         // the four vectors' values at dim d: shared memory or global
         auto qat = [&](int d) -> float4 { return nv4 == 1 ? qs_w[d] : __ldg(q + d); };
@@ -1273,6 +1419,7 @@ struct grm_b200_gqa_bank {
   float* d_kmax = nullptr;
   unsigned char* d_key_bad = nullptr;
   unsigned* d_headmax = nullptr;
+  float* d_amax = nullptr;   // [nodes, heads] scan maxima kept for the filtered refine
   int headmax_heads = 0;
   float* d_lo = nullptr;
   float* d_hi = nullptr;
@@ -1350,9 +1497,10 @@ cudaError_t tma_smem_attr() {
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                TmaLayout<D>::kSmem);
-  if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(refine_tma_kernel<KT, D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             RefLayout<D>::kSmem);
+  for (auto fn : {refine_tma_kernel<KT, D, 0>, refine_tma_kernel<KT, D, 1>,
+                  refine_tma_kernel<KT, D, 2>, refine_tma_kernel<KT, D, 4>})
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, RefLayout<D>::kSmem);
   return e;
 }
 
@@ -1447,11 +1595,23 @@ cudaError_t launch_refine(grm_b200_gqa_bank* b, const RouteParams& p) {
   if constexpr (sizeof(KT) == 2) {
     if (p.qT) {  // staged keys (the TMA scan's tensor map): one CTA per SM
       const dim3 grid(std::max(1, b->sms)), block(kRefWarps * 32);
-      if (b->dim == 128)
-        return launch_chained(refine_tma_kernel<KT, 128>, grid, block,
-                              (size_t)RefLayout<128>::kSmem, b->stream, b->tmap, p);
-      return launch_chained(refine_tma_kernel<KT, 64>, grid, block,
-                            (size_t)RefLayout<64>::kSmem, b->stream, b->tmap, p);
+      // filtered when the scan ran with fragments of nt tiles
+      const int nt = p.amax ? nt_for(p.nv) : 0;
+      auto go = [&](auto kernel, size_t smem) {
+        return launch_chained(kernel, grid, block, smem, b->stream, b->tmap, p);
+      };
+      if (b->dim == 128) {
+        constexpr size_t sm = RefLayout<128>::kSmem;
+        if (nt == 1) return go(refine_tma_kernel<KT, 128, 1>, sm);
+        if (nt == 2) return go(refine_tma_kernel<KT, 128, 2>, sm);
+        if (nt == 4) return go(refine_tma_kernel<KT, 128, 4>, sm);
+        return go(refine_tma_kernel<KT, 128, 0>, sm);
+      }
+      constexpr size_t sm = RefLayout<64>::kSmem;
+      if (nt == 1) return go(refine_tma_kernel<KT, 64, 1>, sm);
+      if (nt == 2) return go(refine_tma_kernel<KT, 64, 2>, sm);
+      if (nt == 4) return go(refine_tma_kernel<KT, 64, 4>, sm);
+      return go(refine_tma_kernel<KT, 64, 0>, sm);
     }
   }
   // one wave: as many blocks as are resident together (measured once)
@@ -1485,10 +1645,13 @@ cudaError_t launch_refine(grm_b200_gqa_bank* b, const RouteParams& p) {
 int ensure_heads(grm_b200_gqa_bank* b, int heads, int nt) {
   if (heads > b->headmax_heads) {
     if (b->d_headmax) cudaFree(b->d_headmax);
+    if (b->d_amax) cudaFree(b->d_amax);
     b->d_headmax = nullptr;
+    b->d_amax = nullptr;
     b->headmax_heads = 0;
     const size_t n = (size_t)b->nodes * heads;
     cudaError_t e = cudaMalloc(&b->d_headmax, n * sizeof(unsigned));
+    if (e == cudaSuccess && b->tma) e = cudaMalloc(&b->d_amax, n * sizeof(float));
     if (e == cudaSuccess) e = cudaMemsetAsync(b->d_headmax, 0, n * sizeof(unsigned), b->stream);
     // later launches may use another stream: finish the zero fill now (first use only)
     if (e == cudaSuccess) e = cudaStreamSynchronize(b->stream);
@@ -1583,6 +1746,11 @@ int route_one(grm_b200_gqa_bank* b, const float* dq, int heads, int qt, int topk
   p.hits = hits;
   p.lex_m = lex_m;
   p.qT = b->tma ? b->d_qT : nullptr;
+  // the filtered refine (approximate dots on tensor cores, exact dots only for
+  // tokens the scan's maxima cannot rule out) needs the scan's fragments
+  p.amax = (b->tma && fast) ? b->d_amax : nullptr;
+  // absolute query-representation error of an f16 split (subnormal lo parts)
+  p.eps_abs = (b->dtype == GRM_B200_F16) ? 2.0e-7f * std::sqrt((float)b->dim) : 1.0e-30f;
   cudaStream_t saved = b->stream;
   b->stream = stream;  // every launch below goes to the caller's stream
   struct Restore {
@@ -1598,8 +1766,7 @@ int route_one(grm_b200_gqa_bank* b, const float* dq, int heads, int qt, int topk
     rc = cuda_status(cudaGetLastError());
   }
   if (rc) return b->err.set(rc, "GQA scan launch failed");
-  // eps_abs: absolute query-representation error of an f16 split (subnormal lo parts)
-  const float eps_abs = (b->dtype == GRM_B200_F16) ? 2.0e-7f * std::sqrt((float)b->dim) : 1.0e-30f;
+  const float eps_abs = p.eps_abs;
   const int nb_grid = (int)std::min<int64_t>(ceil_div64(b->nodes, kWarps), (int64_t)b->sms * 8);
   cudaError_t le =
       launch_chained(node_bounds_kernel, dim3(nb_grid), dim3(kThreads), 0, b->stream, p, eps_abs);
@@ -1659,7 +1826,7 @@ void bank_free(grm_b200_gqa_bank* b) {
   cudaSetDevice(b->device);
   if (b->stream) cudaStreamSynchronize(b->stream);
   if (b->owns_keys && b->d_keys) cudaFree(b->d_keys);
-  void* ptrs[] = {b->d_off, b->d_items, b->d_kmax, b->d_key_bad, b->d_headmax, b->d_lo, b->d_hi,
+  void* ptrs[] = {b->d_off, b->d_items, b->d_kmax, b->d_key_bad, b->d_headmax, b->d_amax, b->d_lo, b->d_hi,
                   b->d_cand, b->d_cand_count, b->d_frag, b->d_qnorm, b->d_qinfo, b->d_result,
                   b->d_queries, b->d_qparts, b->d_qcount, b->d_refined, b->d_qT};
   for (void* q : ptrs)

@@ -83,6 +83,43 @@ def test_random_ragged(sidecar, group, qt):
     bank.close()
 
 
+@pytest.mark.parametrize("group,qt", [(4, 1), (8, 1), (4, 4), (16, 1)])
+def test_refine_near_ties_and_overflowing_bound(sidecar, group, qt):
+    """Near ties: in two nodes every token of a kv head is one base row with a
+    single element nudged by one bf16 ulp, so the tokens' dots differ far
+    inside the approximate pass's error bound and only the exact dots can
+    order them (both scaled by 4, so that they rank in the top 16 and are
+    always refined).  Overflowing bound: one node scaled by 1e28, where |q||k|
+    exceeds the approximation's range and every token is refined exactly."""
+    kh, d = 8, 128
+    keys, off = _ragged(group * 7 + qt, 60, kh, d, 120)
+    T = np.diff(off).astype(np.int64)
+    rng = np.random.default_rng(group + qt)
+    for node in (5, 17):
+        t = int(T[node])
+        base = int(off[node]) * kh * d
+        blk = keys[base: base + t * kh * d].reshape(kh, t, d)
+        blk[:] = synth.bf16_bits(O.bf16_bits_to_f32(blk[:, :1, :]) * np.float32(4.0))
+        for h in range(kh):
+            for tok in range(1, t):
+                j = int(rng.integers(0, d))
+                bits = int(blk[h, tok, j])
+                if bits & 0x7FFF not in (0, 0x7F7F):
+                    blk[h, tok, j] = bits + int(rng.choice([-1, 1]))
+    big = 40
+    sl = slice(int(off[big]) * kh * d, int(off[big + 1]) * kh * d)
+    keys[sl] = synth.bf16_bits(O.bf16_bits_to_f32(keys[sl]) * np.float32(1e28))
+    bank = sidecar.create_bank_csr(keys, off, kh, d, dtype="bf16")
+    assert bank.paths() == {"fast": True, "tma": True}
+    qs = np.random.default_rng(qt).standard_normal((2, kh * group, qt, d), dtype=np.float32)
+    for k in (3, 16):
+        check(bank, keys, off, kh, d, qs, k)
+    ids, _ = raw_route(bank, qs, 16)
+    assert ids[:, 0].tolist() == [big, big]
+    assert all({5, 17} <= set(r.tolist()) for r in ids)
+    bank.close()
+
+
 def test_dim64_and_generic_dim(sidecar):
     for d in (64, 96):
         keys, off = _ragged(d, 40, 4, d, 60)
