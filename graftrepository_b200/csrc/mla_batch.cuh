@@ -18,7 +18,7 @@
 // scaled by 2^8 (no fp16 subnormals) and rounded to fp16, in the same K-major
 // swizzled layout; no separate prep kernel stands between two batches.
 //
-// Roles (one CTA per SM, persistent over 128-row tiles b, b + grid, ...):
+// Roles (one CTA per SM, persistent over the 128-row tiles it claims):
 //   warps 0..7         epilogue: warp w reads tensor-memory lanes 32*(w % 4)..
 //                      (32 queries, one per thread) and one quarter (32) of
 //                      the tile's 128 bank rows; each thread keeps its query's
@@ -67,6 +67,9 @@ constexpr float kBQScale = 256.0f;         // 2^8
 constexpr float kBMinNorm = 0.5f;          // smallest bank row norm the batch path accepts
 constexpr double kBSafeLo = 0.00390625;    // 2^-8: smaller query norms take the exact path
 constexpr uint32_t kBTmemCols = 2 * kBM;   // two accumulator buffers
+constexpr int kBSched = 4;                 // tile-id ring between the producer and the consumers
+constexpr int kBTail = 4;                  // last rounds of tiles claimed, not assigned
+constexpr int kBPub = 8;                   // entries a thread publishes per query at most
 
 template <int D>
 struct BLayout {
@@ -77,7 +80,6 @@ struct BLayout {
   static constexpr int kAtomQ = kBMq * 128;            // 16 KB: 128 query rows x 64 halves
   static constexpr int kStage = SA * kAtomT;
   static constexpr int kQ = KA * kAtomQ;
-  static constexpr int kMerge = kBQ * 4 * 32 * 8;      // end-of-scan list exchange
   // As many stages as fit beside the query image (1 KB alignment slack, 1 KB
   // for the static shared variables), leaving kBCoResident bytes so that the
   // previous batch's merge and resolve blocks fit on the SM beside this CTA
@@ -87,7 +89,6 @@ struct BLayout {
   static constexpr int kSmem = 1024 + kQ + kStages * kStage;  // + alignment slack
   static_assert(D % 64 == 0 && D <= 256, "batched dims: 64, 128, 256");
   static_assert(kStages >= 2 * SPT && kStages <= 16, "stage ring: two tiles at least");
-  static_assert(kMerge <= kStages * kStage, "the list exchange reuses the stages");
 };
 
 struct BatchParams {
@@ -258,30 +259,50 @@ __device__ __forceinline__ float pick32(const float (&v)[32], int c) {
 // q' = q / |q| (fp64 sum of squares, lane-strided then a butterfly, so every
 // CTA builds the same bits), scaled by 2^8 (no fp16 subnormals) and rounded to
 // fp16.  Rows of queries outside the safe range, and rows past the batch, are
-// zero.  Builder warp w of nw takes queries w, w + nw, ...; qsafe[j] records
-// whether query j is inside the batched path's safe range.
+// zero.  Builder warp w of nw takes queries w, w + nw, ...; the loads of
+// kGroup of them are issued together, so the build costs about one memory
+// latency instead of one per query (the stage ring covers only a few
+// microseconds of streaming).  qsafe[j] records whether query j is inside the
+// batched path's safe range.
 template <int D>
 __device__ __forceinline__ void build_query_image(const float* queries, int nq, unsigned char* img,
                                                   int* qsafe, int w, int nw, int lane) {
-  for (int j = w; j < kBQ; j += nw) {
-    bool safe = false;
-    float inv = 0.0f;
-    if (j < nq) {
-      const float* q = queries + (int64_t)j * D;
-      double acc = 0.0;
-      for (int d = lane; d < D; d += 32) acc = fma((double)q[d], (double)q[d], acc);
+  constexpr int kPer = D / 32;
+  constexpr int kGroup = kPer >= 8 ? 4 : 8;  // at most 32 values a lane in flight
+  for (int j0 = w; j0 < kBQ; j0 += nw * kGroup) {
+    float v[kGroup][kPer];
 #pragma unroll
-      for (int o = 16; o >= 1; o >>= 1) acc += __shfl_xor_sync(kFull, acc, o);
-      const double qn = sqrt(acc);
-      safe = isfinite(qn) && qn >= kBSafeLo && qn < kSafeHi;
-      inv = safe ? (float)(1.0 / qn) : 0.0f;
+    for (int g = 0; g < kGroup; ++g) {
+      const int j = j0 + g * nw;
+#pragma unroll
+      for (int i = 0; i < kPer; ++i)
+        v[g][i] = j < nq ? __ldg(queries + (int64_t)j * D + lane + 32 * i) : 0.0f;
     }
-    for (int d = lane; d < D; d += 32) {
-      const __half h = __float2half_rn(safe ? queries[(int64_t)j * D + d] * inv * kBQScale : 0.0f);
-      *reinterpret_cast<__half*>(img + qmat_offset(j, d)) = h;
-      *reinterpret_cast<__half*>(img + qmat_offset(kBQ + j, d)) = h;  // second copy
+#pragma unroll
+    for (int g = 0; g < kGroup; ++g) {
+      const int j = j0 + g * nw;
+      if (j >= kBQ) break;
+      bool safe = false;
+      float inv = 0.0f;
+      if (j < nq) {
+        double acc = 0.0;
+#pragma unroll
+        for (int i = 0; i < kPer; ++i) acc = fma((double)v[g][i], (double)v[g][i], acc);
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) acc += __shfl_xor_sync(kFull, acc, o);
+        const double qn = sqrt(acc);
+        safe = isfinite(qn) && qn >= kBSafeLo && qn < kSafeHi;
+        inv = safe ? (float)(1.0 / qn) : 0.0f;
+      }
+#pragma unroll
+      for (int i = 0; i < kPer; ++i) {
+        const int d = lane + 32 * i;
+        const __half h = __float2half_rn(safe ? v[g][i] * inv * kBQScale : 0.0f);
+        *reinterpret_cast<__half*>(img + qmat_offset(j, d)) = h;
+        *reinterpret_cast<__half*>(img + qmat_offset(kBQ + j, d)) = h;  // second copy
+      }
+      if (lane == 0) qsafe[j] = safe ? 1 : 0;
     }
-    if (lane == 0) qsafe[j] = safe ? 1 : 0;
   }
 }
 
@@ -305,15 +326,26 @@ __global__ void __launch_bounds__(kBThreads, 1)
   unsigned char* const smQ = sm;
   unsigned char* const smT = sm + LY::kQ;
   __shared__ __align__(8) uint64_t full[LY::kStages], empty[LY::kStages], tfull[2], tempty[2], bq_bar,
-      mma_done;
+      mma_done, sfull[kBSched], sempty[kBSched];
+  __shared__ int sh_tile[kBSched];
   __shared__ uint32_t sh_tmem;
   __shared__ int sh_fail;
   __shared__ unsigned sh_issued, sh_consumed;
   __shared__ int sh_qsafe[kBQ];
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t my_tiles =
-      (int64_t)blockIdx.x < p.tiles ? (p.tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  // Tiles: the CTA's first n_static tiles are its own (b, b + grid, ...);
+  // the last kBTail rounds and the remainder (from dyn0 on) are claimed: the
+  // producer takes the next one from the launch's counter (the chunk's first
+  // query header, next; the per-query merge of that query resets it once the
+  // scan has completed) as it needs one and passes its index (-1: none left)
+  // to the MMA issuer and the epilogue warps through the sh_tile ring.  A CTA
+  // that streams slowly or started late takes fewer of them, and the CTAs end
+  // their streams together.
+  Header* const sched = p.scratch.hdr(0);
+  const int64_t rounds = p.tiles / gridDim.x;
+  const int64_t n_static = rounds > kBTail ? rounds - kBTail : 0;
+  const int64_t dyn0 = n_static * gridDim.x;
   // epilogue warps 0..7: tensor-memory lane quarter lq holds queries
   // 32*(lq & 1) + lane (quarters 2, 3: the second copy); the warp takes the
   // tile's bank rows 32*cq .. 32*cq + 31
@@ -345,6 +377,10 @@ __global__ void __launch_bounds__(kBThreads, 1)
     mbar_init(&tempty[1], kBEpi);
     mbar_init(&bq_bar, kBEpi + 1);  // the image builders: warps 0..7 and the MMA warp
     mbar_init(&mma_done, 1);
+    for (int s = 0; s < kBSched; ++s) {
+      mbar_init(&sfull[s], 1);
+      mbar_init(&sempty[s], kBEpi + 1);  // the MMA issuer and the 8 epilogue warps
+    }
     sh_fail = 0;
     sh_issued = 0;
     sh_consumed = 0;
@@ -373,8 +409,30 @@ __global__ void __launch_bounds__(kBThreads, 1)
       int st = 0;
       unsigned ph = 0, issued = 0;
       bool ok = true;
-      for (int64_t i = 0; i < my_tiles && ok; ++i) {
-        const int y = (int)(((int64_t)blockIdx.x + i * gridDim.x) * kBM);
+      // each claim is made one tile ahead, so its round trip to L2 overlaps
+      // the waits for the stages of the tile before
+      auto claim = [&]() { return atomicAdd(&sched->next, 1u); };
+      unsigned c_next = n_static == 0 ? claim() : 0u;
+      for (int64_t i = 0; ok; ++i) {
+        int64_t t;
+        if (i < n_static) {
+          t = blockIdx.x + i * (int64_t)gridDim.x;
+          if (i + 1 == n_static) c_next = claim();
+        } else {
+          const int64_t j = i - n_static;
+          const int slot = (int)(j % kBSched);
+          if (!mbar_wait(&sempty[slot], ((unsigned)(j / kBSched) & 1u) ^ 1u, kWaitLimit)) {
+            ok = false;
+            break;
+          }
+          t = dyn0 + c_next;
+          const bool last = t >= p.tiles;
+          sh_tile[slot] = last ? -1 : (int)t;
+          mbar_arrive(&sfull[slot]);  // releases sh_tile[slot]
+          if (last) break;
+          c_next = claim();
+        }
+        const int y = (int)t * kBM;
         for (int sp = 0; sp < LY::SPT; ++sp) {
           if (!mbar_wait(&empty[st], ph ^ 1u, kWaitLimit)) {
             ok = false;
@@ -400,7 +458,18 @@ __global__ void __launch_bounds__(kBThreads, 1)
       bool ok = mbar_wait(&bq_bar, 0, kWaitLimit);
       int st = 0;
       unsigned ph = 0, consumed = 0;
-      for (int64_t i = 0; i < my_tiles && ok; ++i) {
+      for (int64_t i = 0; ok; ++i) {
+        if (i >= n_static) {  // a claimed tile, or none left
+          const int64_t j = i - n_static;
+          const int slot = (int)(j % kBSched);
+          if (!mbar_wait(&sfull[slot], (unsigned)(j / kBSched) & 1u, kWaitLimit)) {
+            ok = false;
+            break;
+          }
+          const int tile = sh_tile[slot];
+          mbar_arrive(&sempty[slot]);
+          if (tile < 0) break;
+        }
         const int b = (int)(i & 1);
         const unsigned u = (unsigned)(i >> 1);
         if (!mbar_wait(&tempty[b], (u & 1u) ^ 1u, kWaitLimit)) {
@@ -450,22 +519,48 @@ __global__ void __launch_bounds__(kBThreads, 1)
     // 2^-8 / norm of the warp's 32 rows of a tile, lane l holding row l (NaN
     // past the bank and for rows a route filter excludes: their scores never
     // reach a threshold), loaded one tile ahead.
-    auto load_rn = [&](int64_t i) -> float {
-      const int64_t r = ((int64_t)blockIdx.x + i * gridDim.x) * kBM + cq * 32 + lane;
-      return (i < my_tiles && r < p.nodes && policy::row_allowed(p.allow, r))
+    auto load_rn = [&](int tile) -> float {
+      const int64_t r = (int64_t)tile * kBM + cq * 32 + lane;
+      return (tile >= 0 && r < p.nodes && policy::row_allowed(p.allow, r))
                  ? __ldg(p.rnorms + r)
                  : __int_as_float(0x7FC00000);
     };
-    float rn = load_rn(0);
+    // the CTA's i-th tile index (-1: none left), from the producer's ring;
+    // false if the wait gave up
+    auto next_tile = [&](int64_t i, int& tile) -> bool {
+      if (i < n_static) {
+        tile = (int)(blockIdx.x + i * (int64_t)gridDim.x);
+        return true;
+      }
+      const int64_t j = i - n_static;
+      const int slot = (int)(j % kBSched);
+      if (!mbar_wait(&sfull[slot], (unsigned)(j / kBSched) & 1u, kWaitLimit)) return false;
+      tile = sh_tile[slot];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sempty[slot]);
+      return true;
+    };
+    int tile = -1;
+    if (!next_tile(0, tile)) {
+      if (lane == 0) atomicOr(&sh_fail, 1);
+      done_all = false;
+    }
+    float rn = load_rn(tile);
     // The query's header slot lb collects every CTA's k-th approximate score
     // (a lower bound of the final k-th best); it is read one tile ahead.
     int* const lbq = &p.scratch.hdr(active ? qi : 0)->lb;
     float kpub = -INFINITY;
-    for (int64_t i = 0; i < my_tiles; ++i) {
+    for (int64_t i = 0; tile >= 0; ++i) {
       const int b = (int)(i & 1);
       const unsigned u = (unsigned)(i >> 1);
-      const int64_t row0 = ((int64_t)blockIdx.x + i * gridDim.x) * kBM + cq * 32;
-      const float rn_next = load_rn(i + 1);
+      const int64_t row0 = (int64_t)tile * kBM + cq * 32;
+      int tile_next = -1;
+      if (!next_tile(i + 1, tile_next)) {
+        if (lane == 0) atomicOr(&sh_fail, 1);
+        done_all = false;
+        break;
+      }
+      const float rn_next = load_rn(tile_next);
       const int lb_next = active ? __ldcg(lbq) : kOrderedNegInf;
       if (!mbar_wait(&tfull[b], u & 1u, kWaitLimit)) {
         if (lane == 0) atomicOr(&sh_fail, 1);
@@ -520,20 +615,46 @@ __global__ void __launch_bounds__(kBThreads, 1)
       // every CTA's k-th score for this query bounds its final k-th from below
       if (lb_next != kOrderedNegInf) thr = fmaxf(thr, ordered_to_float(lb_next) - m2);
       rn = rn_next;
+      tile = tile_next;
     }
-    // This warp saw the last tile: every MMA has completed and every stage
-    // load was consumed, so the stage buffers are free for the list exchange.
+    // Publish this thread's list.  hdr->lb holds the best k-th score any
+    // thread has reached (each raised it to its own k-th while streaming): a
+    // lower bound of the final approximate k-th best, so entries below it
+    // minus 2 margins cannot reach the final top-k, and the rest (a prefix of
+    // the sorted list, at most kBPub) are appended.  A full list may have
+    // dropped rows below its last entry, and the cap drops the entries past
+    // kBPub: the largest such score goes to hdr->floor, which flags the exact
+    // fallback when it reaches the final threshold.
     if (done_all && active) {
-      Entry* e = reinterpret_cast<Entry*>(smT) + (qi * 4 + cq) * 32;
+      Header* const hdr = p.scratch.hdr(qi);
+      const int lbs = __ldcg(&hdr->lb);
+      const float wthr = lbs == kOrderedNegInf ? -INFINITY : ordered_to_float(lbs) - m2;
+      int c = 0;
 #pragma unroll
-      for (int j = 0; j < 32; ++j) e[j] = j < C ? Entry{L.s[j], L.id[j]} : Entry{-INFINITY, kNoRow};
+      for (int j = 0; j < C; ++j) c += (L.s[j] > -INFINITY && L.s[j] >= wthr) ? 1 : 0;
+      float floor = L.s[C - 1];
+      if constexpr (C > kBPub) {
+        if (c > kBPub) {
+          floor = fmaxf(floor, L.s[kBPub]);
+          c = kBPub;
+        }
+      }
+      if (floor > -INFINITY) atomicMax(&hdr->floor, float_to_ordered(floor));
+      if (c > 0) {
+        Entry* const out = p.scratch.entries(qi) + atomicAdd(&hdr->nent, (unsigned)c);
+#pragma unroll
+        for (int j = 0; j < (C < kBPub ? C : kBPub); ++j)
+          if (j < c) out[j] = Entry{L.s[j], L.id[j]};
+      }
     }
   }
-  asm volatile("griddepcontrol.wait;" ::: "memory");  // every thread, before the publish
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // every thread, before completing
   __syncwarp();
   __syncthreads();
   if (blockIdx.x == 0)  // the merge kernel reads the safe flags
     for (int j = threadIdx.x; j < p.nq; j += blockDim.x) p.scratch.hdr(j)->qsafe = sh_qsafe[j];
+  if (sh_fail)  // the merge reports the batch's queries as failed
+    for (int j = threadIdx.x; j < p.nq; j += blockDim.x) atomicOr(&p.scratch.hdr(j)->err, 1);
 
   // Teardown: every bulk load issued has landed, every MMA has completed.
   if (warp == kBProducerWarp && lane == 0 && sh_fail) {
@@ -546,67 +667,6 @@ __global__ void __launch_bounds__(kBThreads, 1)
     tmem_dealloc(tmem, kBTmemCols);
   }
   asm volatile("griddepcontrol.launch_dependents;");
-
-  // Per-query block lists: each query's four row-quarter lists were written to
-  // shared memory by the epilogue; one warp per query merges them and appends
-  // its entries as scan_finish does.
-  Entry* const mrg = reinterpret_cast<Entry*>(smT);
-  const bool failed = sh_fail != 0;
-  __shared__ int sh_cnt[kBQ];  // per query: published count | first slot << 8
-  for (int q = warp; q < p.nq; q += kBThreads / 32) {
-    Header* hdr = p.scratch.hdr(q);
-    if (failed) {
-      if (lane == 0) atomicOr(&hdr->err, 1);
-      continue;
-    }
-    const Entry* e = mrg + q * 4 * 32;
-    float kbest = -INFINITY, floor = -INFINITY;
-    int best = 0;
-#pragma unroll 1
-    for (int w = 0; w < 4; ++w) {
-      const float kw = e[w * 32 + p.topk - 1].s;
-      if (kw > kbest) {
-        kbest = kw;
-        best = w;
-      }
-      floor = fmaxf(floor, e[w * 32 + C - 1].s);
-    }
-    const int lb_seen = __ldcg(&hdr->lb);  // the best CTA k-th published so far
-    WarpList m;
-    m.s = e[best * 32 + lane].s;
-    m.id = e[best * 32 + lane].id;
-#pragma unroll 1
-    for (int w = 0; w < 4; ++w)
-      if (w != best)
-        m.offer_margin(e[w * 32 + lane].s, e[w * 32 + lane].id, lane, p.topk, 2.0f * kBMargin);
-    const float kth = __shfl_sync(kFull, m.s, p.topk - 1);
-    // Entries below (any CTA's k-th) - 2 margins cannot reach the final top-k:
-    // k rows score at least that k-th, so the final k-th approximate score is
-    // no lower.
-    const float kmax = lb_seen == kOrderedNegInf ? kth : fmaxf(kth, ordered_to_float(lb_seen));
-    const float wthr = isfinite(kmax) ? kmax - 2.0f * kBMargin : -INFINITY;
-    floor = fmaxf(floor, __shfl_sync(kFull, m.s, 31));
-    const int cnt = __popc(__ballot_sync(kFull, isfinite(m.s) && m.s >= wthr));
-    if (lane == 0) {  // fire-and-forget reductions
-      if (isfinite(kth)) atomicMax(&hdr->lb, float_to_ordered(kth));
-      if (isfinite(floor)) atomicMax(&hdr->floor, float_to_ordered(floor));
-      sh_cnt[q] = cnt;
-    }
-    Entry* const out = reinterpret_cast<Entry*>(smT) + q * 4 * 32;  // this warp's own rows
-    out[lane] = Entry{m.s, m.id};  // sorted: the first cnt are the published ones
-  }
-  // One returning atomic per query, all of them in flight together (a warp
-  // taking its queries' slots one after another would wait out a round trip
-  // to L2 per query), then the appends.
-  __syncthreads();
-  if (!failed && (int)threadIdx.x < p.nq && sh_cnt[threadIdx.x] > 0)
-    sh_cnt[threadIdx.x] |= (int)(atomicAdd(&p.scratch.hdr(threadIdx.x)->nent,
-                                           (unsigned)sh_cnt[threadIdx.x]) << 8);
-  __syncthreads();
-  for (int q = warp; q < p.nq && !failed; q += kBThreads / 32) {
-    const int c = sh_cnt[q] & 0xFF, at = sh_cnt[q] >> 8;
-    if (lane < c) p.scratch.entries(q)[at + lane] = mrg[q * 4 * 32 + lane];
-  }
 }
 
 // One block per query of the batch: the final merge and exact refine of
@@ -637,7 +697,8 @@ __global__ void __launch_bounds__(kBMergeWarps * 32)
   if (warp == kBMergeWarps - 1 && lane == 0) fsm.qn = query_norm_seq_t<D>(fsm.qraw);
   asm volatile("griddepcontrol.wait;" ::: "memory");
   const bool safe = __ldcg(&p.scratch.hdr(q)->qsafe) != 0;
-  final_merge<D, __half, false, kBMergeWarps, true>(p, q, kBMargin, safe, lane, warp, fsm);
+  final_merge<D, __half, false, kBMergeWarps, true, false, true>(p, q, kBMargin, safe, lane, warp,
+                                                                  fsm);
 }
 
 }  // namespace mla

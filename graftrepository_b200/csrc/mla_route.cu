@@ -371,8 +371,13 @@ constexpr int kSelR = 4;  // candidates per lane in the final selection (128 per
 // fallback kernel is flagged instead.  QREADY: the caller already filled
 // sm.qd and sm.qn (warp NW-1 then only waits at the barriers).  PRE: every
 // appended entry already carries its exact score (p.scratch.exact), computed
-// by the block that published it, so no row is read here.
-template <int D, typename T, bool INL, int NW, bool QREADY = false, bool PRE = false>
+// by the block that published it, so no row is read here.  KLB: the filter
+// threshold is raised to the k-th best of the first NW * 32 * kSelR entries
+// (each warp takes 32 * kSelR of them; the k-th best of any subset is no
+// higher than the k-th best of all) minus 2*margin, for publishers whose lb
+// is far below the final k-th.
+template <int D, typename T, bool INL, int NW, bool QREADY = false, bool PRE = false,
+          bool KLB = false>
 __device__ __forceinline__ void final_merge(const Params<T>& p, int q, float margin, bool safe,
                                             int lane, int warp, FinishSmem<NW, D>& sm) {
   static_assert(NW >= 2, "final_merge needs two warps");
@@ -380,12 +385,40 @@ __device__ __forceinline__ void final_merge(const Params<T>& p, int q, float mar
   if (threadIdx.x == 0) sm.ncand = 0;
   __syncthreads();
   const int lb = __ldcg(&hdr->lb);
-  const float fthr = lb == kOrderedNegInf ? -INFINITY : ordered_to_float(lb) - 2.0f * margin;
+  float fthr = lb == kOrderedNegInf ? -INFINITY : ordered_to_float(lb) - 2.0f * margin;
   const int nent = min((int)__ldcg(&hdr->nent), p.scratch.blocks * 32);
   const int fl = __ldcg(&hdr->floor);
   const bool failed = __ldcg(&hdr->err) != 0;
   const uint2* ents = reinterpret_cast<const uint2*>(p.scratch.entries(q));
   const float* exs = p.scratch.exact(q);
+  if constexpr (KLB) {
+    float w[kSelR];
+    uint32_t wid[kSelR];
+#pragma unroll
+    for (int r = 0; r < kSelR; ++r) {
+      const int i = (warp * kSelR + r) * 32 + lane;
+      const uint2 e = i < nent ? __ldcg(ents + i) : make_uint2(__float_as_uint(-INFINITY), kNoRow);
+      w[r] = __uint_as_float(e.x);
+      wid[r] = e.y;
+    }
+    float kth = -INFINITY;
+#pragma unroll 1
+    for (int t = 0; t < p.topk; ++t) {
+      float bs;
+      uint32_t bid;
+      warp_best<kSelR>(w, wid, bs, bid);
+      kth = bs;
+#pragma unroll
+      for (int r = 0; r < kSelR; ++r)
+        if (wid[r] == bid && w[r] == bs) w[r] = -INFINITY;
+    }
+    if (lane == 0) sm.kth[warp] = kth;
+    __syncthreads();
+    float kb = -INFINITY;
+#pragma unroll 1
+    for (int j = 0; j < NW; ++j) kb = fmaxf(kb, sm.kth[j]);
+    if (kb > -INFINITY) fthr = fmaxf(fthr, kb - 2.0f * margin);
+  }
   if (warp == NW - 1 && !PRE) {
     if constexpr (!QREADY && !PRE) {
       for (int d = lane; d < D; d += 32) sm.qd[d] = (double)sm.qraw[d];
@@ -1427,8 +1460,14 @@ __device__ __forceinline__ void exact_one(const Params<T>& p, int q, int lane, i
 // kUnsafe (all of them under force_all); queries with kOk (or kError) cost
 // nothing more.  D == 0 means runtime dim (force_all only).  INL: row norms
 // computed inline (see mla_scan_kernel).
+//
+// At most 64 registers a thread (16K a block): the resolve blocks of one
+// route wait, resident, beside the per-query merge blocks of a batched route
+// while the next route's scan CTAs start on the same SMs as the previous
+// scan's CTAs exit, and the three must fit one register file (a scan CTA
+// 33K, a merge block 12K).  The exact pass itself is the rare path.
 template <int D, typename T, bool INL = false>
-__global__ void __launch_bounds__(kThreads) mla_exact_kernel(const __grid_constant__ Params<T> p) {
+__global__ void __launch_bounds__(kThreads, 4) mla_exact_kernel(const __grid_constant__ Params<T> p) {
   __shared__ ExactSmem<D> sm;
   // Launched with programmatic dependent launch after the scan.  Every block
   // of this grid is resident once it reaches the trigger, so the next route's
