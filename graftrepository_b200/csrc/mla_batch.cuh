@@ -697,8 +697,8 @@ __global__ void __launch_bounds__(kBMergeWarps * 32)
   if (warp == kBMergeWarps - 1 && lane == 0) fsm.qn = query_norm_seq_t<D>(fsm.qraw);
   asm volatile("griddepcontrol.wait;" ::: "memory");
   const bool safe = __ldcg(&p.scratch.hdr(q)->qsafe) != 0;
-  final_merge<D, __half, false, kBMergeWarps, true, false, true>(p, q, kBMargin, safe, lane, warp,
-                                                                  fsm);
+  final_merge<D, __half, false, kBMergeWarps, true, false, true, true>(p, q, kBMargin, safe, lane,
+                                                                        warp, fsm);
 }
 
 }  // namespace mla

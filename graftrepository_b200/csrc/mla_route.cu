@@ -375,9 +375,12 @@ constexpr int kSelR = 4;  // candidates per lane in the final selection (128 per
 // threshold is raised to the k-th best of the first NW * 32 * kSelR entries
 // (each warp takes 32 * kSelR of them; the k-th best of any subset is no
 // higher than the k-th best of all) minus 2*margin, for publishers whose lb
-// is far below the final k-th.
+// is far below the final k-th.  XALL: warps 1.. compute the exact scores of
+// the filtered entries (one per lane) while warp 0 selects, so the refine's
+// sequential fp64 dots run beside the selection; the selection then goes as
+// under PRE.
 template <int D, typename T, bool INL, int NW, bool QREADY = false, bool PRE = false,
-          bool KLB = false>
+          bool KLB = false, bool XALL = false>
 __device__ __forceinline__ void final_merge(const Params<T>& p, int q, float margin, bool safe,
                                             int lane, int warp, FinishSmem<NW, D>& sm) {
   static_assert(NW >= 2, "final_merge needs two warps");
@@ -468,7 +471,23 @@ __device__ __forceinline__ void final_merge(const Params<T>& p, int q, float mar
     }
     __syncthreads();
   }
-  if (warp != 0) return;
+  constexpr bool HAVE_EX = PRE || XALL;
+  // XALL: the exact scores are handed to warp 0 through named barrier 1
+  // (every warp arrives once: warps 1.. after their dots, warp 0 after its
+  // selection)
+  if (warp != 0) {
+    if constexpr (XALL) {
+      static_assert(!PRE && NW >= 2, "XALL computes what PRE reads");
+      if (safe && !failed)
+        for (int i = (warp - 1) * 32 + lane; i < n; i += (NW - 1) * 32) {
+          const uint32_t id = sm.id[i];
+          sm.ex[i] = exact_score_tail<D, T, INL>(p.rows + (int64_t)id * D, sm.qd, sm.qn,
+                                                 INL ? 0.0f : __ldg(p.norms + id));
+        }
+      asm volatile("bar.sync 1, %0;" ::"r"(NW * 32) : "memory");
+    }
+    return;
+  }
   const int m = min(n, 32 * kSelR);
   float v[kSelR], w[kSelR], xr[kSelR];
   uint32_t vid[kSelR];
@@ -491,6 +510,14 @@ __device__ __forceinline__ void final_merge(const Params<T>& p, int q, float mar
 #pragma unroll
     for (int r = 0; r < kSelR; ++r)
       if (vid[r] == bid && w[r] == bs) w[r] = -INFINITY;
+  }
+  if constexpr (XALL) {  // the other warps' exact scores are in sm.ex
+    asm volatile("bar.sync 1, %0;" ::"r"(NW * 32) : "memory");
+#pragma unroll
+    for (int r = 0; r < kSelR; ++r) {
+      const int i = r * 32 + lane;
+      xr[r] = i < m ? sm.ex[i] : -INFINITY;
+    }
   }
   float thr = isfinite(T_k) ? T_k - 2.0f * margin : -INFINITY;
   int above = 0;
@@ -533,7 +560,7 @@ __device__ __forceinline__ void final_merge(const Params<T>& p, int q, float mar
       const int pos = base + __popc(bal & ((1u << lane) - 1u));
       sm.s[pos] = v[r];
       sm.id[pos] = vid[r];
-      if constexpr (PRE) sm.ex[pos] = xr[r];
+      if constexpr (HAVE_EX) sm.ex[pos] = xr[r];
     }
     base += __popc(bal);
   }
@@ -542,7 +569,7 @@ __device__ __forceinline__ void final_merge(const Params<T>& p, int q, float mar
   const uint32_t ci = lane < base ? sm.id[lane] : kNoRow;
   float es = -INFINITY;
   if (isfinite(cs)) {
-    if constexpr (PRE) {
+    if constexpr (HAVE_EX) {
       es = sm.ex[lane];
     } else {
       es = exact_score_tail<D, T, INL>(p.rows + (int64_t)ci * D, sm.qd, sm.qn,
