@@ -695,18 +695,33 @@ __global__ void node_bounds_kernel(RouteParams p, float eps_abs) {
     const int64_t T = (int64_t)(p.off[node + 1] - p.off[node]);
     float sum = 0.0f, err = 0.0f;
     bool forced = !fast;
-    for (int h = lane; h < p.heads; h += 32) {
-      unsigned* slot = p.headmax + node * p.heads + h;
-      const float b = __uint_as_float(*slot);
-      *slot = 0u;
-      if (p.amax) p.amax[node * p.heads + h] = b;
-      const float km = p.kmax[node * p.kh_n + h / p.group];
-      const float qn = p.qnorm_h[h];
-      const float mag = qn * km;
-      if (!(mag < kHuge)) forced = true;
-      sum += b;
-      err = fmaf(kEps * p.inv_denom, mag, err);
-      err = fmaf(eps_abs * p.inv_denom, km, err);
+    // heads lane, lane + 32, ... in order; the loads of up to eight of them
+    // are issued together before any is used
+    constexpr int kHB = 8;
+    for (int h0 = lane; h0 < p.heads; h0 += 32 * kHB) {
+      float bv[kHB], kmv[kHB], qnv[kHB];
+#pragma unroll
+      for (int j = 0; j < kHB; ++j) {
+        const int h = h0 + 32 * j;
+        bv[j] = kmv[j] = qnv[j] = 0.0f;
+        if (h < p.heads) {
+          bv[j] = __uint_as_float(p.headmax[node * p.heads + h]);
+          kmv[j] = p.kmax[node * p.kh_n + h / p.group];
+          qnv[j] = p.qnorm_h[h];
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < kHB; ++j) {
+        const int h = h0 + 32 * j;
+        if (h >= p.heads) break;
+        p.headmax[node * p.heads + h] = 0u;
+        if (p.amax) p.amax[node * p.heads + h] = bv[j];
+        const float mag = qnv[j] * kmv[j];
+        if (!(mag < kHuge)) forced = true;
+        sum += bv[j];
+        err = fmaf(kEps * p.inv_denom, mag, err);
+        err = fmaf(eps_abs * p.inv_denom, kmv[j], err);
+      }
     }
 #pragma unroll
     for (int o = 16; o >= 1; o >>= 1) {
@@ -1328,15 +1343,27 @@ __global__ void finalize_kernel(RouteParams p) {
     for (int h0 = 0; h0 < p.heads; h0 += 64) {
       const int hn = min(64, p.heads - h0);
       __syncwarp();
-      for (int c = 0; c < nc; ++c) {
-        unsigned* bc = p.headmax + (int64_t)(base + c) * p.heads + h0;
-        if (lane < hn) {
-          sh_best[c][lane] = __uint_as_float(bc[lane]);
-          bc[lane] = 0u;
+      // eight candidates' loads in flight at a time, then their stores
+      for (int c0 = 0; c0 < nc; c0 += 8) {
+        unsigned a[8], b[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const unsigned* bc = p.headmax + (int64_t)(base + c0 + j) * p.heads + h0;
+          a[j] = (c0 + j < nc && lane < hn) ? bc[lane] : 0u;
+          b[j] = (c0 + j < nc && lane + 32 < hn) ? bc[lane + 32] : 0u;
         }
-        if (lane + 32 < hn) {
-          sh_best[c][lane + 32] = __uint_as_float(bc[lane + 32]);
-          bc[lane + 32] = 0u;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (c0 + j >= nc) break;
+          unsigned* bc = p.headmax + (int64_t)(base + c0 + j) * p.heads + h0;
+          if (lane < hn) {
+            sh_best[c0 + j][lane] = __uint_as_float(a[j]);
+            bc[lane] = 0u;
+          }
+          if (lane + 32 < hn) {
+            sh_best[c0 + j][lane + 32] = __uint_as_float(b[j]);
+            bc[lane + 32] = 0u;
+          }
         }
       }
       __syncwarp();
