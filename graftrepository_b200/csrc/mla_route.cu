@@ -394,14 +394,32 @@ __device__ __forceinline__ void final_merge(const Params<T>& p, int q, float mar
   const bool failed = __ldcg(&hdr->err) != 0;
   const uint2* ents = reinterpret_cast<const uint2*>(p.scratch.entries(q));
   const float* exs = p.scratch.exact(q);
+  // one filtered entry: into the shared list, its row prefetched
+  auto keep = [&](float es, uint32_t id, int i) {
+    const int slot = atomicAdd(&sm.ncand, 1);
+    if (slot < NW * 32) {
+      sm.s[slot] = es;
+      sm.id[slot] = id;
+      if constexpr (PRE) sm.ex[slot] = __ldcg(exs + i);
+    }
+    if constexpr (!PRE) {
+      const char* rb = reinterpret_cast<const char*>(p.rows + (int64_t)id * D);
+#pragma unroll 1
+      for (int o = 0; o < D * (int)sizeof(T); o += 128)
+        asm volatile("prefetch.global.L1 [%0];" ::"l"(rb + o));
+    }
+  };
+  // KLB: the first NW * 32 * kSelR entries are filtered from the registers
+  // that found the bound; the strided loop below takes the rest
+  int first = 0;
   if constexpr (KLB) {
-    float w[kSelR];
+    float w[kSelR], e0[kSelR];
     uint32_t wid[kSelR];
 #pragma unroll
     for (int r = 0; r < kSelR; ++r) {
       const int i = (warp * kSelR + r) * 32 + lane;
       const uint2 e = i < nent ? __ldcg(ents + i) : make_uint2(__float_as_uint(-INFINITY), kNoRow);
-      w[r] = __uint_as_float(e.x);
+      w[r] = e0[r] = __uint_as_float(e.x);
       wid[r] = e.y;
     }
     float kth = -INFINITY;
@@ -421,6 +439,12 @@ __device__ __forceinline__ void final_merge(const Params<T>& p, int q, float mar
 #pragma unroll 1
     for (int j = 0; j < NW; ++j) kb = fmaxf(kb, sm.kth[j]);
     if (kb > -INFINITY) fthr = fmaxf(fthr, kb - 2.0f * margin);
+#pragma unroll
+    for (int r = 0; r < kSelR; ++r) {
+      const int i = (warp * kSelR + r) * 32 + lane;
+      if (i < nent && e0[r] >= fthr) keep(e0[r], wid[r], i);
+    }
+    first = NW * 32 * kSelR;
   }
   if (warp == NW - 1 && !PRE) {
     if constexpr (!QREADY && !PRE) {
@@ -430,23 +454,10 @@ __device__ __forceinline__ void final_merge(const Params<T>& p, int q, float mar
   } else {
     constexpr int FW = PRE ? NW : NW - 1;  // filtering warps
 #pragma unroll 2
-    for (int i = threadIdx.x; i < nent; i += FW * 32) {
+    for (int i = first + threadIdx.x; i < nent; i += FW * 32) {
       const uint2 e = __ldcg(ents + i);
       const float es = __uint_as_float(e.x);
-      if (es >= fthr) {
-        const int slot = atomicAdd(&sm.ncand, 1);
-        if (slot < NW * 32) {
-          sm.s[slot] = es;
-          sm.id[slot] = e.y;
-          if constexpr (PRE) sm.ex[slot] = __ldcg(exs + i);
-        }
-        if constexpr (!PRE) {
-          const char* rb = reinterpret_cast<const char*>(p.rows + (int64_t)e.y * D);
-#pragma unroll 1
-          for (int o = 0; o < D * (int)sizeof(T); o += 128)
-            asm volatile("prefetch.global.L1 [%0];" ::"l"(rb + o));
-        }
-      }
+      if (es >= fthr) keep(es, e.y, i);
     }
   }
   __syncthreads();
